@@ -1,0 +1,164 @@
+/*
+ * nkimoe.h — C ABI of the B200 (sm_100a) Qwen3-MoE token-generation megakernel.
+ *
+ * Plain pointers and sizes only; every pointer named "device" is CUDA device memory owned
+ * by the caller.  No entry point allocates device memory: the caller sizes and passes the
+ * workspace (nkm_qwen3_workspace_bytes).  All bf16 tensors are row-major unless the name
+ * ends in _ft ("fragment-tiled", produced by nkm_pack_ft).
+ *
+ * Each entry point names the reference interface it replaces (paths inside the reference
+ * project KevGomes1403/nki-moe-megakernel).
+ */
+#ifndef NKIMOE_H_
+#define NKIMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (return values and the device status word). */
+#define NKM_OK 0
+#define NKM_ERR_ARG 1          /* bad argument / unsupported shape (host-side check) */
+#define NKM_ERR_CUDA 2         /* a CUDA runtime call failed */
+#define NKM_ERR_TIMEOUT 4      /* a grid barrier or copy wait gave up (device) */
+#define NKM_ERR_INDEX 8        /* a block id or expert id was out of range (device) */
+
+typedef struct CUstream_st* nkm_stream_t; /* == cudaStream_t */
+
+/* Per-layer weights (device pointers, bf16).  Replaces the per-layer argument lists
+ * Wq/Wk/Wv/Wo/qn/kn/gpre/gpost/router/gate_up/down of
+ * megakernels/qwen3_moe/transformer_qwen.py:68-90 (gathered in
+ * megakernels/qwen3_moe/qwen_with_megakernel.py:376-408). */
+typedef struct nkm_qwen3_layer {
+  const void* wqkv_ft;  /* [(nq+2*nkv)*128, H]  rows: q heads, k heads, v heads       */
+  const void* wo_ft;    /* [H, nq*128]                                               */
+  const void* q_norm;   /* [128]                                                     */
+  const void* k_norm;   /* [128]                                                     */
+  const void* ln1;      /* [H] input_layernorm                                       */
+  const void* ln2;      /* [H] post_attention_layernorm                              */
+  const void* router;   /* [E, H] (plain row-major)                                  */
+  const void* w13_ft;   /* [E][2I, H]  gate/up, packed with NKM_PACK_GATE_UP          */
+  const void* w2_ft;    /* [E][H, I]   down                                          */
+  const float* router_bias; /* [E] fp32 added to the router logits, or NULL            */
+} nkm_qwen3_layer;
+
+/* Model description.  Replaces the NxDI model + config objects
+ * (qwen_with_megakernel.py:102-132, 601-695). */
+typedef struct nkm_qwen3_desc {
+  int32_t hidden;       /* H (multiple of 256)                   2048   */
+  int32_t n_q_heads;    /* query heads held by this GPU           32    */
+  int32_t n_kv_heads;   /* kv heads held by this GPU              4     */
+  int32_t head_dim;     /* must be 128                            128   */
+  int32_t n_experts;    /* E (<= 256)                             128   */
+  int32_t top_k;        /* K (<= 8)                               8     */
+  int32_t moe_inter;    /* I (multiple of 32)                     768   */
+  int32_t n_layers;     /* L                                      48    */
+  int32_t vocab;        /* V (multiple of 16), 0 = no LM head     151936*/
+  float rms_eps;        /*                                        1e-6  */
+  const nkm_qwen3_layer* layers; /* host array of n_layers entries      */
+  const void* final_norm;        /* [H] bf16 (may be NULL if vocab==0)  */
+  const void* lm_head_ft;        /* [V, H] bf16 fragment-tiled          */
+  const void* embed;             /* [V, H] bf16 row-major (may be NULL) */
+  const void* rope_cos;          /* [rope_max_pos, 128] bf16            */
+  const void* rope_sin;          /* [rope_max_pos, 128] bf16            */
+  int32_t rope_max_pos;
+  void* k_pool;   /* [L][num_blocks][n_kv_heads][block_size][128] bf16, mutated in place */
+  void* v_pool;   /* same shape as k_pool                                                */
+  int32_t num_blocks;
+  int32_t block_size;  /* must be 128 */
+  int32_t max_batch;   /* largest batch any step will use (<= 32)                         */
+} nkm_qwen3_desc;
+
+typedef struct nkm_qwen3 nkm_qwen3; /* opaque handle (host memory only) */
+
+/* Stage bits for nkm_qwen3_step.stages. */
+#define NKM_STAGE_ATTN 1    /* RMSNorm(ln1)+QKV+q/k-norm+RoPE+KV write+attention+O-proj */
+#define NKM_STAGE_MOE 2     /* RMSNorm(ln2)+router top-k+expert SwiGLU                  */
+#define NKM_STAGE_LMHEAD 4  /* final RMSNorm + LM head (after the last layer run)       */
+
+/* One decode step.  Replaces the kernel call
+ *   get_multilayer_kernel_jit(L)[2](X, *W..., *K_caches, *V_caches, cos, sin, position_ids)
+ * -> (Y, *K_out, *V_out)   (transformer_qwen.py:420-505, call site
+ * qwen_with_megakernel.py:465-473).  K/V are written in place at positions[b]. */
+typedef struct nkm_qwen3_step {
+  int32_t batch;               /* B (1..max_batch)                                        */
+  const int32_t* input_ids;    /* device [B]; if NULL x_in is used                          */
+  const void* x_in;            /* device bf16 [B, H] hidden input (embeddings)              */
+  const int32_t* positions;    /* device [B]: cache slot of the new token = prior length    */
+  const int32_t* block_table;  /* device [B, max_blocks_per_seq]; entry < 0 at the write
+                                  slot skips the K/V write (reference uint32_max skip)      */
+  int32_t max_blocks_per_seq;
+  void* y_out;                 /* device bf16 [B, H]: hidden after the last layer run
+                                  (pre final norm), or the block output for block calls    */
+  float* logits_out;           /* device fp32 [B, V] or NULL (LM head skipped)              */
+  int32_t first_layer;         /* layer range to run: [first_layer, first_layer+num_layers) */
+  int32_t num_layers;          /* 0 = all layers                                            */
+  int32_t stages;              /* NKM_STAGE_* bits; 0 = ATTN|MOE|LMHEAD                      */
+  int32_t residual;            /* 1 = blocks add into the residual stream (decoder layer);
+                                  0 = a single-block call returns the block output only    */
+  /* optional traces (device, NULL to skip), indexed [layer - first_layer] */
+  int32_t* trace_topk_idx;     /* [nl, B, K]                                              */
+  float* trace_topk_w;         /* [nl, B, K] renormalised affinities                      */
+  float* trace_router_logits;  /* [nl, B, E]                                              */
+  void* trace_qkv;             /* bf16 [nl, B, (nq+2nkv)*128] raw projections             */
+  void* trace_resid_mid;       /* bf16 [nl, B, H] after attention + residual              */
+  void* trace_resid_out;       /* bf16 [nl, B, H] after MoE + residual                    */
+} nkm_qwen3_step;
+
+/* Bytes of device workspace a handle needs (caller allocates, 256-byte aligned). */
+size_t nkm_qwen3_workspace_bytes(const nkm_qwen3_desc* desc);
+
+/* Validate the description, lay out the workspace, copy the layer pointer table into it
+ * and encode the K/V tensor maps.  Replaces compile()/load() of the NxDI model
+ * (qwen_with_megakernel.py:601-695).  The calling thread's current device is used. */
+int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspace_bytes,
+                     nkm_qwen3** out);
+void nkm_qwen3_destroy(nkm_qwen3* h);
+
+/* Enqueue one decode step (exactly one cooperative kernel launch, nothing else) on `stream`.
+ * Host-side checks return NKM_ERR_ARG/NKM_ERR_CUDA; device-side errors are reported by
+ * nkm_qwen3_status.  Steps on one handle must not overlap (they share the workspace). */
+int nkm_qwen3_decode_step(nkm_qwen3* h, const nkm_qwen3_step* step, nkm_stream_t stream);
+
+/* Synchronise `stream` and return the device status word (0 = ok).  Device errors are
+ * sticky: they accumulate over steps until this call reads and clears them (a step that
+ * starts while a fatal error is recorded returns at its first barrier). */
+int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream);
+
+/* Single fused attention block on layer `layer` (residual=0: returns the O-projection
+ * output only).  Replaces attn_fused_qwen (megakernels/qwen3_moe/attn_fused_nki.py:50) and
+ * attention_block_tkg (nki_kernels/attention/attention_block_tkg.py:83). */
+int nkm_qwen3_attention_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* step,
+                              nkm_stream_t stream);
+
+/* Single fused MoE block (RMSNorm(ln2) + router top-k + selective-expert SwiGLU) on layer
+ * `layer`.  Replaces _qwen3_moe_sbuf_in_sbuf_out_hoisted / qwen3_moe_fused_tkg_sbuf_io
+ * (megakernels/qwen3_moe/moe_fused_nki.py:769-997) and the primitive pair router_topk +
+ * moe_tkg (nki_kernels/moe/router_topk.py:69, nki_kernels/moe/moe_tkg.py:56). */
+int nkm_qwen3_moe_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* step,
+                        nkm_stream_t stream);
+
+/* Weight layout converter (load time).  src: row-major bf16 [R, K]; dst: fragment-tiled
+ * bf16 of the same size.  mode NKM_PACK_PLAIN keeps row order; NKM_PACK_GATE_UP takes the
+ * Hugging Face experts gate_up [2I, K] (gate rows then up rows) and interleaves 8 gate rows
+ * with the matching 8 up rows in every 16-row strip.  `count` matrices of the same shape
+ * are converted back to back.  Replaces the HF->kernel converters
+ * qwen_with_megakernel.py:171-271. */
+#define NKM_PACK_PLAIN 0
+#define NKM_PACK_GATE_UP 1
+int nkm_pack_ft(const void* src, void* dst, int64_t rows, int64_t cols, int64_t count,
+                int32_t mode, nkm_stream_t stream);
+
+/* Message for the last error returned on this thread ("" if none). */
+const char* nkm_last_error(void);
+
+/* Library version string. */
+const char* nkm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NKIMOE_H_ */

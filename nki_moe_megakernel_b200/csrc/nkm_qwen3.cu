@@ -1,0 +1,380 @@
+// Host side of the C ABI declared in include/nkimoe.h: argument checks, workspace layout,
+// K/V tensor-map encoding, the cooperative launch of the decode kernel and the weight
+// packer.  No entry point allocates device memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <algorithm>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "nkimoe.h"
+#include "nkm_qwen3_kernel.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define NKM_CUDA(call)                                                                         \
+  do {                                                                                         \
+    cudaError_t e_ = (call);                                                                   \
+    if (e_ != cudaSuccess) return fail(NKM_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
+
+// Workspace layout (offsets in bytes from the workspace base).
+struct WsLayout {
+  size_t ctrl, ctrl_bytes;  // bar, status, strip/attn/row counters (zeroed every step)
+  size_t bar, status, strip_cnt, attn_cnt, row_cnt;
+  size_t layers, resid, qkv, attn_out, att_part, rlogits, hbuf, ypair, gpart;
+  size_t total;
+};
+
+constexpr int kMaxStrips = 16384;
+
+WsLayout layout_ws(const nkm_qwen3_desc& d, int num_sms) {
+  WsLayout w{};
+  const size_t Tm = static_cast<size_t>(d.max_batch);
+  const size_t NW = static_cast<size_t>(num_sms) * nkm::kWarps;
+  const size_t R = static_cast<size_t>(d.n_q_heads + 2 * d.n_kv_heads) * d.head_dim;
+  size_t o = 0;
+  w.ctrl = o;
+  w.bar = o;
+  w.status = o + 16;  // bar[0] = arrival count, bar[1] = generation
+  w.strip_cnt = o + 256;
+  w.attn_cnt = w.strip_cnt + kMaxStrips * 4;
+  w.row_cnt = w.attn_cnt + align_up(Tm * d.n_kv_heads * 4);
+  w.ctrl_bytes = align_up(w.row_cnt - o + static_cast<size_t>(d.hidden / 16) * 4);
+  o = align_up(o + w.ctrl_bytes);
+  w.layers = o;
+  o = align_up(o + sizeof(nkm::LayerPtrs) * d.n_layers);
+  w.resid = o;
+  o = align_up(o + Tm * d.hidden * 2);
+  w.qkv = o;
+  o = align_up(o + Tm * R * 2);
+  w.attn_out = o;
+  o = align_up(o + Tm * d.n_q_heads * d.head_dim * 2);
+  w.att_part = o;
+  o = align_up(o + (NW + Tm * d.n_kv_heads) * nkm::kPartFloats * 4);
+  w.rlogits = o;
+  o = align_up(o + Tm * d.n_experts * 4);
+  w.hbuf = o;
+  o = align_up(o + Tm * d.top_k * d.moe_inter * 2);
+  w.ypair = o;
+  o = align_up(o + Tm * d.top_k * d.hidden * 4);
+  w.gpart = o;
+  o = align_up(o + NW * 2 * 4 * 32 * 4 * 4);
+  w.total = o;
+  return w;
+}
+
+int nt_for_batch(int T) { return T <= 8 ? 1 : (T <= 16 ? 2 : 4); }
+
+int check_desc(const nkm_qwen3_desc* d) {
+  if (!d) return fail(NKM_ERR_ARG, "desc is NULL");
+  if (d->head_dim != nkm::kHeadDim) return fail(NKM_ERR_ARG, "head_dim must be 128 (got %d)", d->head_dim);
+  if (d->hidden <= 0 || d->hidden % 256) return fail(NKM_ERR_ARG, "hidden must be a positive multiple of 256");
+  if (d->n_kv_heads <= 0 || d->n_q_heads <= 0 || d->n_q_heads % d->n_kv_heads)
+    return fail(NKM_ERR_ARG, "n_q_heads must be a positive multiple of n_kv_heads");
+  if (d->n_q_heads / d->n_kv_heads > nkm::kAttRows)
+    return fail(NKM_ERR_ARG, "at most %d query heads per kv head", nkm::kAttRows);
+  if (d->n_experts <= 0 || d->n_experts > nkm::kMaxExperts) return fail(NKM_ERR_ARG, "n_experts must be in 1..256");
+  if (d->top_k <= 0 || d->top_k > 8 || d->top_k > d->n_experts) return fail(NKM_ERR_ARG, "top_k must be in 1..8");
+  if (d->moe_inter <= 0 || d->moe_inter % 32) return fail(NKM_ERR_ARG, "moe_inter must be a multiple of 32");
+  if (d->n_layers <= 0 || !d->layers) return fail(NKM_ERR_ARG, "n_layers/layers invalid");
+  if (d->vocab < 0 || d->vocab % 16) return fail(NKM_ERR_ARG, "vocab must be a multiple of 16");
+  if (d->max_batch <= 0 || d->max_batch > 32) return fail(NKM_ERR_ARG, "max_batch must be in 1..32");
+  if (d->max_batch * d->top_k > nkm::kMaxPairs) return fail(NKM_ERR_ARG, "max_batch*top_k too large");
+  if (d->block_size != nkm::kKvBlock) return fail(NKM_ERR_ARG, "block_size must be 128");
+  // every GEMV stage indexes one split-K counter per 16-row strip
+  const int64_t na_max = std::min<int64_t>(d->n_experts, static_cast<int64_t>(d->max_batch) * d->top_k);
+  const int64_t strips[] = {na_max * (2 * d->moe_inter / 16), na_max * (d->hidden / 16), d->vocab / 16,
+                            static_cast<int64_t>(d->n_q_heads + 2 * d->n_kv_heads) * d->head_dim / 16};
+  for (int64_t s : strips)
+    if (s > kMaxStrips) return fail(NKM_ERR_ARG, "shape needs %lld split-K counters (max %d)", (long long)s, kMaxStrips);
+  return NKM_OK;
+}
+
+int current_sms(int* sms, int* dev) {
+  NKM_CUDA(cudaGetDevice(dev));
+  NKM_CUDA(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, *dev));
+  return NKM_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// K or V pool viewed as a 2-D tensor [rows = L*NB*nkv*128, 128] bf16; box 64 x 32 (128-byte
+// inner extent, 128-byte swizzle).
+int encode_kv_map(CUtensorMap* map, void* pool, const nkm_qwen3_desc& d) {
+  memset(map, 0, sizeof(*map));
+  if (!pool) return NKM_OK;
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(NKM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const uint64_t rows = static_cast<uint64_t>(d.n_layers) * d.num_blocks * d.n_kv_heads * nkm::kKvBlock;
+  if (rows >= (1ull << 31)) return fail(NKM_ERR_ARG, "KV pool too large for 32-bit TMA coordinates");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(nkm::kHeadDim), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(nkm::kHeadDim * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(nkm::kAttTile)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, pool, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NKM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return NKM_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+struct nkm_qwen3 {
+  nkm_qwen3_desc desc;
+  std::vector<nkm_qwen3_layer> layers;
+  uint8_t* ws;
+  size_t ws_bytes;
+  WsLayout lay;
+  CUtensorMap kmap, vmap;
+  int device, num_sms;
+  size_t smem[3];
+};
+
+extern "C" {
+
+const char* nkm_last_error(void) { return g_last_error.c_str(); }
+const char* nkm_version(void) { return "nkimoe-b200 0.1.0 (sm_100a)"; }
+
+size_t nkm_qwen3_workspace_bytes(const nkm_qwen3_desc* desc) {
+  if (check_desc(desc) != NKM_OK) return 0;
+  int sms = 0, dev = 0;
+  if (current_sms(&sms, &dev) != NKM_OK) return 0;
+  return layout_ws(*desc, sms).total;
+}
+
+int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspace_bytes, nkm_qwen3** out) {
+  if (!out) return fail(NKM_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  int rc = check_desc(desc);
+  if (rc) return rc;
+  int sms = 0, dev = 0;
+  if ((rc = current_sms(&sms, &dev))) return rc;
+  WsLayout lay = layout_ws(*desc, sms);
+  if (!workspace || workspace_bytes < lay.total)
+    return fail(NKM_ERR_ARG, "workspace too small: need %zu bytes", lay.total);
+  if (reinterpret_cast<uintptr_t>(workspace) % kAlign) return fail(NKM_ERR_ARG, "workspace must be 256-byte aligned");
+  for (int i = 0; i < desc->n_layers; ++i) {
+    const nkm_qwen3_layer& L = desc->layers[i];
+    const void* ps[] = {L.wqkv_ft, L.wo_ft, L.w13_ft, L.w2_ft, L.router, L.ln1, L.ln2, L.q_norm, L.k_norm};
+    for (const void* q : ps)
+      if (q && !aligned16(q)) return fail(NKM_ERR_ARG, "layer %d: weight pointers must be 16-byte aligned", i);
+  }
+  nkm_qwen3* h = new (std::nothrow) nkm_qwen3();
+  if (!h) return fail(NKM_ERR_ARG, "out of host memory");
+  h->desc = *desc;
+  h->layers.assign(desc->layers, desc->layers + desc->n_layers);
+  h->desc.layers = h->layers.data();
+  h->ws = static_cast<uint8_t*>(workspace);
+  h->ws_bytes = workspace_bytes;
+  h->lay = lay;
+  h->device = dev;
+  h->num_sms = sms;
+  std::vector<nkm::LayerPtrs> lp(desc->n_layers);
+  for (int i = 0; i < desc->n_layers; ++i) {
+    const nkm_qwen3_layer& L = desc->layers[i];
+    lp[i] = nkm::LayerPtrs{static_cast<const uint8_t*>(L.wqkv_ft), static_cast<const uint8_t*>(L.wo_ft),
+                           static_cast<const uint16_t*>(L.q_norm),  static_cast<const uint16_t*>(L.k_norm),
+                           static_cast<const uint16_t*>(L.ln1),     static_cast<const uint16_t*>(L.ln2),
+                           static_cast<const uint16_t*>(L.router),  static_cast<const uint8_t*>(L.w13_ft),
+                           static_cast<const uint8_t*>(L.w2_ft),    L.router_bias};
+  }
+  auto cleanup = [&](int code) {
+    delete h;
+    return code;
+  };
+  if (cudaMemcpy(h->ws + lay.layers, lp.data(), sizeof(nkm::LayerPtrs) * lp.size(), cudaMemcpyHostToDevice) !=
+      cudaSuccess)
+    return cleanup(fail(NKM_ERR_CUDA, "copying the layer table failed"));
+  if (cudaMemset(h->ws + lay.ctrl, 0, lay.ctrl_bytes) != cudaSuccess)
+    return cleanup(fail(NKM_ERR_CUDA, "clearing the workspace failed"));
+  if ((rc = encode_kv_map(&h->kmap, desc->k_pool, *desc))) return cleanup(rc);
+  if ((rc = encode_kv_map(&h->vmap, desc->v_pool, *desc))) return cleanup(rc);
+  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
+  const int nts[3] = {1, 2, 4};
+  for (int i = 0; i < 3; ++i) {
+    nkm::SmemLayout sl(desc->hidden, nts[i]);
+    h->smem[i] = sl.total;
+    if (sl.total > 232448) return cleanup(fail(NKM_ERR_ARG, "hidden too large for shared memory"));
+    if (cudaFuncSetAttribute(kfn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sl.total)) !=
+        cudaSuccess)
+      return cleanup(fail(NKM_ERR_CUDA, "cudaFuncSetAttribute failed"));
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn[i], nkm::kThreads, sl.total) != cudaSuccess ||
+        occ < 1)
+      return cleanup(fail(NKM_ERR_CUDA, "decode kernel does not fit on an SM"));
+  }
+  *out = h;
+  g_last_error.clear();
+  return NKM_OK;
+}
+
+void nkm_qwen3_destroy(nkm_qwen3* h) { delete h; }
+
+static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl, int stages, int residual,
+                       cudaStream_t stream) {
+  const nkm_qwen3_desc& d = h->desc;
+  if (!s) return fail(NKM_ERR_ARG, "step is NULL");
+  if (s->batch <= 0 || s->batch > d.max_batch) return fail(NKM_ERR_ARG, "batch %d outside 1..%d", s->batch, d.max_batch);
+  if (first < 0 || nl <= 0 || first + nl > d.n_layers) return fail(NKM_ERR_ARG, "layer range out of bounds");
+  if (!s->y_out || !aligned16(s->y_out)) return fail(NKM_ERR_ARG, "y_out must be a 16-byte aligned device pointer");
+  if (s->input_ids) {
+    if (!d.embed) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");
+  } else if (!s->x_in || !aligned16(s->x_in)) {
+    return fail(NKM_ERR_ARG, "x_in must be a 16-byte aligned device pointer");
+  }
+  if (stages & NKM_STAGE_ATTN) {
+    if (!d.k_pool || !d.v_pool || !d.rope_cos || !d.rope_sin) return fail(NKM_ERR_ARG, "attention needs KV pools and RoPE tables");
+    if (!s->positions || !s->block_table || s->max_blocks_per_seq <= 0)
+      return fail(NKM_ERR_ARG, "attention needs positions and a block table");
+    for (int l = first; l < first + nl; ++l) {
+      const nkm_qwen3_layer& L = d.layers[l];
+      if (!L.wqkv_ft || !L.wo_ft || !L.q_norm || !L.k_norm || !L.ln1)
+        return fail(NKM_ERR_ARG, "layer %d: attention weights missing", l);
+    }
+  }
+  if (stages & NKM_STAGE_MOE) {
+    for (int l = first; l < first + nl; ++l) {
+      const nkm_qwen3_layer& L = d.layers[l];
+      if (!L.router || !L.w13_ft || !L.w2_ft || !L.ln2) return fail(NKM_ERR_ARG, "layer %d: MoE weights missing", l);
+    }
+  }
+  const bool lm = (stages & NKM_STAGE_LMHEAD) && s->logits_out;
+  if (lm && (d.vocab <= 0 || !d.lm_head_ft || !d.final_norm)) return fail(NKM_ERR_ARG, "LM head requested but missing");
+
+  nkm::Params p{};
+  p.T = s->batch;
+  p.H = d.hidden;
+  p.nq = d.n_q_heads;
+  p.nkv = d.n_kv_heads;
+  p.grp = d.n_q_heads / d.n_kv_heads;
+  p.R = (d.n_q_heads + 2 * d.n_kv_heads) * d.head_dim;
+  p.E = d.n_experts;
+  p.K = d.top_k;
+  p.I = d.moe_inter;
+  p.L = d.n_layers;
+  p.V = d.vocab;
+  p.eps = d.rms_eps;
+  p.first_layer = first;
+  p.num_layers = nl;
+  p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | (lm ? NKM_STAGE_LMHEAD : 0));
+  p.residual = residual;
+  p.layers = reinterpret_cast<const nkm::LayerPtrs*>(h->ws + h->lay.layers);
+  p.final_norm = static_cast<const uint16_t*>(d.final_norm);
+  p.lm_head = static_cast<const uint8_t*>(d.lm_head_ft);
+  p.embed = static_cast<const uint16_t*>(d.embed);
+  p.rope_cos = static_cast<const uint16_t*>(d.rope_cos);
+  p.rope_sin = static_cast<const uint16_t*>(d.rope_sin);
+  p.rope_max = d.rope_max_pos;
+  p.k_pool = static_cast<uint16_t*>(d.k_pool);
+  p.v_pool = static_cast<uint16_t*>(d.v_pool);
+  p.num_blocks = d.num_blocks;
+  p.input_ids = s->input_ids;
+  p.x_in = static_cast<const uint16_t*>(s->x_in);
+  p.positions = s->positions;
+  p.block_table = s->block_table;
+  p.max_blocks = s->max_blocks_per_seq;
+  p.y_out = static_cast<uint16_t*>(s->y_out);
+  p.logits_out = lm ? s->logits_out : nullptr;
+  p.tr_topk_idx = s->trace_topk_idx;
+  p.tr_topk_w = s->trace_topk_w;
+  p.tr_rlogits = s->trace_router_logits;
+  p.tr_qkv = static_cast<uint16_t*>(s->trace_qkv);
+  p.tr_mid = static_cast<uint16_t*>(s->trace_resid_mid);
+  p.tr_out = static_cast<uint16_t*>(s->trace_resid_out);
+  uint8_t* ws = h->ws;
+  p.bar = reinterpret_cast<unsigned*>(ws + h->lay.bar);
+  p.status = reinterpret_cast<int*>(ws + h->lay.status);
+  p.strip_cnt = reinterpret_cast<unsigned*>(ws + h->lay.strip_cnt);
+  p.attn_cnt = reinterpret_cast<unsigned*>(ws + h->lay.attn_cnt);
+  p.row_cnt = reinterpret_cast<unsigned*>(ws + h->lay.row_cnt);
+  p.resid = reinterpret_cast<uint16_t*>(ws + h->lay.resid);
+  p.qkv = reinterpret_cast<uint16_t*>(ws + h->lay.qkv);
+  p.attn_out = reinterpret_cast<uint16_t*>(ws + h->lay.attn_out);
+  p.att_part = reinterpret_cast<float*>(ws + h->lay.att_part);
+  p.rlogits = reinterpret_cast<float*>(ws + h->lay.rlogits);
+  p.hbuf = reinterpret_cast<uint16_t*>(ws + h->lay.hbuf);
+  p.ypair = reinterpret_cast<float*>(ws + h->lay.ypair);
+  p.gpart = reinterpret_cast<float*>(ws + h->lay.gpart);
+
+  const int nt = nt_for_batch(p.T);
+  const int ki = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
+  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
+  void* args[3] = {&p, &h->kmap, &h->vmap};
+  NKM_CUDA(cudaLaunchCooperativeKernel(kfn[ki], dim3(h->num_sms), dim3(nkm::kThreads), args, h->smem[ki], stream));
+  return NKM_OK;
+}
+
+int nkm_qwen3_decode_step(nkm_qwen3* h, const nkm_qwen3_step* s, nkm_stream_t stream) {
+  if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
+  if (!s) return fail(NKM_ERR_ARG, "step is NULL");
+  const int nl = s->num_layers > 0 ? s->num_layers : h->desc.n_layers - s->first_layer;
+  const int stages = s->stages ? s->stages : (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_LMHEAD);
+  return launch_step(h, s, s->first_layer, nl, stages, 1, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int nkm_qwen3_attention_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* s, nkm_stream_t stream) {
+  if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
+  if (!s) return fail(NKM_ERR_ARG, "step is NULL");
+  return launch_step(h, s, layer, 1, NKM_STAGE_ATTN, s->residual ? 1 : 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int nkm_qwen3_moe_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* s, nkm_stream_t stream) {
+  if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
+  if (!s) return fail(NKM_ERR_ARG, "step is NULL");
+  return launch_step(h, s, layer, 1, NKM_STAGE_MOE, s->residual ? 1 : 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream) {
+  if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
+  int st = 0;
+  NKM_CUDA(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  NKM_CUDA(cudaMemcpy(&st, h->ws + h->lay.status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st) {
+    fail(st, "device status 0x%x%s%s", st, (st & NKM_ERR_TIMEOUT) ? " (wait timeout)" : "",
+         (st & NKM_ERR_INDEX) ? " (index out of range)" : "");
+    // the status is sticky until read; after a fault the barrier and counters may be mid-way
+    NKM_CUDA(cudaMemset(h->ws + h->lay.ctrl, 0, h->lay.ctrl_bytes));
+  }
+  return st;
+}
+
+}  // extern "C"

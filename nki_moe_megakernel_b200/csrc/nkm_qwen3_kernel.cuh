@@ -1,0 +1,1173 @@
+// Persistent cooperative decode-step kernel for Qwen3-MoE on B200 (sm_100a).
+//
+// One CTA per SM, 8 warps per CTA.  Every warp is an independent "worker" with a private
+// ring of 4 KB shared-memory slots that its lane 0 fills with TMA copies (1-D bulk copies
+// of fragment-tiled weights, 2-D swizzled tensor copies of K/V pages); the warp consumes
+// the slots with mma.sync.  Stages of a layer are separated by grid-wide barriers with
+// bounded waits.  The residual stream lives in a small L2-resident global buffer.
+//
+// Stages per layer (reference order: megakernels/qwen3_moe/transformer_qwen.py:271-378):
+//   A  RMSNorm(ln1) + QKV GEMV                                   -> qkv (raw bf16)
+//   B  q/k RMSNorm + RoPE, KV write at pos, split-context attention -> attn_out
+//   C  O-proj GEMV + residual add                                -> resid
+//   D  RMSNorm(ln2) + fp32 router logits                          -> rlogits
+//   E  softmax/top-k/renorm (per CTA) + gate/up GEMV + SiLU*up    -> h
+//   F  down GEMV * affinity + per-token combine + residual add    -> resid
+#pragma once
+#include "nkm_ptx.cuh"
+
+namespace nkm {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kSlotBytes = 4096;
+constexpr int kUnitBytes = 1024;           // one fragment tile: 16 rows x 32 k, bf16
+constexpr int kChunkUnits = kSlotBytes / kUnitBytes;
+constexpr int kHeadDim = 128;
+constexpr int kKvBlock = 128;
+constexpr int kAttTile = 32;               // tokens per attention tile (one TMA box row count)
+constexpr int kMaxExperts = 256;
+constexpr int kMaxPairs = 256;             // max batch * top_k
+constexpr int kAttRows = 16;               // q heads per kv head handled per mma (<= 16)
+constexpr int kAttQStride = kHeadDim + 8;  // bf16 elements per staged q row
+constexpr int kAttScratch = kAttRows * kAttQStride * 2 + 2 * kHeadDim * 2;  // q + k_new + v_new
+constexpr int kPartFloats = 2 * kAttRows + kAttRows * kHeadDim;            // m, l, o
+constexpr int kStatusFatal = 4;            // NKM_ERR_TIMEOUT
+constexpr int kStatusIndex = 8;            // NKM_ERR_INDEX
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
+
+struct LayerPtrs {
+  const uint8_t* wqkv;
+  const uint8_t* wo;
+  const uint16_t* qn;
+  const uint16_t* kn;
+  const uint16_t* ln1;
+  const uint16_t* ln2;
+  const uint16_t* router;
+  const uint8_t* w13;
+  const uint8_t* w2;
+  const float* router_bias;
+};
+
+struct Params {
+  int T, H, nq, nkv, grp, R, E, K, I, L, V;
+  float eps;
+  int first_layer, num_layers, stages, residual;
+  const LayerPtrs* layers;
+  const uint16_t* final_norm;
+  const uint8_t* lm_head;
+  const uint16_t* embed;
+  const uint16_t* rope_cos;
+  const uint16_t* rope_sin;
+  int rope_max;
+  uint16_t* k_pool;
+  uint16_t* v_pool;
+  int num_blocks;
+  const int* input_ids;
+  const uint16_t* x_in;
+  const int* positions;
+  const int* block_table;
+  int max_blocks;
+  uint16_t* y_out;
+  float* logits_out;
+  int* tr_topk_idx;
+  float* tr_topk_w;
+  float* tr_rlogits;
+  uint16_t* tr_qkv;
+  uint16_t* tr_mid;
+  uint16_t* tr_out;
+  unsigned* bar;
+  int* status;
+  unsigned* strip_cnt;
+  unsigned* attn_cnt;
+  unsigned* row_cnt;
+  uint16_t* resid;
+  uint16_t* qkv;
+  uint16_t* attn_out;
+  float* att_part;
+  float* rlogits;
+  uint16_t* hbuf;
+  float* ypair;
+  float* gpart;
+};
+
+struct Route {
+  int nA;
+  int act_e[kMaxExperts];
+  int act_off[kMaxExperts];
+  int act_cnt[kMaxExperts];
+  int cnt[kMaxExperts];
+  int topk_idx[kMaxPairs];
+  float topk_w[kMaxPairs];
+  int pmap[kMaxPairs];
+  int pair_tok[kMaxPairs];
+  float pair_w[kMaxPairs];
+};
+
+// Shared-memory layout, identical on host (sizing) and device.
+struct SmemLayout {
+  int nslot;
+  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, flag_off, total;
+  __host__ __device__ static int nslot_for(int NT) { return NT == 1 ? 5 : (NT == 2 ? 4 : 2); }
+  __host__ __device__ SmemLayout(int H, int NT) {
+    nslot = nslot_for(NT);
+    ring_off = 0;
+    uint32_t ring = static_cast<uint32_t>(kWarps * nslot * kSlotBytes);
+    xs_off = ring;
+    uint32_t xs = static_cast<uint32_t>(8 * NT * (H + 32) * 2);
+    uint32_t att = static_cast<uint32_t>(kWarps * kAttScratch);
+    uint32_t u = xs > att ? xs : att;
+    bars_off = xs_off + ((u + 127u) & ~127u);
+    rstd_off = bars_off + static_cast<uint32_t>(kWarps * nslot * 8);
+    route_off = rstd_off + 32 * 4;
+    flag_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
+    total = flag_off + 16 + 1024;  // + alignment slack for the ring base
+  }
+};
+
+// ------------------------------------------------------------------ per-warp context
+struct Ctx {
+  uint8_t* ring;
+  uint64_t* bars;
+  uint32_t phase;
+  int head;
+  int nslot;
+  int worker, nworkers;
+  uint64_t pol;
+  uint16_t* xs;
+  int xs_stride;  // elements per X row
+  uint8_t* att;
+  float* rstd;
+  Route* rt;
+  int* flag;
+};
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ void set_status(const Params& p, int bit) { atomicOr(p.status, bit); }
+
+// Bounded wait on a slot's mbarrier.  On timeout the fatal status bit is set and the caller
+// continues (the next grid barrier then aborts every CTA).
+__device__ __forceinline__ void slot_wait(const Params& p, Ctx& c, int slot) {
+  uint32_t par = (c.phase >> slot) & 1u;
+  if (!mbar_try_wait(&c.bars[slot], par)) {
+    uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&c.bars[slot], par)) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (lane_id() == 0) set_status(p, kStatusFatal);
+        break;
+      }
+    }
+  }
+  c.phase ^= (1u << slot);
+}
+
+// Grid-wide barrier (sense reversal): the last CTA to arrive resets the arrival count and
+// bumps the generation word the others spin on, so the counter is zero again when the kernel
+// ends (no per-launch reset needed).  Co-residency is guaranteed by the cooperative launch.
+// Returns false if any CTA recorded a fatal status or the wait timed out.
+__device__ __noinline__ bool grid_barrier(const Params& p, Ctx& c) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* count = p.bar;
+    unsigned* gen = p.bar + 1;
+    const unsigned g0 = ld_acquire_u32(gen);
+    __threadfence();
+    const unsigned old = atom_acqrel_add_u32(count, 1u);
+    int ok = 1;
+    if (old == gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned*>(count) = 0u;
+      st_release_u32(gen, g0 + 1u);
+    } else if (ld_acquire_u32(gen) == g0) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_u32(gen) == g0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_status(p, kStatusFatal);
+          ok = 0;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    if (ld_volatile_i32(p.status) & kStatusFatal) ok = 0;
+    *c.flag = ok;
+  }
+  __syncthreads();
+  return *c.flag != 0;
+}
+
+// ------------------------------------------------------------------ fixed-order reductions
+__device__ __forceinline__ float warp_sum_fixed(float s) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+  return s;
+}
+__device__ __forceinline__ float warp_max(float s) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, off));
+  return s;
+}
+__device__ __forceinline__ float rstd_fixed(float sumsq, int n, float eps) {
+  const float v = __fadd_rn(__fmul_rn(sumsq, 1.0f / static_cast<float>(n)), eps);
+  return __fdiv_rn(1.0f, __fsqrt_rn(v));
+}
+
+// Sum of squares of one bf16 row of length H (multiple of 256) in the documented order:
+// lane l owns k = 256*i + 8*l + j, accumulated i-outer / j-inner, then a xor butterfly.
+__device__ __forceinline__ float row_sumsq(const uint16_t* row, int H) {
+  const int lane = lane_id();
+  float s = 0.f;
+  for (int i = 0; i < H / 256; ++i) {
+    uint4 v = ldcg128(row + 256 * i + 8 * lane);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a = lo_bf(w[j]), b = hi_bf(w[j]);
+      s = __fadd_rn(s, __fmul_rn(a, a));
+      s = __fadd_rn(s, __fmul_rn(b, b));
+    }
+  }
+  return warp_sum_fixed(s);
+}
+
+// RMSNorm of the residual rows into X shared memory (bf16), one warp per token.
+// gamma_first=false: (x*r)*g (attn_fused_nki.py:306-309); true: (x*g)*r (moe_fused_nki.py:114-147).
+__device__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first,
+                                  bool write_x) {
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  for (int t = warp; t < p.T; t += kWarps) {
+    const uint16_t* row = p.resid + static_cast<size_t>(t) * p.H;
+    const float r = rstd_fixed(row_sumsq(row, p.H), p.H, p.eps);
+    if (lane == 0) c.rstd[t] = r;
+    if (!write_x) continue;
+    uint16_t* xr = c.xs + static_cast<size_t>(t) * c.xs_stride;
+    for (int k0 = 8 * lane; k0 < p.H; k0 += 256) {
+      uint4 xv = ldcg128(row + k0);
+      uint4 gv = ldnc128(gamma + k0);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float x0 = lo_bf(xw[j]), x1 = hi_bf(xw[j]), g0 = lo_bf(gw[j]), g1 = hi_bf(gw[j]);
+        float y0 = gamma_first ? __fmul_rn(__fmul_rn(x0, g0), r) : __fmul_rn(__fmul_rn(x0, r), g0);
+        float y1 = gamma_first ? __fmul_rn(__fmul_rn(x1, g1), r) : __fmul_rn(__fmul_rn(x1, r), g1);
+        o[j] = pack_bf2(y0, y1);
+      }
+      *reinterpret_cast<uint4*>(xr + k0) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ fragment-tiled GEMV
+enum GemvKind { GK_QKV = 0, GK_OPROJ = 1, GK_GATEUP = 2, GK_DOWN = 3, GK_LMHEAD = 4 };
+
+struct GemvGeom {
+  const uint8_t* base;   // weights of segment 0 (dense) or of expert 0 (experts)
+  uint64_t seg_bytes;    // byte stride between experts
+  int nseg;              // segments (1 dense, nA experts)
+  int sps;               // strips (16 output rows) per segment
+  int kt;                // k-tiles (32) per strip
+  int kdim;              // K in elements
+  int layer;
+};
+
+template <int KIND>
+__device__ __forceinline__ const uint8_t* seg_base(const GemvGeom& G, const Ctx& c, int seg) {
+  if constexpr (KIND == GK_GATEUP || KIND == GK_DOWN) {
+    return G.base + static_cast<uint64_t>(c.rt->act_e[seg]) * G.seg_bytes;
+  } else {
+    return G.base;
+  }
+}
+
+// number of columns (tokens) of a segment
+template <int KIND>
+__device__ __forceinline__ int seg_cols(const Params& p, const Ctx& c, int seg) {
+  if constexpr (KIND == GK_GATEUP || KIND == GK_DOWN) {
+    return c.rt->act_cnt[seg];
+  } else {
+    return p.T;
+  }
+}
+
+// B fragment (16 bytes: 8 consecutive k of one column) for lane (g,t), n-tile nt.
+template <int KIND>
+__device__ __forceinline__ uint4 load_bfrag(const Params& p, const Ctx& c, int seg, int kt, int nt, int ncols) {
+  const int lane = lane_id();
+  const int col = nt * 8 + (lane >> 2);
+  const int k = kt * 32 + 8 * (lane & 3);
+  if (col >= ncols) return make_uint4(0, 0, 0, 0);
+  if constexpr (KIND == GK_QKV || KIND == GK_LMHEAD) {
+    return lds128(smem_addr(c.xs + static_cast<size_t>(col) * c.xs_stride + k));
+  } else if constexpr (KIND == GK_GATEUP) {
+    const int tok = c.rt->pair_tok[c.rt->act_off[seg] + col];
+    return lds128(smem_addr(c.xs + static_cast<size_t>(tok) * c.xs_stride + k));
+  } else if constexpr (KIND == GK_OPROJ) {
+    return ldcg128(p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + k);
+  } else {  // GK_DOWN
+    const int pair = c.rt->act_off[seg] + col;
+    return ldcg128(p.hbuf + static_cast<size_t>(pair) * p.I + k);
+  }
+}
+
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// Final write of one strip's accumulators (all of K reduced).
+template <int NT, int KIND>
+__device__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4]) {
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
+  const int ncols = seg_cols<KIND>(p, c, seg);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int col = nt * 8 + 2 * t4 + e;
+      if (col >= ncols) continue;
+      const float v0 = acc[nt][e], v1 = acc[nt][2 + e];  // rows g and g+8
+      if constexpr (KIND == GK_QKV) {
+        const int r0 = strip * 16 + g;
+        uint16_t* q = p.qkv + static_cast<size_t>(col) * p.R;
+        q[r0] = f2bf(v0);
+        q[r0 + 8] = f2bf(v1);
+        if (p.tr_qkv) {
+          uint16_t* tq = p.tr_qkv + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.R;
+          tq[r0] = f2bf(v0);
+          tq[r0 + 8] = f2bf(v1);
+        }
+      } else if constexpr (KIND == GK_OPROJ) {
+        const int r0 = strip * 16 + g;
+        uint16_t* x = p.resid + static_cast<size_t>(col) * p.H;
+        const float b0 = p.residual ? bf2f(x[r0]) : 0.f, b1 = p.residual ? bf2f(x[r0 + 8]) : 0.f;
+        const uint16_t n0 = f2bf(b0 + rbf(v0)), n1 = f2bf(b1 + rbf(v1));
+        x[r0] = n0;
+        x[r0 + 8] = n1;
+        if (p.tr_mid) {
+          uint16_t* tm = p.tr_mid + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.H;
+          tm[r0] = n0;
+          tm[r0 + 8] = n1;
+        }
+      } else if constexpr (KIND == GK_GATEUP) {
+        // rows 0-7 of the strip are gate rows 8*strip+g, rows 8-15 the matching up rows
+        const int pair = c.rt->act_off[seg] + col;
+        const float gt = rbf(v0), up = rbf(v1);
+        const float h = rbf(rbf(silu_f(gt)) * up);
+        p.hbuf[static_cast<size_t>(pair) * p.I + strip * 8 + g] = f2bf(h);
+      } else if constexpr (KIND == GK_DOWN) {
+        const int pair = c.rt->act_off[seg] + col;
+        const float w = c.rt->pair_w[pair];
+        float* y = p.ypair + static_cast<size_t>(pair) * p.H + strip * 16 + g;
+        y[0] = v0 * w;
+        y[8] = v1 * w;
+      } else {  // GK_LMHEAD
+        float* lo = p.logits_out + static_cast<size_t>(col) * p.V + strip * 16 + g;
+        lo[0] = v0;
+        lo[8] = v1;
+      }
+    }
+  }
+  if constexpr (KIND == GK_DOWN) {
+    // Level-2 combine: when every active expert has finished this row strip, sum the
+    // top-k slots of each token in slot order and add into the residual.
+    __threadfence();
+    __syncwarp();
+    unsigned old = 0;
+    if (lane == 0) old = atom_acqrel_add_u32(&p.row_cnt[strip], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == static_cast<unsigned>(c.rt->nA - 1)) {
+      __threadfence();
+      for (int idx = lane; idx < 16 * p.T; idx += 32) {
+        const int t = idx >> 4, row = strip * 16 + (idx & 15);
+        float a = 0.f;
+        for (int k = 0; k < p.K; ++k) a += ldcg_f(p.ypair + static_cast<size_t>(c.rt->pmap[t * p.K + k]) * p.H + row);
+        uint16_t* x = p.resid + static_cast<size_t>(t) * p.H + row;
+        const float base = p.residual ? bf2f(*x) : 0.f;
+        const uint16_t nv = f2bf(base + rbf(a));
+        *x = nv;
+        if (p.tr_out) p.tr_out[(static_cast<size_t>(G.layer - p.first_layer) * p.T + t) * p.H + row] = nv;
+      }
+      if (lane == 0) p.row_cnt[strip] = 0u;
+    }
+  }
+}
+
+__device__ __forceinline__ int64_t range_lo(int64_t NU, int w, int NW) { return NU * w / NW; }
+__device__ __forceinline__ int worker_of(int64_t u, int64_t NU, int NW) {
+  int w = static_cast<int>((u * NW) / NU);
+  while (w + 1 < NW && range_lo(NU, w + 1, NW) <= u) ++w;
+  while (w > 0 && range_lo(NU, w, NW) > u) --w;
+  return w;
+}
+
+// Split-K partial of a strip: store it, and if this worker is the last contributor, sum all
+// contributions in worker order and run the epilogue.
+template <int NT, int KIND>
+__device__ void gemv_partial(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4],
+                             int64_t u0, int64_t NU, int NWe) {
+  const int lane = lane_id();
+  const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
+  const int64_t s0 = seg * upseg + static_cast<int64_t>(strip) * G.kt, s1 = s0 + G.kt;
+  const int slot = (u0 >= s0 && u0 < s1) ? 0 : 1;
+  float* dst = p.gpart + ((static_cast<size_t>(c.worker) * 2 + slot) * NT * 32 + lane) * 4;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+    *reinterpret_cast<float4*>(dst + nt * 128) = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+  __threadfence();
+  __syncwarp();
+  const int wf = worker_of(s0, NU, NWe), wl = worker_of(s1 - 1, NU, NWe);
+  const int gstrip = seg * G.sps + strip;
+  unsigned old = 0;
+  if (lane == 0) old = atom_acqrel_add_u32(&p.strip_cnt[gstrip], 1u);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != static_cast<unsigned>(wl - wf)) return;
+  __threadfence();
+  float sum[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) sum[nt][0] = sum[nt][1] = sum[nt][2] = sum[nt][3] = 0.f;
+  for (int w = wf; w <= wl; ++w) {
+    const int64_t wu0 = range_lo(NU, w, NWe);
+    const int sl = (wu0 >= s0 && wu0 < s1) ? 0 : 1;
+    const float* src = p.gpart + ((static_cast<size_t>(w) * 2 + sl) * NT * 32 + lane) * 4;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float4 v = ldcg_f4(src + nt * 128);
+      sum[nt][0] += v.x;
+      sum[nt][1] += v.y;
+      sum[nt][2] += v.z;
+      sum[nt][3] += v.w;
+    }
+  }
+  if (lane == 0) p.strip_cnt[gstrip] = 0u;
+  gemv_epilogue<NT, KIND>(p, c, G, seg, strip, sum);
+}
+
+// One GEMV stage: the unit space (segments x strips x k-tiles, 1 KB each) is split into
+// contiguous ranges, one per worker; each worker streams its range through its TMA ring.
+template <int NT, int KIND>
+__device__ void gemv_stage(const Params& p, Ctx& c, const GemvGeom& G) {
+  const int lane = lane_id();
+  const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
+  const int64_t NU = upseg * G.nseg;
+  if (NU <= 0) return;
+  int64_t NWe = NU / 2;
+  if (NWe > c.nworkers) NWe = c.nworkers;
+  if (NWe < 1) NWe = 1;
+  if (c.worker >= NWe) return;
+  const int64_t u0 = range_lo(NU, c.worker, static_cast<int>(NWe));
+  const int64_t u1 = range_lo(NU, c.worker + 1, static_cast<int>(NWe));
+  if (u0 >= u1) return;
+  auto chunk_len = [&](int64_t u) -> int {
+    int64_t segend = (u / upseg + 1) * upseg;
+    int64_t e = u1 < segend ? u1 : segend;
+    int64_t n = e - u;
+    return static_cast<int>(n < kChunkUnits ? n : kChunkUnits);
+  };
+  auto issue = [&](int64_t u, int n, int slot) {
+    if (lane == 0) {
+      const int seg = static_cast<int>(u / upseg);
+      const uint8_t* src = seg_base<KIND>(G, c, seg) + static_cast<uint64_t>(u - seg * upseg) * kUnitBytes;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
+      bulk_g2s(c.ring + slot * kSlotBytes, src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
+    }
+  };
+  // fill the ring
+  int64_t pu = u0;
+  {
+    int s = c.head;
+    for (int i = 0; i < c.nslot && pu < u1; ++i) {
+      const int n = chunk_len(pu);
+      issue(pu, n, s);
+      pu += n;
+      s = (s + 1 == c.nslot) ? 0 : s + 1;
+    }
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  int cur_seg = -1, cur_strip = -1, cur_kt0 = 0, cur_ktn = 0;
+  int cs = c.head;
+  int64_t cu = u0;
+  int seg = static_cast<int>(u0 / upseg);
+  int strip = static_cast<int>((u0 - seg * upseg) / G.kt);
+  int kt = static_cast<int>((u0 - seg * upseg) % G.kt);
+  while (cu < u1) {
+    const int n = chunk_len(cu);
+    const int ncols = seg_cols<KIND>(p, c, seg);
+    const int ntiles = (ncols + 7) >> 3;
+    // B fragments of the whole chunk first (global loads overlap the slot wait)
+    uint4 bf[kChunkUnits][NT];
+    {
+      int kk = kt;
+#pragma unroll
+      for (int i = 0; i < kChunkUnits; ++i) {
+        if (i < n) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            bf[i][nt] = (nt < ntiles) ? load_bfrag<KIND>(p, c, seg, kk, nt, ncols) : make_uint4(0, 0, 0, 0);
+        }
+        if (++kk == G.kt) kk = 0;
+      }
+    }
+    slot_wait(p, c, cs);
+    const uint32_t sbase = smem_addr(c.ring + cs * kSlotBytes) + lane * 16;
+#pragma unroll
+    for (int i = 0; i < kChunkUnits; ++i) {
+      if (i < n) {
+        if (strip != cur_strip || seg != cur_seg) {
+          if (cur_seg >= 0) {
+            if (cur_kt0 == 0 && cur_ktn == G.kt)
+              gemv_epilogue<NT, KIND>(p, c, G, cur_seg, cur_strip, acc);
+            else
+              gemv_partial<NT, KIND>(p, c, G, cur_seg, cur_strip, acc, u0, NU, static_cast<int>(NWe));
+          }
+          cur_seg = seg;
+          cur_strip = strip;
+          cur_kt0 = kt;
+          cur_ktn = 0;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        }
+        const uint4 a0 = lds128(sbase + i * kUnitBytes);
+        const uint4 a1 = lds128(sbase + i * kUnitBytes + 512);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (nt < ntiles) {
+            mma_bf16(acc[nt], a0.x, a1.x, a0.y, a1.y, bf[i][nt].x, bf[i][nt].y);
+            mma_bf16(acc[nt], a0.z, a1.z, a0.w, a1.w, bf[i][nt].z, bf[i][nt].w);
+          }
+        }
+        ++cur_ktn;
+        if (++kt == G.kt) {
+          kt = 0;
+          if (++strip == G.sps) {
+            strip = 0;
+            ++seg;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (pu < u1) {
+      const int m = chunk_len(pu);
+      issue(pu, m, cs);
+      pu += m;
+    }
+    cs = (cs + 1 == c.nslot) ? 0 : cs + 1;
+    cu += n;
+  }
+  if (cur_seg >= 0) {
+    if (cur_kt0 == 0 && cur_ktn == G.kt)
+      gemv_epilogue<NT, KIND>(p, c, G, cur_seg, cur_strip, acc);
+    else
+      gemv_partial<NT, KIND>(p, c, G, cur_seg, cur_strip, acc, u0, NU, static_cast<int>(NWe));
+  }
+  c.head = cs;
+}
+
+// ------------------------------------------------------------------ attention
+// q/k head RMSNorm + RoPE for the 4 elements d = 4*lane .. 4*lane+3 of one head
+// (rounding points of attn_fused_nki.py:393-451,494-586).
+__device__ __forceinline__ void head_norm_rope(float (&x)[4], const uint16_t* w, const uint16_t* cs,
+                                               const uint16_t* sn, float eps) {
+  const int lane = lane_id();
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s = __fadd_rn(s, __fmul_rn(x[j], x[j]));
+  s = warp_sum_fixed(s);
+  const float r = rstd_fixed(s, kHeadDim, eps);
+  float xn[4], rot[4];
+  const uint2 wv = *reinterpret_cast<const uint2*>(w + 4 * lane);
+  const float wf[4] = {lo_bf(wv.x), hi_bf(wv.x), lo_bf(wv.y), hi_bf(wv.y)};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) xn[j] = rbf(__fmul_rn(__fmul_rn(x[j], r), wf[j]));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float o = __shfl_xor_sync(0xffffffffu, xn[j], 16);
+    rot[j] = lane < 16 ? -o : o;
+  }
+  const uint2 cv = *reinterpret_cast<const uint2*>(cs + 4 * lane);
+  const uint2 sv = *reinterpret_cast<const uint2*>(sn + 4 * lane);
+  const float cf[4] = {lo_bf(cv.x), hi_bf(cv.x), lo_bf(cv.y), hi_bf(cv.y)};
+  const float sf[4] = {lo_bf(sv.x), hi_bf(sv.x), lo_bf(sv.y), hi_bf(sv.y)};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = rbf(__fadd_rn(rbf(__fmul_rn(xn[j], cf[j])), rbf(__fmul_rn(rot[j], sf[j]))));
+}
+
+__device__ __forceinline__ void load4_bf(const uint16_t* src, float (&x)[4]) {
+  const uint2 v = ldcg64(src);
+  x[0] = lo_bf(v.x);
+  x[1] = hi_bf(v.x);
+  x[2] = lo_bf(v.y);
+  x[3] = hi_bf(v.y);
+}
+
+constexpr float kScoreScale = 0.08838834764831845f;  // 1/sqrt(128)
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float score_round(float acc) { return rbf(rbf(acc) * kScoreScale); }
+
+// Attention for one (sequence b, kv head h, context chunk ch) item.
+__device__ void attention_item(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch, int CT, int item,
+                               const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
+  const int pos = __ldg(p.positions + b);
+  const int tok_beg = ch * CT;
+  const int tok_end = min(pos, (ch + 1) * CT);
+  const bool last = (ch == nch - 1);
+  uint16_t* qs = reinterpret_cast<uint16_t*>(c.att);
+  uint16_t* kn = qs + kAttRows * kAttQStride;
+  uint16_t* vn = kn + kHeadDim;
+  const int prow = min(max(pos, 0), p.rope_max - 1);
+  const uint16_t* cosr = p.rope_cos + static_cast<size_t>(prow) * kHeadDim;
+  const uint16_t* sinr = p.rope_sin + static_cast<size_t>(prow) * kHeadDim;
+  const LayerPtrs& lw = p.layers[layer];
+  const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
+
+  // --- q heads of the group: norm + RoPE -> staged bf16 rows
+  for (int i = 0; i < kAttRows; ++i) {
+    uint2 outv = make_uint2(0, 0);
+    if (i < p.grp) {
+      float x[4];
+      load4_bf(qkv_b + static_cast<size_t>(h * p.grp + i) * kHeadDim + 4 * lane, x);
+      head_norm_rope(x, lw.qn, cosr, sinr, p.eps);
+      outv = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
+    }
+    *reinterpret_cast<uint2*>(qs + i * kAttQStride + 4 * lane) = outv;
+  }
+  // --- the new token's K/V (last chunk only): stage, and write into the paged cache
+  if (last) {
+    float kx[4], vx[4];
+    load4_bf(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim + 4 * lane, kx);
+    load4_bf(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane, vx);
+    head_norm_rope(kx, lw.kn, cosr, sinr, p.eps);
+    const uint2 kw = make_uint2(pack_bf2(kx[0], kx[1]), pack_bf2(kx[2], kx[3]));
+    const uint2 vw = make_uint2(pack_bf2(vx[0], vx[1]), pack_bf2(vx[2], vx[3]));
+    *reinterpret_cast<uint2*>(kn + 4 * lane) = kw;
+    *reinterpret_cast<uint2*>(vn + 4 * lane) = vw;
+    const int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
+    if (blk >= 0 && blk < p.num_blocks) {
+      const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * kKvBlock * kHeadDim +
+                         static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
+      *reinterpret_cast<uint2*>(p.k_pool + off) = kw;
+      *reinterpret_cast<uint2*>(p.v_pool + off) = vw;
+    } else if (blk >= p.num_blocks && lane == 0) {
+      set_status(p, kStatusIndex);
+    }
+  }
+  __syncwarp();
+  uint32_t qa[8][4];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint16_t* r0 = qs + g * kAttQStride + 16 * ks + 2 * t4;
+    const uint16_t* r1 = qs + (g + 8) * kAttQStride + 16 * ks + 2 * t4;
+    qa[ks][0] = *reinterpret_cast<const uint32_t*>(r0);
+    qa[ks][1] = *reinterpret_cast<const uint32_t*>(r1);
+    qa[ks][2] = *reinterpret_cast<const uint32_t*>(r0 + 8);
+    qa[ks][3] = *reinterpret_cast<const uint32_t*>(r1 + 8);
+  }
+  float m[2] = {-1e30f, -1e30f}, l[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+
+  // --- prior context tiles, streamed as 4 TMA boxes per tile: K[d0:64], K[d64:128], V[..], V[..]
+  const int ntile = tok_end > tok_beg ? (tok_end - tok_beg + kAttTile - 1) / kAttTile : 0;
+  const int nbox = 4 * ntile;
+  const size_t head_rows = static_cast<size_t>(layer) * p.num_blocks;
+  auto issue_box = [&](int bi, int slot) {
+    if (lane == 0) {
+      const int tile = bi >> 2, kind = bi & 3;
+      const int tok0 = tok_beg + tile * kAttTile;
+      int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + tok0 / kKvBlock);
+      if (blk < 0 || blk >= p.num_blocks) {
+        set_status(p, kStatusIndex);
+        blk = 0;
+      }
+      const int row = static_cast<int>(((head_rows + blk) * p.nkv + h) * kKvBlock + (tok0 % kKvBlock));
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[slot], kSlotBytes);
+      tma_load_2d(c.ring + slot * kSlotBytes, kind < 2 ? kmap : vmap, (kind & 1) * 64, row, &c.bars[slot]);
+    }
+  };
+  int pb = 0, ps = c.head;
+  for (; pb < nbox && pb < c.nslot; ++pb) {
+    issue_box(pb, ps);
+    ps = (ps + 1 == c.nslot) ? 0 : ps + 1;
+  }
+  int cs = c.head;
+  auto next_slot = [&](int s) { return (s + 1 == c.nslot) ? 0 : s + 1; };
+  auto refill = [&](int slot) {
+    __syncwarp();
+    if (pb < nbox) {
+      issue_box(pb, slot);
+      ++pb;
+    }
+  };
+  for (int tile = 0; tile < ntile; ++tile) {
+    const int tok0 = tok_beg + tile * kAttTile;
+    const int nvalid = min(kAttTile, tok_end - tok0);
+    // ---- S = Q K^T  (16 rows x 32 tokens)
+    const int sk0 = cs, sk1 = next_slot(cs);
+    slot_wait(p, c, sk0);
+    slot_wait(p, c, sk1);
+    float sc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int kp = 0; kp < 4; ++kp) {
+      const uint32_t box = smem_addr(c.ring + (kp < 2 ? sk0 : sk1) * kSlotBytes);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int row = 8 * j + (lane & 7);
+        const int chunk = 4 * (kp & 1) + (lane >> 3);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(box + row * 128 + ((chunk ^ (row & 7)) << 4), r0, r1, r2, r3);
+        mma_bf16(sc[j], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], r0, r1);
+        mma_bf16(sc[j], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], r2, r3);
+      }
+    }
+    refill(sk0);
+    refill(sk1);
+    cs = next_slot(sk1);
+    // ---- online softmax (rows g and g+8 of this lane)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = (8 * j + 2 * t4 + e) < nvalid;
+        sc[j][e] = valid ? score_round(sc[j][e]) : -INFINITY;
+        sc[j][2 + e] = valid ? score_round(sc[j][2 + e]) : -INFINITY;
+        mx0 = fmaxf(mx0, sc[j][e]);
+        mx1 = fmaxf(mx1, sc[j][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+    const float al0 = exp2f((m[0] - mn0) * kLog2e), al1 = exp2f((m[1] - mn1) * kLog2e);
+    m[0] = mn0;
+    m[1] = mn1;
+    l[0] *= al0;
+    l[1] *= al1;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      o[nt][0] *= al0;
+      o[nt][1] *= al0;
+      o[nt][2] *= al1;
+      o[nt][3] *= al1;
+    }
+    uint32_t pa[2][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float p0 = exp2f((sc[j][0] - mn0) * kLog2e), p1 = exp2f((sc[j][1] - mn0) * kLog2e);
+      const float p2 = exp2f((sc[j][2] - mn1) * kLog2e), p3 = exp2f((sc[j][3] - mn1) * kLog2e);
+      l[0] += p0 + p1;
+      l[1] += p2 + p3;
+      const int ks = j >> 1;
+      if ((j & 1) == 0) {
+        pa[ks][0] = pack_bf2(p0, p1);
+        pa[ks][1] = pack_bf2(p2, p3);
+      } else {
+        pa[ks][2] = pack_bf2(p0, p1);
+        pa[ks][3] = pack_bf2(p2, p3);
+      }
+    }
+    // ---- O += P V  (two boxes: d 0..63, d 64..127)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int sv = cs;
+      slot_wait(p, c, sv);
+      uint8_t* vbox = c.ring + sv * kSlotBytes;
+      if (nvalid < kAttTile) {  // rows past the end of the context may hold anything
+        for (int idx = lane; idx < (kAttTile - nvalid) * 8; idx += 32)
+          reinterpret_cast<uint4*>(vbox + nvalid * 128)[idx] = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+      }
+      const uint32_t vb = smem_addr(vbox);
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          const int row = 16 * ks + ((lane >> 3) & 1) * 8 + (lane & 7);
+          const int chunk = 2 * np + (lane >> 4);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(vb + row * 128 + ((chunk ^ (row & 7)) << 4), r0, r1, r2, r3);
+          const int nt = half * 8 + 2 * np;
+          mma_bf16(o[nt], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], r0, r1);
+          mma_bf16(o[nt + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], r2, r3);
+        }
+      }
+      refill(sv);
+      cs = next_slot(sv);
+    }
+  }
+  c.head = cs;
+
+  // --- the active token (position pos): score with the fresh K, value the fresh V
+  if (last) {
+    float d0 = 0.f, d1 = 0.f;
+    for (int d = 32 * t4; d < 32 * t4 + 32; d += 2) {
+      const uint32_t kw = *reinterpret_cast<const uint32_t*>(kn + d);
+      const uint32_t q0 = *reinterpret_cast<const uint32_t*>(qs + g * kAttQStride + d);
+      const uint32_t q1 = *reinterpret_cast<const uint32_t*>(qs + (g + 8) * kAttQStride + d);
+      d0 = fmaf(lo_bf(q0), lo_bf(kw), fmaf(hi_bf(q0), hi_bf(kw), d0));
+      d1 = fmaf(lo_bf(q1), lo_bf(kw), fmaf(hi_bf(q1), hi_bf(kw), d1));
+    }
+    d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+    d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+    const float s0 = score_round(d0), s1 = score_round(d1);
+    const float mn0 = fmaxf(m[0], s0), mn1 = fmaxf(m[1], s1);
+    const float al0 = exp2f((m[0] - mn0) * kLog2e), al1 = exp2f((m[1] - mn1) * kLog2e);
+    const float pa0 = exp2f((s0 - mn0) * kLog2e), pa1 = exp2f((s1 - mn1) * kLog2e);
+    m[0] = mn0;
+    m[1] = mn1;
+    l[0] = l[0] * al0 + (t4 == 0 ? pa0 : 0.f);
+    l[1] = l[1] * al1 + (t4 == 0 ? pa1 : 0.f);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const uint32_t vw = *reinterpret_cast<const uint32_t*>(vn + 8 * nt + 2 * t4);
+      o[nt][0] = o[nt][0] * al0 + pa0 * lo_bf(vw);
+      o[nt][1] = o[nt][1] * al0 + pa0 * hi_bf(vw);
+      o[nt][2] = o[nt][2] * al1 + pa1 * lo_bf(vw);
+      o[nt][3] = o[nt][3] * al1 + pa1 * hi_bf(vw);
+    }
+  }
+  l[0] += __shfl_xor_sync(0xffffffffu, l[0], 1);
+  l[0] += __shfl_xor_sync(0xffffffffu, l[0], 2);
+  l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
+  l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
+
+  const size_t out_row = static_cast<size_t>(b) * (p.nq * kHeadDim);
+  if (nch == 1) {
+    const float i0 = 1.f / l[0], i1 = 1.f / l[1];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int d = 8 * nt + 2 * t4;
+      if (g < p.grp)
+        *reinterpret_cast<uint32_t*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + g) * kHeadDim + d) =
+            pack_bf2(o[nt][0] * i0, o[nt][1] * i0);
+      if (g + 8 < p.grp)
+        *reinterpret_cast<uint32_t*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + g + 8) * kHeadDim + d) =
+            pack_bf2(o[nt][2] * i1, o[nt][3] * i1);
+    }
+    return;
+  }
+  // --- split context: store (m, l, o) and let the last chunk of (b, h) combine in chunk order
+  float* part = p.att_part + static_cast<size_t>(item) * kPartFloats;
+  if (t4 == 0) {
+    part[g] = m[0];
+    part[g + 8] = m[1];
+    part[kAttRows + g] = l[0];
+    part[kAttRows + g + 8] = l[1];
+  }
+  float* po = part + 2 * kAttRows;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int d = 8 * nt + 2 * t4;
+    *reinterpret_cast<float2*>(po + g * kHeadDim + d) = make_float2(o[nt][0], o[nt][1]);
+    *reinterpret_cast<float2*>(po + (g + 8) * kHeadDim + d) = make_float2(o[nt][2], o[nt][3]);
+  }
+  __threadfence();
+  __syncwarp();
+  unsigned old = 0;
+  if (lane == 0) old = atom_acqrel_add_u32(&p.attn_cnt[b * p.nkv + h], 1u);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != static_cast<unsigned>(nch - 1)) return;
+  __threadfence();
+  const int item0 = item - ch;  // items of one (b, h) are consecutive, chunk-major
+  for (int r = 0; r < p.grp; ++r) {
+    float M = -1e30f;
+    for (int k = 0; k < nch; ++k) M = fmaxf(M, ldcg_f(p.att_part + static_cast<size_t>(item0 + k) * kPartFloats + r));
+    float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < nch; ++k) {
+      const float* pk = p.att_part + static_cast<size_t>(item0 + k) * kPartFloats;
+      const float sc = exp2f((ldcg_f(pk + r) - M) * kLog2e);
+      L += ldcg_f(pk + kAttRows + r) * sc;
+      const float4 v = ldcg_f4(pk + 2 * kAttRows + r * kHeadDim + 4 * lane);
+      acc[0] += v.x * sc;
+      acc[1] += v.y * sc;
+      acc[2] += v.z * sc;
+      acc[3] += v.w * sc;
+    }
+    const float il = 1.f / L;
+    *reinterpret_cast<uint2*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + r) * kHeadDim + 4 * lane) =
+        make_uint2(pack_bf2(acc[0] * il, acc[1] * il), pack_bf2(acc[2] * il, acc[3] * il));
+  }
+  if (lane == 0) p.attn_cnt[b * p.nkv + h] = 0u;
+}
+
+__device__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  // context chunk length CT: a multiple of 32 chosen so that the number of 32-token tiles per
+  // worker is about one chunk (identical in every warp)
+  int tiles = 0;
+  for (int b = 0; b < p.T; ++b) {
+    const int pos = max(__ldg(p.positions + b), 0);
+    tiles += p.nkv * ((pos + kAttTile - 1) / kAttTile);
+  }
+  int per = (tiles + c.nworkers - 1) / c.nworkers;
+  if (per < 1) per = 1;
+  const int CT = kAttTile * per;
+  int nitems = 0;
+  for (int b = 0; b < p.T; ++b) {
+    const int pos = max(__ldg(p.positions + b), 0);
+    nitems += p.nkv * max(1, (pos + CT - 1) / CT);
+  }
+  for (int it = c.worker; it < nitems; it += c.nworkers) {
+    int base = 0, b = 0, nch = 1;
+    for (b = 0; b < p.T; ++b) {
+      const int pos = max(__ldg(p.positions + b), 0);
+      nch = max(1, (pos + CT - 1) / CT);
+      if (it < base + p.nkv * nch) break;
+      base += p.nkv * nch;
+    }
+    const int r = it - base;
+    attention_item(p, c, layer, b, r / nch, r % nch, nch, CT, it, kmap, vmap);
+  }
+}
+
+// ------------------------------------------------------------------ router (stage D)
+__device__ void router_stage(const Params& p, Ctx& c, int layer) {
+  const int lane = lane_id();
+  const LayerPtrs& lw = p.layers[layer];
+  const int nitems = p.T * p.E;
+  for (int it = c.worker; it < nitems; it += c.nworkers) {
+    const int t = it / p.E, e = it % p.E;
+    const float r = c.rstd[t];
+    const uint16_t* xr = p.resid + static_cast<size_t>(t) * p.H;
+    const uint16_t* wr = lw.router + static_cast<size_t>(e) * p.H;
+    float s = 0.f;
+    for (int i = 0; i < p.H / 256; ++i) {
+      const int k0 = 256 * i + 8 * lane;
+      const uint4 xv = ldcg128(xr + k0), gv = ldnc128(lw.ln2 + k0), wv = ldnc128(wr + k0);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w},
+                     ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x0 = __fmul_rn(__fmul_rn(lo_bf(xw[j]), lo_bf(gw[j])), r);
+        const float x1 = __fmul_rn(__fmul_rn(hi_bf(xw[j]), hi_bf(gw[j])), r);
+        s = __fadd_rn(s, __fmul_rn(lo_bf(ww[j]), x0));
+        s = __fadd_rn(s, __fmul_rn(hi_bf(ww[j]), x1));
+      }
+    }
+    s = warp_sum_fixed(s);
+    if (lw.router_bias) s = __fadd_rn(s, __ldg(lw.router_bias + e));
+    if (lane == 0) {
+      p.rlogits[it] = s;
+      if (p.tr_rlogits) p.tr_rlogits[static_cast<size_t>(layer - p.first_layer) * nitems + it] = s;
+    }
+  }
+}
+
+// Softmax / top-k / renorm per token (one warp per token) and the expert tables, in every CTA
+// (moe_fused_nki.py:224-272, 404-418).
+__device__ void routing_prologue(const Params& p, Ctx& c, int layer) {
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  Route* rt = c.rt;
+  const int E = p.E, K = p.K;
+  for (int t = warp; t < p.T; t += kWarps) {
+    float v[8];
+    int ids[8];
+    const int per = (E + 31) / 32;
+    float mx = -INFINITY;
+    for (int q = 0; q < 8; ++q) {
+      const int e = q * 32 + lane;
+      ids[q] = e;
+      v[q] = (q < per && e < E) ? ldcg_f(p.rlogits + static_cast<size_t>(t) * E + e) : -INFINITY;
+      mx = fmaxf(mx, v[q]);
+    }
+    mx = warp_max(mx);
+    float se = 0.f;
+    for (int q = 0; q < 8; ++q) se += (q < per && ids[q] < E) ? __expf(v[q] - mx) : 0.f;
+    se = warp_sum_fixed(se);
+    const float inv = 1.f / se;
+    float vals[8];
+    for (int k = 0; k < K; ++k) {
+      // lane-local best (value desc, index asc)
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int q = 0; q < 8; ++q)
+        if (v[q] > bv || (v[q] == bv && ids[q] < bi)) {
+          bv = v[q];
+          bi = ids[q];
+        }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      for (int q = 0; q < 8; ++q)
+        if (ids[q] == bi) v[q] = -INFINITY;
+      vals[k] = rbf(__expf(bv - mx) * inv);
+      if (lane == 0) rt->topk_idx[t * K + k] = bi;
+    }
+    float sk = 0.f;
+    for (int k = 0; k < K; ++k) sk += vals[k];
+    const float inv2 = 1.f / sk;
+    if (lane == 0) {
+      for (int k = 0; k < K; ++k) rt->topk_w[t * K + k] = rbf(vals[k] * inv2);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int NP = p.T * K;
+    for (int e = lane; e < E; e += 32) rt->cnt[e] = 0;
+    __syncwarp();
+    for (int i = lane; i < NP; i += 32) {
+      const int e = rt->topk_idx[i];
+      if (e >= 0 && e < E) atomicAdd(&rt->cnt[e], 1);
+    }
+    __syncwarp();
+    // active experts in ascending id order, with pair offsets
+    int nA = 0, off = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int cnt = (e < E) ? rt->cnt[e] : 0;
+      const unsigned act = __ballot_sync(0xffffffffu, cnt > 0);
+      int incl = cnt;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += y;
+      }
+      if (cnt > 0) {
+        const int j = nA + __popc(act & ((1u << lane) - 1u));
+        rt->act_e[j] = e;
+        rt->act_cnt[j] = cnt;
+        rt->act_off[j] = off + incl - cnt;
+        rt->cnt[e] = off + incl - cnt;  // reuse as the expert's pair offset
+      }
+      nA += __popc(act);
+      off += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    __syncwarp();
+    for (int i = lane; i < NP; i += 32) {
+      const int e = rt->topk_idx[i];
+      int rank = 0;
+      for (int j = 0; j < i; ++j) rank += (rt->topk_idx[j] == e);
+      const int pr = rt->cnt[e] + rank;
+      rt->pmap[i] = pr;
+      rt->pair_tok[pr] = i / K;
+      rt->pair_w[pr] = rt->topk_w[i];
+    }
+    if (lane == 0) rt->nA = nA;
+    if (blockIdx.x == 0 && p.tr_topk_idx) {
+      for (int i = lane; i < NP; i += 32) {
+        p.tr_topk_idx[static_cast<size_t>(layer - p.first_layer) * NP + i] = rt->topk_idx[i];
+        p.tr_topk_w[static_cast<size_t>(layer - p.first_layer) * NP + i] = rt->topk_w[i];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    qwen3_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const SmemLayout lay(p.H, NT);
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  Ctx c;
+  c.nslot = lay.nslot;
+  c.ring = smem + lay.ring_off + warp * lay.nslot * kSlotBytes;
+  c.bars = reinterpret_cast<uint64_t*>(smem + lay.bars_off) + warp * lay.nslot;
+  c.phase = 0;
+  c.head = 0;
+  c.worker = blockIdx.x * kWarps + warp;
+  c.nworkers = gridDim.x * kWarps;
+  c.pol = policy_evict_first();
+  c.xs = reinterpret_cast<uint16_t*>(smem + lay.xs_off);
+  c.xs_stride = p.H + 32;
+  c.att = smem + lay.xs_off + warp * kAttScratch;
+  c.rstd = reinterpret_cast<float*>(smem + lay.rstd_off);
+  c.rt = reinterpret_cast<Route*>(smem + lay.route_off);
+  c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
+  if (lane == 0) {
+    for (int s = 0; s < lay.nslot; ++s) mbar_init(&c.bars[s], 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x == 0 && (p.stages & 1)) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  __syncwarp();
+
+  // stage 0: residual <- embeddings / hidden input
+  {
+    const int nvec = p.T * p.H / 8;
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads) {
+      const int t = (i * 8) / p.H, k = (i * 8) % p.H;
+      const uint16_t* src;
+      if (p.input_ids) {
+        const int id = __ldg(p.input_ids + t);
+        src = p.embed + static_cast<size_t>(id) * p.H + k;
+      } else {
+        src = p.x_in + static_cast<size_t>(t) * p.H + k;
+      }
+      *reinterpret_cast<uint4*>(p.resid + static_cast<size_t>(t) * p.H + k) = ldnc128(src);
+    }
+  }
+  if (!grid_barrier(p, c)) return;
+
+  for (int layer = p.first_layer; layer < p.first_layer + p.num_layers; ++layer) {
+    const LayerPtrs& lw = p.layers[layer];
+    if (p.stages & 1) {
+      // A: RMSNorm(ln1) + QKV
+      norm_rows_to_smem(p, c, lw.ln1, false, true);
+      __syncthreads();
+      GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
+      gemv_stage<NT, GK_QKV>(p, c, ga);
+      if (!grid_barrier(p, c)) return;
+      // B: attention (+ KV write)
+      attention_stage(p, c, layer, &kmap, &vmap);
+      if (!grid_barrier(p, c)) return;
+      // C: O-proj + residual
+      GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
+      gemv_stage<NT, GK_OPROJ>(p, c, gc);
+      if (!grid_barrier(p, c)) return;
+    }
+    if (p.stages & 2) {
+      // D: router logits (fp32, fixed order)
+      norm_rows_to_smem(p, c, lw.ln2, true, false);
+      __syncthreads();
+      router_stage(p, c, layer);
+      if (!grid_barrier(p, c)) return;
+      // E: routing tables + normed activations + gate/up
+      routing_prologue(p, c, layer);
+      norm_rows_to_smem(p, c, lw.ln2, true, true);
+      __syncthreads();
+      GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
+      gemv_stage<NT, GK_GATEUP>(p, c, ge);
+      if (!grid_barrier(p, c)) return;
+      // F: down + affinity + combine + residual
+      GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
+      gemv_stage<NT, GK_DOWN>(p, c, gf);
+      if (!grid_barrier(p, c)) return;
+    }
+  }
+  // outputs
+  {
+    const int nvec = p.T * p.H / 8;
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads)
+      reinterpret_cast<uint4*>(p.y_out)[i] = ldcg128(p.resid + static_cast<size_t>(i) * 8);
+  }
+  if ((p.stages & 4) && p.logits_out) {
+    norm_rows_to_smem(p, c, p.final_norm, false, true);
+    __syncthreads();
+    GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, p.first_layer + p.num_layers - 1};
+    gemv_stage<NT, GK_LMHEAD>(p, c, gl);
+  }
+}
+
+}  // namespace nkm

@@ -1,0 +1,228 @@
+"""Host-side owner of a Qwen3-MoE decode megakernel instance.
+
+Holds the weights (converted once to the GPU layouts), the paged K/V pools, the RoPE tables
+and the workspace, and calls the C ABI (``libnkimoe.so``) for each decode step.  torch is
+used for device memory and streams only; all compute of the step runs in the library's
+kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class Qwen3MoeShape:
+    """Model dimensions (Hugging Face ``Qwen3MoeConfig`` names) as held by one GPU."""
+
+    hidden_size: int = 2048
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 4
+    head_dim: int = 128
+    num_experts: int = 128
+    num_experts_per_tok: int = 8
+    moe_intermediate_size: int = 768
+    num_hidden_layers: int = 48
+    vocab_size: int = 151936
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    block_size: int = 128
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def pack_ft(src: torch.Tensor, mode: int = _lib.NKM_PACK_PLAIN, stream=None) -> torch.Tensor:
+    """Convert row-major bf16 ``[..., R, K]`` (CUDA) to the fragment-tiled layout."""
+    assert src.is_cuda and src.dtype == BF16
+    src = src.contiguous()
+    R, K = src.shape[-2], src.shape[-1]
+    count = src.numel() // (R * K)
+    dst = torch.empty_like(src)
+    s = stream if stream is not None else torch.cuda.current_stream(src.device)
+    check(lib().nkm_pack_ft(src.data_ptr(), dst.data_ptr(), R, K, count, mode, s.cuda_stream), "nkm_pack_ft")
+    return dst
+
+
+def rope_tables(max_pos: int, head_dim: int, theta: float, device) -> tuple:
+    """bf16 cos/sin ``[max_pos, head_dim]`` (HF default RoPE, computed in fp32 then cast)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(torch.float32) / head_dim))
+    pos = torch.arange(max_pos, dtype=torch.float32)
+    freqs = pos[:, None] * inv_freq[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(BF16).to(device), emb.sin().to(BF16).to(device)
+
+
+class GpuLayer:
+    """One decoder layer's weights in the kernel layouts (device tensors)."""
+
+    def __init__(self, wq, wk, wv, wo, q_norm, k_norm, ln1, ln2, router, gate_up, down, router_bias=None,
+                 attention=True, moe=True):
+        if attention:
+            self.wqkv_ft = pack_ft(torch.cat([wq, wk, wv], 0).to(BF16))
+            self.wo_ft = pack_ft(wo.to(BF16))
+            self.q_norm = q_norm.to(BF16).contiguous()
+            self.k_norm = k_norm.to(BF16).contiguous()
+            self.ln1 = ln1.to(BF16).contiguous()
+        else:
+            self.wqkv_ft = self.wo_ft = self.q_norm = self.k_norm = self.ln1 = None
+        if moe:
+            self.ln2 = ln2.to(BF16).contiguous()
+            self.router = router.to(BF16).contiguous()
+            self.w13_ft = pack_ft(gate_up.to(BF16), _lib.NKM_PACK_GATE_UP)
+            self.w2_ft = pack_ft(down.to(BF16))
+            self.router_bias = None if router_bias is None else router_bias.to(torch.float32).contiguous()
+        else:
+            self.ln2 = self.router = self.w13_ft = self.w2_ft = self.router_bias = None
+
+    def c_struct(self) -> _lib.nkm_qwen3_layer:
+        return _lib.nkm_qwen3_layer(_ptr(self.wqkv_ft), _ptr(self.wo_ft), _ptr(self.q_norm), _ptr(self.k_norm),
+                                    _ptr(self.ln1), _ptr(self.ln2), _ptr(self.router), _ptr(self.w13_ft),
+                                    _ptr(self.w2_ft), _ptr(self.router_bias))
+
+
+class Qwen3MoeMegakernel:
+    """A decode-megakernel instance on one GPU.
+
+    ``layers`` may repeat the same ``GpuLayer`` object (weights shared by several layers);
+    each layer still has its own K/V pages.
+    """
+
+    def __init__(self, shape: Qwen3MoeShape, layers: Sequence[GpuLayer], *, max_batch: int, num_blocks: int,
+                 final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
+                 embed: Optional[torch.Tensor] = None, rope_max_pos: int = 40960, device=None,
+                 kv_pools: bool = True):
+        self.shape = shape
+        self.device = torch.device(device if device is not None else "cuda")
+        self.layers = list(layers)
+        assert len(self.layers) == shape.num_hidden_layers
+        self.max_batch = max_batch
+        self.num_blocks = num_blocks
+        L, nkv, D = shape.num_hidden_layers, shape.num_key_value_heads, shape.head_dim
+        if kv_pools:
+            self.k_pool = torch.zeros(L, num_blocks, nkv, shape.block_size, D, dtype=BF16, device=self.device)
+            self.v_pool = torch.zeros_like(self.k_pool)
+            self.rope_cos, self.rope_sin = rope_tables(rope_max_pos, D, shape.rope_theta, self.device)
+        else:
+            self.k_pool = self.v_pool = self.rope_cos = self.rope_sin = None
+            rope_max_pos = 0
+        self.final_norm = None if final_norm is None else final_norm.to(BF16).contiguous()
+        self.lm_head_ft = None if lm_head is None else pack_ft(lm_head.to(BF16))
+        self.embed = None if embed is None else embed.to(BF16).contiguous()
+        self._layer_structs = (_lib.nkm_qwen3_layer * L)(*[l.c_struct() for l in self.layers])
+        vocab = shape.vocab_size if lm_head is not None else 0
+        self._desc = _lib.nkm_qwen3_desc(
+            shape.hidden_size, shape.num_attention_heads, nkv, D, shape.num_experts, shape.num_experts_per_tok,
+            shape.moe_intermediate_size, L, vocab, shape.rms_norm_eps, self._layer_structs,
+            _ptr(self.final_norm), _ptr(self.lm_head_ft), _ptr(self.embed), _ptr(self.rope_cos),
+            _ptr(self.rope_sin), rope_max_pos, _ptr(self.k_pool), _ptr(self.v_pool), num_blocks,
+            shape.block_size, max_batch)
+        nbytes = lib().nkm_qwen3_workspace_bytes(ctypes.byref(self._desc))
+        if nbytes == 0:
+            raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_qwen3_workspace_bytes")
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        h = ctypes.c_void_p()
+        check(lib().nkm_qwen3_create(ctypes.byref(self._desc), self.workspace.data_ptr(), nbytes, ctypes.byref(h)),
+              "nkm_qwen3_create")
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                lib().nkm_qwen3_destroy(h)
+            except Exception:
+                pass
+
+    # ------------------------------------------------------------------ calls
+    def _step_struct(self, batch, *, x=None, input_ids=None, positions=None, block_table=None, y=None,
+                     logits=None, first_layer=0, num_layers=0, stages=0, residual=1, traces=None):
+        tr = traces or {}
+        return _lib.nkm_qwen3_step(
+            batch, _ptr(input_ids), _ptr(x), _ptr(positions), _ptr(block_table),
+            0 if block_table is None else block_table.shape[1], _ptr(y), _ptr(logits), first_layer, num_layers,
+            stages, residual, _ptr(tr.get("topk_idx")), _ptr(tr.get("topk_w")), _ptr(tr.get("router_logits")),
+            _ptr(tr.get("qkv")), _ptr(tr.get("resid_mid")), _ptr(tr.get("resid_out")))
+
+    def _alloc_traces(self, batch, nl) -> Dict[str, torch.Tensor]:
+        s, dev = self.shape, self.device
+        R = (s.num_attention_heads + 2 * s.num_key_value_heads) * s.head_dim
+        return {
+            "topk_idx": torch.full((nl, batch, s.num_experts_per_tok), -1, dtype=torch.int32, device=dev),
+            "topk_w": torch.zeros(nl, batch, s.num_experts_per_tok, dtype=torch.float32, device=dev),
+            "router_logits": torch.zeros(nl, batch, s.num_experts, dtype=torch.float32, device=dev),
+            "qkv": torch.zeros(nl, batch, R, dtype=BF16, device=dev),
+            "resid_mid": torch.zeros(nl, batch, s.hidden_size, dtype=BF16, device=dev),
+            "resid_out": torch.zeros(nl, batch, s.hidden_size, dtype=BF16, device=dev),
+        }
+
+    def decode_step(self, positions: torch.Tensor, block_table: torch.Tensor, *, x: Optional[torch.Tensor] = None,
+                    input_ids: Optional[torch.Tensor] = None, want_logits: bool = True, trace: bool = False,
+                    first_layer: int = 0, num_layers: int = 0, out: Optional[Dict[str, torch.Tensor]] = None,
+                    stream=None) -> Dict[str, torch.Tensor]:
+        """Run one decode step (all layers by default).  K/V pools are updated in place.
+
+        Returns ``{"hidden": [B,H] bf16, "logits": [B,V] fp32 (if requested), traces...}``.
+        """
+        B = int(positions.shape[0])
+        nl = num_layers or (self.shape.num_hidden_layers - first_layer)
+        res = out if out is not None else {}
+        if "hidden" not in res:
+            res["hidden"] = torch.empty(B, self.shape.hidden_size, dtype=BF16, device=self.device)
+        if want_logits and self.lm_head_ft is not None and "logits" not in res:
+            res["logits"] = torch.empty(B, self.shape.vocab_size, dtype=torch.float32, device=self.device)
+        traces = self._alloc_traces(B, nl) if trace else None
+        st = self._step_struct(B, x=x, input_ids=input_ids, positions=positions, block_table=block_table,
+                               y=res["hidden"], logits=res.get("logits") if want_logits else None,
+                               first_layer=first_layer, num_layers=nl, traces=traces)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        check(lib().nkm_qwen3_decode_step(self._h, ctypes.byref(st), s.cuda_stream), "nkm_qwen3_decode_step")
+        if traces:
+            res.update(traces)
+        return res
+
+    def attention_block(self, layer: int, x: torch.Tensor, positions: torch.Tensor, block_table: torch.Tensor,
+                        residual: bool = False, trace: bool = False, stream=None) -> Dict[str, torch.Tensor]:
+        B = int(x.shape[0])
+        y = torch.empty(B, self.shape.hidden_size, dtype=BF16, device=self.device)
+        traces = self._alloc_traces(B, 1) if trace else None
+        st = self._step_struct(B, x=x, positions=positions, block_table=block_table, y=y, residual=int(residual),
+                               first_layer=layer, num_layers=1, traces=traces)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        check(lib().nkm_qwen3_attention_block(self._h, layer, ctypes.byref(st), s.cuda_stream),
+              "nkm_qwen3_attention_block")
+        res = {"hidden": y}
+        if traces:
+            res.update(traces)
+        return res
+
+    def moe_block(self, layer: int, x: torch.Tensor, residual: bool = False, trace: bool = False,
+                  stream=None) -> Dict[str, torch.Tensor]:
+        B = int(x.shape[0])
+        y = torch.empty(B, self.shape.hidden_size, dtype=BF16, device=self.device)
+        traces = self._alloc_traces(B, 1) if trace else None
+        st = self._step_struct(B, x=x, y=y, residual=int(residual), first_layer=layer, num_layers=1, traces=traces)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        check(lib().nkm_qwen3_moe_block(self._h, layer, ctypes.byref(st), s.cuda_stream), "nkm_qwen3_moe_block")
+        res = {"hidden": y}
+        if traces:
+            res.update(traces)
+        return res
+
+    def status(self, stream=None) -> int:
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return lib().nkm_qwen3_status(self._h, s.cuda_stream)
+
+    def check_status(self, stream=None) -> None:
+        st = self.status(stream)
+        if st != 0:
+            raise _lib.NkmError(st, "decode kernel")

@@ -142,6 +142,7 @@ class LayerWeights:
     router: torch.Tensor  # [E, H]
     gate_up: torch.Tensor  # [E, 2I, H]
     down: torch.Tensor    # [E, H, I]
+    router_bias: Optional[torch.Tensor] = None  # [E] fp32 added to the logits (router_topk.py:69 bias)
 
 
 @dataclass
@@ -291,25 +292,26 @@ def experts_forward(xn: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
                     gate_up: torch.Tensor, down: torch.Tensor, mode: str) -> torch.Tensor:
     """Selective-expert SwiGLU MLP.  ``xn`` [T,H] (bf16-valued fp32 in faithful mode).
 
-    Output fp32 ``[T, H]`` = sum over k (slot order) of ``w[t,k] * down_e(h)``.
+    Output fp32 ``[T, H]`` = sum over k in slot order 0..K-1 of ``w[t,k] * down_e(h)``
+    (each expert's GEMVs are evaluated once for all of its tokens).
     """
     T, K = idx.shape
     I = down.shape[-1]
+    contrib = torch.zeros(T, K, xn.shape[-1], dtype=F32)
+    for e in torch.unique(idx).tolist():
+        tok, slot = torch.nonzero(idx == e, as_tuple=True)
+        gu = xn[tok].to(F32) @ gate_up[e].to(F32).t()
+        g, u = gu[:, :I], gu[:, I:]
+        if mode == "faithful":
+            g, u = rbf(g), rbf(u)
+            h = rbf(rbf(torch.nn.functional.silu(g)) * u)
+        else:
+            h = torch.nn.functional.silu(g) * u
+        d = h @ down[e].to(F32).t()
+        contrib[tok, slot] = d * w[tok, slot][:, None]
     out = torch.zeros(T, xn.shape[-1], dtype=F32)
-    for t in range(T):
-        acc = torch.zeros(xn.shape[-1], dtype=F32)
-        for k in range(K):
-            e = int(idx[t, k])
-            gu = gate_up[e].to(F32) @ xn[t].to(F32)
-            g, u = gu[:I], gu[I:]
-            if mode == "faithful":
-                g, u = rbf(g), rbf(u)
-                h = rbf(rbf(torch.nn.functional.silu(g)) * u)
-            else:
-                h = torch.nn.functional.silu(g) * u
-            d = down[e].to(F32) @ h
-            acc = acc + d * w[t, k]
-        out[t] = acc
+    for k in range(K):
+        out = out + contrib[:, k]
     return out
 
 
@@ -327,6 +329,8 @@ def moe_block(x_bf16: torch.Tensor, lw: LayerWeights, cfg: QwenConfig, mode: str
     else:
         xn = rmsnorm_fp32(x_bf16, lw.ln2, cfg.rms_eps)
         logits = xn @ lw.router.to(F32).t()
+    if lw.router_bias is not None:
+        logits = logits + lw.router_bias.to(F32)
     idx, w = router_topk(logits, cfg.top_k, mode)
     out = experts_forward(xn, idx, w, lw.gate_up, lw.down, mode)
     if trace is not None:
