@@ -1,0 +1,372 @@
+#!/usr/bin/env python
+"""Benchmark: the full Qwen3-30B-A3B decode step (48 layers + final norm + LM head) at
+batch 8, context 2048 (paged KV, block 128), bf16, through the sm_100a megakernel.
+
+Prints ONE JSON line (rank 0).  ``--impl reference`` times the CPU restatement of the
+reference's decode path (the oracle, on the host cores) on the same configuration.
+
+Inputs: seeded random-init weights of the Qwen3-30B-A3B architecture (no checkpoints in this
+environment), a KV prefix ~N(0,1).  The weights streamed per step (~27 GB) are far larger
+than L2 (126 MB), so no L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Qwen3-30B-A3B decode tokens/s and p50 ms/step at B=8 ctx 2048; % HBM roofline"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--stage-times", action="store_true", help="print a per-stage time breakdown to stderr")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- model build
+def build_engine(args, device, seed):
+    import torch
+
+    from nki_moe_megakernel_b200.engine import GpuLayer, Qwen3MoeMegakernel, Qwen3MoeShape
+
+    shape = Qwen3MoeShape(num_hidden_layers=args.layers)
+    H, D, E, I = shape.hidden_size, shape.head_dim, shape.num_experts, shape.moe_intermediate_size
+    nq, nkv, V = shape.num_attention_heads, shape.num_key_value_heads, shape.vocab_size
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def n(*s):
+        return (torch.randn(*s, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    def one(*s):
+        return (1.0 + torch.randn(*s, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    layers = []
+    for _ in range(args.layers):
+        layers.append(GpuLayer(n(nq * D, H), n(nkv * D, H), n(nkv * D, H), n(H, nq * D), one(D), one(D), one(H),
+                               one(H), n(E, H), n(E, 2 * I, H), n(E, H, I)))
+        torch.cuda.empty_cache()
+    lm_head = n(V, H)
+    embed = torch.randn(V, H, generator=g, device=device).to(torch.bfloat16)
+    B = args.batch
+    blocks_per_seq = args.ctx // shape.block_size + 1
+    NB = B * blocks_per_seq
+    eng = Qwen3MoeMegakernel(shape, layers, max_batch=B, num_blocks=NB, final_norm=one(H), lm_head=lm_head,
+                             embed=embed, rope_max_pos=max(4096, args.ctx + 1), device=device)
+    del lm_head
+    eng.k_pool.normal_(generator=g)
+    eng.v_pool.normal_(generator=g)
+    perm = torch.randperm(NB, generator=torch.Generator().manual_seed(seed))
+    table = perm.view(B, blocks_per_seq).to(torch.int32)
+    positions = torch.full((B,), args.ctx, dtype=torch.int32)
+    ids = torch.randint(0, V, (B,), generator=torch.Generator().manual_seed(seed + 1), dtype=torch.int32)
+    return eng, shape, table, positions, ids
+
+
+def algorithmic_bytes(shape, args, distinct_per_layer):
+    H, D, E, I = shape.hidden_size, shape.head_dim, shape.num_experts, shape.moe_intermediate_size
+    nq, nkv, V = shape.num_attention_heads, shape.num_key_value_heads, shape.vocab_size
+    B, ctx = args.batch, args.ctx
+    attn_w = ((nq + 2 * nkv) * D * H + H * nq * D) * 2 + (2 * H + 2 * D) * 2
+    router = E * H * 2
+    expert = (2 * I * H + H * I) * 2
+    kv_read = B * ctx * nkv * D * 2 * 2
+    kv_write = B * nkv * D * 2 * 2
+    per_layer_fixed = attn_w + router + kv_read + kv_write
+    total = sum(per_layer_fixed + d * expert for d in distinct_per_layer)
+    total += V * H * 2 + H * 2 + B * H * 2  # LM head, final norm, embedding rows
+    return total
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_layer_sample(args, repeats: int):
+    """Time the oracle (faithful mode) for one decoder layer at the bench shape plus the LM head.
+
+    Returns (seconds per layer list, seconds for the LM head, threads)."""
+    import torch
+
+    from oracle import qwen3_moe_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = O.QwenConfig()
+    gen = torch.Generator().manual_seed(args.seed)
+    lw = O.random_layer(cfg, gen)
+    B, ctx = args.batch, args.ctx
+    nb = ctx // 128 + 1
+    NB = B * nb
+    kc = torch.randn(NB, cfg.n_kv_heads, 128, cfg.head_dim, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(NB, cfg.n_kv_heads, 128, cfg.head_dim, generator=gen).to(torch.bfloat16)
+    table = torch.arange(NB, dtype=torch.int32).view(B, nb)
+    pos = torch.full((B,), ctx, dtype=torch.int32)
+    cos, sin = O.rope_tables(ctx + 1, cfg.head_dim, cfg.rope_theta)
+    x = torch.randn(B, cfg.hidden, generator=gen).to(torch.bfloat16)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        O.decoder_layer(x, lw, cfg, kc, vc, pos, table, cos, sin, "faithful")
+        times.append(time.perf_counter() - t0)
+    lm = (torch.randn(cfg.vocab, cfg.hidden, generator=gen) * 0.02).to(torch.bfloat16)
+    fn = torch.ones(cfg.hidden, dtype=torch.bfloat16)
+    t0 = time.perf_counter()
+    xn = O.rbf(O.rmsnorm_hidden_faithful(x, fn, cfg.rms_eps, gamma_first=False))
+    _ = xn @ lm.float().t()
+    t_head = time.perf_counter() - t0
+    return times, t_head, threads
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times, t_head, threads = cpu_layer_sample(args, args.warmup + args.steps)
+    timed = times[args.warmup:] if len(times) > args.warmup else times
+    step_s = [t * args.layers + t_head for t in timed]
+    value = args.batch / statistics.median(step_s)
+    sample = (f"oracle (faithful PyTorch CPU restatement) of 1 of {args.layers} decoder layers per step at B="
+              f"{args.batch} ctx {args.ctx}, extrapolated x{args.layers}, plus the LM head timed once")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(step_s) * 1e3,
+            "p50_ms": statistics.median(step_s) * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
+            "config": {"workload": "qwen3-30b-a3b decode step (48 layers + LM head)", "batch": args.batch,
+                       "ctx": args.ctx, "kv_block": 128},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def print_stage_times(eng, pos_d, table_d, ids_d, args):
+    """Per-stage durations from the kernel's globaltimer stamps (CTA 0), averaged over layers."""
+    import torch
+
+    names = ["qkv", "attention", "o_proj", "router", "gate_up", "down"]
+    acc = {n: [] for n in names}
+    for _ in range(3):
+        r = eng.decode_step(pos_d, table_d, input_ids=ids_d, stage_times=True)
+        torch.cuda.synchronize()
+        ts = r["stage_ns"].cpu().tolist()
+        d = [(ts[i + 1] - ts[i]) / 1e3 for i in range(len(ts) - 1)]
+        # d[0]: kernel start -> first barrier (input copy); then 6 per layer; last: output + LM head
+        for l in range(args.layers):
+            for k, n in enumerate(names):
+                acc[n].append(d[1 + 6 * l + k])
+        acc.setdefault("input", []).append(d[0])
+        acc.setdefault("lm_head+out", []).append(d[-1])
+        acc.setdefault("total", []).append((ts[-1] - ts[0]) / 1e3)
+    out = {k: round(statistics.median(v), 2) for k, v in acc.items()}
+    per_layer = sum(out[n] for n in names)
+    print(json.dumps({"stage_us_median": out, "per_layer_us": round(per_layer, 2)}), file=sys.stderr, flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    eng, shape, table, positions, ids = build_engine(args, device, args.seed + rank)
+    table_d, pos_d, ids_d = table.to(device), positions.to(device), ids.to(device)
+    out = {"hidden": torch.empty(args.batch, shape.hidden_size, dtype=torch.bfloat16, device=device),
+           "logits": torch.empty(args.batch, shape.vocab_size, dtype=torch.float32, device=device)}
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        eng.decode_step(pos_d, table_d, input_ids=ids_d, out=out)
+
+    # routing of the timed step (identical every step: same inputs, the KV slot is rewritten)
+    tr = eng.decode_step(pos_d, table_d, input_ids=ids_d, trace=True)
+    eng.check_status()
+    distinct = [len(torch.unique(tr["topk_idx"][l])) for l in range(args.layers)]
+    del tr
+    for _ in range(args.warmup):
+        step()
+    eng.check_status()
+    if args.stage_times:
+        print_stage_times(eng, pos_d, table_d, ids_d, args)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clk:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            step()
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    eng.check_status()
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = evs[0].elapsed_time(evs[-1])
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms = total_ms / args.steps
+    value = world * args.batch / (ms / 1e3)
+
+    # end to end through the public API: pinned host inputs in, logits out, every step
+    e2e = None
+    if not args.no_e2e:
+        ids_h = ids.pin_memory()
+        pos_h = positions.pin_memory()
+        tab_h = table.pin_memory()
+        logits_h = torch.empty(args.batch, shape.vocab_size, dtype=torch.float32).pin_memory()
+        for _ in range(2):
+            ids_d.copy_(ids_h, non_blocking=True)
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            ids_d.copy_(ids_h, non_blocking=True)
+            pos_d.copy_(pos_h, non_blocking=True)
+            table_d.copy_(tab_h, non_blocking=True)
+            step()
+            logits_h.copy_(out["logits"], non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * args.batch / (e2e_ms / args.steps / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": ids_h.numel() * 4 + pos_h.numel() * 4 + tab_h.numel() * 4,
+               "d2h_bytes_per_step": logits_h.numel() * 4}
+        eng.check_status()
+
+    nbytes = algorithmic_bytes(shape, args, distinct)
+    peak, peak_kind = measured_peaks()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    traffic_path = os.path.join(ROOT, "profiles", "decode_step_dram_traffic.json")
+    traffic = None
+    if os.path.exists(traffic_path):
+        try:
+            traffic = json.load(open(traffic_path)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times, t_head, threads = cpu_layer_sample(args, 2)
+        step_s = min(times) * args.layers + t_head
+        cpu = {"value": args.batch / step_s, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"oracle (faithful PyTorch CPU restatement), 1 of {args.layers} layers at B={args.batch} "
+                         f"ctx {args.ctx} timed (best of 2) and extrapolated x{args.layers}, plus the LM head"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "p50_ms": statistics.median(per),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights of the Qwen3-30B-A3B architecture, KV prefix ~N(0,1))",
+            "config": {"workload": "qwen3-30b-a3b decode step (48 layers + final norm + LM head)",
+                       "global_batch": world * args.batch, "batch_per_gpu": args.batch, "ctx": args.ctx,
+                       "kv_block": 128, "layers": args.layers,
+                       "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                       "l2": "no flush: ~27 GB of weights streamed per step >> 126 MB L2",
+                       "distinct_experts_per_layer_mean": sum(distinct) / len(distinct)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_step": nbytes,
+                         "kernel": "qwen3_decode_kernel (one launch per step)"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

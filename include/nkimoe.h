@@ -48,7 +48,7 @@ typedef struct nkm_qwen3_layer {
 /* Model description.  Replaces the NxDI model + config objects
  * (qwen_with_megakernel.py:102-132, 601-695). */
 typedef struct nkm_qwen3_desc {
-  int32_t hidden;       /* H (multiple of 256)                   2048   */
+  int32_t hidden;       /* H (multiple of 256, <= 2048)          2048   */
   int32_t n_q_heads;    /* query heads held by this GPU           32    */
   int32_t n_kv_heads;   /* kv heads held by this GPU              4     */
   int32_t head_dim;     /* must be 128                            128   */
@@ -104,8 +104,10 @@ typedef struct nkm_qwen3_step {
   float* trace_topk_w;         /* [nl, B, K] renormalised affinities                      */
   float* trace_router_logits;  /* [nl, B, E]                                              */
   void* trace_qkv;             /* bf16 [nl, B, (nq+2nkv)*128] raw projections             */
-  void* trace_resid_mid;       /* bf16 [nl, B, H] after attention + residual              */
-  void* trace_resid_out;       /* bf16 [nl, B, H] after MoE + residual                    */
+  float* trace_resid_mid;      /* fp32 [nl, B, H] residual stream after attention         */
+  float* trace_resid_out;      /* fp32 [nl, B, H] residual stream after the MoE block     */
+  unsigned long long* trace_stage_ns; /* [3 + 6*nl] globaltimer stamps of CTA 0: kernel start,
+                                  every grid barrier, kernel end (stage timing)            */
 } nkm_qwen3_step;
 
 /* Bytes of device workspace a handle needs (caller allocates, 256-byte aligned). */

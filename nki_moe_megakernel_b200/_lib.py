@@ -47,7 +47,7 @@ class nkm_qwen3_step(ctypes.Structure):
                 ("logits_out", c_void_p), ("first_layer", c_int32), ("num_layers", c_int32),
                 ("stages", c_int32), ("residual", c_int32), ("trace_topk_idx", c_void_p),
                 ("trace_topk_w", c_void_p), ("trace_router_logits", c_void_p), ("trace_qkv", c_void_p),
-                ("trace_resid_mid", c_void_p), ("trace_resid_out", c_void_p)]
+                ("trace_resid_mid", c_void_p), ("trace_resid_out", c_void_p), ("trace_stage_ns", c_void_p)]
 
 
 # name -> (restype, argtypes); every symbol declared in include/nkimoe.h

@@ -66,7 +66,7 @@ WsLayout layout_ws(const nkm_qwen3_desc& d, int num_sms) {
   w.layers = o;
   o = align_up(o + sizeof(nkm::LayerPtrs) * d.n_layers);
   w.resid = o;
-  o = align_up(o + Tm * d.hidden * 2);
+  o = align_up(o + Tm * d.hidden * 4);
   w.qkv = o;
   o = align_up(o + Tm * R * 2);
   w.attn_out = o;
@@ -90,7 +90,8 @@ int nt_for_batch(int T) { return T <= 8 ? 1 : (T <= 16 ? 2 : 4); }
 int check_desc(const nkm_qwen3_desc* d) {
   if (!d) return fail(NKM_ERR_ARG, "desc is NULL");
   if (d->head_dim != nkm::kHeadDim) return fail(NKM_ERR_ARG, "head_dim must be 128 (got %d)", d->head_dim);
-  if (d->hidden <= 0 || d->hidden % 256) return fail(NKM_ERR_ARG, "hidden must be a positive multiple of 256");
+  if (d->hidden <= 0 || d->hidden % 256 || d->hidden > nkm::kMaxHidden)
+    return fail(NKM_ERR_ARG, "hidden must be a positive multiple of 256 and at most %d", nkm::kMaxHidden);
   if (d->n_kv_heads <= 0 || d->n_q_heads <= 0 || d->n_q_heads % d->n_kv_heads)
     return fail(NKM_ERR_ARG, "n_q_heads must be a positive multiple of n_kv_heads");
   if (d->n_q_heads / d->n_kv_heads > nkm::kAttRows)
@@ -316,15 +317,16 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.tr_topk_w = s->trace_topk_w;
   p.tr_rlogits = s->trace_router_logits;
   p.tr_qkv = static_cast<uint16_t*>(s->trace_qkv);
-  p.tr_mid = static_cast<uint16_t*>(s->trace_resid_mid);
-  p.tr_out = static_cast<uint16_t*>(s->trace_resid_out);
+  p.tr_mid = s->trace_resid_mid;
+  p.tr_out = s->trace_resid_out;
+  p.tr_stage = s->trace_stage_ns;
   uint8_t* ws = h->ws;
   p.bar = reinterpret_cast<unsigned*>(ws + h->lay.bar);
   p.status = reinterpret_cast<int*>(ws + h->lay.status);
   p.strip_cnt = reinterpret_cast<unsigned*>(ws + h->lay.strip_cnt);
   p.attn_cnt = reinterpret_cast<unsigned*>(ws + h->lay.attn_cnt);
   p.row_cnt = reinterpret_cast<unsigned*>(ws + h->lay.row_cnt);
-  p.resid = reinterpret_cast<uint16_t*>(ws + h->lay.resid);
+  p.resid = reinterpret_cast<float*>(ws + h->lay.resid);
   p.qkv = reinterpret_cast<uint16_t*>(ws + h->lay.qkv);
   p.attn_out = reinterpret_cast<uint16_t*>(ws + h->lay.attn_out);
   p.att_part = reinterpret_cast<float*>(ws + h->lay.att_part);

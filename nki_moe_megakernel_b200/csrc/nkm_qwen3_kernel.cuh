@@ -1,18 +1,20 @@
 // Persistent cooperative decode-step kernel for Qwen3-MoE on B200 (sm_100a).
 //
-// One CTA per SM, 8 warps per CTA.  Every warp is an independent "worker" with a private
-// ring of 4 KB shared-memory slots that its lane 0 fills with TMA copies (1-D bulk copies
-// of fragment-tiled weights, 2-D swizzled tensor copies of K/V pages); the warp consumes
-// the slots with mma.sync.  Stages of a layer are separated by grid-wide barriers with
-// bounded waits.  The residual stream lives in a small L2-resident global buffer.
+// One CTA per SM, 8 warps per CTA.  In the GEMV stages every warp is an independent
+// "worker" with a private ring of 4 KB shared-memory slots that its lane 0 fills with TMA
+// bulk copies of fragment-tiled weights; the warp consumes the slots with mma.sync.  In the
+// attention stage a CTA owns one (sequence, kv head, context chunk) item and its warps stream
+// the K/V pages through their rings with 2-D swizzled TMA tensor copies.  Stages of a layer
+// are separated by grid-wide barriers with bounded waits.  The residual stream is kept in
+// fp32 in a small L2-resident global buffer.
 //
 // Stages per layer (reference order: megakernels/qwen3_moe/transformer_qwen.py:271-378):
-//   A  RMSNorm(ln1) + QKV GEMV                                   -> qkv (raw bf16)
-//   B  q/k RMSNorm + RoPE, KV write at pos, split-context attention -> attn_out
-//   C  O-proj GEMV + residual add                                -> resid
-//   D  RMSNorm(ln2) + fp32 router logits                          -> rlogits
-//   E  softmax/top-k/renorm (per CTA) + gate/up GEMV + SiLU*up    -> h
-//   F  down GEMV * affinity + per-token combine + residual add    -> resid
+//   A  RMSNorm(ln1) + QKV GEMV                                      -> qkv (raw bf16)
+//   B  q/k RMSNorm + RoPE, KV write at pos, split-context attention -> attn_out (bf16)
+//   C  O-proj GEMV + residual add                                   -> resid (fp32)
+//   D  RMSNorm(ln2) + fp32 router logits                            -> rlogits
+//   E  softmax/top-k/renorm (per CTA) + gate/up GEMV + SiLU*up      -> h (bf16)
+//   F  down GEMV * affinity + per-token combine + residual add      -> resid (fp32)
 #pragma once
 #include "nkm_ptx.cuh"
 
@@ -25,13 +27,15 @@ constexpr int kUnitBytes = 1024;           // one fragment tile: 16 rows x 32 k,
 constexpr int kChunkUnits = kSlotBytes / kUnitBytes;
 constexpr int kHeadDim = 128;
 constexpr int kKvBlock = 128;
-constexpr int kAttTile = 32;               // tokens per attention tile (one TMA box row count)
+constexpr int kAttTile = 32;               // tokens per attention tile (rows of one TMA box)
 constexpr int kMaxExperts = 256;
 constexpr int kMaxPairs = 256;             // max batch * top_k
-constexpr int kAttRows = 16;               // q heads per kv head handled per mma (<= 16)
+constexpr int kMaxHidden = 2048;           // register-resident row loads: 8 groups of 256
+constexpr int kHidGroups = kMaxHidden / 256;
+constexpr int kAttRows = 16;               // q heads per kv head handled by one mma (<= 16)
 constexpr int kAttQStride = kHeadDim + 8;  // bf16 elements per staged q row
-constexpr int kAttScratch = kAttRows * kAttQStride * 2 + 2 * kHeadDim * 2;  // q + k_new + v_new
-constexpr int kPartFloats = 2 * kAttRows + kAttRows * kHeadDim;            // m, l, o
+constexpr int kAttShared = kAttRows * kAttQStride * 2 + 2 * kHeadDim * 2 + kWarps * 2 * kAttRows * 4 + 16;
+constexpr int kPartFloats = 2 * kAttRows + kAttRows * kHeadDim;  // m, l, o of one CTA chunk
 constexpr int kStatusFatal = 4;            // NKM_ERR_TIMEOUT
 constexpr int kStatusIndex = 8;            // NKM_ERR_INDEX
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
@@ -74,14 +78,15 @@ struct Params {
   float* tr_topk_w;
   float* tr_rlogits;
   uint16_t* tr_qkv;
-  uint16_t* tr_mid;
-  uint16_t* tr_out;
+  float* tr_mid;
+  float* tr_out;
+  unsigned long long* tr_stage;
   unsigned* bar;
   int* status;
   unsigned* strip_cnt;
   unsigned* attn_cnt;
   unsigned* row_cnt;
-  uint16_t* resid;
+  float* resid;
   uint16_t* qkv;
   uint16_t* attn_out;
   float* att_part;
@@ -115,7 +120,7 @@ struct SmemLayout {
     uint32_t ring = static_cast<uint32_t>(kWarps * nslot * kSlotBytes);
     xs_off = ring;
     uint32_t xs = static_cast<uint32_t>(8 * NT * (H + 32) * 2);
-    uint32_t att = static_cast<uint32_t>(kWarps * kAttScratch);
+    uint32_t att = static_cast<uint32_t>(kAttShared);
     uint32_t u = xs > att ? xs : att;
     bars_off = xs_off + ((u + 127u) & ~127u);
     rstd_off = bars_off + static_cast<uint32_t>(kWarps * nslot * 8);
@@ -127,7 +132,8 @@ struct SmemLayout {
 
 // ------------------------------------------------------------------ per-warp context
 struct Ctx {
-  uint8_t* ring;
+  uint8_t* ring;       // this warp's ring
+  uint8_t* ring_all;   // ring of warp 0 (rings are contiguous, nslot*4 KB each)
   uint64_t* bars;
   uint32_t phase;
   int head;
@@ -136,15 +142,21 @@ struct Ctx {
   uint64_t pol;
   uint16_t* xs;
   int xs_stride;  // elements per X row
-  uint8_t* att;
+  uint8_t* att;   // CTA-shared attention staging (aliases xs)
   float* rstd;
   Route* rt;
   int* flag;
+  int stage_idx;
 };
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
 __device__ __forceinline__ void set_status(const Params& p, int bit) { atomicOr(p.status, bit); }
+
+__device__ __forceinline__ void stamp(const Params& p, Ctx& c) {
+  if (p.tr_stage && blockIdx.x == 0 && threadIdx.x == 0) p.tr_stage[c.stage_idx] = globaltimer_ns();
+  ++c.stage_idx;
+}
 
 // Bounded wait on a slot's mbarrier.  On timeout the fatal status bit is set and the caller
 // continues (the next grid barrier then aborts every CTA).
@@ -193,6 +205,7 @@ __device__ __noinline__ bool grid_barrier(const Params& p, Ctx& c) {
     *c.flag = ok;
   }
   __syncthreads();
+  stamp(p, c);
   return *c.flag != 0;
 }
 
@@ -212,48 +225,73 @@ __device__ __forceinline__ float rstd_fixed(float sumsq, int n, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(v));
 }
 
-// Sum of squares of one bf16 row of length H (multiple of 256) in the documented order:
-// lane l owns k = 256*i + 8*l + j, accumulated i-outer / j-inner, then a xor butterfly.
-__device__ __forceinline__ float row_sumsq(const uint16_t* row, int H) {
+// One fp32 hidden row in registers: lane l holds k = 256*i + 8*l + j (i < H/256, j < 8).
+struct RowRegs {
+  float v[kHidGroups][8];
+};
+__device__ __forceinline__ void load_row(const float* row, int H, RowRegs& x) {
   const int lane = lane_id();
-  float s = 0.f;
-  for (int i = 0; i < H / 256; ++i) {
-    uint4 v = ldcg128(row + 256 * i + 8 * lane);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float a = lo_bf(w[j]), b = hi_bf(w[j]);
-      s = __fadd_rn(s, __fmul_rn(a, a));
-      s = __fadd_rn(s, __fmul_rn(b, b));
+  for (int i = 0; i < kHidGroups; ++i) {
+    if (i < H / 256) {
+      const float4 a = ldcg_f4(row + 256 * i + 8 * lane);
+      const float4 b = ldcg_f4(row + 256 * i + 8 * lane + 4);
+      x.v[i][0] = a.x; x.v[i][1] = a.y; x.v[i][2] = a.z; x.v[i][3] = a.w;
+      x.v[i][4] = b.x; x.v[i][5] = b.y; x.v[i][6] = b.z; x.v[i][7] = b.w;
+    }
+  }
+}
+// Sum of squares in the documented order (lane-sequential i-outer / j-inner, then a xor
+// butterfly) — the oracle's lane_sum_hidden.
+__device__ __forceinline__ float row_sumsq(const RowRegs& x, int H) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kHidGroups; ++i) {
+    if (i < H / 256) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s = __fadd_rn(s, __fmul_rn(x.v[i][j], x.v[i][j]));
     }
   }
   return warp_sum_fixed(s);
 }
+__device__ __forceinline__ void load_gamma(const uint16_t* g, int H, uint4 (&gv)[kHidGroups]) {
+  const int lane = lane_id();
+#pragma unroll
+  for (int i = 0; i < kHidGroups; ++i)
+    if (i < H / 256) gv[i] = ldnc128(g + 256 * i + 8 * lane);
+}
+__device__ __forceinline__ float gam(const uint4 (&gv)[kHidGroups], int i, int j) {
+  const uint32_t w = (j < 2) ? gv[i].x : (j < 4) ? gv[i].y : (j < 6) ? gv[i].z : gv[i].w;
+  return (j & 1) ? hi_bf(w) : lo_bf(w);
+}
 
-// RMSNorm of the residual rows into X shared memory (bf16), one warp per token.
-// gamma_first=false: (x*r)*g (attn_fused_nki.py:306-309); true: (x*g)*r (moe_fused_nki.py:114-147).
-__device__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first,
-                                  bool write_x) {
+// RMSNorm of the residual rows into X shared memory (bf16), one warp per token; also stores
+// the row's rstd.  gamma_first=false: (x*r)*g (attn_fused_nki.py:306-309);
+// true: (x*g)*r (moe_fused_nki.py:114-147).
+__device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
   for (int t = warp; t < p.T; t += kWarps) {
-    const uint16_t* row = p.resid + static_cast<size_t>(t) * p.H;
-    const float r = rstd_fixed(row_sumsq(row, p.H), p.H, p.eps);
+    RowRegs x;
+    uint4 gv[kHidGroups];
+    load_row(p.resid + static_cast<size_t>(t) * p.H, p.H, x);
+    load_gamma(gamma, p.H, gv);
+    const float r = rstd_fixed(row_sumsq(x, p.H), p.H, p.eps);
     if (lane == 0) c.rstd[t] = r;
-    if (!write_x) continue;
     uint16_t* xr = c.xs + static_cast<size_t>(t) * c.xs_stride;
-    for (int k0 = 8 * lane; k0 < p.H; k0 += 256) {
-      uint4 xv = ldcg128(row + k0);
-      uint4 gv = ldnc128(gamma + k0);
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
-      uint32_t o[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float x0 = lo_bf(xw[j]), x1 = hi_bf(xw[j]), g0 = lo_bf(gw[j]), g1 = hi_bf(gw[j]);
-        float y0 = gamma_first ? __fmul_rn(__fmul_rn(x0, g0), r) : __fmul_rn(__fmul_rn(x0, r), g0);
-        float y1 = gamma_first ? __fmul_rn(__fmul_rn(x1, g1), r) : __fmul_rn(__fmul_rn(x1, r), g1);
-        o[j] = pack_bf2(y0, y1);
+    for (int i = 0; i < kHidGroups; ++i) {
+      if (i < p.H / 256) {
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float g0 = gam(gv, i, 2 * j), g1 = gam(gv, i, 2 * j + 1);
+          const float x0 = x.v[i][2 * j], x1 = x.v[i][2 * j + 1];
+          const float y0 = gamma_first ? __fmul_rn(__fmul_rn(x0, g0), r) : __fmul_rn(__fmul_rn(x0, r), g0);
+          const float y1 = gamma_first ? __fmul_rn(__fmul_rn(x1, g1), r) : __fmul_rn(__fmul_rn(x1, r), g1);
+          o[j] = pack_bf2(y0, y1);
+        }
+        *reinterpret_cast<uint4*>(xr + 256 * i + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      *reinterpret_cast<uint4*>(xr + k0) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
@@ -312,9 +350,44 @@ __device__ __forceinline__ uint4 load_bfrag(const Params& p, const Ctx& c, int s
 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// Level-2 combine of the MoE output for one 16-row strip: sum the top-k slots of every token
+// in slot order (moe_fused_nki.py:542-568) and add into the residual.
+__device__ __noinline__ void moe_row_combine(const Params& p, Ctx& c, int strip, int layer) {
+  const int lane = lane_id();
+  const int n = 16 * p.T;
+  for (int base = 0; base < n; base += 32 * 4) {
+    float v[4][8];
+    int tt[4], rr[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = base + u * 32 + lane;
+      tt[u] = idx >> 4;
+      rr[u] = strip * 16 + (idx & 15);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        v[u][k] = (idx < n && k < p.K)
+                      ? ldcg_f(p.ypair + static_cast<size_t>(c.rt->pmap[tt[u] * p.K + k]) * p.H + rr[u])
+                      : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = base + u * 32 + lane;
+      if (idx >= n) continue;
+      float a = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < p.K) a += v[u][k];
+      float* x = p.resid + static_cast<size_t>(tt[u]) * p.H + rr[u];
+      const float nv = (p.residual ? *x : 0.f) + rbf(a);
+      *x = nv;
+      if (p.tr_out) p.tr_out[(static_cast<size_t>(layer - p.first_layer) * p.T + tt[u]) * p.H + rr[u]] = nv;
+    }
+  }
+}
+
 // Final write of one strip's accumulators (all of K reduced).
 template <int NT, int KIND>
-__device__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4]) {
+__device__ __forceinline__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4]) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int ncols = seg_cols<KIND>(p, c, seg);
 #pragma unroll
@@ -336,13 +409,13 @@ __device__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int se
         }
       } else if constexpr (KIND == GK_OPROJ) {
         const int r0 = strip * 16 + g;
-        uint16_t* x = p.resid + static_cast<size_t>(col) * p.H;
-        const float b0 = p.residual ? bf2f(x[r0]) : 0.f, b1 = p.residual ? bf2f(x[r0 + 8]) : 0.f;
-        const uint16_t n0 = f2bf(b0 + rbf(v0)), n1 = f2bf(b1 + rbf(v1));
+        float* x = p.resid + static_cast<size_t>(col) * p.H;
+        const float n0 = (p.residual ? x[r0] : 0.f) + rbf(v0);
+        const float n1 = (p.residual ? x[r0 + 8] : 0.f) + rbf(v1);
         x[r0] = n0;
         x[r0 + 8] = n1;
         if (p.tr_mid) {
-          uint16_t* tm = p.tr_mid + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.H;
+          float* tm = p.tr_mid + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.H;
           tm[r0] = n0;
           tm[r0 + 8] = n1;
         }
@@ -366,8 +439,7 @@ __device__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int se
     }
   }
   if constexpr (KIND == GK_DOWN) {
-    // Level-2 combine: when every active expert has finished this row strip, sum the
-    // top-k slots of each token in slot order and add into the residual.
+    // when every active expert has finished this row strip, combine it into the residual
     __threadfence();
     __syncwarp();
     unsigned old = 0;
@@ -375,16 +447,7 @@ __device__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int se
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old == static_cast<unsigned>(c.rt->nA - 1)) {
       __threadfence();
-      for (int idx = lane; idx < 16 * p.T; idx += 32) {
-        const int t = idx >> 4, row = strip * 16 + (idx & 15);
-        float a = 0.f;
-        for (int k = 0; k < p.K; ++k) a += ldcg_f(p.ypair + static_cast<size_t>(c.rt->pmap[t * p.K + k]) * p.H + row);
-        uint16_t* x = p.resid + static_cast<size_t>(t) * p.H + row;
-        const float base = p.residual ? bf2f(*x) : 0.f;
-        const uint16_t nv = f2bf(base + rbf(a));
-        *x = nv;
-        if (p.tr_out) p.tr_out[(static_cast<size_t>(G.layer - p.first_layer) * p.T + t) * p.H + row] = nv;
-      }
+      moe_row_combine(p, c, strip, G.layer);
       if (lane == 0) p.row_cnt[strip] = 0u;
     }
   }
@@ -401,7 +464,7 @@ __device__ __forceinline__ int worker_of(int64_t u, int64_t NU, int NW) {
 // Split-K partial of a strip: store it, and if this worker is the last contributor, sum all
 // contributions in worker order and run the epilogue.
 template <int NT, int KIND>
-__device__ void gemv_partial(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4],
+__device__ __forceinline__ void gemv_partial(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4],
                              int64_t u0, int64_t NU, int NWe) {
   const int lane = lane_id();
   const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
@@ -423,17 +486,30 @@ __device__ void gemv_partial(const Params& p, Ctx& c, const GemvGeom& G, int seg
   float sum[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) sum[nt][0] = sum[nt][1] = sum[nt][2] = sum[nt][3] = 0.f;
-  for (int w = wf; w <= wl; ++w) {
-    const int64_t wu0 = range_lo(NU, w, NWe);
-    const int sl = (wu0 >= s0 && wu0 < s1) ? 0 : 1;
-    const float* src = p.gpart + ((static_cast<size_t>(w) * 2 + sl) * NT * 32 + lane) * 4;
+  for (int w0 = wf; w0 <= wl; w0 += 4) {
+    float4 v[4][NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      float4 v = ldcg_f4(src + nt * 128);
-      sum[nt][0] += v.x;
-      sum[nt][1] += v.y;
-      sum[nt][2] += v.z;
-      sum[nt][3] += v.w;
+    for (int u = 0; u < 4; ++u) {
+      const int w = w0 + u;
+      if (w <= wl) {
+        const int64_t wu0 = range_lo(NU, w, NWe);
+        const int sl = (wu0 >= s0 && wu0 < s1) ? 0 : 1;
+        const float* src = p.gpart + ((static_cast<size_t>(w) * 2 + sl) * NT * 32 + lane) * 4;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) v[u][nt] = ldcg_f4(src + nt * 128);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (w0 + u <= wl) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          sum[nt][0] += v[u][nt].x;
+          sum[nt][1] += v[u][nt].y;
+          sum[nt][2] += v[u][nt].z;
+          sum[nt][3] += v[u][nt].w;
+        }
+      }
     }
   }
   if (lane == 0) p.strip_cnt[gstrip] = 0u;
@@ -443,7 +519,7 @@ __device__ void gemv_partial(const Params& p, Ctx& c, const GemvGeom& G, int seg
 // One GEMV stage: the unit space (segments x strips x k-tiles, 1 KB each) is split into
 // contiguous ranges, one per worker; each worker streams its range through its TMA ring.
 template <int NT, int KIND>
-__device__ void gemv_stage(const Params& p, Ctx& c, const GemvGeom& G) {
+__device__ __noinline__ void gemv_stage(const Params& p, Ctx& c, const GemvGeom& G) {
   const int lane = lane_id();
   const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
   const int64_t NU = upseg * G.nseg;
@@ -593,8 +669,7 @@ __device__ __forceinline__ void head_norm_rope(float (&x)[4], const uint16_t* w,
   for (int j = 0; j < 4; ++j) x[j] = rbf(__fadd_rn(rbf(__fmul_rn(xn[j], cf[j])), rbf(__fmul_rn(rot[j], sf[j]))));
 }
 
-__device__ __forceinline__ void load4_bf(const uint16_t* src, float (&x)[4]) {
-  const uint2 v = ldcg64(src);
+__device__ __forceinline__ void unpack4(uint2 v, float (&x)[4]) {
   x[0] = lo_bf(v.x);
   x[1] = hi_bf(v.x);
   x[2] = lo_bf(v.y);
@@ -606,77 +681,20 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float score_round(float acc) { return rbf(rbf(acc) * kScoreScale); }
 
-// Attention for one (sequence b, kv head h, context chunk ch) item.
-__device__ void attention_item(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch, int CT, int item,
-                               const CUtensorMap* kmap, const CUtensorMap* vmap) {
-  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const int pos = __ldg(p.positions + b);
-  const int tok_beg = ch * CT;
-  const int tok_end = min(pos, (ch + 1) * CT);
-  const bool last = (ch == nch - 1);
-  uint16_t* qs = reinterpret_cast<uint16_t*>(c.att);
-  uint16_t* kn = qs + kAttRows * kAttQStride;
-  uint16_t* vn = kn + kHeadDim;
-  const int prow = min(max(pos, 0), p.rope_max - 1);
-  const uint16_t* cosr = p.rope_cos + static_cast<size_t>(prow) * kHeadDim;
-  const uint16_t* sinr = p.rope_sin + static_cast<size_t>(prow) * kHeadDim;
-  const LayerPtrs& lw = p.layers[layer];
-  const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
-
-  // --- q heads of the group: norm + RoPE -> staged bf16 rows
-  for (int i = 0; i < kAttRows; ++i) {
-    uint2 outv = make_uint2(0, 0);
-    if (i < p.grp) {
-      float x[4];
-      load4_bf(qkv_b + static_cast<size_t>(h * p.grp + i) * kHeadDim + 4 * lane, x);
-      head_norm_rope(x, lw.qn, cosr, sinr, p.eps);
-      outv = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
-    }
-    *reinterpret_cast<uint2*>(qs + i * kAttQStride + 4 * lane) = outv;
-  }
-  // --- the new token's K/V (last chunk only): stage, and write into the paged cache
-  if (last) {
-    float kx[4], vx[4];
-    load4_bf(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim + 4 * lane, kx);
-    load4_bf(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane, vx);
-    head_norm_rope(kx, lw.kn, cosr, sinr, p.eps);
-    const uint2 kw = make_uint2(pack_bf2(kx[0], kx[1]), pack_bf2(kx[2], kx[3]));
-    const uint2 vw = make_uint2(pack_bf2(vx[0], vx[1]), pack_bf2(vx[2], vx[3]));
-    *reinterpret_cast<uint2*>(kn + 4 * lane) = kw;
-    *reinterpret_cast<uint2*>(vn + 4 * lane) = vw;
-    const int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
-    if (blk >= 0 && blk < p.num_blocks) {
-      const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * kKvBlock * kHeadDim +
-                         static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
-      *reinterpret_cast<uint2*>(p.k_pool + off) = kw;
-      *reinterpret_cast<uint2*>(p.v_pool + off) = vw;
-    } else if (blk >= p.num_blocks && lane == 0) {
-      set_status(p, kStatusIndex);
-    }
-  }
-  __syncwarp();
-  uint32_t qa[8][4];
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    const uint16_t* r0 = qs + g * kAttQStride + 16 * ks + 2 * t4;
-    const uint16_t* r1 = qs + (g + 8) * kAttQStride + 16 * ks + 2 * t4;
-    qa[ks][0] = *reinterpret_cast<const uint32_t*>(r0);
-    qa[ks][1] = *reinterpret_cast<const uint32_t*>(r1);
-    qa[ks][2] = *reinterpret_cast<const uint32_t*>(r0 + 8);
-    qa[ks][3] = *reinterpret_cast<const uint32_t*>(r1 + 8);
-  }
-  float m[2] = {-1e30f, -1e30f}, l[2] = {0.f, 0.f};
-  float o[16][4];
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-
-  // --- prior context tiles, streamed as 4 TMA boxes per tile: K[d0:64], K[d64:128], V[..], V[..]
-  const int ntile = tok_end > tok_beg ? (tok_end - tok_beg + kAttTile - 1) / kAttTile : 0;
+// Per-warp flash-decode over the 32-token tiles tile_first, tile_first+step, ... of
+// [tok_beg, tok_end).  Leaves the unnormalised (m, l, o) of rows g and g+8 in registers.
+__device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg, int tok_end,
+                                int tile_first, int tile_step, const uint32_t (&qa)[8][4], float (&m)[2],
+                                float (&l)[2], float (&o)[16][4], const CUtensorMap* kmap,
+                                const CUtensorMap* vmap) {
+  const int lane = lane_id(), t4 = lane & 3;
+  const int ntile_all = tok_end > tok_beg ? (tok_end - tok_beg + kAttTile - 1) / kAttTile : 0;
+  const int ntile = ntile_all > tile_first ? (ntile_all - tile_first + tile_step - 1) / tile_step : 0;
   const int nbox = 4 * ntile;
   const size_t head_rows = static_cast<size_t>(layer) * p.num_blocks;
   auto issue_box = [&](int bi, int slot) {
     if (lane == 0) {
-      const int tile = bi >> 2, kind = bi & 3;
+      const int tile = tile_first + (bi >> 2) * tile_step, kind = bi & 3;
       const int tok0 = tok_beg + tile * kAttTile;
       int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + tok0 / kKvBlock);
       if (blk < 0 || blk >= p.num_blocks) {
@@ -689,13 +707,15 @@ __device__ void attention_item(const Params& p, Ctx& c, int layer, int b, int h,
       tma_load_2d(c.ring + slot * kSlotBytes, kind < 2 ? kmap : vmap, (kind & 1) * 64, row, &c.bars[slot]);
     }
   };
-  int pb = 0, ps = c.head;
-  for (; pb < nbox && pb < c.nslot; ++pb) {
-    issue_box(pb, ps);
-    ps = (ps + 1 == c.nslot) ? 0 : ps + 1;
-  }
-  int cs = c.head;
   auto next_slot = [&](int s) { return (s + 1 == c.nslot) ? 0 : s + 1; };
+  int pb = 0;
+  {
+    int ps = c.head;
+    for (; pb < nbox && pb < c.nslot; ++pb) {
+      issue_box(pb, ps);
+      ps = next_slot(ps);
+    }
+  }
   auto refill = [&](int slot) {
     __syncwarp();
     if (pb < nbox) {
@@ -703,8 +723,9 @@ __device__ void attention_item(const Params& p, Ctx& c, int layer, int b, int h,
       ++pb;
     }
   };
-  for (int tile = 0; tile < ntile; ++tile) {
-    const int tok0 = tok_beg + tile * kAttTile;
+  int cs = c.head;
+  for (int i = 0; i < ntile; ++i) {
+    const int tok0 = tok_beg + (tile_first + i * tile_step) * kAttTile;
     const int nvalid = min(kAttTile, tok_end - tok0);
     // ---- S = Q K^T  (16 rows x 32 tokens)
     const int sk0 = cs, sk1 = next_slot(cs);
@@ -805,9 +826,89 @@ __device__ void attention_item(const Params& p, Ctx& c, int layer, int b, int h,
     }
   }
   c.head = cs;
+}
+
+// One (sequence b, kv head h, context chunk ch) item, processed by the whole CTA.
+__device__ __noinline__ void attention_cta_item(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch, int CT,
+                                   int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  const int warp = threadIdx.x >> 5, lane = lane_id(), g = lane >> 2, t4 = lane & 3;
+  const int pos = max(__ldg(p.positions + b), 0);
+  const int tok_beg = ch * CT;
+  const int tok_end = min(pos, (ch + 1) * CT);
+  const bool last = (ch == nch - 1);
+  uint16_t* qs = reinterpret_cast<uint16_t*>(c.att);
+  uint16_t* kn = qs + kAttRows * kAttQStride;
+  uint16_t* vn = kn + kHeadDim;
+  float* wml = reinterpret_cast<float*>(vn + kHeadDim);  // [warp][m 16 | l 16]
+  int* cflag = reinterpret_cast<int*>(wml + kWarps * 2 * kAttRows);
+  const int prow = min(pos, p.rope_max - 1);
+  const uint16_t* cosr = p.rope_cos + static_cast<size_t>(prow) * kHeadDim;
+  const uint16_t* sinr = p.rope_sin + static_cast<size_t>(prow) * kHeadDim;
+  const LayerPtrs& lw = p.layers[layer];
+  const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
+
+  // --- stage q (rows warp, warp+8) and, in the last chunk, the new token's K/V
+  {
+    const int r0 = warp, r1 = warp + kWarps;
+    uint2 q0 = make_uint2(0, 0), q1 = make_uint2(0, 0), kv = make_uint2(0, 0), vv = make_uint2(0, 0);
+    const bool doK = last && warp == 0;
+    if (r0 < p.grp) q0 = ldcg64(qkv_b + static_cast<size_t>(h * p.grp + r0) * kHeadDim + 4 * lane);
+    if (r1 < p.grp) q1 = ldcg64(qkv_b + static_cast<size_t>(h * p.grp + r1) * kHeadDim + 4 * lane);
+    if (doK) {
+      kv = ldcg64(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim + 4 * lane);
+      vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
+    }
+    float x[4];
+    uint2 out = make_uint2(0, 0);
+    if (r0 < p.grp) {
+      unpack4(q0, x);
+      head_norm_rope(x, lw.qn, cosr, sinr, p.eps);
+      out = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
+    }
+    *reinterpret_cast<uint2*>(qs + r0 * kAttQStride + 4 * lane) = out;
+    out = make_uint2(0, 0);
+    if (r1 < p.grp) {
+      unpack4(q1, x);
+      head_norm_rope(x, lw.qn, cosr, sinr, p.eps);
+      out = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
+    }
+    if (r1 < kAttRows) *reinterpret_cast<uint2*>(qs + r1 * kAttQStride + 4 * lane) = out;
+    if (doK) {
+      unpack4(kv, x);
+      head_norm_rope(x, lw.kn, cosr, sinr, p.eps);
+      const uint2 kw = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
+      *reinterpret_cast<uint2*>(kn + 4 * lane) = kw;
+      *reinterpret_cast<uint2*>(vn + 4 * lane) = vv;
+      const int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
+      if (blk >= 0 && blk < p.num_blocks) {
+        const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * kKvBlock * kHeadDim +
+                           static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
+        *reinterpret_cast<uint2*>(p.k_pool + off) = kw;
+        *reinterpret_cast<uint2*>(p.v_pool + off) = vv;
+      } else if (blk >= p.num_blocks && lane == 0) {
+        set_status(p, kStatusIndex);
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t qa[8][4];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint16_t* a0 = qs + g * kAttQStride + 16 * ks + 2 * t4;
+    const uint16_t* a1 = qs + (g + 8) * kAttQStride + 16 * ks + 2 * t4;
+    qa[ks][0] = *reinterpret_cast<const uint32_t*>(a0);
+    qa[ks][1] = *reinterpret_cast<const uint32_t*>(a1);
+    qa[ks][2] = *reinterpret_cast<const uint32_t*>(a0 + 8);
+    qa[ks][3] = *reinterpret_cast<const uint32_t*>(a1 + 8);
+  }
+  float m[2] = {-1e30f, -1e30f}, l[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  attention_tiles(p, c, layer, b, h, tok_beg, tok_end, warp, kWarps, qa, m, l, o, kmap, vmap);
 
   // --- the active token (position pos): score with the fresh K, value the fresh V
-  if (last) {
+  if (last && warp == 0) {
     float d0 = 0.f, d1 = 0.f;
     for (int d = 32 * t4; d < 32 * t4 + 32; d += 2) {
       const uint32_t kw = *reinterpret_cast<const uint32_t*>(kn + d);
@@ -842,82 +943,130 @@ __device__ void attention_item(const Params& p, Ctx& c, int layer, int b, int h,
   l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
   l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
 
-  const size_t out_row = static_cast<size_t>(b) * (p.nq * kHeadDim);
-  if (nch == 1) {
-    const float i0 = 1.f / l[0], i1 = 1.f / l[1];
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const int d = 8 * nt + 2 * t4;
-      if (g < p.grp)
-        *reinterpret_cast<uint32_t*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + g) * kHeadDim + d) =
-            pack_bf2(o[nt][0] * i0, o[nt][1] * i0);
-      if (g + 8 < p.grp)
-        *reinterpret_cast<uint32_t*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + g + 8) * kHeadDim + d) =
-            pack_bf2(o[nt][2] * i1, o[nt][3] * i1);
-    }
-    return;
-  }
-  // --- split context: store (m, l, o) and let the last chunk of (b, h) combine in chunk order
-  float* part = p.att_part + static_cast<size_t>(item) * kPartFloats;
-  if (t4 == 0) {
-    part[g] = m[0];
-    part[g + 8] = m[1];
-    part[kAttRows + g] = l[0];
-    part[kAttRows + g + 8] = l[1];
-  }
-  float* po = part + 2 * kAttRows;
+  // --- per-warp partials into the warp's own (drained) ring; (m, l) into the shared table
+  float* po = reinterpret_cast<float*>(c.ring);  // [16][128]
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
     const int d = 8 * nt + 2 * t4;
     *reinterpret_cast<float2*>(po + g * kHeadDim + d) = make_float2(o[nt][0], o[nt][1]);
     *reinterpret_cast<float2*>(po + (g + 8) * kHeadDim + d) = make_float2(o[nt][2], o[nt][3]);
   }
-  __threadfence();
-  __syncwarp();
-  unsigned old = 0;
-  if (lane == 0) old = atom_acqrel_add_u32(&p.attn_cnt[b * p.nkv + h], 1u);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != static_cast<unsigned>(nch - 1)) return;
-  __threadfence();
-  const int item0 = item - ch;  // items of one (b, h) are consecutive, chunk-major
-  for (int r = 0; r < p.grp; ++r) {
+  if (t4 == 0) {
+    wml[warp * 2 * kAttRows + g] = m[0];
+    wml[warp * 2 * kAttRows + g + 8] = m[1];
+    wml[warp * 2 * kAttRows + kAttRows + g] = l[0];
+    wml[warp * 2 * kAttRows + kAttRows + g + 8] = l[1];
+  }
+  __syncthreads();
+  // --- CTA combine over the 8 warps: warp w owns rows w and w+8
+  const size_t out_row = static_cast<size_t>(b) * (p.nq * kHeadDim);
+  float* part = p.att_part + static_cast<size_t>(item) * kPartFloats;
+  for (int r = warp; r < p.grp; r += kWarps) {
     float M = -1e30f;
-    for (int k = 0; k < nch; ++k) M = fmaxf(M, ldcg_f(p.att_part + static_cast<size_t>(item0 + k) * kPartFloats + r));
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wml[w * 2 * kAttRows + r]);
     float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < nch; ++k) {
-      const float* pk = p.att_part + static_cast<size_t>(item0 + k) * kPartFloats;
-      const float sc = exp2f((ldcg_f(pk + r) - M) * kLog2e);
-      L += ldcg_f(pk + kAttRows + r) * sc;
-      const float4 v = ldcg_f4(pk + 2 * kAttRows + r * kHeadDim + 4 * lane);
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float sc = exp2f((wml[w * 2 * kAttRows + r] - M) * kLog2e);
+      L += wml[w * 2 * kAttRows + kAttRows + r] * sc;
+      const float4 v = *reinterpret_cast<const float4*>(
+          reinterpret_cast<const float*>(c.ring_all + w * c.nslot * kSlotBytes) + r * kHeadDim + 4 * lane);
       acc[0] += v.x * sc;
       acc[1] += v.y * sc;
       acc[2] += v.z * sc;
       acc[3] += v.w * sc;
     }
+    if (nch == 1) {
+      const float il = 1.f / L;
+      *reinterpret_cast<uint2*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + r) * kHeadDim + 4 * lane) =
+          make_uint2(pack_bf2(acc[0] * il, acc[1] * il), pack_bf2(acc[2] * il, acc[3] * il));
+    } else {
+      if (lane == 0) {
+        part[r] = M;
+        part[kAttRows + r] = L;
+      }
+      *reinterpret_cast<float4*>(part + 2 * kAttRows + r * kHeadDim + 4 * lane) =
+          make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+  }
+  if (nch == 1) {
+    __syncthreads();  // the rings are reused by the next item
+    return;
+  }
+  // --- split context: the last CTA of (b, h) combines the chunk partials in chunk order
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atom_acqrel_add_u32(&p.attn_cnt[b * p.nkv + h], 1u);
+    *cflag = (old == static_cast<unsigned>(nch - 1));
+  }
+  __syncthreads();
+  if (!*cflag) return;
+  __threadfence();
+  const int item0 = item - ch;  // items of one (b, h) are consecutive, chunk-major
+  for (int r = warp; r < p.grp; r += kWarps) {
+    // lane k holds chunk k's (m, l) (chunks beyond 32 are folded in a loop)
+    float M = -1e30f;
+    for (int k0 = 0; k0 < nch; k0 += 32) {
+      const int k = k0 + lane;
+      if (k < nch) M = fmaxf(M, ldcg_f(p.att_part + static_cast<size_t>(item0 + k) * kPartFloats + r));
+    }
+    M = warp_max(M);
+    float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < nch; k0 += 8) {
+      float4 v[8];
+      float ms[8], ls[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (k0 + u < nch) {
+          const float* pk = p.att_part + static_cast<size_t>(item0 + k0 + u) * kPartFloats;
+          ms[u] = ldcg_f(pk + r);
+          ls[u] = ldcg_f(pk + kAttRows + r);
+          v[u] = ldcg_f4(pk + 2 * kAttRows + r * kHeadDim + 4 * lane);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (k0 + u < nch) {
+          const float sc = exp2f((ms[u] - M) * kLog2e);
+          L += ls[u] * sc;
+          acc[0] += v[u].x * sc;
+          acc[1] += v[u].y * sc;
+          acc[2] += v[u].z * sc;
+          acc[3] += v[u].w * sc;
+        }
+      }
+    }
     const float il = 1.f / L;
     *reinterpret_cast<uint2*>(p.attn_out + out_row + static_cast<size_t>(h * p.grp + r) * kHeadDim + 4 * lane) =
         make_uint2(pack_bf2(acc[0] * il, acc[1] * il), pack_bf2(acc[2] * il, acc[3] * il));
   }
-  if (lane == 0) p.attn_cnt[b * p.nkv + h] = 0u;
+  if (threadIdx.x == 0) p.attn_cnt[b * p.nkv + h] = 0u;
+  __syncthreads();
 }
 
-__device__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
-  // context chunk length CT: a multiple of 32 chosen so that the number of 32-token tiles per
-  // worker is about one chunk (identical in every warp)
-  int tiles = 0;
+__device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  // chunk length CT (multiple of 32) such that the (b, h, chunk) items fill the grid once
+  const int G = gridDim.x;
+  int tiles = 0, longest = 1;
   for (int b = 0; b < p.T; ++b) {
-    const int pos = max(__ldg(p.positions + b), 0);
-    tiles += p.nkv * ((pos + kAttTile - 1) / kAttTile);
+    const int nt = (max(__ldg(p.positions + b), 0) + kAttTile - 1) / kAttTile;
+    tiles += p.nkv * nt;
+    longest = max(longest, nt);
   }
-  int per = (tiles + c.nworkers - 1) / c.nworkers;
-  if (per < 1) per = 1;
-  const int CT = kAttTile * per;
+  int per = max(1, (tiles + G - 1) / G);
   int nitems = 0;
-  for (int b = 0; b < p.T; ++b) {
-    const int pos = max(__ldg(p.positions + b), 0);
-    nitems += p.nkv * max(1, (pos + CT - 1) / CT);
+  for (;; ++per) {
+    nitems = 0;
+    for (int b = 0; b < p.T; ++b) {
+      const int pos = max(__ldg(p.positions + b), 0);
+      nitems += p.nkv * max(1, (pos + kAttTile * per - 1) / (kAttTile * per));
+    }
+    if (nitems <= G || per >= longest) break;
   }
-  for (int it = c.worker; it < nitems; it += c.nworkers) {
+  const int CT = kAttTile * per;
+  for (int it = blockIdx.x; it < nitems; it += G) {
     int base = 0, b = 0, nch = 1;
     for (b = 0; b < p.T; ++b) {
       const int pos = max(__ldg(p.positions + b), 0);
@@ -926,32 +1075,36 @@ __device__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtens
       base += p.nkv * nch;
     }
     const int r = it - base;
-    attention_item(p, c, layer, b, r / nch, r % nch, nch, CT, it, kmap, vmap);
+    attention_cta_item(p, c, layer, b, r / nch, r % nch, nch, CT, it, kmap, vmap);
   }
 }
 
 // ------------------------------------------------------------------ router (stage D)
-__device__ void router_stage(const Params& p, Ctx& c, int layer) {
+// fp32 logits of (token, expert) items, one warp per item, fixed summation order
+// (moe_fused_nki.py:186-218).
+__device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer) {
   const int lane = lane_id();
   const LayerPtrs& lw = p.layers[layer];
   const int nitems = p.T * p.E;
   for (int it = c.worker; it < nitems; it += c.nworkers) {
     const int t = it / p.E, e = it % p.E;
-    const float r = c.rstd[t];
-    const uint16_t* xr = p.resid + static_cast<size_t>(t) * p.H;
+    RowRegs x;
+    load_row(p.resid + static_cast<size_t>(t) * p.H, p.H, x);
     const uint16_t* wr = lw.router + static_cast<size_t>(e) * p.H;
+    const float r = rstd_fixed(row_sumsq(x, p.H), p.H, p.eps);
     float s = 0.f;
-    for (int i = 0; i < p.H / 256; ++i) {
-      const int k0 = 256 * i + 8 * lane;
-      const uint4 xv = ldcg128(xr + k0), gv = ldnc128(lw.ln2 + k0), wv = ldnc128(wr + k0);
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w},
-                     ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float x0 = __fmul_rn(__fmul_rn(lo_bf(xw[j]), lo_bf(gw[j])), r);
-        const float x1 = __fmul_rn(__fmul_rn(hi_bf(xw[j]), hi_bf(gw[j])), r);
-        s = __fadd_rn(s, __fmul_rn(lo_bf(ww[j]), x0));
-        s = __fadd_rn(s, __fmul_rn(hi_bf(ww[j]), x1));
+    for (int i = 0; i < kHidGroups; ++i) {
+      if (i < p.H / 256) {
+        const uint4 g4 = ldnc128(lw.ln2 + 256 * i + 8 * lane), w4 = ldnc128(wr + 256 * i + 8 * lane);
+        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float gj = (j & 1) ? hi_bf(gw[j >> 1]) : lo_bf(gw[j >> 1]);
+          const float wj = (j & 1) ? hi_bf(ww[j >> 1]) : lo_bf(ww[j >> 1]);
+          const float xn = __fmul_rn(__fmul_rn(x.v[i][j], gj), r);
+          s = __fadd_rn(s, __fmul_rn(wj, xn));
+        }
       }
     }
     s = warp_sum_fixed(s);
@@ -965,7 +1118,7 @@ __device__ void router_stage(const Params& p, Ctx& c, int layer) {
 
 // Softmax / top-k / renorm per token (one warp per token) and the expert tables, in every CTA
 // (moe_fused_nki.py:224-272, 404-418).
-__device__ void routing_prologue(const Params& p, Ctx& c, int layer) {
+__device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
   Route* rt = c.rt;
   const int E = p.E, K = p.K;
@@ -974,6 +1127,7 @@ __device__ void routing_prologue(const Params& p, Ctx& c, int layer) {
     int ids[8];
     const int per = (E + 31) / 32;
     float mx = -INFINITY;
+#pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int e = q * 32 + lane;
       ids[q] = e;
@@ -982,14 +1136,18 @@ __device__ void routing_prologue(const Params& p, Ctx& c, int layer) {
     }
     mx = warp_max(mx);
     float se = 0.f;
+#pragma unroll
     for (int q = 0; q < 8; ++q) se += (q < per && ids[q] < E) ? __expf(v[q] - mx) : 0.f;
     se = warp_sum_fixed(se);
     const float inv = 1.f / se;
     float vals[8];
-    for (int k = 0; k < K; ++k) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k >= K) break;
       // lane-local best (value desc, index asc)
       float bv = -INFINITY;
       int bi = 0x7fffffff;
+#pragma unroll
       for (int q = 0; q < 8; ++q)
         if (v[q] > bv || (v[q] == bv && ids[q] < bi)) {
           bv = v[q];
@@ -1004,6 +1162,7 @@ __device__ void routing_prologue(const Params& p, Ctx& c, int layer) {
           bi = oi;
         }
       }
+#pragma unroll
       for (int q = 0; q < 8; ++q)
         if (ids[q] == bi) v[q] = -INFINITY;
       vals[k] = rbf(__expf(bv - mx) * inv);
@@ -1049,14 +1208,25 @@ __device__ void routing_prologue(const Params& p, Ctx& c, int layer) {
       off += __shfl_sync(0xffffffffu, incl, 31);
     }
     __syncwarp();
-    for (int i = lane; i < NP; i += 32) {
-      const int e = rt->topk_idx[i];
+    // rank of each (token, slot) entry among the entries of its expert (entry order)
+    for (int i0 = 0; i0 < NP; i0 += 32) {
+      const int i = i0 + lane;
+      const int e = (i < NP) ? rt->topk_idx[i] : -1;
       int rank = 0;
-      for (int j = 0; j < i; ++j) rank += (rt->topk_idx[j] == e);
-      const int pr = rt->cnt[e] + rank;
-      rt->pmap[i] = pr;
-      rt->pair_tok[pr] = i / K;
-      rt->pair_w[pr] = rt->topk_w[i];
+      for (int j0 = 0; j0 < i0; j0 += 32) {
+        const int ej = (j0 + lane < NP) ? rt->topk_idx[j0 + lane] : -2;
+        for (int q = 0; q < 32; ++q) rank += (__shfl_sync(0xffffffffu, ej, q) == e);
+      }
+      for (int q = 0; q < 32; ++q) {
+        const int eq = __shfl_sync(0xffffffffu, e, q);
+        if (q < lane && eq == e) ++rank;
+      }
+      if (i < NP) {
+        const int pr = rt->cnt[e] + rank;
+        rt->pmap[i] = pr;
+        rt->pair_tok[pr] = i / K;
+        rt->pair_w[pr] = rt->topk_w[i];
+      }
     }
     if (lane == 0) rt->nA = nA;
     if (blockIdx.x == 0 && p.tr_topk_idx) {
@@ -1080,7 +1250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = lane_id();
   Ctx c;
   c.nslot = lay.nslot;
-  c.ring = smem + lay.ring_off + warp * lay.nslot * kSlotBytes;
+  c.ring_all = smem + lay.ring_off;
+  c.ring = c.ring_all + warp * lay.nslot * kSlotBytes;
   c.bars = reinterpret_cast<uint64_t*>(smem + lay.bars_off) + warp * lay.nslot;
   c.phase = 0;
   c.head = 0;
@@ -1089,10 +1260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.pol = policy_evict_first();
   c.xs = reinterpret_cast<uint16_t*>(smem + lay.xs_off);
   c.xs_stride = p.H + 32;
-  c.att = smem + lay.xs_off + warp * kAttScratch;
+  c.att = smem + lay.xs_off;
   c.rstd = reinterpret_cast<float*>(smem + lay.rstd_off);
   c.rt = reinterpret_cast<Route*>(smem + lay.route_off);
   c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
+  c.stage_idx = 0;
+  stamp(p, c);
   if (lane == 0) {
     for (int s = 0; s < lay.nslot; ++s) mbar_init(&c.bars[s], 1);
     fence_mbar_init();
@@ -1103,7 +1276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncwarp();
 
-  // stage 0: residual <- embeddings / hidden input
+  // stage 0: residual (fp32) <- embeddings / hidden input (bf16)
   {
     const int nvec = p.T * p.H / 8;
     for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads) {
@@ -1115,7 +1288,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         src = p.x_in + static_cast<size_t>(t) * p.H + k;
       }
-      *reinterpret_cast<uint4*>(p.resid + static_cast<size_t>(t) * p.H + k) = ldnc128(src);
+      const uint4 v = ldnc128(src);
+      float* dst = p.resid + static_cast<size_t>(t) * p.H + k;
+      *reinterpret_cast<float4*>(dst) = make_float4(lo_bf(v.x), hi_bf(v.x), lo_bf(v.y), hi_bf(v.y));
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(lo_bf(v.z), hi_bf(v.z), lo_bf(v.w), hi_bf(v.w));
     }
   }
   if (!grid_barrier(p, c)) return;
@@ -1124,7 +1300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const LayerPtrs& lw = p.layers[layer];
     if (p.stages & 1) {
       // A: RMSNorm(ln1) + QKV
-      norm_rows_to_smem(p, c, lw.ln1, false, true);
+      norm_rows_to_smem(p, c, lw.ln1, false);
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
       gemv_stage<NT, GK_QKV>(p, c, ga);
@@ -1139,13 +1315,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (p.stages & 2) {
       // D: router logits (fp32, fixed order)
-      norm_rows_to_smem(p, c, lw.ln2, true, false);
-      __syncthreads();
       router_stage(p, c, layer);
       if (!grid_barrier(p, c)) return;
       // E: routing tables + normed activations + gate/up
       routing_prologue(p, c, layer);
-      norm_rows_to_smem(p, c, lw.ln2, true, true);
+      norm_rows_to_smem(p, c, lw.ln2, true);
       __syncthreads();
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
       gemv_stage<NT, GK_GATEUP>(p, c, ge);
@@ -1159,14 +1333,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   // outputs
   {
     const int nvec = p.T * p.H / 8;
-    for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads)
-      reinterpret_cast<uint4*>(p.y_out)[i] = ldcg128(p.resid + static_cast<size_t>(i) * 8);
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads) {
+      const float4 a = ldcg_f4(p.resid + static_cast<size_t>(i) * 8);
+      const float4 b = ldcg_f4(p.resid + static_cast<size_t>(i) * 8 + 4);
+      reinterpret_cast<uint4*>(p.y_out)[i] =
+          make_uint4(pack_bf2(a.x, a.y), pack_bf2(a.z, a.w), pack_bf2(b.x, b.y), pack_bf2(b.z, b.w));
+    }
   }
   if ((p.stages & 4) && p.logits_out) {
-    norm_rows_to_smem(p, c, p.final_norm, false, true);
+    norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
     GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, p.first_layer + p.num_layers - 1};
     gemv_stage<NT, GK_LMHEAD>(p, c, gl);
+  }
+  if (p.tr_stage) {
+    __syncthreads();
+    stamp(p, c);
   }
 }
 

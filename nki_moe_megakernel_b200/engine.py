@@ -151,7 +151,7 @@ class Qwen3MoeMegakernel:
             batch, _ptr(input_ids), _ptr(x), _ptr(positions), _ptr(block_table),
             0 if block_table is None else block_table.shape[1], _ptr(y), _ptr(logits), first_layer, num_layers,
             stages, residual, _ptr(tr.get("topk_idx")), _ptr(tr.get("topk_w")), _ptr(tr.get("router_logits")),
-            _ptr(tr.get("qkv")), _ptr(tr.get("resid_mid")), _ptr(tr.get("resid_out")))
+            _ptr(tr.get("qkv")), _ptr(tr.get("resid_mid")), _ptr(tr.get("resid_out")), _ptr(tr.get("stage_ns")))
 
     def _alloc_traces(self, batch, nl) -> Dict[str, torch.Tensor]:
         s, dev = self.shape, self.device
@@ -161,17 +161,20 @@ class Qwen3MoeMegakernel:
             "topk_w": torch.zeros(nl, batch, s.num_experts_per_tok, dtype=torch.float32, device=dev),
             "router_logits": torch.zeros(nl, batch, s.num_experts, dtype=torch.float32, device=dev),
             "qkv": torch.zeros(nl, batch, R, dtype=BF16, device=dev),
-            "resid_mid": torch.zeros(nl, batch, s.hidden_size, dtype=BF16, device=dev),
-            "resid_out": torch.zeros(nl, batch, s.hidden_size, dtype=BF16, device=dev),
+            "resid_mid": torch.zeros(nl, batch, s.hidden_size, dtype=torch.float32, device=dev),
+            "resid_out": torch.zeros(nl, batch, s.hidden_size, dtype=torch.float32, device=dev),
+            "stage_ns": torch.zeros(3 + 6 * nl, dtype=torch.int64, device=dev),
         }
 
     def decode_step(self, positions: torch.Tensor, block_table: torch.Tensor, *, x: Optional[torch.Tensor] = None,
                     input_ids: Optional[torch.Tensor] = None, want_logits: bool = True, trace: bool = False,
                     first_layer: int = 0, num_layers: int = 0, out: Optional[Dict[str, torch.Tensor]] = None,
-                    stream=None) -> Dict[str, torch.Tensor]:
+                    stage_times: bool = False, stream=None) -> Dict[str, torch.Tensor]:
         """Run one decode step (all layers by default).  K/V pools are updated in place.
 
-        Returns ``{"hidden": [B,H] bf16, "logits": [B,V] fp32 (if requested), traces...}``.
+        Returns ``{"hidden": [B,H] bf16, "logits": [B,V] fp32 (if requested), traces...}``;
+        ``stage_times`` adds ``stage_ns``: globaltimer stamps of CTA 0 at kernel start, after
+        every grid barrier and at kernel end.
         """
         B = int(positions.shape[0])
         nl = num_layers or (self.shape.num_hidden_layers - first_layer)
@@ -181,6 +184,8 @@ class Qwen3MoeMegakernel:
         if want_logits and self.lm_head_ft is not None and "logits" not in res:
             res["logits"] = torch.empty(B, self.shape.vocab_size, dtype=torch.float32, device=self.device)
         traces = self._alloc_traces(B, nl) if trace else None
+        if stage_times and not trace:
+            traces = {"stage_ns": torch.zeros(3 + 6 * nl, dtype=torch.int64, device=self.device)}
         st = self._step_struct(B, x=x, input_ids=input_ids, positions=positions, block_table=block_table,
                                y=res["hidden"], logits=res.get("logits") if want_logits else None,
                                first_layer=first_layer, num_layers=nl, traces=traces)

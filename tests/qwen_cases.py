@@ -24,7 +24,7 @@ def make_layers(cfg: O.QwenConfig, n_distinct: int, seed: int) -> List[O.LayerWe
     return [O.random_layer(cfg, gen) for _ in range(n_distinct)]
 
 
-def skew_bias(cfg: O.QwenConfig, hot: Sequence[int] = (3, 17, 64, 101), value: float = 2.0) -> torch.Tensor:
+def skew_bias(cfg: O.QwenConfig, hot: Sequence[int] = (3, 17, 64, 101), value: float = 4.0) -> torch.Tensor:
     """Router bias that sends about half of all top-k slots to 4 hot experts."""
     b = torch.zeros(cfg.n_experts, dtype=torch.float32)
     for e in hot:

@@ -61,7 +61,7 @@ int main(void) {
   printf("nkm_qwen3_desc %zu\n", sizeof(nkm_qwen3_desc));
   printf("nkm_qwen3_step %zu\n", sizeof(nkm_qwen3_step));
   P(nkm_qwen3_desc, layers) P(nkm_qwen3_desc, rope_max_pos) P(nkm_qwen3_desc, max_batch)
-  P(nkm_qwen3_step, max_blocks_per_seq) P(nkm_qwen3_step, trace_resid_out) P(nkm_qwen3_layer, router_bias)
+  P(nkm_qwen3_step, max_blocks_per_seq) P(nkm_qwen3_step, trace_resid_out) P(nkm_qwen3_step, trace_stage_ns) P(nkm_qwen3_layer, router_bias)
   return 0;
 }
 """
@@ -80,6 +80,7 @@ int main(void) {
     assert int(got["nkm_qwen3_desc.max_batch"]) == L.nkm_qwen3_desc.max_batch.offset
     assert int(got["nkm_qwen3_step.max_blocks_per_seq"]) == L.nkm_qwen3_step.max_blocks_per_seq.offset
     assert int(got["nkm_qwen3_step.trace_resid_out"]) == L.nkm_qwen3_step.trace_resid_out.offset
+    assert int(got["nkm_qwen3_step.trace_stage_ns"]) == L.nkm_qwen3_step.trace_stage_ns.offset
     assert int(got["nkm_qwen3_layer.router_bias"]) == L.nkm_qwen3_layer.router_bias.offset
 
 
@@ -95,7 +96,7 @@ def _desc(L, **kw):
     return d, layer
 
 
-@pytest.mark.parametrize("bad", [dict(head_dim=64), dict(hidden=2000), dict(top_k=9), dict(max_batch=64),
+@pytest.mark.parametrize("bad", [dict(head_dim=64), dict(hidden=2000), dict(hidden=4096), dict(top_k=9), dict(max_batch=64),
                                  dict(n_q_heads=30), dict(moe_inter=100), dict(block_size=64),
                                  dict(n_experts=300), dict(vocab=100)])
 def test_create_rejects_bad_descriptions(L, bad):

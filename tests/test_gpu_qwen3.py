@@ -91,7 +91,7 @@ def test_moe_block(dev, T, skewed):
     torch.testing.assert_close(res["topk_w"][0].cpu(), w_ref, rtol=8e-3, atol=1e-6)  # 1 bf16 ulp
     if skewed:
         hot = torch.isin(idx, torch.tensor([3, 17, 64, 101])).float().mean().item()
-        assert hot >= 0.4, hot
+        assert hot >= 0.45, hot
     ref = O.moe_block(x, lw, cfg, "fp32")
     _close(res["hidden"], ref, what="moe out vs fp32")
 
@@ -187,7 +187,7 @@ def test_decoder_layer_config0(dev):
     ref = O.decoder_layer(x, lw, cfg, k0.clone()[0], v0.clone()[0], pos, table,
                           *O.rope_tables(4096, cfg.head_dim, cfg.rope_theta, torch.float32), "fp32")
     _close(res["hidden"], ref, what="layer out vs fp32")
-    _close(res["resid_out"][0], res["hidden"], atol=0, cos=1.0, what="trace == output")
+    assert bits_equal(res["resid_out"][0].to(BF16).cpu(), res["hidden"].cpu()), "trace == output"
     # router on the GPU's own post-attention residual: bit-exact
     mid = res["resid_mid"][0].cpu()
     logits = O.router_logits_fixed(O.rmsnorm_hidden_faithful(mid, lw.ln2, cfg.rms_eps, True), lw.router)
