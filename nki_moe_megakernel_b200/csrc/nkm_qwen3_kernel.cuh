@@ -161,13 +161,20 @@ __device__ __forceinline__ void stamp(const Params& p, Ctx& c) {
 // Bounded wait on a slot's mbarrier.  On timeout the fatal status bit is set and the caller
 // continues (the next grid barrier then aborts every CTA).
 __device__ __forceinline__ void slot_wait(const Params& p, Ctx& c, int slot) {
-  uint32_t par = (c.phase >> slot) & 1u;
+  const uint32_t par = (c.phase >> slot) & 1u;
   if (!mbar_try_wait(&c.bars[slot], par)) {
-    uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(&c.bars[slot], par)) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        if (lane_id() == 0) set_status(p, kStatusFatal);
-        break;
+    // try_wait itself suspends for a while; read the (slow) global timer only every 64 tries
+    uint64_t t0 = 0;
+    for (uint32_t it = 1;; ++it) {
+      if (mbar_try_wait(&c.bars[slot], par)) break;
+      if ((it & 63u) == 0) {
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitLimitNs) {
+          if (lane_id() == 0) set_status(p, kStatusFatal);
+          break;
+        }
       }
     }
   }
@@ -352,7 +359,7 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + _
 
 // Level-2 combine of the MoE output for one 16-row strip: sum the top-k slots of every token
 // in slot order (moe_fused_nki.py:542-568) and add into the residual.
-__device__ __noinline__ void moe_row_combine(const Params& p, Ctx& c, int strip, int layer) {
+__device__ __noinline__ void moe_row_combine(const Params& p, const Route* rt, int strip, int layer) {
   const int lane = lane_id();
   const int n = 16 * p.T;
   for (int base = 0; base < n; base += 32 * 4) {
@@ -366,7 +373,7 @@ __device__ __noinline__ void moe_row_combine(const Params& p, Ctx& c, int strip,
 #pragma unroll
       for (int k = 0; k < 8; ++k)
         v[u][k] = (idx < n && k < p.K)
-                      ? ldcg_f(p.ypair + static_cast<size_t>(c.rt->pmap[tt[u] * p.K + k]) * p.H + rr[u])
+                      ? ldcg_f(p.ypair + static_cast<size_t>(rt->pmap[tt[u] * p.K + k]) * p.H + rr[u])
                       : 0.f;
     }
 #pragma unroll
@@ -447,7 +454,7 @@ __device__ __forceinline__ void gemv_epilogue(const Params& p, Ctx& c, const Gem
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old == static_cast<unsigned>(c.rt->nA - 1)) {
       __threadfence();
-      moe_row_combine(p, c, strip, G.layer);
+      moe_row_combine(p, c.rt, strip, G.layer);
       if (lane == 0) p.row_cnt[strip] = 0u;
     }
   }
@@ -519,7 +526,8 @@ __device__ __forceinline__ void gemv_partial(const Params& p, Ctx& c, const Gemv
 // One GEMV stage: the unit space (segments x strips x k-tiles, 1 KB each) is split into
 // contiguous ranges, one per worker; each worker streams its range through its TMA ring.
 template <int NT, int KIND>
-__device__ __noinline__ void gemv_stage(const Params& p, Ctx& c, const GemvGeom& G) {
+__device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGeom& G) {
+  Ctx c = cref;  // register-resident copy for the streaming loop
   const int lane = lane_id();
   const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
   const int64_t NU = upseg * G.nseg;
@@ -637,7 +645,8 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& c, const GemvGeom&
     else
       gemv_partial<NT, KIND>(p, c, G, cur_seg, cur_strip, acc, u0, NU, static_cast<int>(NWe));
   }
-  c.head = cs;
+  cref.head = cs;
+  cref.phase = c.phase;
 }
 
 // ------------------------------------------------------------------ attention
@@ -829,8 +838,8 @@ __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int lay
 }
 
 // One (sequence b, kv head h, context chunk ch) item, processed by the whole CTA.
-__device__ __noinline__ void attention_cta_item(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch, int CT,
-                                   int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+__device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch,
+                                                  int CT, int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
   const int warp = threadIdx.x >> 5, lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int pos = max(__ldg(p.positions + b), 0);
   const int tok_beg = ch * CT;
@@ -1044,6 +1053,14 @@ __device__ __noinline__ void attention_cta_item(const Params& p, Ctx& c, int lay
   }
   if (threadIdx.x == 0) p.attn_cnt[b * p.nkv + h] = 0u;
   __syncthreads();
+}
+
+__device__ __noinline__ void attention_cta_item(const Params& p, Ctx& cref, int layer, int b, int h, int ch, int nch,
+                                                int CT, int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  Ctx c = cref;  // register-resident copy
+  attention_cta_body(p, c, layer, b, h, ch, nch, CT, item, kmap, vmap);
+  cref.head = c.head;
+  cref.phase = c.phase;
 }
 
 __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
