@@ -22,9 +22,9 @@ namespace nkm {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kSlotBytes = 4096;
+constexpr int kSlotBytes = 4096;           // attention ring slot: one 32-token x 64-dim TMA box
 constexpr int kUnitBytes = 1024;           // one fragment tile: 16 rows x 32 k, bf16
-constexpr int kChunkUnits = kSlotBytes / kUnitBytes;
+constexpr int kMaxBars = 4;                // mbarriers per warp (attention uses up to 4 slots)
 constexpr int kHeadDim = 128;
 constexpr int kKvBlock = 128;
 constexpr int kAttTile = 32;               // tokens per attention tile (rows of one TMA box)
@@ -109,21 +109,31 @@ struct Route {
   float pair_w[kMaxPairs];
 };
 
-// Shared-memory layout, identical on host (sizing) and device.
+// Shared-memory layout, identical on host (sizing) and device.  Each warp owns a ring of
+// ring_bytes: the GEMV stages use it as 2 slots of (chunk units x 1 KB), the attention stage
+// as 4 KB slots.
+template <int NT>
+struct RingGeom {
+  static constexpr int kRingBytes = NT == 4 ? 8192 : 16384;
+  static constexpr int kChunk = NT == 4 ? 4 : 8;      // GEMV units per TMA chunk
+  static constexpr int kGemvSlots = kRingBytes / (kChunk * kUnitBytes);
+  static constexpr int kAttSlots = kRingBytes / kSlotBytes;
+  static constexpr int kAccSets = NT == 1 ? 4 : 2;    // independent accumulator chains
+};
+
 struct SmemLayout {
-  int nslot;
+  uint32_t ring_bytes;
   uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, flag_off, total;
-  __host__ __device__ static int nslot_for(int NT) { return NT == 1 ? 5 : (NT == 2 ? 4 : 2); }
   __host__ __device__ SmemLayout(int H, int NT) {
-    nslot = nslot_for(NT);
+    ring_bytes = NT == 4 ? 8192u : 16384u;
     ring_off = 0;
-    uint32_t ring = static_cast<uint32_t>(kWarps * nslot * kSlotBytes);
+    uint32_t ring = static_cast<uint32_t>(kWarps) * ring_bytes;
     xs_off = ring;
     uint32_t xs = static_cast<uint32_t>(8 * NT * (H + 32) * 2);
     uint32_t att = static_cast<uint32_t>(kAttShared);
     uint32_t u = xs > att ? xs : att;
     bars_off = xs_off + ((u + 127u) & ~127u);
-    rstd_off = bars_off + static_cast<uint32_t>(kWarps * nslot * 8);
+    rstd_off = bars_off + static_cast<uint32_t>(kWarps * kMaxBars * 8);
     route_off = rstd_off + 32 * 4;
     flag_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
     total = flag_off + 16 + 1024;  // + alignment slack for the ring base
@@ -133,7 +143,8 @@ struct SmemLayout {
 // ------------------------------------------------------------------ per-warp context
 struct Ctx {
   uint8_t* ring;       // this warp's ring
-  uint8_t* ring_all;   // ring of warp 0 (rings are contiguous, nslot*4 KB each)
+  uint8_t* ring_all;   // ring of warp 0 (rings are contiguous, ring_bytes each)
+  int ring_bytes;
   uint64_t* bars;
   uint32_t phase;
   int head;
@@ -277,6 +288,7 @@ __device__ __forceinline__ float gam(const uint4 (&gv)[kHidGroups], int i, int j
 // true: (x*g)*r (moe_fused_nki.py:114-147).
 __device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
+#pragma unroll 1
   for (int t = warp; t < p.T; t += kWarps) {
     RowRegs x;
     uint4 gv[kHidGroups];
@@ -292,10 +304,10 @@ __device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const ui
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float g0 = gam(gv, i, 2 * j), g1 = gam(gv, i, 2 * j + 1);
-          const float x0 = x.v[i][2 * j], x1 = x.v[i][2 * j + 1];
-          const float y0 = gamma_first ? __fmul_rn(__fmul_rn(x0, g0), r) : __fmul_rn(__fmul_rn(x0, r), g0);
-          const float y1 = gamma_first ? __fmul_rn(__fmul_rn(x1, g1), r) : __fmul_rn(__fmul_rn(x1, r), g1);
-          o[j] = pack_bf2(y0, y1);
+          // (x*r)*g or (x*g)*r without duplicating the code path
+          const float a0 = gamma_first ? g0 : r, b0 = gamma_first ? r : g0;
+          const float a1 = gamma_first ? g1 : r, b1 = gamma_first ? r : g1;
+          o[j] = pack_bf2(__fmul_rn(__fmul_rn(x.v[i][2 * j], a0), b0), __fmul_rn(__fmul_rn(x.v[i][2 * j + 1], a1), b1));
         }
         *reinterpret_cast<uint4*>(xr + 256 * i + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -304,6 +316,10 @@ __device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const ui
 }
 
 // ------------------------------------------------------------------ fragment-tiled GEMV
+// Code size matters here: the persistent kernel runs every stage once per layer, so each
+// stage's instructions are cold in the instruction caches unless the whole per-layer code
+// stays small.  The streaming loop below is kept compact; strip flushes (epilogues and the
+// split-K fix-up) are out of line.
 enum GemvKind { GK_QKV = 0, GK_OPROJ = 1, GK_GATEUP = 2, GK_DOWN = 3, GK_LMHEAD = 4 };
 
 struct GemvGeom {
@@ -316,43 +332,33 @@ struct GemvGeom {
   int layer;
 };
 
-template <int KIND>
-__device__ __forceinline__ const uint8_t* seg_base(const GemvGeom& G, const Ctx& c, int seg) {
-  if constexpr (KIND == GK_GATEUP || KIND == GK_DOWN) {
-    return G.base + static_cast<uint64_t>(c.rt->act_e[seg]) * G.seg_bytes;
-  } else {
-    return G.base;
-  }
+template <int NT>
+struct Acc {
+  float v[NT][4];
+};
+
+__device__ __forceinline__ bool kind_experts(int kind) { return kind == GK_GATEUP || kind == GK_DOWN; }
+
+__device__ __forceinline__ const uint8_t* seg_base(const GemvGeom& G, const Route* rt, int kind, int seg) {
+  return kind_experts(kind) ? G.base + static_cast<uint64_t>(rt->act_e[seg]) * G.seg_bytes : G.base;
 }
 
 // number of columns (tokens) of a segment
-template <int KIND>
-__device__ __forceinline__ int seg_cols(const Params& p, const Ctx& c, int seg) {
-  if constexpr (KIND == GK_GATEUP || KIND == GK_DOWN) {
-    return c.rt->act_cnt[seg];
-  } else {
-    return p.T;
-  }
+__device__ __forceinline__ int seg_cols(const Params& p, const Route* rt, int kind, int seg) {
+  return kind_experts(kind) ? rt->act_cnt[seg] : p.T;
 }
 
 // B fragment (16 bytes: 8 consecutive k of one column) for lane (g,t), n-tile nt.
-template <int KIND>
-__device__ __forceinline__ uint4 load_bfrag(const Params& p, const Ctx& c, int seg, int kt, int nt, int ncols) {
+__device__ __forceinline__ uint4 load_bfrag(const Params& p, const uint16_t* xs, int xs_stride, const Route* rt,
+                                            int kind, int seg, int kt, int nt, int ncols) {
   const int lane = lane_id();
   const int col = nt * 8 + (lane >> 2);
   const int k = kt * 32 + 8 * (lane & 3);
   if (col >= ncols) return make_uint4(0, 0, 0, 0);
-  if constexpr (KIND == GK_QKV || KIND == GK_LMHEAD) {
-    return lds128(smem_addr(c.xs + static_cast<size_t>(col) * c.xs_stride + k));
-  } else if constexpr (KIND == GK_GATEUP) {
-    const int tok = c.rt->pair_tok[c.rt->act_off[seg] + col];
-    return lds128(smem_addr(c.xs + static_cast<size_t>(tok) * c.xs_stride + k));
-  } else if constexpr (KIND == GK_OPROJ) {
-    return ldcg128(p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + k);
-  } else {  // GK_DOWN
-    const int pair = c.rt->act_off[seg] + col;
-    return ldcg128(p.hbuf + static_cast<size_t>(pair) * p.I + k);
-  }
+  if (kind == GK_OPROJ) return ldcg128(p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + k);
+  if (kind == GK_DOWN) return ldcg128(p.hbuf + static_cast<size_t>(rt->act_off[seg] + col) * p.I + k);
+  const int row = kind == GK_GATEUP ? rt->pair_tok[rt->act_off[seg] + col] : col;
+  return lds128(smem_addr(xs + static_cast<size_t>(row) * xs_stride + k));
 }
 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
@@ -362,125 +368,125 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + _
 __device__ __noinline__ void moe_row_combine(const Params& p, const Route* rt, int strip, int layer) {
   const int lane = lane_id();
   const int n = 16 * p.T;
-  for (int base = 0; base < n; base += 32 * 4) {
-    float v[4][8];
-    int tt[4], rr[4];
+#pragma unroll 1
+  for (int idx = lane; idx < n; idx += 32) {
+    const int t = idx >> 4, row = strip * 16 + (idx & 15);
+    float v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int idx = base + u * 32 + lane;
-      tt[u] = idx >> 4;
-      rr[u] = strip * 16 + (idx & 15);
+    for (int k = 0; k < 8; ++k)
+      v[k] = k < p.K ? ldcg_f(p.ypair + static_cast<size_t>(rt->pmap[t * p.K + k]) * p.H + row) : 0.f;
+    float a = 0.f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        v[u][k] = (idx < n && k < p.K)
-                      ? ldcg_f(p.ypair + static_cast<size_t>(rt->pmap[tt[u] * p.K + k]) * p.H + rr[u])
-                      : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int idx = base + u * 32 + lane;
-      if (idx >= n) continue;
-      float a = 0.f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (k < p.K) a += v[u][k];
-      float* x = p.resid + static_cast<size_t>(tt[u]) * p.H + rr[u];
-      const float nv = (p.residual ? *x : 0.f) + rbf(a);
-      *x = nv;
-      if (p.tr_out) p.tr_out[(static_cast<size_t>(layer - p.first_layer) * p.T + tt[u]) * p.H + rr[u]] = nv;
-    }
+    for (int k = 0; k < 8; ++k) a += v[k];
+    float* x = p.resid + static_cast<size_t>(t) * p.H + row;
+    const float nv = (p.residual ? *x : 0.f) + rbf(a);
+    *x = nv;
+    if (p.tr_out) p.tr_out[(static_cast<size_t>(layer - p.first_layer) * p.T + t) * p.H + row] = nv;
   }
 }
 
-// Final write of one strip's accumulators (all of K reduced).
-template <int NT, int KIND>
-__device__ __forceinline__ void gemv_epilogue(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4]) {
+// Final write of one strip's accumulators (all of K reduced): element (row r, column col).
+__device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, const GemvGeom& G, int kind, int seg,
+                                           int strip, int g, int col, float v0, float v1) {
+  if (kind == GK_QKV) {
+    const int r0 = strip * 16 + g;
+    uint16_t* q = p.qkv + static_cast<size_t>(col) * p.R;
+    q[r0] = f2bf(v0);
+    q[r0 + 8] = f2bf(v1);
+    if (p.tr_qkv) {
+      uint16_t* tq = p.tr_qkv + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.R;
+      tq[r0] = f2bf(v0);
+      tq[r0 + 8] = f2bf(v1);
+    }
+  } else if (kind == GK_OPROJ) {
+    const int r0 = strip * 16 + g;
+    float* x = p.resid + static_cast<size_t>(col) * p.H;
+    const float n0 = (p.residual ? x[r0] : 0.f) + rbf(v0);
+    const float n1 = (p.residual ? x[r0 + 8] : 0.f) + rbf(v1);
+    x[r0] = n0;
+    x[r0 + 8] = n1;
+    if (p.tr_mid) {
+      float* tm = p.tr_mid + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.H;
+      tm[r0] = n0;
+      tm[r0 + 8] = n1;
+    }
+  } else if (kind == GK_GATEUP) {
+    // rows 0-7 of the strip are gate rows 8*strip+g, rows 8-15 the matching up rows
+    const int pair = rt->act_off[seg] + col;
+    const float h = rbf(rbf(silu_f(rbf(v0))) * rbf(v1));
+    p.hbuf[static_cast<size_t>(pair) * p.I + strip * 8 + g] = f2bf(h);
+  } else if (kind == GK_DOWN) {
+    const int pair = rt->act_off[seg] + col;
+    const float w = rt->pair_w[pair];
+    float* y = p.ypair + static_cast<size_t>(pair) * p.H + strip * 16 + g;
+    y[0] = v0 * w;
+    y[8] = v1 * w;
+  } else {  // GK_LMHEAD
+    float* lo = p.logits_out + static_cast<size_t>(col) * p.V + strip * 16 + g;
+    lo[0] = v0;
+    lo[8] = v1;
+  }
+}
+
+template <int NT>
+__device__ __noinline__ void gemv_epilogue(const Params& p, const Route* rt, const GemvGeom& G, int kind, int seg,
+                                              int strip, Acc<NT> acc) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const int ncols = seg_cols<KIND>(p, c, seg);
+  const int ncols = seg_cols(p, rt, kind, seg);
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int col = nt * 8 + 2 * t4 + e;
-      if (col >= ncols) continue;
-      const float v0 = acc[nt][e], v1 = acc[nt][2 + e];  // rows g and g+8
-      if constexpr (KIND == GK_QKV) {
-        const int r0 = strip * 16 + g;
-        uint16_t* q = p.qkv + static_cast<size_t>(col) * p.R;
-        q[r0] = f2bf(v0);
-        q[r0 + 8] = f2bf(v1);
-        if (p.tr_qkv) {
-          uint16_t* tq = p.tr_qkv + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.R;
-          tq[r0] = f2bf(v0);
-          tq[r0 + 8] = f2bf(v1);
-        }
-      } else if constexpr (KIND == GK_OPROJ) {
-        const int r0 = strip * 16 + g;
-        float* x = p.resid + static_cast<size_t>(col) * p.H;
-        const float n0 = (p.residual ? x[r0] : 0.f) + rbf(v0);
-        const float n1 = (p.residual ? x[r0 + 8] : 0.f) + rbf(v1);
-        x[r0] = n0;
-        x[r0 + 8] = n1;
-        if (p.tr_mid) {
-          float* tm = p.tr_mid + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.H;
-          tm[r0] = n0;
-          tm[r0 + 8] = n1;
-        }
-      } else if constexpr (KIND == GK_GATEUP) {
-        // rows 0-7 of the strip are gate rows 8*strip+g, rows 8-15 the matching up rows
-        const int pair = c.rt->act_off[seg] + col;
-        const float gt = rbf(v0), up = rbf(v1);
-        const float h = rbf(rbf(silu_f(gt)) * up);
-        p.hbuf[static_cast<size_t>(pair) * p.I + strip * 8 + g] = f2bf(h);
-      } else if constexpr (KIND == GK_DOWN) {
-        const int pair = c.rt->act_off[seg] + col;
-        const float w = c.rt->pair_w[pair];
-        float* y = p.ypair + static_cast<size_t>(pair) * p.H + strip * 16 + g;
-        y[0] = v0 * w;
-        y[8] = v1 * w;
-      } else {  // GK_LMHEAD
-        float* lo = p.logits_out + static_cast<size_t>(col) * p.V + strip * 16 + g;
-        lo[0] = v0;
-        lo[8] = v1;
-      }
+      if (col < ncols) gemv_store(p, rt, G, kind, seg, strip, g, col, acc.v[nt][e], acc.v[nt][2 + e]);
     }
   }
-  if constexpr (KIND == GK_DOWN) {
+  if (kind == GK_DOWN) {
     // when every active expert has finished this row strip, combine it into the residual
     __threadfence();
     __syncwarp();
     unsigned old = 0;
     if (lane == 0) old = atom_acqrel_add_u32(&p.row_cnt[strip], 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == static_cast<unsigned>(c.rt->nA - 1)) {
+    if (old == static_cast<unsigned>(rt->nA - 1)) {
       __threadfence();
-      moe_row_combine(p, c.rt, strip, G.layer);
+      moe_row_combine(p, rt, strip, G.layer);
       if (lane == 0) p.row_cnt[strip] = 0u;
     }
   }
 }
 
-__device__ __forceinline__ int64_t range_lo(int64_t NU, int w, int NW) { return NU * w / NW; }
-__device__ __forceinline__ int worker_of(int64_t u, int64_t NU, int NW) {
-  int w = static_cast<int>((u * NW) / NU);
+// unit range of worker w among NW workers (NU * NW < 2^31 is checked on the host)
+__device__ __forceinline__ int range_lo(int NU, int w, int NW) {
+  return static_cast<int>(static_cast<unsigned>(NU) * static_cast<unsigned>(w) / static_cast<unsigned>(NW));
+}
+__device__ __forceinline__ int worker_of(int u, int NU, int NW) {
+  int w = static_cast<int>(static_cast<unsigned>(u) * static_cast<unsigned>(NW) / static_cast<unsigned>(NU));
   while (w + 1 < NW && range_lo(NU, w + 1, NW) <= u) ++w;
   while (w > 0 && range_lo(NU, w, NW) > u) --w;
   return w;
 }
 
-// Split-K partial of a strip: store it, and if this worker is the last contributor, sum all
-// contributions in worker order and run the epilogue.
-template <int NT, int KIND>
-__device__ __forceinline__ void gemv_partial(const Params& p, Ctx& c, const GemvGeom& G, int seg, int strip, float (&acc)[NT][4],
-                             int64_t u0, int64_t NU, int NWe) {
+// Out-of-line strip flush.  `full`: the worker reduced all of K itself.  Otherwise the
+// partial is stored and the last contributor sums all partials in worker order (split-K
+// fix-up, deterministic) and runs the epilogue.  Partial slot: 0 if the strip is the
+// contributor's first strip, else 1 (only the first contributor can start before it).
+template <int NT>
+__device__ __noinline__ void gemv_flush(const Params& p, const Route* rt, const GemvGeom& G, int kind, int worker,
+                                        int seg, int strip, bool full, int u0, int NU, int NWe, Acc<NT> acc) {
+  if (full) {
+    gemv_epilogue<NT>(p, rt, G, kind, seg, strip, acc);
+    return;
+  }
   const int lane = lane_id();
-  const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
-  const int64_t s0 = seg * upseg + static_cast<int64_t>(strip) * G.kt, s1 = s0 + G.kt;
-  const int slot = (u0 >= s0 && u0 < s1) ? 0 : 1;
-  float* dst = p.gpart + ((static_cast<size_t>(c.worker) * 2 + slot) * NT * 32 + lane) * 4;
+  const int upseg = G.sps * G.kt;
+  const int s0 = seg * upseg + strip * G.kt, s1 = s0 + G.kt;
+  const int slot = (u0 >= s0) ? 0 : 1;
+  float* dst = p.gpart + ((static_cast<size_t>(worker) * 2 + slot) * NT * 32 + lane) * 4;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
-    *reinterpret_cast<float4*>(dst + nt * 128) = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    *reinterpret_cast<float4*>(dst + nt * 128) =
+        make_float4(acc.v[nt][0], acc.v[nt][1], acc.v[nt][2], acc.v[nt][3]);
   __threadfence();
   __syncwarp();
   const int wf = worker_of(s0, NU, NWe), wl = worker_of(s1 - 1, NU, NWe);
@@ -490,162 +496,187 @@ __device__ __forceinline__ void gemv_partial(const Params& p, Ctx& c, const Gemv
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != static_cast<unsigned>(wl - wf)) return;
   __threadfence();
-  float sum[NT][4];
+  const int slot_f = range_lo(NU, wf, NWe) == s0 ? 0 : 1;
+  Acc<NT> sum;
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) sum[nt][0] = sum[nt][1] = sum[nt][2] = sum[nt][3] = 0.f;
+  for (int nt = 0; nt < NT; ++nt) sum.v[nt][0] = sum.v[nt][1] = sum.v[nt][2] = sum.v[nt][3] = 0.f;
+#pragma unroll 1
   for (int w0 = wf; w0 <= wl; w0 += 4) {
     float4 v[4][NT];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int w = w0 + u;
-      if (w <= wl) {
-        const int64_t wu0 = range_lo(NU, w, NWe);
-        const int sl = (wu0 >= s0 && wu0 < s1) ? 0 : 1;
-        const float* src = p.gpart + ((static_cast<size_t>(w) * 2 + sl) * NT * 32 + lane) * 4;
+      const int sl = (w == wf) ? slot_f : 0;
+      const float* src = p.gpart + ((static_cast<size_t>(w) * 2 + sl) * NT * 32 + lane) * 4;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) v[u][nt] = ldcg_f4(src + nt * 128);
-      }
+      for (int nt = 0; nt < NT; ++nt)
+        v[u][nt] = (w <= wl) ? ldcg_f4(src + nt * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      if (w0 + u <= wl) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          sum[nt][0] += v[u][nt].x;
-          sum[nt][1] += v[u][nt].y;
-          sum[nt][2] += v[u][nt].z;
-          sum[nt][3] += v[u][nt].w;
-        }
+      for (int nt = 0; nt < NT; ++nt) {
+        sum.v[nt][0] += v[u][nt].x;
+        sum.v[nt][1] += v[u][nt].y;
+        sum.v[nt][2] += v[u][nt].z;
+        sum.v[nt][3] += v[u][nt].w;
       }
     }
   }
   if (lane == 0) p.strip_cnt[gstrip] = 0u;
-  gemv_epilogue<NT, KIND>(p, c, G, seg, strip, sum);
+  gemv_epilogue<NT>(p, rt, G, kind, seg, strip, sum);
 }
 
 // One GEMV stage: the unit space (segments x strips x k-tiles, 1 KB each) is split into
-// contiguous ranges, one per worker; each worker streams its range through its TMA ring.
-template <int NT, int KIND>
-__device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGeom& G) {
+// contiguous ranges, one per worker; each worker streams its range through its TMA ring in
+// chunks of up to RingGeom::kChunk units that never cross a strip.  Per segment the B-fragment
+// row addresses are computed once; consecutive units feed independent accumulator sets so
+// that the mma dependency chains stay short.
+template <int NT>
+__device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGeom& G, int kind) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
   Ctx c = cref;  // register-resident copy for the streaming loop
-  const int lane = lane_id();
-  const int64_t upseg = static_cast<int64_t>(G.sps) * G.kt;
-  const int64_t NU = upseg * G.nseg;
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
+  const int KT = G.kt, SPS = G.sps;
+  const int upseg = SPS * KT;
+  const int NU = upseg * G.nseg;
   if (NU <= 0) return;
-  int64_t NWe = NU / 2;
-  if (NWe > c.nworkers) NWe = c.nworkers;
-  if (NWe < 1) NWe = 1;
+  const int NWe = max(1, min(c.nworkers, NU / 2));
   if (c.worker >= NWe) return;
-  const int64_t u0 = range_lo(NU, c.worker, static_cast<int>(NWe));
-  const int64_t u1 = range_lo(NU, c.worker + 1, static_cast<int>(NWe));
+  const int u0 = range_lo(NU, c.worker, NWe), u1 = range_lo(NU, c.worker + 1, NWe);
   if (u0 >= u1) return;
-  auto chunk_len = [&](int64_t u) -> int {
-    int64_t segend = (u / upseg + 1) * upseg;
-    int64_t e = u1 < segend ? u1 : segend;
-    int64_t n = e - u;
-    return static_cast<int>(n < kChunkUnits ? n : kChunkUnits);
-  };
-  auto issue = [&](int64_t u, int n, int slot) {
+  const Route* rt = c.rt;
+  const bool smem_b = !(kind == GK_OPROJ || kind == GK_DOWN);
+  // producer cursor
+  int pu = u0, pseg = u0 / upseg, pstrip = (u0 - pseg * upseg) / KT, pkt = u0 - pseg * upseg - pstrip * KT;
+  const uint8_t* pbase = seg_base(G, rt, kind, pseg);
+  auto issue = [&](int slot) {
+    const int n = min(CU, min(KT - pkt, u1 - pu));
     if (lane == 0) {
-      const int seg = static_cast<int>(u / upseg);
-      const uint8_t* src = seg_base<KIND>(G, c, seg) + static_cast<uint64_t>(u - seg * upseg) * kUnitBytes;
+      const uint8_t* src = pbase + static_cast<uint64_t>(pstrip * KT + pkt) * kUnitBytes;
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
-      bulk_g2s(c.ring + slot * kSlotBytes, src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
+      bulk_g2s(c.ring + slot * (CU * kUnitBytes), src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
     }
-  };
-  // fill the ring
-  int64_t pu = u0;
-  {
-    int s = c.head;
-    for (int i = 0; i < c.nslot && pu < u1; ++i) {
-      const int n = chunk_len(pu);
-      issue(pu, n, s);
-      pu += n;
-      s = (s + 1 == c.nslot) ? 0 : s + 1;
-    }
-  }
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  int cur_seg = -1, cur_strip = -1, cur_kt0 = 0, cur_ktn = 0;
-  int cs = c.head;
-  int64_t cu = u0;
-  int seg = static_cast<int>(u0 / upseg);
-  int strip = static_cast<int>((u0 - seg * upseg) / G.kt);
-  int kt = static_cast<int>((u0 - seg * upseg) % G.kt);
-  while (cu < u1) {
-    const int n = chunk_len(cu);
-    const int ncols = seg_cols<KIND>(p, c, seg);
-    const int ntiles = (ncols + 7) >> 3;
-    // B fragments of the whole chunk first (global loads overlap the slot wait)
-    uint4 bf[kChunkUnits][NT];
-    {
-      int kk = kt;
-#pragma unroll
-      for (int i = 0; i < kChunkUnits; ++i) {
-        if (i < n) {
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            bf[i][nt] = (nt < ntiles) ? load_bfrag<KIND>(p, c, seg, kk, nt, ncols) : make_uint4(0, 0, 0, 0);
-        }
-        if (++kk == G.kt) kk = 0;
+    pu += n;
+    pkt += n;
+    if (pkt == KT) {
+      pkt = 0;
+      if (++pstrip == SPS) {
+        pstrip = 0;
+        ++pseg;
+        if (pu < u1) pbase = seg_base(G, rt, kind, pseg);
       }
     }
+  };
+#pragma unroll
+  for (int i = 0; i < NS; ++i)
+    if (pu < u1) issue(i);
+  // consumer cursor and per-segment B-fragment rows
+  int cu = u0, cseg = u0 / upseg, cstrip = (u0 - cseg * upseg) / KT, ckt = u0 - cseg * upseg - cstrip * KT;
+  uint32_t brow_s[NT];        // shared-memory byte address of this lane's B row (smem sources)
+  const uint16_t* brow_g[NT]; // global B row (global sources)
+  int ntiles = 0;
+  auto seg_setup = [&](int seg) {
+    const int ncols = seg_cols(p, rt, kind, seg);
+    ntiles = (ncols + 7) >> 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = nt * 8 + g;
+      const bool ok = col < ncols;
+      if (smem_b) {
+        const int row = (kind == GK_GATEUP && ok) ? rt->pair_tok[rt->act_off[seg] + col] : col;
+        brow_s[nt] = ok ? smem_addr(c.xs + static_cast<size_t>(row) * c.xs_stride + 8 * t4) : 0u;
+        brow_g[nt] = nullptr;
+      } else {
+        brow_s[nt] = 0u;
+        brow_g[nt] = !ok ? nullptr
+                         : (kind == GK_OPROJ ? p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + 8 * t4
+                                             : p.hbuf + static_cast<size_t>(rt->act_off[seg] + col) * p.I + 8 * t4);
+      }
+    }
+  };
+  seg_setup(cseg);
+  float acc[NA][NT][4];
+#pragma unroll
+  for (int a = 0; a < NA; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
+  int strip_kt0 = ckt;
+  int cs = 0;
+#pragma unroll 1
+  while (cu < u1) {
+    const int n = min(CU, min(KT - ckt, u1 - cu));
+    // B fragments of the whole chunk (before the slot wait, so global loads overlap it)
+    uint4 bf[CU][NT];
+    if (smem_b) {
+#pragma unroll
+      for (int i = 0; i < CU; ++i)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          bf[i][nt] = (i < n && brow_s[nt]) ? lds128(brow_s[nt] + (ckt + i) * 64) : make_uint4(0, 0, 0, 0);
+    } else {
+#pragma unroll
+      for (int i = 0; i < CU; ++i)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          bf[i][nt] = (i < n && brow_g[nt]) ? ldcg128(brow_g[nt] + (ckt + i) * 32) : make_uint4(0, 0, 0, 0);
+    }
     slot_wait(p, c, cs);
-    const uint32_t sbase = smem_addr(c.ring + cs * kSlotBytes) + lane * 16;
+    const uint32_t sbase = smem_addr(c.ring + cs * (CU * kUnitBytes)) + lane * 16;
+    uint4 a0[CU], a1[CU];
 #pragma unroll
-    for (int i = 0; i < kChunkUnits; ++i) {
+    for (int i = 0; i < CU; ++i) {
       if (i < n) {
-        if (strip != cur_strip || seg != cur_seg) {
-          if (cur_seg >= 0) {
-            if (cur_kt0 == 0 && cur_ktn == G.kt)
-              gemv_epilogue<NT, KIND>(p, c, G, cur_seg, cur_strip, acc);
-            else
-              gemv_partial<NT, KIND>(p, c, G, cur_seg, cur_strip, acc, u0, NU, static_cast<int>(NWe));
-          }
-          cur_seg = seg;
-          cur_strip = strip;
-          cur_kt0 = kt;
-          cur_ktn = 0;
+        a0[i] = lds128(sbase + i * kUnitBytes);
+        a1[i] = lds128(sbase + i * kUnitBytes + 512);
+      }
+    }
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-        }
-        const uint4 a0 = lds128(sbase + i * kUnitBytes);
-        const uint4 a1 = lds128(sbase + i * kUnitBytes + 512);
+    for (int i = 0; i < CU; ++i) {
+      if (i < n) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           if (nt < ntiles) {
-            mma_bf16(acc[nt], a0.x, a1.x, a0.y, a1.y, bf[i][nt].x, bf[i][nt].y);
-            mma_bf16(acc[nt], a0.z, a1.z, a0.w, a1.w, bf[i][nt].z, bf[i][nt].w);
-          }
-        }
-        ++cur_ktn;
-        if (++kt == G.kt) {
-          kt = 0;
-          if (++strip == G.sps) {
-            strip = 0;
-            ++seg;
+            mma_bf16(acc[i % NA][nt], a0[i].x, a1[i].x, a0[i].y, a1[i].y, bf[i][nt].x, bf[i][nt].y);
+            mma_bf16(acc[i % NA][nt], a0[i].z, a1[i].z, a0[i].w, a1[i].w, bf[i][nt].z, bf[i][nt].w);
           }
         }
       }
     }
     __syncwarp();
-    if (pu < u1) {
-      const int m = chunk_len(pu);
-      issue(pu, m, cs);
-      pu += m;
-    }
-    cs = (cs + 1 == c.nslot) ? 0 : cs + 1;
+    if (pu < u1) issue(cs);
+    cs = (cs + 1 == NS) ? 0 : cs + 1;
     cu += n;
+    ckt += n;
+    if (ckt == KT || cu == u1) {
+      Acc<NT> sum;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v = 0.f;
+#pragma unroll
+          for (int a = 0; a < NA; ++a) v += acc[a][nt][e];
+          sum.v[nt][e] = v;
+        }
+      gemv_flush<NT>(p, rt, G, kind, c.worker, cseg, cstrip, strip_kt0 == 0 && ckt == KT, u0, NU, NWe, sum);
+#pragma unroll
+      for (int a = 0; a < NA; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
+      if (ckt == KT) {
+        ckt = 0;
+        if (++cstrip == SPS) {
+          cstrip = 0;
+          ++cseg;
+          if (cu < u1) seg_setup(cseg);
+        }
+      }
+      strip_kt0 = ckt;
+    }
   }
-  if (cur_seg >= 0) {
-    if (cur_kt0 == 0 && cur_ktn == G.kt)
-      gemv_epilogue<NT, KIND>(p, c, G, cur_seg, cur_strip, acc);
-    else
-      gemv_partial<NT, KIND>(p, c, G, cur_seg, cur_strip, acc, u0, NU, static_cast<int>(NWe));
-  }
-  cref.head = cs;
   cref.phase = c.phase;
 }
 
@@ -690,6 +721,15 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float score_round(float acc) { return rbf(rbf(acc) * kScoreScale); }
 
+// Load one raw bf16 head (4 elements per lane), apply head RMSNorm + RoPE, return bf16x4.
+__device__ __noinline__ uint2 stage_head(const uint16_t* src, const uint16_t* w, const uint16_t* cs,
+                                         const uint16_t* sn, float eps) {
+  float x[4];
+  unpack4(ldcg64(src + 4 * lane_id()), x);
+  head_norm_rope(x, w, cs, sn, eps);
+  return make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
+}
+
 // Per-warp flash-decode over the 32-token tiles tile_first, tile_first+step, ... of
 // [tok_beg, tok_end).  Leaves the unnormalised (m, l, o) of rows g and g+8 in registers.
 __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg, int tok_end,
@@ -733,6 +773,7 @@ __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int lay
     }
   };
   int cs = c.head;
+#pragma unroll 1
   for (int i = 0; i < ntile; ++i) {
     const int tok0 = tok_beg + (tile_first + i * tile_step) * kAttTile;
     const int nvalid = min(kAttTile, tok_end - tok0);
@@ -857,46 +898,26 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
 
   // --- stage q (rows warp, warp+8) and, in the last chunk, the new token's K/V
-  {
-    const int r0 = warp, r1 = warp + kWarps;
-    uint2 q0 = make_uint2(0, 0), q1 = make_uint2(0, 0), kv = make_uint2(0, 0), vv = make_uint2(0, 0);
-    const bool doK = last && warp == 0;
-    if (r0 < p.grp) q0 = ldcg64(qkv_b + static_cast<size_t>(h * p.grp + r0) * kHeadDim + 4 * lane);
-    if (r1 < p.grp) q1 = ldcg64(qkv_b + static_cast<size_t>(h * p.grp + r1) * kHeadDim + 4 * lane);
-    if (doK) {
-      kv = ldcg64(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim + 4 * lane);
-      vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
-    }
-    float x[4];
-    uint2 out = make_uint2(0, 0);
-    if (r0 < p.grp) {
-      unpack4(q0, x);
-      head_norm_rope(x, lw.qn, cosr, sinr, p.eps);
-      out = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
-    }
-    *reinterpret_cast<uint2*>(qs + r0 * kAttQStride + 4 * lane) = out;
-    out = make_uint2(0, 0);
-    if (r1 < p.grp) {
-      unpack4(q1, x);
-      head_norm_rope(x, lw.qn, cosr, sinr, p.eps);
-      out = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
-    }
-    if (r1 < kAttRows) *reinterpret_cast<uint2*>(qs + r1 * kAttQStride + 4 * lane) = out;
-    if (doK) {
-      unpack4(kv, x);
-      head_norm_rope(x, lw.kn, cosr, sinr, p.eps);
-      const uint2 kw = make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
-      *reinterpret_cast<uint2*>(kn + 4 * lane) = kw;
-      *reinterpret_cast<uint2*>(vn + 4 * lane) = vv;
-      const int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
-      if (blk >= 0 && blk < p.num_blocks) {
-        const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * kKvBlock * kHeadDim +
-                           static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
-        *reinterpret_cast<uint2*>(p.k_pool + off) = kw;
-        *reinterpret_cast<uint2*>(p.v_pool + off) = vv;
-      } else if (blk >= p.num_blocks && lane == 0) {
-        set_status(p, kStatusIndex);
-      }
+#pragma unroll 1
+  for (int r = warp; r < kAttRows; r += kWarps) {
+    const uint2 out = r < p.grp ? stage_head(qkv_b + static_cast<size_t>(h * p.grp + r) * kHeadDim, lw.qn, cosr,
+                                             sinr, p.eps)
+                                : make_uint2(0, 0);
+    *reinterpret_cast<uint2*>(qs + r * kAttQStride + 4 * lane) = out;
+  }
+  if (last && warp == kWarps - 1) {
+    const uint2 kw = stage_head(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim, lw.kn, cosr, sinr, p.eps);
+    const uint2 vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
+    *reinterpret_cast<uint2*>(kn + 4 * lane) = kw;
+    *reinterpret_cast<uint2*>(vn + 4 * lane) = vv;
+    const int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
+    if (blk >= 0 && blk < p.num_blocks) {
+      const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * kKvBlock * kHeadDim +
+                         static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
+      *reinterpret_cast<uint2*>(p.k_pool + off) = kw;
+      *reinterpret_cast<uint2*>(p.v_pool + off) = vv;
+    } else if (blk >= p.num_blocks && lane == 0) {
+      set_status(p, kStatusIndex);
     }
   }
   __syncthreads();
@@ -972,15 +993,15 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   float* part = p.att_part + static_cast<size_t>(item) * kPartFloats;
   for (int r = warp; r < p.grp; r += kWarps) {
     float M = -1e30f;
-#pragma unroll
+#pragma unroll 1
     for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wml[w * 2 * kAttRows + r]);
     float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+#pragma unroll 2
     for (int w = 0; w < kWarps; ++w) {
       const float sc = exp2f((wml[w * 2 * kAttRows + r] - M) * kLog2e);
       L += wml[w * 2 * kAttRows + kAttRows + r] * sc;
       const float4 v = *reinterpret_cast<const float4*>(
-          reinterpret_cast<const float*>(c.ring_all + w * c.nslot * kSlotBytes) + r * kHeadDim + 4 * lane);
+          reinterpret_cast<const float*>(c.ring_all + w * c.ring_bytes) + r * kHeadDim + 4 * lane);
       acc[0] += v.x * sc;
       acc[1] += v.y * sc;
       acc[2] += v.z * sc;
@@ -1023,11 +1044,12 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
     }
     M = warp_max(M);
     float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k0 = 0; k0 < nch; k0 += 8) {
-      float4 v[8];
-      float ms[8], ls[8];
+#pragma unroll 1
+    for (int k0 = 0; k0 < nch; k0 += 4) {
+      float4 v[4];
+      float ms[4], ls[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 4; ++u) {
         if (k0 + u < nch) {
           const float* pk = p.att_part + static_cast<size_t>(item0 + k0 + u) * kPartFloats;
           ms[u] = ldcg_f(pk + r);
@@ -1036,7 +1058,7 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
         }
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 4; ++u) {
         if (k0 + u < nch) {
           const float sc = exp2f((ms[u] - M) * kLog2e);
           L += ls[u] * sc;
@@ -1103,6 +1125,7 @@ __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer) {
   const int lane = lane_id();
   const LayerPtrs& lw = p.layers[layer];
   const int nitems = p.T * p.E;
+#pragma unroll 1
   for (int it = c.worker; it < nitems; it += c.nworkers) {
     const int t = it / p.E, e = it % p.E;
     RowRegs x;
@@ -1110,7 +1133,7 @@ __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer) {
     const uint16_t* wr = lw.router + static_cast<size_t>(e) * p.H;
     const float r = rstd_fixed(row_sumsq(x, p.H), p.H, p.eps);
     float s = 0.f;
-#pragma unroll
+#pragma unroll 2
     for (int i = 0; i < kHidGroups; ++i) {
       if (i < p.H / 256) {
         const uint4 g4 = ldnc128(lw.ln2 + 256 * i + 8 * lane), w4 = ldnc128(wr + 256 * i + 8 * lane);
@@ -1139,6 +1162,7 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
   const int warp = threadIdx.x >> 5, lane = lane_id();
   Route* rt = c.rt;
   const int E = p.E, K = p.K;
+#pragma unroll 1
   for (int t = warp; t < p.T; t += kWarps) {
     float v[8];
     int ids[8];
@@ -1158,9 +1182,8 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
     se = warp_sum_fixed(se);
     const float inv = 1.f / se;
     float vals[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (k >= K) break;
+#pragma unroll 1
+    for (int k = 0; k < K; ++k) {
       // lane-local best (value desc, index asc)
       float bv = -INFINITY;
       int bi = 0x7fffffff;
@@ -1186,17 +1209,21 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
       if (lane == 0) rt->topk_idx[t * K + k] = bi;
     }
     float sk = 0.f;
+#pragma unroll 1
     for (int k = 0; k < K; ++k) sk += vals[k];
     const float inv2 = 1.f / sk;
     if (lane == 0) {
+#pragma unroll 1
       for (int k = 0; k < K; ++k) rt->topk_w[t * K + k] = rbf(vals[k] * inv2);
     }
   }
   __syncthreads();
   if (warp == 0) {
     const int NP = p.T * K;
+#pragma unroll 1
     for (int e = lane; e < E; e += 32) rt->cnt[e] = 0;
     __syncwarp();
+#pragma unroll 1
     for (int i = lane; i < NP; i += 32) {
       const int e = rt->topk_idx[i];
       if (e >= 0 && e < E) atomicAdd(&rt->cnt[e], 1);
@@ -1204,6 +1231,7 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
     __syncwarp();
     // active experts in ascending id order, with pair offsets
     int nA = 0, off = 0;
+#pragma unroll 1
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
       const int cnt = (e < E) ? rt->cnt[e] : 0;
@@ -1226,14 +1254,18 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
     }
     __syncwarp();
     // rank of each (token, slot) entry among the entries of its expert (entry order)
+#pragma unroll 1
     for (int i0 = 0; i0 < NP; i0 += 32) {
       const int i = i0 + lane;
       const int e = (i < NP) ? rt->topk_idx[i] : -1;
       int rank = 0;
+#pragma unroll 1
       for (int j0 = 0; j0 < i0; j0 += 32) {
         const int ej = (j0 + lane < NP) ? rt->topk_idx[j0 + lane] : -2;
+#pragma unroll 4
         for (int q = 0; q < 32; ++q) rank += (__shfl_sync(0xffffffffu, ej, q) == e);
       }
+#pragma unroll 4
       for (int q = 0; q < 32; ++q) {
         const int eq = __shfl_sync(0xffffffffu, e, q);
         if (q < lane && eq == e) ++rank;
@@ -1266,10 +1298,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const SmemLayout lay(p.H, NT);
   const int warp = threadIdx.x >> 5, lane = lane_id();
   Ctx c;
-  c.nslot = lay.nslot;
+  c.ring_bytes = lay.ring_bytes;
+  c.nslot = lay.ring_bytes / kSlotBytes;
   c.ring_all = smem + lay.ring_off;
-  c.ring = c.ring_all + warp * lay.nslot * kSlotBytes;
-  c.bars = reinterpret_cast<uint64_t*>(smem + lay.bars_off) + warp * lay.nslot;
+  c.ring = c.ring_all + warp * lay.ring_bytes;
+  c.bars = reinterpret_cast<uint64_t*>(smem + lay.bars_off) + warp * kMaxBars;
   c.phase = 0;
   c.head = 0;
   c.worker = blockIdx.x * kWarps + warp;
@@ -1284,7 +1317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.stage_idx = 0;
   stamp(p, c);
   if (lane == 0) {
-    for (int s = 0; s < lay.nslot; ++s) mbar_init(&c.bars[s], 1);
+    for (int s = 0; s < kMaxBars; ++s) mbar_init(&c.bars[s], 1);
     fence_mbar_init();
   }
   if (threadIdx.x == 0 && (p.stages & 1)) {
@@ -1320,14 +1353,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       norm_rows_to_smem(p, c, lw.ln1, false);
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
-      gemv_stage<NT, GK_QKV>(p, c, ga);
+      gemv_stage<NT>(p, c, ga, GK_QKV);
       if (!grid_barrier(p, c)) return;
       // B: attention (+ KV write)
       attention_stage(p, c, layer, &kmap, &vmap);
       if (!grid_barrier(p, c)) return;
       // C: O-proj + residual
       GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
-      gemv_stage<NT, GK_OPROJ>(p, c, gc);
+      gemv_stage<NT>(p, c, gc, GK_OPROJ);
       if (!grid_barrier(p, c)) return;
     }
     if (p.stages & 2) {
@@ -1339,11 +1372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       norm_rows_to_smem(p, c, lw.ln2, true);
       __syncthreads();
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
-      gemv_stage<NT, GK_GATEUP>(p, c, ge);
+      gemv_stage<NT>(p, c, ge, GK_GATEUP);
       if (!grid_barrier(p, c)) return;
       // F: down + affinity + combine + residual
       GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
-      gemv_stage<NT, GK_DOWN>(p, c, gf);
+      gemv_stage<NT>(p, c, gf, GK_DOWN);
       if (!grid_barrier(p, c)) return;
     }
   }
@@ -1361,7 +1394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
     GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, p.first_layer + p.num_layers - 1};
-    gemv_stage<NT, GK_LMHEAD>(p, c, gl);
+    gemv_stage<NT>(p, c, gl, GK_LMHEAD);
   }
   if (p.tr_stage) {
     __syncthreads();
