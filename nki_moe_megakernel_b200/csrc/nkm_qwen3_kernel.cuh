@@ -575,7 +575,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
     if (pu < u1) issue(i);
   // consumer cursor and per-segment B-fragment rows
   int cu = u0, cseg = u0 / upseg, cstrip = (u0 - cseg * upseg) / KT, ckt = u0 - cseg * upseg - cstrip * KT;
-  uint32_t brow_s[NT];        // shared-memory byte address of this lane's B row (smem sources)
+  const uint4* brow_s[NT];    // this lane's B row in shared memory (smem sources)
   const uint16_t* brow_g[NT]; // global B row (global sources)
   int ntiles = 0;
   auto seg_setup = [&](int seg) {
@@ -587,10 +587,11 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
       const bool ok = col < ncols;
       if (smem_b) {
         const int row = (kind == GK_GATEUP && ok) ? rt->pair_tok[rt->act_off[seg] + col] : col;
-        brow_s[nt] = ok ? smem_addr(c.xs + static_cast<size_t>(row) * c.xs_stride + 8 * t4) : 0u;
+        brow_s[nt] = ok ? reinterpret_cast<const uint4*>(c.xs + static_cast<size_t>(row) * c.xs_stride + 8 * t4)
+                        : nullptr;
         brow_g[nt] = nullptr;
       } else {
-        brow_s[nt] = 0u;
+        brow_s[nt] = nullptr;
         brow_g[nt] = !ok ? nullptr
                          : (kind == GK_OPROJ ? p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + 8 * t4
                                              : p.hbuf + static_cast<size_t>(rt->act_off[seg] + col) * p.I + 8 * t4);
@@ -615,7 +616,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
       for (int i = 0; i < CU; ++i)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-          bf[i][nt] = (i < n && brow_s[nt]) ? lds128(brow_s[nt] + (ckt + i) * 64) : make_uint4(0, 0, 0, 0);
+          bf[i][nt] = (i < n && brow_s[nt]) ? brow_s[nt][(ckt + i) * 4] : make_uint4(0, 0, 0, 0);
     } else {
 #pragma unroll
       for (int i = 0; i < CU; ++i)
@@ -624,23 +625,18 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
           bf[i][nt] = (i < n && brow_g[nt]) ? ldcg128(brow_g[nt] + (ckt + i) * 32) : make_uint4(0, 0, 0, 0);
     }
     slot_wait(p, c, cs);
-    const uint32_t sbase = smem_addr(c.ring + cs * (CU * kUnitBytes)) + lane * 16;
-    uint4 a0[CU], a1[CU];
+    // A fragments: plain shared loads (scheduled by the compiler around the mma chain)
+    const uint4* sa = reinterpret_cast<const uint4*>(c.ring + cs * (CU * kUnitBytes)) + lane;
 #pragma unroll
     for (int i = 0; i < CU; ++i) {
       if (i < n) {
-        a0[i] = lds128(sbase + i * kUnitBytes);
-        a1[i] = lds128(sbase + i * kUnitBytes + 512);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < CU; ++i) {
-      if (i < n) {
+        const uint4 a0 = sa[i * (kUnitBytes / 16)];
+        const uint4 a1 = sa[i * (kUnitBytes / 16) + 32];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           if (nt < ntiles) {
-            mma_bf16(acc[i % NA][nt], a0[i].x, a1[i].x, a0[i].y, a1[i].y, bf[i][nt].x, bf[i][nt].y);
-            mma_bf16(acc[i % NA][nt], a0[i].z, a1[i].z, a0[i].w, a1[i].w, bf[i][nt].z, bf[i][nt].w);
+            mma_bf16(acc[i % NA][nt], a0.x, a1.x, a0.y, a1.y, bf[i][nt].x, bf[i][nt].y);
+            mma_bf16(acc[i % NA][nt], a0.z, a1.z, a0.w, a1.w, bf[i][nt].z, bf[i][nt].w);
           }
         }
       }
