@@ -158,6 +158,7 @@ struct Ctx {
   Route* rt;
   int* flag;
   int stage_idx;
+  int primed;  // the next GEMV stage's first chunks are already in flight
 };
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
@@ -286,28 +287,34 @@ __device__ __forceinline__ float gam(const uint4 (&gv)[kHidGroups], int i, int j
 // RMSNorm of the residual rows into X shared memory (bf16), one warp per token; also stores
 // the row's rstd.  gamma_first=false: (x*r)*g (attn_fused_nki.py:306-309);
 // true: (x*g)*r (moe_fused_nki.py:114-147).
-__device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first) {
+// When x32 is non-null the fp32 normalised rows are also stored there (row stride H).
+__device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first,
+                                               float* x32 = nullptr) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
 #pragma unroll 1
   for (int t = warp; t < p.T; t += kWarps) {
     RowRegs x;
-    uint4 gv[kHidGroups];
     load_row(p.resid + static_cast<size_t>(t) * p.H, p.H, x);
-    load_gamma(gamma, p.H, gv);
     const float r = rstd_fixed(row_sumsq(x, p.H), p.H, p.eps);
     if (lane == 0) c.rstd[t] = r;
     uint16_t* xr = c.xs + static_cast<size_t>(t) * c.xs_stride;
 #pragma unroll
     for (int i = 0; i < kHidGroups; ++i) {
       if (i < p.H / 256) {
+        const uint4 gv = ldnc128(gamma + 256 * i + 8 * lane);
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float g0 = gam(gv, i, 2 * j), g1 = gam(gv, i, 2 * j + 1);
+          const float g0 = lo_bf(gw[j]), g1 = hi_bf(gw[j]);
           // (x*r)*g or (x*g)*r without duplicating the code path
           const float a0 = gamma_first ? g0 : r, b0 = gamma_first ? r : g0;
           const float a1 = gamma_first ? g1 : r, b1 = gamma_first ? r : g1;
-          o[j] = pack_bf2(__fmul_rn(__fmul_rn(x.v[i][2 * j], a0), b0), __fmul_rn(__fmul_rn(x.v[i][2 * j + 1], a1), b1));
+          const float y0 = __fmul_rn(__fmul_rn(x.v[i][2 * j], a0), b0);
+          const float y1 = __fmul_rn(__fmul_rn(x.v[i][2 * j + 1], a1), b1);
+          o[j] = pack_bf2(y0, y1);
+          if (x32) *reinterpret_cast<float2*>(x32 + static_cast<size_t>(t) * p.H + 256 * i + 8 * lane + 2 * j) =
+              make_float2(y0, y1);
         }
         *reinterpret_cast<uint4*>(xr + 256 * i + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -472,11 +479,11 @@ __device__ __forceinline__ int worker_of(int u, int NU, int NW) {
 // fix-up, deterministic) and runs the epilogue.  Partial slot: 0 if the strip is the
 // contributor's first strip, else 1 (only the first contributor can start before it).
 template <int NT>
-__device__ __noinline__ void gemv_flush(const Params& p, const Route* rt, const GemvGeom& G, int kind, int worker,
+__device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const GemvGeom& G, int kind, int worker,
                                         int seg, int strip, bool full, int u0, int NU, int NWe, Acc<NT> acc) {
   if (full) {
     gemv_epilogue<NT>(p, rt, G, kind, seg, strip, acc);
-    return;
+    return true;
   }
   const int lane = lane_id();
   const int upseg = G.sps * G.kt;
@@ -494,7 +501,7 @@ __device__ __noinline__ void gemv_flush(const Params& p, const Route* rt, const 
   unsigned old = 0;
   if (lane == 0) old = atom_acqrel_add_u32(&p.strip_cnt[gstrip], 1u);
   old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != static_cast<unsigned>(wl - wf)) return;
+  if (old != static_cast<unsigned>(wl - wf)) return false;
   __threadfence();
   const int slot_f = range_lo(NU, wf, NWe) == s0 ? 0 : 1;
   Acc<NT> sum;
@@ -525,6 +532,7 @@ __device__ __noinline__ void gemv_flush(const Params& p, const Route* rt, const 
   }
   if (lane == 0) p.strip_cnt[gstrip] = 0u;
   gemv_epilogue<NT>(p, rt, G, kind, seg, strip, sum);
+  return true;
 }
 
 // One GEMV stage: the unit space (segments x strips x k-tiles, 1 KB each) is split into
@@ -532,11 +540,49 @@ __device__ __noinline__ void gemv_flush(const Params& p, const Route* rt, const 
 // chunks of up to RingGeom::kChunk units that never cross a strip.  Per segment the B-fragment
 // row addresses are computed once; consecutive units feed independent accumulator sets so
 // that the mma dependency chains stay short.
+// Issue the first ring chunks of a GEMV stage early (before the grid barrier that precedes
+// it): the weights do not depend on the barrier, so their latency overlaps the barrier.
+template <int NT>
+__device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom& G, int kind) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
+  const int lane = lane_id();
+  const int KT = G.kt, SPS = G.sps, upseg = SPS * KT, NU = upseg * G.nseg;
+  c.primed = 1;
+  if (NU <= 0) return;
+  const int NWe = max(1, min(c.nworkers, NU / 2));
+  if (c.worker >= NWe) return;
+  const int u0 = range_lo(NU, c.worker, NWe), u1 = range_lo(NU, c.worker + 1, NWe);
+  int pu = u0, pseg = u0 / upseg, pstrip = (u0 - pseg * upseg) / KT, pkt = u0 - pseg * upseg - pstrip * KT;
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    if (pu >= u1) break;
+    const int n = min(CU, min(KT - pkt, u1 - pu));
+    if (lane == 0) {
+      const uint8_t* src = seg_base(G, c.rt, kind, pseg) + static_cast<uint64_t>(pstrip * KT + pkt) * kUnitBytes;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[i], static_cast<uint32_t>(n * kUnitBytes));
+      bulk_g2s(c.ring + i * (CU * kUnitBytes), src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[i], c.pol);
+    }
+    pu += n;
+    pkt += n;
+    if (pkt == KT) {
+      pkt = 0;
+      if (++pstrip == SPS) {
+        pstrip = 0;
+        ++pseg;
+      }
+    }
+  }
+}
+
 template <int NT>
 __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGeom& G, int kind) {
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
   Ctx c = cref;  // register-resident copy for the streaming loop
+  const bool primed = c.primed != 0;
+  cref.primed = 0;
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int KT = G.kt, SPS = G.sps;
   const int upseg = SPS * KT;
@@ -551,9 +597,9 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
   // producer cursor
   int pu = u0, pseg = u0 / upseg, pstrip = (u0 - pseg * upseg) / KT, pkt = u0 - pseg * upseg - pstrip * KT;
   const uint8_t* pbase = seg_base(G, rt, kind, pseg);
-  auto issue = [&](int slot) {
+  auto issue = [&](int slot, bool dry) {
     const int n = min(CU, min(KT - pkt, u1 - pu));
-    if (lane == 0) {
+    if (lane == 0 && !dry) {
       const uint8_t* src = pbase + static_cast<uint64_t>(pstrip * KT + pkt) * kUnitBytes;
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
@@ -572,7 +618,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
   };
 #pragma unroll
   for (int i = 0; i < NS; ++i)
-    if (pu < u1) issue(i);
+    if (pu < u1) issue(i, primed);
   // consumer cursor and per-segment B-fragment rows
   int cu = u0, cseg = u0 / upseg, cstrip = (u0 - cseg * upseg) / KT, ckt = u0 - cseg * upseg - cstrip * KT;
   const uint4* brow_s[NT];    // this lane's B row in shared memory (smem sources)
@@ -642,7 +688,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
       }
     }
     __syncwarp();
-    if (pu < u1) issue(cs);
+    if (pu < u1) issue(cs, false);
     cs = (cs + 1 == NS) ? 0 : cs + 1;
     cu += n;
     ckt += n;
@@ -671,6 +717,223 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
         }
       }
       strip_kt0 = ckt;
+    }
+  }
+  cref.phase = c.phase;
+}
+
+// ------------------------------------------------------------------ MoE down projection
+// Work items are (16-row output strip s, active expert j) pairs in strip-major order; an item
+// is one expert's whole K (= I / 32 units, contiguous in the fragment-tiled w2).  Workers own
+// contiguous item ranges, so each worker sees a run of experts for one or two row strips.
+// Per item the accumulators are scaled by the routing affinity and added into a per-warp
+// shared-memory tile acc[token][16 rows]; when the worker leaves a row strip the tile is
+// either final (the worker covered every expert of the strip: it adds the tile into the
+// residual) or a partial (stored; the last contributor sums the partials in worker order and
+// adds them).  The MoE output of a token is therefore sum_experts(w * down(h)) in fp32,
+// rounded to bf16 once before the residual add (moe_fused_nki.py:542-568, 748-757).
+__device__ __forceinline__ const uint8_t* down_item_src(const GemvGeom& G, const Route* rt, int item, int kt) {
+  const int s = item / G.nseg, j = item - s * G.nseg;
+  return G.base + static_cast<uint64_t>(rt->act_e[j]) * G.seg_bytes +
+         static_cast<uint64_t>(s * G.kt + kt) * kUnitBytes;
+}
+
+template <int NT>
+__device__ __noinline__ void down_prime(const Params& p, Ctx& c, const GemvGeom& G) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
+  const int lane = lane_id();
+  const int NI = G.sps * G.nseg, KT = G.kt;
+  c.primed = 1;
+  if (NI <= 0) return;
+  const int NWe = max(1, min(c.nworkers, NI));
+  if (c.worker >= NWe) return;
+  const int i0 = range_lo(NI, c.worker, NWe), i1 = range_lo(NI, c.worker + 1, NWe);
+  int pi = i0, pkt = 0;
+#pragma unroll
+  for (int k = 0; k < NS; ++k) {
+    if (pi >= i1) break;
+    const int n = min(CU, KT - pkt);
+    if (lane == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[k], static_cast<uint32_t>(n * kUnitBytes));
+      bulk_g2s(c.ring + k * (CU * kUnitBytes), down_item_src(G, c.rt, pi, pkt), static_cast<uint32_t>(n * kUnitBytes),
+               &c.bars[k], c.pol);
+    }
+    pkt += n;
+    if (pkt == KT) {
+      pkt = 0;
+      ++pi;
+    }
+  }
+}
+
+// Flush the per-warp row-strip tile `tile` ([T][16] fp32) of strip s.
+__device__ __noinline__ void down_flush(const Params& p, float* tile, int layer, int s, int worker, int i0, int i1,
+                                        int NI, int NWe, int nA) {
+  const int lane = lane_id();
+  const int n = p.T * 16;
+  const int s_lo = s * nA, s_hi = s_lo + nA;  // item range of the strip
+  const bool full = (i0 <= s_lo && s_hi <= i1);
+  __syncwarp();
+  if (!full) {
+    const int slot = (i0 >= s_lo) ? 0 : 1;  // 0: the strip is this worker's first
+    float* dst = p.gpart + (static_cast<size_t>(worker) * 2 + slot) * n;
+#pragma unroll 1
+    for (int e = lane; e < n; e += 32) dst[e] = tile[e];
+    __threadfence();
+    __syncwarp();
+    const int wf = worker_of(s_lo, NI, NWe), wl = worker_of(s_hi - 1, NI, NWe);
+    unsigned old = 0;
+    if (lane == 0) old = atom_acqrel_add_u32(&p.strip_cnt[s], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != static_cast<unsigned>(wl - wf)) {
+#pragma unroll 1
+      for (int e = lane; e < n; e += 32) tile[e] = 0.f;
+      __syncwarp();
+      return;
+    }
+    __threadfence();
+    const int slot_f = (range_lo(NI, wf, NWe) >= s_lo) ? 0 : 1;
+#pragma unroll 1
+    for (int e = lane; e < n; e += 32) {
+      float a = 0.f;
+#pragma unroll 1
+      for (int w = wf; w <= wl; ++w)
+        a += ldcg_f(p.gpart + (static_cast<size_t>(w) * 2 + (w == wf ? slot_f : 0)) * n + e);
+      tile[e] = a;
+    }
+    if (lane == 0) p.strip_cnt[s] = 0u;
+  }
+#pragma unroll 1
+  for (int e = lane; e < n; e += 32) {
+    const int t = e >> 4, row = s * 16 + (e & 15);
+    float* x = p.resid + static_cast<size_t>(t) * p.H + row;
+    const float nv = (p.residual ? *x : 0.f) + rbf(tile[e]);
+    *x = nv;
+    if (p.tr_out) p.tr_out[(static_cast<size_t>(layer - p.first_layer) * p.T + t) * p.H + row] = nv;
+    tile[e] = 0.f;
+  }
+  __syncwarp();
+}
+
+template <int NT>
+__device__ __noinline__ void down_stage(const Params& p, Ctx& cref, const GemvGeom& G) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
+  Ctx c = cref;
+  const bool primed = c.primed != 0;
+  cref.primed = 0;
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3, warp = threadIdx.x >> 5;
+  const int nA = G.nseg, KT = G.kt, NI = G.sps * nA;
+  if (NI <= 0) return;
+  const int NWe = max(1, min(c.nworkers, NI));
+  if (c.worker >= NWe) return;
+  const int i0 = range_lo(NI, c.worker, NWe), i1 = range_lo(NI, c.worker + 1, NWe);
+  if (i0 >= i1) return;
+  const Route* rt = c.rt;
+  float* tile = reinterpret_cast<float*>(c.xs) + warp * (p.T * 16);
+#pragma unroll 1
+  for (int e = lane; e < p.T * 16; e += 32) tile[e] = 0.f;
+  __syncwarp();
+  int pi = i0, pkt = 0;
+  auto issue = [&](int slot, bool dry) {
+    const int n = min(CU, KT - pkt);
+    if (lane == 0 && !dry) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
+      bulk_g2s(c.ring + slot * (CU * kUnitBytes), down_item_src(G, rt, pi, pkt), static_cast<uint32_t>(n * kUnitBytes),
+               &c.bars[slot], c.pol);
+    }
+    pkt += n;
+    if (pkt == KT) {
+      pkt = 0;
+      ++pi;
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < NS; ++k)
+    if (pi < i1) issue(k, primed);
+  float acc[NA][NT][4];
+#pragma unroll
+  for (int a = 0; a < NA; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
+  int ci = i0, ckt = 0, cs = 0;
+  int cj = ci % nA, ncols = rt->act_cnt[cj], off = rt->act_off[cj], ntiles = (ncols + 7) >> 3;
+  const uint16_t* brow[NT];
+  auto item_setup = [&]() {
+    cj = ci % nA;
+    ncols = rt->act_cnt[cj];
+    off = rt->act_off[cj];
+    ntiles = (ncols + 7) >> 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = nt * 8 + g;
+      brow[nt] = col < ncols ? p.hbuf + static_cast<size_t>(off + col) * p.I + 8 * t4 : nullptr;
+    }
+  };
+  item_setup();
+#pragma unroll 1
+  while (ci < i1) {
+    const int n = min(CU, KT - ckt);
+    uint4 bf[CU][NT];
+#pragma unroll
+    for (int i = 0; i < CU; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        bf[i][nt] = (i < n && brow[nt]) ? ldcg128(brow[nt] + (ckt + i) * 32) : make_uint4(0, 0, 0, 0);
+    slot_wait(p, c, cs);
+    const uint4* sa = reinterpret_cast<const uint4*>(c.ring + cs * (CU * kUnitBytes)) + lane;
+#pragma unroll
+    for (int i = 0; i < CU; ++i) {
+      if (i < n) {
+        const uint4 a0 = sa[i * (kUnitBytes / 16)];
+        const uint4 a1 = sa[i * (kUnitBytes / 16) + 32];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (nt < ntiles) {
+            mma_bf16(acc[i % NA][nt], a0.x, a1.x, a0.y, a1.y, bf[i][nt].x, bf[i][nt].y);
+            mma_bf16(acc[i % NA][nt], a0.z, a1.z, a0.w, a1.w, bf[i][nt].z, bf[i][nt].w);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (pi < i1) issue(cs, false);
+    cs = (cs + 1 == NS) ? 0 : cs + 1;
+    ckt += n;
+    if (ckt == KT) {
+      // item done: scale by the affinity and add into the warp's row-strip tile
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = nt * 8 + 2 * t4 + e;
+          float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+          for (int a = 0; a < NA; ++a) {
+            v0 += acc[a][nt][e];
+            v1 += acc[a][nt][2 + e];
+          }
+          if (col < ncols) {
+            const int pair = off + col;
+            const float w = rt->pair_w[pair];
+            float* trow = tile + rt->pair_tok[pair] * 16;
+            trow[g] += v0 * w;
+            trow[g + 8] += v1 * w;
+          }
+        }
+      }
+#pragma unroll
+      for (int a = 0; a < NA; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[a][nt][0] = acc[a][nt][1] = acc[a][nt][2] = acc[a][nt][3] = 0.f;
+      const int s_now = ci / nA;
+      ++ci;
+      ckt = 0;
+      if (ci == i1 || ci / nA != s_now) down_flush(p, tile, G.layer, s_now, c.worker, i0, i1, NI, NWe, nA);
+      if (ci < i1) item_setup();
     }
   }
   cref.phase = c.phase;
@@ -1117,29 +1380,44 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
 // ------------------------------------------------------------------ router (stage D)
 // fp32 logits of (token, expert) items, one warp per item, fixed summation order
 // (moe_fused_nki.py:186-218).
-__device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer) {
+// x32: fp32 normalised rows in shared memory (row stride H), or nullptr to normalise on the
+// fly from the residual with the per-CTA rstd (large batches whose rows do not fit).
+__device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer, const float* x32) {
   const int lane = lane_id();
   const LayerPtrs& lw = p.layers[layer];
   const int nitems = p.T * p.E;
 #pragma unroll 1
   for (int it = c.worker; it < nitems; it += c.nworkers) {
     const int t = it / p.E, e = it % p.E;
-    RowRegs x;
-    load_row(p.resid + static_cast<size_t>(t) * p.H, p.H, x);
     const uint16_t* wr = lw.router + static_cast<size_t>(e) * p.H;
-    const float r = rstd_fixed(row_sumsq(x, p.H), p.H, p.eps);
+    const float r = c.rstd[t];
     float s = 0.f;
-#pragma unroll 2
+#pragma unroll
     for (int i = 0; i < kHidGroups; ++i) {
       if (i < p.H / 256) {
-        const uint4 g4 = ldnc128(lw.ln2 + 256 * i + 8 * lane), w4 = ldnc128(wr + 256 * i + 8 * lane);
-        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+        const int k0 = 256 * i + 8 * lane;
+        const uint4 w4 = ldnc128(wr + k0);
+        float xv[8];
+        if (x32) {
+          const float4 x0 = *reinterpret_cast<const float4*>(x32 + static_cast<size_t>(t) * p.H + k0);
+          const float4 x1 = *reinterpret_cast<const float4*>(x32 + static_cast<size_t>(t) * p.H + k0 + 4);
+          xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+          xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+        } else {
+          const float4 x0 = ldcg_f4(p.resid + static_cast<size_t>(t) * p.H + k0);
+          const float4 x1 = ldcg_f4(p.resid + static_cast<size_t>(t) * p.H + k0 + 4);
+          const uint4 g4 = ldnc128(lw.ln2 + k0);
+          const float raw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            xv[j] = __fmul_rn(__fmul_rn(raw[j], (j & 1) ? hi_bf(gw[j >> 1]) : lo_bf(gw[j >> 1])), r);
+        }
+        const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float gj = (j & 1) ? hi_bf(gw[j >> 1]) : lo_bf(gw[j >> 1]);
           const float wj = (j & 1) ? hi_bf(ww[j >> 1]) : lo_bf(ww[j >> 1]);
-          const float xn = __fmul_rn(__fmul_rn(x.v[i][j], gj), r);
-          s = __fadd_rn(s, __fmul_rn(wj, xn));
+          s = __fadd_rn(s, __fmul_rn(wj, xv[j]));
         }
       }
     }
@@ -1311,6 +1589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.rt = reinterpret_cast<Route*>(smem + lay.route_off);
   c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
   c.stage_idx = 0;
+  c.primed = 0;
   stamp(p, c);
   if (lane == 0) {
     for (int s = 0; s < kMaxBars; ++s) mbar_init(&c.bars[s], 1);
@@ -1340,9 +1619,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<float4*>(dst + 4) = make_float4(lo_bf(v.z), hi_bf(v.z), lo_bf(v.w), hi_bf(v.w));
     }
   }
+  if ((p.stages & 1) && p.num_layers > 0) {  // the first QKV weights stream during the barrier
+    const LayerPtrs& l0 = p.layers[p.first_layer];
+    GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
+    gemv_prime<NT>(p, c, ga, GK_QKV);
+  }
   if (!grid_barrier(p, c)) return;
 
-  for (int layer = p.first_layer; layer < p.first_layer + p.num_layers; ++layer) {
+  const int layer_end = p.first_layer + p.num_layers;
+  const bool want_lm = (p.stages & 4) && p.logits_out;
+  // prime whatever GEMV follows the last stage of `layer` (next layer's QKV, or the LM head)
+  auto prime_after = [&](int layer) {
+    if (layer + 1 < layer_end) {
+      if (p.stages & 1) {
+        const LayerPtrs& nl = p.layers[layer + 1];
+        GemvGeom ga{nl.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer + 1};
+        gemv_prime<NT>(p, c, ga, GK_QKV);
+      }
+    } else if (want_lm) {
+      GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer};
+      gemv_prime<NT>(p, c, gl, GK_LMHEAD);
+    }
+  };
+  for (int layer = p.first_layer; layer < layer_end; ++layer) {
     const LayerPtrs& lw = p.layers[layer];
     if (p.stages & 1) {
       // A: RMSNorm(ln1) + QKV
@@ -1351,28 +1650,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
       gemv_stage<NT>(p, c, ga, GK_QKV);
       if (!grid_barrier(p, c)) return;
-      // B: attention (+ KV write)
+      // B: attention (+ KV write); the O-proj weights start streaming before the barrier
       attention_stage(p, c, layer, &kmap, &vmap);
+      GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
+      gemv_prime<NT>(p, c, gc, GK_OPROJ);
       if (!grid_barrier(p, c)) return;
       // C: O-proj + residual
-      GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
       gemv_stage<NT>(p, c, gc, GK_OPROJ);
+      if (!(p.stages & 2)) prime_after(layer);
       if (!grid_barrier(p, c)) return;
     }
     if (p.stages & 2) {
-      // D: router logits (fp32, fixed order)
-      router_stage(p, c, layer);
-      if (!grid_barrier(p, c)) return;
-      // E: routing tables + normed activations + gate/up
-      routing_prologue(p, c, layer);
-      norm_rows_to_smem(p, c, lw.ln2, true);
+      // D: RMSNorm(ln2) once per CTA (fp32 rows into the idle rings, bf16 rows into X for the
+      // experts), then the router logits (fp32, fixed order)
+      float* x32 = (static_cast<uint32_t>(p.T * p.H * 4) <= static_cast<uint32_t>(kWarps * c.ring_bytes))
+                       ? reinterpret_cast<float*>(c.ring_all)
+                       : nullptr;
+      norm_rows_to_smem(p, c, lw.ln2, true, x32);
       __syncthreads();
+      router_stage(p, c, layer, x32);
+      if (!grid_barrier(p, c)) return;
+      // E: routing tables + gate/up (X from stage D); the down weights start streaming early
+      routing_prologue(p, c, layer);
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
       gemv_stage<NT>(p, c, ge, GK_GATEUP);
+      GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
+      down_prime<NT>(p, c, gf);
       if (!grid_barrier(p, c)) return;
       // F: down + affinity + combine + residual
-      GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
-      gemv_stage<NT>(p, c, gf, GK_DOWN);
+      down_stage<NT>(p, c, gf);
+      prime_after(layer);
       if (!grid_barrier(p, c)) return;
     }
   }
@@ -1386,10 +1693,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           make_uint4(pack_bf2(a.x, a.y), pack_bf2(a.z, a.w), pack_bf2(b.x, b.y), pack_bf2(b.z, b.w));
     }
   }
-  if ((p.stages & 4) && p.logits_out) {
+  if (want_lm) {
     norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
-    GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, p.first_layer + p.num_layers - 1};
+    GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer_end - 1};
     gemv_stage<NT>(p, c, gl, GK_LMHEAD);
   }
   if (p.tr_stage) {
