@@ -1,0 +1,357 @@
+"""Qwen3-MoE model with the B200 decode megakernel (drop-in for the reference module
+``megakernels/qwen3_moe/qwen_with_megakernel.py``).
+
+Same public names as the reference: ``Qwen3MoEV3MultilayerNeuronConfig`` (reference
+:102-132), ``convert_qwen3_moe_hf_to_neuron_state_dict`` (:171-271),
+``NeuronQwen3MoeForCausalLMV3`` with ``get_neuron_config_cls`` / ``get_config_cls`` /
+``convert_hf_to_neuron_state_dict`` / ``compile`` / ``load`` (:601-695) and the alias
+``NeuronQwen3MoeForCausalLM`` (:728).
+
+Token generation (TKG) runs every decoder layer, the final norm and the LM head in ONE
+persistent sm_100a kernel per step (``libnkimoe.so``, C ABI ``include/nkimoe.h``), writing
+each layer's K/V in place into a paged cache (block 128).  Prompt tokens are fed through the
+same decode kernel one position per step (per-sequence positions), so a batch can mix
+sequences that are still reading their prompt with sequences that are generating.
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from ...engine import GpuLayer, Qwen3MoeMegakernel, Qwen3MoeShape
+
+BF16 = torch.bfloat16
+
+
+# ---------------------------------------------------------------------------
+# configs
+# ---------------------------------------------------------------------------
+class Qwen3MoEV3MultilayerNeuronConfig:
+    """Serving configuration (the subset of the reference's MoENeuronConfig that the decode
+    path uses).  Unknown keyword arguments are kept as attributes, like NxDI's config."""
+
+    def __init__(self, batch_size: int = 1, max_batch_size: Optional[int] = None, seq_len: int = 640,
+                 max_context_length: Optional[int] = None, max_length: Optional[int] = None,
+                 tp_degree: int = 1, moe_ep_degree: int = 1, moe_tp_degree: int = 1,
+                 torch_dtype=BF16, pa_block_size: int = 128, pa_num_blocks: Optional[int] = None,
+                 top_k: int = 1, do_sample: bool = False, temperature: float = 1.0, **kwargs):
+        self.batch_size = batch_size
+        self.max_batch_size = max_batch_size or batch_size
+        self.seq_len = seq_len
+        self.max_context_length = max_context_length or seq_len
+        self.max_length = max_length or seq_len
+        self.tp_degree = tp_degree
+        self.moe_ep_degree = moe_ep_degree
+        self.moe_tp_degree = moe_tp_degree
+        self.torch_dtype = torch_dtype
+        self.pa_block_size = pa_block_size
+        blocks_per_seq = (self.max_length + pa_block_size) // pa_block_size
+        self.pa_num_blocks = pa_num_blocks or self.max_batch_size * blocks_per_seq
+        self.top_k = top_k
+        self.do_sample = do_sample
+        self.temperature = temperature
+        for k, v in kwargs.items():
+            setattr(self, k, v)
+        if torch_dtype not in (BF16, "bfloat16"):
+            raise ValueError("the decode megakernel computes in bf16")
+        if tp_degree != 1 or moe_ep_degree != 1:
+            # one GPU per model instance; TP/EP sharding is described by the desc of each rank
+            self.per_rank = True
+
+
+def load_pretrained_config(model_path: Optional[str]):
+    """Return a callable that fills a config from ``<model_path>/config.json`` (reference
+    ``main.py`` passes ``load_config=load_pretrained_config(model_path)``)."""
+
+    def _load(cfg):
+        if model_path and os.path.exists(os.path.join(model_path, "config.json")):
+            with open(os.path.join(model_path, "config.json")) as f:
+                d = json.load(f)
+            for k, v in d.items():
+                setattr(cfg, k, v)
+    return _load
+
+
+class Qwen3MoeInferenceConfig:
+    """Model hyper-parameters (Hugging Face ``Qwen3MoeConfig`` names).  Defaults are
+    Qwen3-30B-A3B.  Router in fp32, softmax, top-k renormalised (reference ``qwen.py:251-277``)."""
+
+    def __init__(self, neuron_config: Qwen3MoEV3MultilayerNeuronConfig, load_config=None, **kwargs):
+        self.neuron_config = neuron_config
+        self.hidden_size = 2048
+        self.num_attention_heads = 32
+        self.num_key_value_heads = 4
+        self.head_dim = 128
+        self.num_experts = 128
+        self.num_experts_per_tok = 8
+        self.moe_intermediate_size = 768
+        self.num_hidden_layers = 48
+        self.vocab_size = 151936
+        self.rms_norm_eps = 1e-6
+        self.rope_theta = 1e6
+        self.max_position_embeddings = 40960
+        self.norm_topk_prob = True
+        self.tie_word_embeddings = False
+        if load_config is not None:
+            load_config(self)
+        for k, v in kwargs.items():
+            setattr(self, k, v)
+        rp = getattr(self, "rope_parameters", None)
+        if isinstance(rp, dict) and "rope_theta" in rp:
+            self.rope_theta = rp["rope_theta"]
+        if getattr(self, "num_local_experts", None) and not kwargs.get("num_experts"):
+            self.num_experts = self.num_local_experts
+        if not self.norm_topk_prob:
+            raise ValueError("the megakernel implements Qwen3's renormalised top-k (norm_topk_prob=True)")
+
+    def shape(self) -> Qwen3MoeShape:
+        return Qwen3MoeShape(hidden_size=self.hidden_size, num_attention_heads=self.num_attention_heads,
+                             num_key_value_heads=self.num_key_value_heads, head_dim=self.head_dim,
+                             num_experts=self.num_experts, num_experts_per_tok=self.num_experts_per_tok,
+                             moe_intermediate_size=self.moe_intermediate_size,
+                             num_hidden_layers=self.num_hidden_layers, vocab_size=self.vocab_size,
+                             rms_norm_eps=self.rms_norm_eps, rope_theta=self.rope_theta,
+                             block_size=self.neuron_config.pa_block_size)
+
+
+# ---------------------------------------------------------------------------
+# checkpoint conversion
+# ---------------------------------------------------------------------------
+def convert_qwen3_moe_hf_to_neuron_state_dict(state_dict: Dict[str, torch.Tensor], config) -> Dict[str, torch.Tensor]:
+    """Normalise a Hugging Face Qwen3-MoE state dict to the per-layer tensors the kernel packs.
+
+    Accepts both checkpoint formats: fused experts (``mlp.experts.gate_up_proj [E, 2I, H]``,
+    ``mlp.experts.down_proj [E, H, I]``, transformers >= 5) and per-expert
+    ``mlp.experts.{e}.{gate,up,down}_proj.weight`` (original checkpoints), which are stacked
+    into the fused form (gate rows then up rows, as the reference's converter builds
+    ``gate_up [E, H, 2I]`` at ``qwen_with_megakernel.py:226-253`` before transposing).
+    FP8 block-quantised weights with ``*_scale_inv`` are dequantised (reference :146-162).
+    Returned keys: ``layers.{l}.{wq,wk,wv,wo,q_norm,k_norm,ln1,ln2,router,gate_up,down}``,
+    ``embed``, ``final_norm``, ``lm_head``.
+    """
+    sd = dict(state_dict)
+    pre = "model." if any(k.startswith("model.") for k in sd) else ""
+    # fp8 block dequant
+    qc = getattr(config, "quantization_config", None)
+    for k in [k for k in sd if k.endswith("_scale_inv")]:
+        base = k[: -len("_scale_inv")]
+        bs = (qc or {}).get("weight_block_size", [128, 128])
+        scales = sd.pop(k).to(torch.float32)
+        w = sd[base].to(torch.float32)
+        s = scales.repeat_interleave(bs[0], 0).repeat_interleave(bs[1], 1)[: w.shape[0], : w.shape[1]]
+        sd[base] = (w * s).to(BF16)
+    out: Dict[str, torch.Tensor] = {}
+    E = config.num_experts
+    for l in range(config.num_hidden_layers):
+        p = f"{pre}layers.{l}."
+        o = f"layers.{l}."
+        out[o + "wq"] = sd[p + "self_attn.q_proj.weight"]
+        out[o + "wk"] = sd[p + "self_attn.k_proj.weight"]
+        out[o + "wv"] = sd[p + "self_attn.v_proj.weight"]
+        out[o + "wo"] = sd[p + "self_attn.o_proj.weight"]
+        out[o + "q_norm"] = sd[p + "self_attn.q_norm.weight"]
+        out[o + "k_norm"] = sd[p + "self_attn.k_norm.weight"]
+        out[o + "ln1"] = sd[p + "input_layernorm.weight"]
+        out[o + "ln2"] = sd[p + "post_attention_layernorm.weight"]
+        out[o + "router"] = sd[p + "mlp.gate.weight"]
+        if p + "mlp.experts.gate_up_proj" in sd:
+            out[o + "gate_up"] = sd[p + "mlp.experts.gate_up_proj"]
+            out[o + "down"] = sd[p + "mlp.experts.down_proj"]
+        else:
+            out[o + "gate_up"] = torch.stack([torch.cat([sd[p + f"mlp.experts.{e}.gate_proj.weight"],
+                                                         sd[p + f"mlp.experts.{e}.up_proj.weight"]], 0)
+                                              for e in range(E)])
+            out[o + "down"] = torch.stack([sd[p + f"mlp.experts.{e}.down_proj.weight"] for e in range(E)])
+    out["embed"] = sd[pre + "embed_tokens.weight"]
+    out["final_norm"] = sd[pre + "norm.weight"]
+    out["lm_head"] = sd.get("lm_head.weight", out["embed"])
+    return out
+
+
+def _load_safetensors(model_path: str) -> Dict[str, torch.Tensor]:
+    from safetensors.torch import load_file  # noqa: PLC0415  (optional dependency)
+
+    sd: Dict[str, torch.Tensor] = {}
+    for f in sorted(glob.glob(os.path.join(model_path, "*.safetensors"))):
+        sd.update(load_file(f))
+    if not sd:
+        raise FileNotFoundError(f"no *.safetensors under {model_path}")
+    return sd
+
+
+# ---------------------------------------------------------------------------
+# model
+# ---------------------------------------------------------------------------
+class NeuronQwen3MoeForCausalLMV3:
+    """Qwen3-MoE CausalLM whose token-generation step is one megakernel launch.
+
+    ``model_path=None`` builds seeded random-init weights of the configured shape (the
+    environment has no checkpoints); otherwise Hugging Face safetensors are read.
+    """
+
+    def __init__(self, model_path: Optional[str], config: Qwen3MoeInferenceConfig, device=None, seed: int = 0,
+                 state_dict: Optional[Dict[str, torch.Tensor]] = None):
+        self.model_path = model_path
+        self.state_dict = state_dict
+        self.config = config
+        self.neuron_config = config.neuron_config
+        self.device = torch.device(device if device is not None else "cuda")
+        self.seed = seed
+        self._layers: List[GpuLayer] = []
+        self._head: Dict[str, torch.Tensor] = {}
+        self.kernel: Optional[Qwen3MoeMegakernel] = None
+
+    @classmethod
+    def get_neuron_config_cls(cls):
+        return Qwen3MoEV3MultilayerNeuronConfig
+
+    @classmethod
+    def get_config_cls(cls):
+        return Qwen3MoeInferenceConfig
+
+    @staticmethod
+    def convert_hf_to_neuron_state_dict(state_dict: dict, config) -> dict:
+        return convert_qwen3_moe_hf_to_neuron_state_dict(state_dict, config)
+
+    # -- weights ------------------------------------------------------------
+    def _random_hf_state_dict(self) -> Dict[str, torch.Tensor]:
+        """Seeded random-init weights in Hugging Face layout (on the model's device)."""
+        c, dev = self.config, self.device
+        g = torch.Generator(device=dev).manual_seed(self.seed)
+        H, D, E, I = c.hidden_size, c.head_dim, c.num_experts, c.moe_intermediate_size
+
+        def n(*s):
+            return (torch.randn(*s, generator=g, device=dev) * 0.02).to(BF16)
+
+        def one(*s):
+            return (1.0 + torch.randn(*s, generator=g, device=dev) * 0.02).to(BF16)
+
+        sd = {"model.embed_tokens.weight": torch.randn(c.vocab_size, H, generator=g, device=dev).to(BF16),
+              "model.norm.weight": one(H), "lm_head.weight": n(c.vocab_size, H)}
+        for l in range(c.num_hidden_layers):
+            p = f"model.layers.{l}."
+            sd[p + "self_attn.q_proj.weight"] = n(c.num_attention_heads * D, H)
+            sd[p + "self_attn.k_proj.weight"] = n(c.num_key_value_heads * D, H)
+            sd[p + "self_attn.v_proj.weight"] = n(c.num_key_value_heads * D, H)
+            sd[p + "self_attn.o_proj.weight"] = n(H, c.num_attention_heads * D)
+            sd[p + "self_attn.q_norm.weight"] = one(D)
+            sd[p + "self_attn.k_norm.weight"] = one(D)
+            sd[p + "input_layernorm.weight"] = one(H)
+            sd[p + "post_attention_layernorm.weight"] = one(H)
+            sd[p + "mlp.gate.weight"] = n(E, H)
+            sd[p + "mlp.experts.gate_up_proj"] = n(E, 2 * I, H)
+            sd[p + "mlp.experts.down_proj"] = n(E, H, I)
+        return sd
+
+    def hf_state_dict(self) -> Dict[str, torch.Tensor]:
+        """The model's weights in Hugging Face layout (re-created or re-read on demand: the
+        instance keeps only the kernel layouts)."""
+        if self.state_dict is not None:
+            return self.state_dict
+        if self.model_path:
+            return _load_safetensors(self.model_path)
+        return self._random_hf_state_dict()
+
+    def _build_layers(self, raw: Dict[str, torch.Tensor]):
+        sd = self.convert_hf_to_neuron_state_dict(raw, self.config)
+        dev = self.device
+        for l in range(self.config.num_hidden_layers):
+            t = {k: sd.pop(f"layers.{l}.{k}").to(dev) for k in ("wq", "wk", "wv", "wo", "q_norm", "k_norm", "ln1",
+                                                               "ln2", "router", "gate_up", "down")}
+            self._layers.append(GpuLayer(t["wq"], t["wk"], t["wv"], t["wo"], t["q_norm"], t["k_norm"], t["ln1"],
+                                         t["ln2"], t["router"], t["gate_up"], t["down"]))
+        self._head = {k: sd[k].to(dev) for k in ("embed", "final_norm", "lm_head")}
+
+    def compile(self, compiled_model_path: Optional[str] = None, debug: bool = False):
+        """Convert the weights to the kernel layouts on the GPU (the kernel itself is prebuilt)."""
+        if self._layers:
+            return
+        self._build_layers(self.hf_state_dict())
+
+    def load(self, compiled_model_path: Optional[str] = None):
+        """Allocate the paged K/V pools and the workspace and create the kernel instance."""
+        if not self._layers:
+            self.compile(compiled_model_path)
+        nc = self.neuron_config
+        self.kernel = Qwen3MoeMegakernel(self.config.shape(), self._layers, max_batch=nc.max_batch_size,
+                                         num_blocks=nc.pa_num_blocks, final_norm=self._head["final_norm"],
+                                         lm_head=self._head["lm_head"], embed=self._head["embed"],
+                                         rope_max_pos=max(self.config.max_position_embeddings, nc.max_length + 1),
+                                         device=self.device)
+        self.reset()
+
+    # -- KV cache bookkeeping ----------------------------------------------
+    def reset(self):
+        """Fresh block table: sequence b owns blocks [b*nb, (b+1)*nb)."""
+        nc = self.neuron_config
+        nb = (nc.max_length + nc.pa_block_size) // nc.pa_block_size
+        B = nc.max_batch_size
+        if B * nb > nc.pa_num_blocks:
+            raise ValueError("pa_num_blocks too small for max_batch_size x max_length")
+        self.block_table = torch.arange(B * nb, dtype=torch.int32, device=self.device).view(B, nb)
+
+    # -- decode ---------------------------------------------------------------
+    def forward(self, input_ids: torch.Tensor, position_ids: torch.Tensor) -> torch.Tensor:
+        """One token-generation step: ``input_ids [B]`` at ``position_ids [B]`` -> logits
+        ``[B, vocab]`` fp32.  K/V of every layer are written at ``position_ids``."""
+        if self.kernel is None:
+            raise RuntimeError("call load() first")
+        ids = input_ids.to(self.device, torch.int32).view(-1)
+        pos = position_ids.to(self.device, torch.int32).view(-1)
+        B = ids.shape[0]
+        res = self.kernel.decode_step(pos, self.block_table[:B], input_ids=ids)
+        return res["logits"]
+
+    def teacher_forced_logits(self, tokens: Sequence[int]) -> torch.Tensor:
+        """Feed ``tokens`` one position per step (sequence 0) and return every step's logits
+        ``[len(tokens), vocab]`` fp32."""
+        self.reset()
+        out = []
+        for t, tok in enumerate(tokens):
+            out.append(self.forward(torch.tensor([tok], dtype=torch.int32), torch.tensor([t], dtype=torch.int32)))
+        self.kernel.check_status()
+        return torch.cat(out, 0)
+
+    def sample(self, logits: torch.Tensor, generator: Optional[torch.Generator] = None) -> torch.Tensor:
+        nc = self.neuron_config
+        if not nc.do_sample or nc.top_k <= 1:
+            return logits.argmax(-1)
+        v, i = torch.topk(logits / max(nc.temperature, 1e-5), nc.top_k, dim=-1)
+        probs = torch.softmax(v, -1)
+        pick = torch.multinomial(probs, 1, generator=generator).squeeze(-1)
+        return i.gather(-1, pick[:, None]).squeeze(-1)
+
+    def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int) -> List[List[int]]:
+        """Greedy (or top-k) generation for a batch of token-id prompts.  Every step feeds each
+        sequence one token at its own position: prompt tokens first, then sampled tokens."""
+        self.reset()
+        B = len(prompts)
+        lens = [len(p) for p in prompts]
+        if min(lens) == 0:
+            raise ValueError("empty prompt")
+        total = max(lens) + max_new_tokens
+        if total > self.neuron_config.max_length:
+            raise ValueError("prompt + new tokens exceed max_length")
+        outs: List[List[int]] = [[] for _ in range(B)]
+        cur = [p[0] for p in prompts]
+        pos = [0] * B
+        while any(len(o) < max_new_tokens for o in outs):
+            logits = self.forward(torch.tensor(cur, dtype=torch.int32), torch.tensor(pos, dtype=torch.int32))
+            nxt = self.sample(logits).tolist()
+            for b in range(B):
+                pos[b] += 1
+                if pos[b] < lens[b]:
+                    cur[b] = prompts[b][pos[b]]
+                elif len(outs[b]) < max_new_tokens:
+                    outs[b].append(int(nxt[b]))
+                    cur[b] = int(nxt[b])
+        self.kernel.check_status()
+        return outs
+
+
+# Alias expected by main.py's `NeuronQwen3MoeForCausalLM` convention (reference :728).
+NeuronQwen3MoeForCausalLM = NeuronQwen3MoeForCausalLMV3
