@@ -143,6 +143,27 @@ int nkm_qwen3_attention_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step*
 int nkm_qwen3_moe_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* step,
                         nkm_stream_t stream);
 
+/* Size of the device scratch array behind nkm_qwen3_moe_block_noalloc: 8 MiB, a static
+ * array that every GPU which loads this library holds until the process exits. */
+#define NKM_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* The MoE block of nkm_qwen3_moe_block (same kernel, same results) for callers that cannot
+ * allocate device memory: runtimes whose memory pool owns the whole GPU and forbids library
+ * allocations, and latency-critical loops where a cudaMalloc/cudaFree would synchronise the
+ * device.  It takes the model description directly (no handle, no workspace) and allocates
+ * nothing: its scratch (barrier, counters, residual rows, router logits, expert activations,
+ * split-K partials) lives in a static device array of NKM_NOALLOC_SCRATCH_BYTES; a shape
+ * whose scratch does not fit (hidden, top_k, moe_inter and batch set the size) is rejected
+ * with NKM_ERR_ARG.  The first call on a device looks up that device's array address and
+ * must come before any stream capture on that device.  Each call clears the part of the
+ * scratch that must start at zero; all calls share the one array per device, so calls that
+ * overlap on the GPU (other streams, other host threads) race: serialise them.  K/V pools,
+ * RoPE tables and the LM head of `desc` are not used (they may be NULL).  `status_out`
+ * (device int32, may be NULL) receives the device status word of this call (0 = ok).
+ * No counterpart in the reference. */
+int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t layer, const nkm_qwen3_step* step,
+                                int32_t* status_out, nkm_stream_t stream);
+
 /* Weight layout converter (load time).  src: row-major bf16 [R, K]; dst: fragment-tiled
  * bf16 of the same size.  mode NKM_PACK_PLAIN keeps row order; NKM_PACK_GATE_UP takes the
  * Hugging Face experts gate_up [2I, K] (gate rows then up rows) and interleaves 8 gate rows

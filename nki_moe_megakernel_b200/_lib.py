@@ -59,6 +59,8 @@ SIGNATURES = {
     "nkm_qwen3_status": (c_int, [c_void_p, c_void_p]),
     "nkm_qwen3_attention_block": (c_int, [c_void_p, c_int32, POINTER(nkm_qwen3_step), c_void_p]),
     "nkm_qwen3_moe_block": (c_int, [c_void_p, c_int32, POINTER(nkm_qwen3_step), c_void_p]),
+    "nkm_qwen3_moe_block_noalloc": (c_int, [POINTER(nkm_qwen3_desc), c_int32, POINTER(nkm_qwen3_step), c_void_p,
+                                            c_void_p]),
     "nkm_pack_ft": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
     "nkm_last_error": (c_char_p, []),
     "nkm_version": (c_char_p, []),

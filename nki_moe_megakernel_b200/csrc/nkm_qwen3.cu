@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -380,3 +381,179 @@ int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// MoE block without a handle or workspace, for callers that may not allocate device memory.
+// Its scratch is the static array below (one per device that loads the library); the
+// address of the calling device's copy is looked up once per device, on the first call.
+// ---------------------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NKM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxNoAllocDevices = 64;
+
+struct NoAllocDevice {
+  uint8_t* scratch;  // device address of this device's g_noalloc_scratch
+  int num_sms;
+};
+
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[kMaxNoAllocDevices];
+
+// Scratch layout of one MoE-block call of batch T: the control words of the decode
+// kernel (barrier, status, split-K strip counters, attention and row counters), the layer
+// pointer table, then the MoE block's buffers.  The attention buffers are not needed.
+struct NoAllocLayout {
+  size_t bar, status, strip_cnt, attn_cnt, row_cnt, ctrl_bytes;
+  size_t layers, resid, rlogits, hbuf, ypair, gpart, total;
+};
+
+NoAllocLayout layout_noalloc(const nkm_qwen3_desc& d, int T, int num_sms) {
+  NoAllocLayout w{};
+  const size_t Tm = static_cast<size_t>(T);
+  const size_t NW = static_cast<size_t>(num_sms) * nkm::kWarps;
+  w.bar = 0;
+  w.status = 16;
+  w.strip_cnt = 256;
+  w.attn_cnt = w.strip_cnt + kMaxStrips * 4;
+  w.row_cnt = w.attn_cnt + align_up(Tm * d.n_kv_heads * 4);
+  w.ctrl_bytes = align_up(w.row_cnt + static_cast<size_t>(d.hidden / 16) * 4);
+  size_t o = w.ctrl_bytes;
+  w.layers = o;
+  o = align_up(o + sizeof(nkm::LayerPtrs) * d.n_layers);
+  w.resid = o;
+  o = align_up(o + Tm * d.hidden * 4);
+  w.rlogits = o;
+  o = align_up(o + Tm * d.n_experts * 4);
+  w.hbuf = o;
+  o = align_up(o + Tm * d.top_k * d.moe_inter * 2);
+  w.ypair = o;
+  o = align_up(o + Tm * d.top_k * d.hidden * 4);
+  w.gpart = o;
+  o = align_up(o + NW * 2 * 4 * 32 * 4 * 4);
+  w.total = o;
+  return w;
+}
+
+// Once per device, with that device current: the address of its scratch array.
+int noalloc_device(NoAllocDevice* out) {
+  int dev = 0;
+  NKM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxNoAllocDevices) return fail(NKM_ERR_ARG, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& s = g_noalloc_dev[dev];
+  if (!s.scratch) {
+    void* ptr = nullptr;
+    NKM_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    int sms = 0;
+    NKM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    s.num_sms = sms;
+    s.scratch = static_cast<uint8_t*>(ptr);
+  }
+  *out = s;
+  return NKM_OK;
+}
+
+// Zero the control words (every call starts from a clean barrier, status and counters) and
+// store the layer's pointer table entry; runs on the caller's stream before the MoE kernel.
+__global__ void noalloc_prepare_kernel(nkm::LayerPtrs lp, nkm::LayerPtrs* slot, uint4* ctrl, int n16) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x)
+    ctrl[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *slot = lp;
+}
+
+}  // namespace
+
+extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t layer, const nkm_qwen3_step* s,
+                                           int32_t* status_out, nkm_stream_t stream_) {
+  int rc = check_desc(desc);
+  if (rc) return rc;
+  const nkm_qwen3_desc& d = *desc;
+  if (!s) return fail(NKM_ERR_ARG, "step is NULL");
+  if (layer < 0 || layer >= d.n_layers) return fail(NKM_ERR_ARG, "layer %d outside 0..%d", layer, d.n_layers - 1);
+  if (s->batch <= 0 || s->batch > d.max_batch) return fail(NKM_ERR_ARG, "batch %d outside 1..%d", s->batch, d.max_batch);
+  if (!s->y_out || !aligned16(s->y_out)) return fail(NKM_ERR_ARG, "y_out must be a 16-byte aligned device pointer");
+  if (s->input_ids) {
+    if (!d.embed) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");
+  } else if (!s->x_in || !aligned16(s->x_in)) {
+    return fail(NKM_ERR_ARG, "x_in must be a 16-byte aligned device pointer");
+  }
+  const nkm_qwen3_layer& L = d.layers[layer];
+  if (!L.router || !L.w13_ft || !L.w2_ft || !L.ln2) return fail(NKM_ERR_ARG, "layer %d: MoE weights missing", layer);
+  const void* ps[] = {L.w13_ft, L.w2_ft, L.router, L.ln2};
+  for (const void* q : ps)
+    if (!aligned16(q)) return fail(NKM_ERR_ARG, "layer %d: weight pointers must be 16-byte aligned", layer);
+
+  NoAllocDevice dv{};
+  if ((rc = noalloc_device(&dv))) return rc;
+  const NoAllocLayout lay = layout_noalloc(d, s->batch, dv.num_sms);
+  if (lay.total > NKM_NOALLOC_SCRATCH_BYTES)
+    return fail(NKM_ERR_ARG, "this shape and batch need %zu bytes of scratch; the static scratch holds %zu",
+                lay.total, static_cast<size_t>(NKM_NOALLOC_SCRATCH_BYTES));
+
+  const int nt = nt_for_batch(s->batch);
+  const int ki = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
+  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
+  const nkm::SmemLayout sl(d.hidden, nt);
+  if (sl.total > 232448) return fail(NKM_ERR_ARG, "hidden too large for shared memory");
+  NKM_CUDA(cudaFuncSetAttribute(kfn[ki], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sl.total)));
+
+  uint8_t* ws = dv.scratch;
+  nkm::Params p{};
+  p.T = s->batch;
+  p.H = d.hidden;
+  p.nq = d.n_q_heads;
+  p.nkv = d.n_kv_heads;
+  p.grp = d.n_q_heads / d.n_kv_heads;
+  p.R = (d.n_q_heads + 2 * d.n_kv_heads) * d.head_dim;
+  p.E = d.n_experts;
+  p.K = d.top_k;
+  p.I = d.moe_inter;
+  p.L = d.n_layers;
+  p.V = d.vocab;
+  p.eps = d.rms_eps;
+  p.first_layer = layer;
+  p.num_layers = 1;
+  p.stages = NKM_STAGE_MOE;
+  p.residual = s->residual ? 1 : 0;
+  p.layers = reinterpret_cast<const nkm::LayerPtrs*>(ws + lay.layers);
+  p.embed = static_cast<const uint16_t*>(d.embed);
+  p.input_ids = s->input_ids;
+  p.x_in = static_cast<const uint16_t*>(s->x_in);
+  p.y_out = static_cast<uint16_t*>(s->y_out);
+  p.tr_topk_idx = s->trace_topk_idx;
+  p.tr_topk_w = s->trace_topk_w;
+  p.tr_rlogits = s->trace_router_logits;
+  p.tr_mid = s->trace_resid_mid;
+  p.tr_out = s->trace_resid_out;
+  p.tr_stage = s->trace_stage_ns;
+  p.bar = reinterpret_cast<unsigned*>(ws + lay.bar);
+  p.status = reinterpret_cast<int*>(ws + lay.status);
+  p.strip_cnt = reinterpret_cast<unsigned*>(ws + lay.strip_cnt);
+  p.attn_cnt = reinterpret_cast<unsigned*>(ws + lay.attn_cnt);
+  p.row_cnt = reinterpret_cast<unsigned*>(ws + lay.row_cnt);
+  p.resid = reinterpret_cast<float*>(ws + lay.resid);
+  p.rlogits = reinterpret_cast<float*>(ws + lay.rlogits);
+  p.hbuf = reinterpret_cast<uint16_t*>(ws + lay.hbuf);
+  p.ypair = reinterpret_cast<float*>(ws + lay.ypair);
+  p.gpart = reinterpret_cast<float*>(ws + lay.gpart);
+
+  const nkm::LayerPtrs lp{nullptr, nullptr, nullptr, nullptr, nullptr,
+                          static_cast<const uint16_t*>(L.ln2), static_cast<const uint16_t*>(L.router),
+                          static_cast<const uint8_t*>(L.w13_ft), static_cast<const uint8_t*>(L.w2_ft),
+                          L.router_bias};
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  noalloc_prepare_kernel<<<16, 256, 0, stream>>>(lp, reinterpret_cast<nkm::LayerPtrs*>(ws + lay.layers) + layer,
+                                                  reinterpret_cast<uint4*>(ws), static_cast<int>(lay.ctrl_bytes / 16));
+  NKM_CUDA(cudaGetLastError());
+  CUtensorMap nomap;
+  memset(&nomap, 0, sizeof(nomap));
+  void* args[3] = {&p, &nomap, &nomap};
+  NKM_CUDA(cudaLaunchCooperativeKernel(kfn[ki], dim3(dv.num_sms), dim3(nkm::kThreads), args, sl.total, stream));
+  if (status_out)
+    NKM_CUDA(cudaMemcpyAsync(status_out, ws + lay.status, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream));
+  return NKM_OK;
+}
