@@ -24,7 +24,8 @@ extern "C" {
 #define NKM_ERR_ARG 1          /* bad argument / unsupported shape (host-side check) */
 #define NKM_ERR_CUDA 2         /* a CUDA runtime call failed */
 #define NKM_ERR_TIMEOUT 4      /* a grid barrier or copy wait gave up (device) */
-#define NKM_ERR_INDEX 8        /* a block id or expert id was out of range (device) */
+#define NKM_ERR_INDEX 8        /* a token id, position or block id was out of range (device;
+                                  the access is clamped or skipped) */
 
 typedef struct CUstream_st* nkm_stream_t; /* == cudaStream_t */
 
@@ -56,7 +57,7 @@ typedef struct nkm_qwen3_desc {
   int32_t top_k;        /* K (<= 8)                               8     */
   int32_t moe_inter;    /* I (multiple of 32)                     768   */
   int32_t n_layers;     /* L                                      48    */
-  int32_t vocab;        /* V (multiple of 16), 0 = no LM head     151936*/
+  int32_t vocab;        /* V (multiple of 16): rows of embed and lm_head_ft; 0 = neither 151936*/
   float rms_eps;        /*                                        1e-6  */
   const nkm_qwen3_layer* layers; /* host array of n_layers entries      */
   const void* final_norm;        /* [H] bf16 (may be NULL if vocab==0)  */
@@ -87,7 +88,8 @@ typedef struct nkm_qwen3_step {
   int32_t batch;               /* B (1..max_batch)                                        */
   const int32_t* input_ids;    /* device [B]; if NULL x_in is used                          */
   const void* x_in;            /* device bf16 [B, H] hidden input (embeddings)              */
-  const int32_t* positions;    /* device [B]: cache slot of the new token = prior length    */
+  const int32_t* positions;    /* device [B]: cache slot of the new token = prior length;
+                                  must be < min(rope_max_pos, 128*max_blocks_per_seq)      */
   const int32_t* block_table;  /* device [B, max_blocks_per_seq]; entry < 0 at the write
                                   slot skips the K/V write (reference uint32_max skip)      */
   int32_t max_blocks_per_seq;

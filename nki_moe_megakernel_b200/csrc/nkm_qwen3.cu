@@ -257,7 +257,7 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   if (first < 0 || nl <= 0 || first + nl > d.n_layers) return fail(NKM_ERR_ARG, "layer range out of bounds");
   if (!s->y_out || !aligned16(s->y_out)) return fail(NKM_ERR_ARG, "y_out must be a 16-byte aligned device pointer");
   if (s->input_ids) {
-    if (!d.embed) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");
+    if (!d.embed || d.vocab <= 0) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");
   } else if (!s->x_in || !aligned16(s->x_in)) {
     return fail(NKM_ERR_ARG, "x_in must be a 16-byte aligned device pointer");
   }
@@ -475,7 +475,7 @@ extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t l
   if (s->batch <= 0 || s->batch > d.max_batch) return fail(NKM_ERR_ARG, "batch %d outside 1..%d", s->batch, d.max_batch);
   if (!s->y_out || !aligned16(s->y_out)) return fail(NKM_ERR_ARG, "y_out must be a 16-byte aligned device pointer");
   if (s->input_ids) {
-    if (!d.embed) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");
+    if (!d.embed || d.vocab <= 0) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");
   } else if (!s->x_in || !aligned16(s->x_in)) {
     return fail(NKM_ERR_ARG, "x_in must be a 16-byte aligned device pointer");
   }

@@ -165,6 +165,18 @@ __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
 __device__ __forceinline__ void set_status(const Params& p, int bit) { atomicOr(p.status, bit); }
 
+// Position of sequence b's new token, clamped to what the RoPE tables and the block-table row
+// can address; a position outside that range records NKM_ERR_INDEX.
+__device__ __forceinline__ int seq_pos(const Params& p, int b) {
+  const int raw = __ldg(p.positions + b);
+  const int hi = min(p.rope_max, p.max_blocks * kKvBlock) - 1;
+  if (raw < 0 || raw > hi) {
+    set_status(p, kStatusIndex);
+    return max(0, min(raw, hi));
+  }
+  return raw;
+}
+
 __device__ __forceinline__ void stamp(const Params& p, Ctx& c) {
   if (p.tr_stage && blockIdx.x == 0 && threadIdx.x == 0) p.tr_stage[c.stage_idx] = globaltimer_ns();
   ++c.stage_idx;
@@ -1141,7 +1153,7 @@ __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int lay
 __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch,
                                                   int CT, int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
   const int warp = threadIdx.x >> 5, lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const int pos = max(__ldg(p.positions + b), 0);
+  const int pos = seq_pos(p, b);
   const int tok_beg = ch * CT;
   const int tok_end = min(pos, (ch + 1) * CT);
   const bool last = (ch == nch - 1);
@@ -1349,7 +1361,7 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
   const int G = gridDim.x;
   int tiles = 0, longest = 1;
   for (int b = 0; b < p.T; ++b) {
-    const int nt = (max(__ldg(p.positions + b), 0) + kAttTile - 1) / kAttTile;
+    const int nt = (seq_pos(p, b) + kAttTile - 1) / kAttTile;
     tiles += p.nkv * nt;
     longest = max(longest, nt);
   }
@@ -1358,7 +1370,7 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
   for (;; ++per) {
     nitems = 0;
     for (int b = 0; b < p.T; ++b) {
-      const int pos = max(__ldg(p.positions + b), 0);
+      const int pos = seq_pos(p, b);
       nitems += p.nkv * max(1, (pos + kAttTile * per - 1) / (kAttTile * per));
     }
     if (nitems <= G || per >= longest) break;
@@ -1367,7 +1379,7 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
   for (int it = blockIdx.x; it < nitems; it += G) {
     int base = 0, b = 0, nch = 1;
     for (b = 0; b < p.T; ++b) {
-      const int pos = max(__ldg(p.positions + b), 0);
+      const int pos = seq_pos(p, b);
       nch = max(1, (pos + CT - 1) / CT);
       if (it < base + p.nkv * nch) break;
       base += p.nkv * nch;
@@ -1608,7 +1620,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = (i * 8) / p.H, k = (i * 8) % p.H;
       const uint16_t* src;
       if (p.input_ids) {
-        const int id = __ldg(p.input_ids + t);
+        int id = __ldg(p.input_ids + t);
+        if (id < 0 || id >= p.V) {
+          set_status(p, kStatusIndex);
+          id = 0;
+        }
         src = p.embed + static_cast<size_t>(id) * p.H + k;
       } else {
         src = p.x_in + static_cast<size_t>(t) * p.H + k;

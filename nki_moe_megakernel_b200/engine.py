@@ -119,7 +119,7 @@ class Qwen3MoeMegakernel:
         self.lm_head_ft = None if lm_head is None else pack_ft(lm_head.to(BF16))
         self.embed = None if embed is None else embed.to(BF16).contiguous()
         self._layer_structs = (_lib.nkm_qwen3_layer * L)(*[l.c_struct() for l in self.layers])
-        vocab = shape.vocab_size if lm_head is not None else 0
+        vocab = shape.vocab_size if (lm_head is not None or embed is not None) else 0
         self._desc = _lib.nkm_qwen3_desc(
             shape.hidden_size, shape.num_attention_heads, nkv, D, shape.num_experts, shape.num_experts_per_tok,
             shape.moe_intermediate_size, L, vocab, shape.rms_norm_eps, self._layer_structs,

@@ -168,6 +168,36 @@ def test_attention_skip_write_and_bad_block(dev):
             assert bits_equal(kg[0, blk], k0[0, blk]), blk
 
 
+def test_out_of_range_token_id_and_position_flagged(dev):
+    """A token id >= vocab and a position beyond the block-table row are clamped in bounds and
+    reported as NKM_ERR_INDEX; the next valid step reports 0 again."""
+    from nki_moe_megakernel_b200 import _lib
+    from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
+
+    cfg = qwen_cfg(n_layers=1)
+    lw = make_layers(cfg, 1, seed=13)[0]
+    positions = [5, 100]
+    NB = 4
+    k0, v0, table = make_kv(cfg, 1, positions, NB, seed=14, nan_fill=False)   # one block per sequence
+    V = 64
+    embed = torch.randn(V, cfg.hidden, generator=torch.Generator().manual_seed(15)).to(BF16)
+    eng = Qwen3MoeMegakernel(shape_of(cfg, 1, V), gpu_layers([lw], dev), max_batch=2, num_blocks=NB,
+                             embed=embed.to(dev))
+    eng.k_pool.copy_(k0.to(dev))
+    eng.v_pool.copy_(v0.to(dev))
+    tab = table.to(dev)
+    ok_ids = torch.tensor([1, 2], dtype=torch.int32, device=dev)
+    ok_pos = torch.tensor(positions, dtype=torch.int32, device=dev)
+    eng.decode_step(ok_pos, tab, input_ids=ok_ids)
+    assert eng.status() == 0
+    eng.decode_step(ok_pos, tab, input_ids=torch.tensor([1, V], dtype=torch.int32, device=dev))
+    assert eng.status() == _lib.NKM_ERR_INDEX
+    eng.decode_step(torch.tensor([5, 128], dtype=torch.int32, device=dev), tab, input_ids=ok_ids)
+    assert eng.status() == _lib.NKM_ERR_INDEX
+    eng.decode_step(ok_pos, tab, input_ids=ok_ids)
+    assert eng.status() == 0
+
+
 # ----------------------------------------------------------------------------- layers / step
 def test_decoder_layer_config0(dev):
     """Config 0: one layer, B=4, ctx 1024 (attention + MoE + residuals)."""
