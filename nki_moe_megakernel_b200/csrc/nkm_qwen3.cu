@@ -255,6 +255,7 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   if (!s) return fail(NKM_ERR_ARG, "step is NULL");
   if (s->batch <= 0 || s->batch > d.max_batch) return fail(NKM_ERR_ARG, "batch %d outside 1..%d", s->batch, d.max_batch);
   if (first < 0 || nl <= 0 || first + nl > d.n_layers) return fail(NKM_ERR_ARG, "layer range out of bounds");
+  if (nl > nkm::kMaxLaunchLayers) return fail(NKM_ERR_ARG, "at most %d layers per step", nkm::kMaxLaunchLayers);
   if (!s->y_out || !aligned16(s->y_out)) return fail(NKM_ERR_ARG, "y_out must be a 16-byte aligned device pointer");
   if (s->input_ids) {
     if (!d.embed || d.vocab <= 0) return fail(NKM_ERR_ARG, "input_ids given but the model has no embedding table");

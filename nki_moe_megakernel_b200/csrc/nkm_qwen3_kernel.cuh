@@ -32,6 +32,7 @@ constexpr int kMaxExperts = 256;
 constexpr int kMaxPairs = 256;             // max batch * top_k
 constexpr int kMaxHidden = 2048;           // register-resident row loads: 8 groups of 256
 constexpr int kHidGroups = kMaxHidden / 256;
+constexpr int kMaxLaunchLayers = 128;       // layer pointer table held in shared memory
 constexpr int kAttRows = 16;               // q heads per kv head handled by one mma (<= 16)
 constexpr int kAttQStride = kHeadDim + 8;  // bf16 elements per staged q row
 constexpr int kAttShared = kAttRows * kAttQStride * 2 + 2 * kHeadDim * 2 + kWarps * 2 * kAttRows * 4 + 16;
@@ -123,7 +124,7 @@ struct RingGeom {
 
 struct SmemLayout {
   uint32_t ring_bytes;
-  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, flag_off, total;
+  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, flag_off, total;
   __host__ __device__ SmemLayout(int H, int NT) {
     ring_bytes = NT == 4 ? 8192u : 16384u;
     ring_off = 0;
@@ -135,7 +136,8 @@ struct SmemLayout {
     bars_off = xs_off + ((u + 127u) & ~127u);
     rstd_off = bars_off + static_cast<uint32_t>(kWarps * kMaxBars * 8);
     route_off = rstd_off + 32 * 4;
-    flag_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
+    lt_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
+    flag_off = lt_off + static_cast<uint32_t>(kMaxLaunchLayers * sizeof(LayerPtrs));
     total = flag_off + 16 + 1024;  // + alignment slack for the ring base
   }
 };
@@ -156,6 +158,7 @@ struct Ctx {
   uint8_t* att;   // CTA-shared attention staging (aliases xs)
   float* rstd;
   Route* rt;
+  const LayerPtrs* lt;  // pointer table of layers first_layer .. first_layer + num_layers - 1
   int* flag;
   int stage_idx;
   int primed;  // the next GEMV stage's first chunks are already in flight
@@ -303,6 +306,12 @@ __device__ __forceinline__ float gam(const uint4 (&gv)[kHidGroups], int i, int j
 __device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first,
                                                float* x32 = nullptr) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
+  if (warp >= p.T) return;
+  // gamma and the first row are requested together: one memory latency, not one per group
+  uint4 gam[kHidGroups];
+#pragma unroll
+  for (int i = 0; i < kHidGroups; ++i)
+    gam[i] = (i < p.H / 256) ? ldnc128(gamma + 256 * i + 8 * lane) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll 1
   for (int t = warp; t < p.T; t += kWarps) {
     RowRegs x;
@@ -313,7 +322,7 @@ __device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const ui
 #pragma unroll
     for (int i = 0; i < kHidGroups; ++i) {
       if (i < p.H / 256) {
-        const uint4 gv = ldnc128(gamma + 256 * i + 8 * lane);
+        const uint4 gv = gam[i];
         const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
         uint32_t o[4];
 #pragma unroll
@@ -780,19 +789,22 @@ __device__ __noinline__ void down_prime(const Params& p, Ctx& c, const GemvGeom&
   }
 }
 
-// Flush the per-warp row-strip tile `tile` ([T][16] fp32) of strip s.
+// Flush the per-warp row-strip tile `tile` ([T][16] fp32) of strip s.  Lane l handles the
+// float4 groups q = l, l + 32, ... of the tile (token q / 4, rows 4 (q % 4) .. + 3); the
+// partials of the other contributors are read four workers at a time.
 __device__ __noinline__ void down_flush(const Params& p, float* tile, int layer, int s, int worker, int i0, int i1,
                                         int NI, int NWe, int nA) {
   const int lane = lane_id();
-  const int n = p.T * 16;
+  const int n = p.T * 16, n4 = n / 4;
   const int s_lo = s * nA, s_hi = s_lo + nA;  // item range of the strip
   const bool full = (i0 <= s_lo && s_hi <= i1);
+  float4* tile4 = reinterpret_cast<float4*>(tile);
   __syncwarp();
   if (!full) {
     const int slot = (i0 >= s_lo) ? 0 : 1;  // 0: the strip is this worker's first
-    float* dst = p.gpart + (static_cast<size_t>(worker) * 2 + slot) * n;
+    float4* dst = reinterpret_cast<float4*>(p.gpart + (static_cast<size_t>(worker) * 2 + slot) * n);
 #pragma unroll 1
-    for (int e = lane; e < n; e += 32) dst[e] = tile[e];
+    for (int q = lane; q < n4; q += 32) dst[q] = tile4[q];
     __threadfence();
     __syncwarp();
     const int wf = worker_of(s_lo, NI, NWe), wl = worker_of(s_hi - 1, NI, NWe);
@@ -801,30 +813,47 @@ __device__ __noinline__ void down_flush(const Params& p, float* tile, int layer,
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != static_cast<unsigned>(wl - wf)) {
 #pragma unroll 1
-      for (int e = lane; e < n; e += 32) tile[e] = 0.f;
+      for (int q = lane; q < n4; q += 32) tile4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
       __syncwarp();
       return;
     }
     __threadfence();
     const int slot_f = (range_lo(NI, wf, NWe) >= s_lo) ? 0 : 1;
 #pragma unroll 1
-    for (int e = lane; e < n; e += 32) {
-      float a = 0.f;
+    for (int q = lane; q < n4; q += 32) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-      for (int w = wf; w <= wl; ++w)
-        a += ldcg_f(p.gpart + (static_cast<size_t>(w) * 2 + (w == wf ? slot_f : 0)) * n + e);
-      tile[e] = a;
+      for (int w0 = wf; w0 <= wl; w0 += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int w = w0 + u;
+          v[u] = (w <= wl) ? ldcg_f4(p.gpart + (static_cast<size_t>(w) * 2 + (w == wf ? slot_f : 0)) * n + 4 * q)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          a.x += v[u].x;
+          a.y += v[u].y;
+          a.z += v[u].z;
+          a.w += v[u].w;
+        }
+      }
+      tile4[q] = a;
     }
     if (lane == 0) p.strip_cnt[s] = 0u;
   }
 #pragma unroll 1
-  for (int e = lane; e < n; e += 32) {
-    const int t = e >> 4, row = s * 16 + (e & 15);
-    float* x = p.resid + static_cast<size_t>(t) * p.H + row;
-    const float nv = (p.residual ? *x : 0.f) + rbf(tile[e]);
+  for (int q = lane; q < n4; q += 32) {
+    const int t = q >> 2, row = s * 16 + 4 * (q & 3);
+    float4* x = reinterpret_cast<float4*>(p.resid + static_cast<size_t>(t) * p.H + row);
+    const float4 old = p.residual ? *x : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 tv = tile4[q];
+    const float4 nv = make_float4(old.x + rbf(tv.x), old.y + rbf(tv.y), old.z + rbf(tv.z), old.w + rbf(tv.w));
     *x = nv;
-    if (p.tr_out) p.tr_out[(static_cast<size_t>(layer - p.first_layer) * p.T + t) * p.H + row] = nv;
-    tile[e] = 0.f;
+    if (p.tr_out)
+      *reinterpret_cast<float4*>(p.tr_out + (static_cast<size_t>(layer - p.first_layer) * p.T + t) * p.H + row) = nv;
+    tile4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncwarp();
 }
@@ -954,8 +983,7 @@ __device__ __noinline__ void down_stage(const Params& p, Ctx& cref, const GemvGe
 // ------------------------------------------------------------------ attention
 // q/k head RMSNorm + RoPE for the 4 elements d = 4*lane .. 4*lane+3 of one head
 // (rounding points of attn_fused_nki.py:393-451,494-586).
-__device__ __forceinline__ void head_norm_rope(float (&x)[4], const uint16_t* w, const uint16_t* cs,
-                                               const uint16_t* sn, float eps) {
+__device__ __forceinline__ void head_norm_rope(float (&x)[4], uint2 wv, uint2 cv, uint2 sv, float eps) {
   const int lane = lane_id();
   float s = 0.f;
 #pragma unroll
@@ -963,7 +991,6 @@ __device__ __forceinline__ void head_norm_rope(float (&x)[4], const uint16_t* w,
   s = warp_sum_fixed(s);
   const float r = rstd_fixed(s, kHeadDim, eps);
   float xn[4], rot[4];
-  const uint2 wv = *reinterpret_cast<const uint2*>(w + 4 * lane);
   const float wf[4] = {lo_bf(wv.x), hi_bf(wv.x), lo_bf(wv.y), hi_bf(wv.y)};
 #pragma unroll
   for (int j = 0; j < 4; ++j) xn[j] = rbf(__fmul_rn(__fmul_rn(x[j], r), wf[j]));
@@ -972,8 +999,6 @@ __device__ __forceinline__ void head_norm_rope(float (&x)[4], const uint16_t* w,
     const float o = __shfl_xor_sync(0xffffffffu, xn[j], 16);
     rot[j] = lane < 16 ? -o : o;
   }
-  const uint2 cv = *reinterpret_cast<const uint2*>(cs + 4 * lane);
-  const uint2 sv = *reinterpret_cast<const uint2*>(sn + 4 * lane);
   const float cf[4] = {lo_bf(cv.x), hi_bf(cv.x), lo_bf(cv.y), hi_bf(cv.y)};
   const float sf[4] = {lo_bf(sv.x), hi_bf(sv.x), lo_bf(sv.y), hi_bf(sv.y)};
 #pragma unroll
@@ -992,54 +1017,93 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float score_round(float acc) { return rbf(rbf(acc) * kScoreScale); }
 
-// Load one raw bf16 head (4 elements per lane), apply head RMSNorm + RoPE, return bf16x4.
-__device__ __noinline__ uint2 stage_head(const uint16_t* src, const uint16_t* w, const uint16_t* cs,
-                                         const uint16_t* sn, float eps) {
+// One raw bf16 head (4 elements per lane) and its norm weight and RoPE rows: loaded together,
+// then normalised + rotated (head_finish) to bf16x4.
+struct HeadIn {
+  uint2 raw, w, c, s;
+};
+__device__ __forceinline__ HeadIn head_load(const uint16_t* src, const uint16_t* w, const uint16_t* cs,
+                                            const uint16_t* sn) {
+  const int lane = lane_id();
+  HeadIn in;
+  in.raw = ldcg64(src + 4 * lane);
+  in.w = *reinterpret_cast<const uint2*>(w + 4 * lane);
+  in.c = *reinterpret_cast<const uint2*>(cs + 4 * lane);
+  in.s = *reinterpret_cast<const uint2*>(sn + 4 * lane);
+  return in;
+}
+__device__ __forceinline__ uint2 head_finish(const HeadIn& in, float eps) {
   float x[4];
-  unpack4(ldcg64(src + 4 * lane_id()), x);
-  head_norm_rope(x, w, cs, sn, eps);
+  unpack4(in.raw, x);
+  head_norm_rope(x, in.w, in.c, in.s, eps);
   return make_uint2(pack_bf2(x[0], x[1]), pack_bf2(x[2], x[3]));
 }
 
 // Per-warp flash-decode over the 32-token tiles tile_first, tile_first+step, ... of
 // [tok_beg, tok_end).  Leaves the unnormalised (m, l, o) of rows g and g+8 in registers.
+// Block ids of the K/V blocks a context chunk [tok_beg, tok_end) touches: lane j holds the
+// id of block tok_beg/128 + j (j < 32; -1 past the chunk).  One coalesced load per warp.
+__device__ __forceinline__ int att_chunk_blocks(const Params& p, int b, int tok_beg, int tok_end) {
+  const int j = tok_beg / kKvBlock + lane_id();
+  const int jend = tok_end > tok_beg ? (tok_end - 1) / kKvBlock : -1;
+  return (j <= jend && j < p.max_blocks) ? __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + j) : -1;
+}
+
+// TMA box bi of this warp's tiles (tile bi/4; boxes K d0-63, K d64-127, V d0-63, V d64-127)
+// into ring slot `slot`.  All lanes call it (the block id is shuffled from blk_lane); lane 0
+// issues the copy.
+__device__ __forceinline__ void att_issue_box(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg,
+                                              int tile_first, int tile_step, int blk_lane, int bi, int slot,
+                                              const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  const int tile = tile_first + (bi >> 2) * tile_step, kind = bi & 3;
+  const int tok0 = tok_beg + tile * kAttTile;
+  const int off = tok0 / kKvBlock - tok_beg / kKvBlock;
+  int blk = __shfl_sync(0xffffffffu, blk_lane, off & 31);
+  if (off >= 32) blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + tok0 / kKvBlock);
+  if (lane_id() == 0) {
+    if (blk < 0 || blk >= p.num_blocks) {
+      set_status(p, kStatusIndex);
+      blk = 0;
+    }
+    const size_t head_rows = static_cast<size_t>(layer) * p.num_blocks;
+    const int row = static_cast<int>(((head_rows + blk) * p.nkv + h) * kKvBlock + (tok0 % kKvBlock));
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&c.bars[slot], kSlotBytes);
+    tma_load_2d(c.ring + slot * kSlotBytes, kind < 2 ? kmap : vmap, (kind & 1) * 64, row, &c.bars[slot]);
+  }
+}
+
+__device__ __forceinline__ int att_ntile(int tok_beg, int tok_end, int tile_first, int tile_step) {
+  const int ntile_all = tok_end > tok_beg ? (tok_end - tok_beg + kAttTile - 1) / kAttTile : 0;
+  return ntile_all > tile_first ? (ntile_all - tile_first + tile_step - 1) / tile_step : 0;
+}
+
+// Fill the warp's ring with its first boxes (before the q heads are staged, so that the K/V
+// copies overlap the staging).  Returns the number of boxes issued.
+__device__ __forceinline__ int att_prime(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg, int tok_end,
+                                         int tile_first, int tile_step, int blk_lane, const CUtensorMap* kmap,
+                                         const CUtensorMap* vmap) {
+  const int nbox = 4 * att_ntile(tok_beg, tok_end, tile_first, tile_step);
+  int pb = 0, ps = c.head;
+  for (; pb < nbox && pb < c.nslot; ++pb) {
+    att_issue_box(p, c, layer, b, h, tok_beg, tile_first, tile_step, blk_lane, pb, ps, kmap, vmap);
+    ps = (ps + 1 == c.nslot) ? 0 : ps + 1;
+  }
+  return pb;
+}
+
 __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg, int tok_end,
-                                int tile_first, int tile_step, const uint32_t (&qa)[8][4], float (&m)[2],
-                                float (&l)[2], float (&o)[16][4], const CUtensorMap* kmap,
+                                int tile_first, int tile_step, int blk_lane, int pb, const uint32_t (&qa)[8][4],
+                                float (&m)[2], float (&l)[2], float (&o)[16][4], const CUtensorMap* kmap,
                                 const CUtensorMap* vmap) {
   const int lane = lane_id(), t4 = lane & 3;
-  const int ntile_all = tok_end > tok_beg ? (tok_end - tok_beg + kAttTile - 1) / kAttTile : 0;
-  const int ntile = ntile_all > tile_first ? (ntile_all - tile_first + tile_step - 1) / tile_step : 0;
+  const int ntile = att_ntile(tok_beg, tok_end, tile_first, tile_step);
   const int nbox = 4 * ntile;
-  const size_t head_rows = static_cast<size_t>(layer) * p.num_blocks;
-  auto issue_box = [&](int bi, int slot) {
-    if (lane == 0) {
-      const int tile = tile_first + (bi >> 2) * tile_step, kind = bi & 3;
-      const int tok0 = tok_beg + tile * kAttTile;
-      int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + tok0 / kKvBlock);
-      if (blk < 0 || blk >= p.num_blocks) {
-        set_status(p, kStatusIndex);
-        blk = 0;
-      }
-      const int row = static_cast<int>(((head_rows + blk) * p.nkv + h) * kKvBlock + (tok0 % kKvBlock));
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&c.bars[slot], kSlotBytes);
-      tma_load_2d(c.ring + slot * kSlotBytes, kind < 2 ? kmap : vmap, (kind & 1) * 64, row, &c.bars[slot]);
-    }
-  };
   auto next_slot = [&](int s) { return (s + 1 == c.nslot) ? 0 : s + 1; };
-  int pb = 0;
-  {
-    int ps = c.head;
-    for (; pb < nbox && pb < c.nslot; ++pb) {
-      issue_box(pb, ps);
-      ps = next_slot(ps);
-    }
-  }
   auto refill = [&](int slot) {
     __syncwarp();
     if (pb < nbox) {
-      issue_box(pb, slot);
+      att_issue_box(p, c, layer, b, h, tok_beg, tile_first, tile_step, blk_lane, pb, slot, kmap, vmap);
       ++pb;
     }
   };
@@ -1151,9 +1215,9 @@ __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int lay
 
 // One (sequence b, kv head h, context chunk ch) item, processed by the whole CTA.
 __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch,
-                                                  int CT, int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+                                                  int CT, int item, int pos, const CUtensorMap* kmap,
+                                                  const CUtensorMap* vmap) {
   const int warp = threadIdx.x >> 5, lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const int pos = seq_pos(p, b);
   const int tok_beg = ch * CT;
   const int tok_end = min(pos, (ch + 1) * CT);
   const bool last = (ch == nch - 1);
@@ -1165,29 +1229,41 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   const int prow = min(pos, p.rope_max - 1);
   const uint16_t* cosr = p.rope_cos + static_cast<size_t>(prow) * kHeadDim;
   const uint16_t* sinr = p.rope_sin + static_cast<size_t>(prow) * kHeadDim;
-  const LayerPtrs& lw = p.layers[layer];
+  const LayerPtrs& lw = c.lt[layer - p.first_layer];
   const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
+  const int blk_lane = att_chunk_blocks(p, b, tok_beg, tok_end);
+  const int pb = att_prime(p, c, layer, b, h, tok_beg, tok_end, warp, kWarps, blk_lane, kmap, vmap);
 
-  // --- stage q (rows warp, warp+8) and, in the last chunk, the new token's K/V
-#pragma unroll 1
-  for (int r = warp; r < kAttRows; r += kWarps) {
-    const uint2 out = r < p.grp ? stage_head(qkv_b + static_cast<size_t>(h * p.grp + r) * kHeadDim, lw.qn, cosr,
-                                             sinr, p.eps)
-                                : make_uint2(0, 0);
+  // --- stage the q heads (rows warp, warp + 8) and, in the last chunk, the new token's K
+  // (warp 7) and V (warp 6); every load is issued before the first one is used
+  const bool do_k = last && warp == kWarps - 1, do_v = last && warp == kWarps - 2;
+  HeadIn qin[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = warp + i * kWarps;
+    qin[i] = r < p.grp ? head_load(qkv_b + static_cast<size_t>(h * p.grp + r) * kHeadDim, lw.qn, cosr, sinr)
+                       : HeadIn{};
+  }
+  HeadIn kin{};
+  uint2 vv = make_uint2(0u, 0u);
+  int wblk = -1;
+  if (do_k) kin = head_load(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim, lw.kn, cosr, sinr);
+  if (do_v) vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
+  if (do_k || do_v) wblk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = warp + i * kWarps;
+    const uint2 out = r < p.grp ? head_finish(qin[i], p.eps) : make_uint2(0u, 0u);
     *reinterpret_cast<uint2*>(qs + r * kAttQStride + 4 * lane) = out;
   }
-  if (last && warp == kWarps - 1) {
-    const uint2 kw = stage_head(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim, lw.kn, cosr, sinr, p.eps);
-    const uint2 vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
-    *reinterpret_cast<uint2*>(kn + 4 * lane) = kw;
-    *reinterpret_cast<uint2*>(vn + 4 * lane) = vv;
-    const int blk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
-    if (blk >= 0 && blk < p.num_blocks) {
-      const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * kKvBlock * kHeadDim +
+  if (do_k || do_v) {
+    const uint2 val = do_k ? head_finish(kin, p.eps) : vv;
+    *reinterpret_cast<uint2*>((do_k ? kn : vn) + 4 * lane) = val;
+    if (wblk >= 0 && wblk < p.num_blocks) {
+      const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + wblk) * p.nkv + h) * kKvBlock * kHeadDim +
                          static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
-      *reinterpret_cast<uint2*>(p.k_pool + off) = kw;
-      *reinterpret_cast<uint2*>(p.v_pool + off) = vv;
-    } else if (blk >= p.num_blocks && lane == 0) {
+      *reinterpret_cast<uint2*>((do_k ? p.k_pool : p.v_pool) + off) = val;
+    } else if (wblk >= p.num_blocks && lane == 0) {
       set_status(p, kStatusIndex);
     }
   }
@@ -1206,7 +1282,7 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   float o[16][4];
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-  attention_tiles(p, c, layer, b, h, tok_beg, tok_end, warp, kWarps, qa, m, l, o, kmap, vmap);
+  attention_tiles(p, c, layer, b, h, tok_beg, tok_end, warp, kWarps, blk_lane, pb, qa, m, l, o, kmap, vmap);
 
   // --- the active token (position pos): score with the fresh K, value the fresh V
   if (last && warp == 0) {
@@ -1349,43 +1425,52 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
 }
 
 __device__ __noinline__ void attention_cta_item(const Params& p, Ctx& cref, int layer, int b, int h, int ch, int nch,
-                                                int CT, int item, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+                                                int CT, int item, int pos, const CUtensorMap* kmap,
+                                                const CUtensorMap* vmap) {
   Ctx c = cref;  // register-resident copy
-  attention_cta_body(p, c, layer, b, h, ch, nch, CT, item, kmap, vmap);
+  attention_cta_body(p, c, layer, b, h, ch, nch, CT, item, pos, kmap, vmap);
   cref.head = c.head;
   cref.phase = c.phase;
 }
 
 __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
-  // chunk length CT (multiple of 32) such that the (b, h, chunk) items fill the grid once
-  const int G = gridDim.x;
-  int tiles = 0, longest = 1;
-  for (int b = 0; b < p.T; ++b) {
-    const int nt = (seq_pos(p, b) + kAttTile - 1) / kAttTile;
-    tiles += p.nkv * nt;
-    longest = max(longest, nt);
+  // chunk length CT (multiple of 32) such that the (b, h, chunk) items fill the grid once.
+  // Lane b holds sequence b's position (batch <= 32), so one load serves the whole plan.
+  const int G = gridDim.x, lane = lane_id();
+  const int mypos = lane < p.T ? seq_pos(p, lane) : 0;
+  const int mytiles = lane < p.T ? (mypos + kAttTile - 1) / kAttTile : 0;
+  int tiles = p.nkv * mytiles, longest = max(1, mytiles);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    tiles += __shfl_xor_sync(0xffffffffu, tiles, off);
+    longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, off));
   }
   int per = max(1, (tiles + G - 1) / G);
   int nitems = 0;
   for (;; ++per) {
-    nitems = 0;
-    for (int b = 0; b < p.T; ++b) {
-      const int pos = seq_pos(p, b);
-      nitems += p.nkv * max(1, (pos + kAttTile * per - 1) / (kAttTile * per));
-    }
+    int mine = lane < p.T ? p.nkv * max(1, (mypos + kAttTile * per - 1) / (kAttTile * per)) : 0;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, off);
+    nitems = mine;
     if (nitems <= G || per >= longest) break;
   }
   const int CT = kAttTile * per;
+  // inclusive prefix of the items of sequences 0..lane
+  const int mynch = lane < p.T ? max(1, (mypos + CT - 1) / CT) : 0;
+  int incl = p.nkv * mynch;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
   for (int it = blockIdx.x; it < nitems; it += G) {
-    int base = 0, b = 0, nch = 1;
-    for (b = 0; b < p.T; ++b) {
-      const int pos = seq_pos(p, b);
-      nch = max(1, (pos + CT - 1) / CT);
-      if (it < base + p.nkv * nch) break;
-      base += p.nkv * nch;
-    }
+    const unsigned before = __ballot_sync(0xffffffffu, lane < p.T && incl <= it);
+    const int b = __popc(before);  // sequences whose items all precede `it`
+    const int base = b > 0 ? __shfl_sync(0xffffffffu, incl, b - 1) : 0;
+    const int nch = __shfl_sync(0xffffffffu, mynch, b);
+    const int pos = __shfl_sync(0xffffffffu, mypos, b);
     const int r = it - base;
-    attention_cta_item(p, c, layer, b, r / nch, r % nch, nch, CT, it, kmap, vmap);
+    attention_cta_item(p, c, layer, b, r / nch, r % nch, nch, CT, it, pos, kmap, vmap);
   }
 }
 
@@ -1396,19 +1481,24 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
 // fly from the residual with the per-CTA rstd (large batches whose rows do not fit).
 __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer, const float* x32) {
   const int lane = lane_id();
-  const LayerPtrs& lw = p.layers[layer];
+  const LayerPtrs& lw = c.lt[layer - p.first_layer];
   const int nitems = p.T * p.E;
 #pragma unroll 1
   for (int it = c.worker; it < nitems; it += c.nworkers) {
     const int t = it / p.E, e = it % p.E;
     const uint16_t* wr = lw.router + static_cast<size_t>(e) * p.H;
     const float r = c.rstd[t];
+    // all weight loads of the row first: one memory latency per item, not one per group
+    uint4 wv[kHidGroups];
+#pragma unroll
+    for (int i = 0; i < kHidGroups; ++i)
+      wv[i] = (i < p.H / 256) ? ldnc128(wr + 256 * i + 8 * lane) : make_uint4(0u, 0u, 0u, 0u);
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < kHidGroups; ++i) {
       if (i < p.H / 256) {
         const int k0 = 256 * i + 8 * lane;
-        const uint4 w4 = ldnc128(wr + k0);
+        const uint4 w4 = wv[i];
         float xv[8];
         if (x32) {
           const float4 x0 = *reinterpret_cast<const float4*>(x32 + static_cast<size_t>(t) * p.H + k0);
@@ -1444,6 +1534,16 @@ __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer, co
 
 // Softmax / top-k / renorm per token (one warp per token) and the expert tables, in every CTA
 // (moe_fused_nki.py:224-272, 404-418).
+// Order-preserving key of a float (larger float -> larger key; -0 and +0 map to one key) and
+// its inverse.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f == 0.f ? 0.f : f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
   Route* rt = c.rt;
@@ -1467,54 +1567,60 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
     for (int q = 0; q < 8; ++q) se += (q < per && ids[q] < E) ? __expf(v[q] - mx) : 0.f;
     se = warp_sum_fixed(se);
     const float inv = 1.f / se;
+    // top-K by (value desc, index asc): order-preserving uint32 keys (-0 folded into +0),
+    // one warp max-reduction per pick; the lowest index wins among equal keys
+    uint32_t key[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) key[q] = (q < per && ids[q] < E) ? order_key(v[q]) : 0u;
     float vals[8];
-#pragma unroll 1
-    for (int k = 0; k < K; ++k) {
-      // lane-local best (value desc, index asc)
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (v[q] > bv || (v[q] == bv && ids[q] < bi)) {
-          bv = v[q];
-          bi = ids[q];
+    for (int k = 0; k < 8; ++k) {
+      if (k < K) {
+        uint32_t lb = 0u;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) lb = max(lb, key[q]);
+        const uint32_t wmax = __reduce_max_sync(0xffffffffu, lb);
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int q = 7; q >= 0; --q) {
+          const unsigned m = __ballot_sync(0xffffffffu, key[q] == wmax);
+          if (m) bi = q * 32 + __ffs(m) - 1;
         }
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
+        for (int q = 0; q < 8; ++q)
+          if (ids[q] == bi) key[q] = 0u;
+        vals[k] = rbf(__expf(key_value(wmax) - mx) * inv);
+        if (lane == 0) rt->topk_idx[t * K + k] = bi;
       }
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (ids[q] == bi) v[q] = -INFINITY;
-      vals[k] = rbf(__expf(bv - mx) * inv);
-      if (lane == 0) rt->topk_idx[t * K + k] = bi;
     }
     float sk = 0.f;
-#pragma unroll 1
-    for (int k = 0; k < K; ++k) sk += vals[k];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < K) sk += vals[k];
     const float inv2 = 1.f / sk;
     if (lane == 0) {
-#pragma unroll 1
-      for (int k = 0; k < K; ++k) rt->topk_w[t * K + k] = rbf(vals[k] * inv2);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < K) rt->topk_w[t * K + k] = rbf(vals[k] * inv2);
     }
   }
   __syncthreads();
+  // entry i = threadIdx.x (NP <= kMaxPairs == kThreads): its expert and its rank among the
+  // entries of that expert in entry order (token-major), computed by every thread at once
+  static_assert(kMaxPairs <= kThreads, "one thread per (token, slot) entry");
+  const int NP = p.T * K;
+  const int ie = threadIdx.x;
+  const int e_i = (ie < NP) ? rt->topk_idx[ie] : -1;
+  const bool valid = e_i >= 0 && e_i < E;
+  int rank = 0;
+#pragma unroll 8
+  for (int j = 0; j < ie && j < NP; ++j) rank += (rt->topk_idx[j] == e_i);
+#pragma unroll 1
+  for (int e = threadIdx.x; e < E; e += kThreads) rt->cnt[e] = 0;
+  __syncthreads();
+  if (valid) atomicAdd(&rt->cnt[e_i], 1);
+  __syncthreads();
   if (warp == 0) {
-    const int NP = p.T * K;
-#pragma unroll 1
-    for (int e = lane; e < E; e += 32) rt->cnt[e] = 0;
-    __syncwarp();
-#pragma unroll 1
-    for (int i = lane; i < NP; i += 32) {
-      const int e = rt->topk_idx[i];
-      if (e >= 0 && e < E) atomicAdd(&rt->cnt[e], 1);
-    }
-    __syncwarp();
     // active experts in ascending id order, with pair offsets
     int nA = 0, off = 0;
 #pragma unroll 1
@@ -1538,37 +1644,17 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
       nA += __popc(act);
       off += __shfl_sync(0xffffffffu, incl, 31);
     }
-    __syncwarp();
-    // rank of each (token, slot) entry among the entries of its expert (entry order)
-#pragma unroll 1
-    for (int i0 = 0; i0 < NP; i0 += 32) {
-      const int i = i0 + lane;
-      const int e = (i < NP) ? rt->topk_idx[i] : -1;
-      int rank = 0;
-#pragma unroll 1
-      for (int j0 = 0; j0 < i0; j0 += 32) {
-        const int ej = (j0 + lane < NP) ? rt->topk_idx[j0 + lane] : -2;
-#pragma unroll 4
-        for (int q = 0; q < 32; ++q) rank += (__shfl_sync(0xffffffffu, ej, q) == e);
-      }
-#pragma unroll 4
-      for (int q = 0; q < 32; ++q) {
-        const int eq = __shfl_sync(0xffffffffu, e, q);
-        if (q < lane && eq == e) ++rank;
-      }
-      if (i < NP) {
-        const int pr = rt->cnt[e] + rank;
-        rt->pmap[i] = pr;
-        rt->pair_tok[pr] = i / K;
-        rt->pair_w[pr] = rt->topk_w[i];
-      }
-    }
     if (lane == 0) rt->nA = nA;
+  }
+  __syncthreads();
+  if (valid) {
+    const int pr = rt->cnt[e_i] + rank;
+    rt->pmap[ie] = pr;
+    rt->pair_tok[pr] = ie / K;
+    rt->pair_w[pr] = rt->topk_w[ie];
     if (blockIdx.x == 0 && p.tr_topk_idx) {
-      for (int i = lane; i < NP; i += 32) {
-        p.tr_topk_idx[static_cast<size_t>(layer - p.first_layer) * NP + i] = rt->topk_idx[i];
-        p.tr_topk_w[static_cast<size_t>(layer - p.first_layer) * NP + i] = rt->topk_w[i];
-      }
+      p.tr_topk_idx[static_cast<size_t>(layer - p.first_layer) * NP + ie] = e_i;
+      p.tr_topk_w[static_cast<size_t>(layer - p.first_layer) * NP + ie] = rt->topk_w[ie];
     }
   }
   __syncthreads();
@@ -1602,6 +1688,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
   c.stage_idx = 0;
   c.primed = 0;
+  {
+    // the layer pointer table, once per launch: every stage reads its pointers from shared memory
+    static_assert(sizeof(LayerPtrs) % 16 == 0, "LayerPtrs is copied as uint4");
+    LayerPtrs* lt = reinterpret_cast<LayerPtrs*>(smem + lay.lt_off);
+    const uint4* src = reinterpret_cast<const uint4*>(p.layers + p.first_layer);
+    const int n16 = p.num_layers * static_cast<int>(sizeof(LayerPtrs) / 16);
+    for (int i = threadIdx.x; i < n16; i += kThreads) reinterpret_cast<uint4*>(lt)[i] = src[i];
+    c.lt = lt;
+    __syncthreads();
+  }
   stamp(p, c);
   if (lane == 0) {
     for (int s = 0; s < kMaxBars; ++s) mbar_init(&c.bars[s], 1);
@@ -1636,7 +1732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if ((p.stages & 1) && p.num_layers > 0) {  // the first QKV weights stream during the barrier
-    const LayerPtrs& l0 = p.layers[p.first_layer];
+    const LayerPtrs& l0 = c.lt[0];
     GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
     gemv_prime<NT>(p, c, ga, GK_QKV);
   }
@@ -1648,7 +1744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto prime_after = [&](int layer) {
     if (layer + 1 < layer_end) {
       if (p.stages & 1) {
-        const LayerPtrs& nl = p.layers[layer + 1];
+        const LayerPtrs& nl = c.lt[layer + 1 - p.first_layer];
         GemvGeom ga{nl.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer + 1};
         gemv_prime<NT>(p, c, ga, GK_QKV);
       }
@@ -1658,7 +1754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
   for (int layer = p.first_layer; layer < layer_end; ++layer) {
-    const LayerPtrs& lw = p.layers[layer];
+    const LayerPtrs& lw = c.lt[layer - p.first_layer];
     if (p.stages & 1) {
       // A: RMSNorm(ln1) + QKV
       norm_rows_to_smem(p, c, lw.ln1, false);
