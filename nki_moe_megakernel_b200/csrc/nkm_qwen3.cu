@@ -233,7 +233,7 @@ int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspa
   for (int i = 0; i < 3; ++i) {
     nkm::SmemLayout sl(desc->hidden, nts[i]);
     h->smem[i] = sl.total;
-    if (sl.total > 232448) return cleanup(fail(NKM_ERR_ARG, "hidden too large for shared memory"));
+    if (sl.total > 232448 - 1024) return cleanup(fail(NKM_ERR_ARG, "hidden too large for shared memory"));
     if (cudaFuncSetAttribute(kfn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sl.total)) !=
         cudaSuccess)
       return cleanup(fail(NKM_ERR_CUDA, "cudaFuncSetAttribute failed"));
@@ -499,7 +499,7 @@ extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t l
                   reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
                   reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
   const nkm::SmemLayout sl(d.hidden, nt);
-  if (sl.total > 232448) return fail(NKM_ERR_ARG, "hidden too large for shared memory");
+  if (sl.total > 232448 - 1024) return fail(NKM_ERR_ARG, "hidden too large for shared memory");
   NKM_CUDA(cudaFuncSetAttribute(kfn[ki], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sl.total)));
 
   uint8_t* ws = dv.scratch;

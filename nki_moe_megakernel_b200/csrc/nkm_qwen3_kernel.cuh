@@ -305,39 +305,50 @@ __device__ __forceinline__ float gam(const uint4 (&gv)[kHidGroups], int i, int j
 // When x32 is non-null the fp32 normalised rows are also stored there (row stride H).
 __device__ __noinline__ void norm_rows_to_smem(const Params& p, Ctx& c, const uint16_t* gamma, bool gamma_first,
                                                float* x32 = nullptr) {
+  // every field is read once into a register: stores through the row pointers below could
+  // otherwise alias p and c and force reloads on the dependency chain
   const int warp = threadIdx.x >> 5, lane = lane_id();
-  if (warp >= p.T) return;
+  const int T = p.T, H = p.H, ng = H / 256;
+  const float eps = p.eps;
+  const float* __restrict__ resid = p.resid;
+  uint16_t* __restrict__ xs = c.xs;
+  float* __restrict__ rstd = c.rstd;
+  const int stride = c.xs_stride;
+  if (warp >= T) return;
   // gamma and the first row are requested together: one memory latency, not one per group
   uint4 gam[kHidGroups];
 #pragma unroll
   for (int i = 0; i < kHidGroups; ++i)
-    gam[i] = (i < p.H / 256) ? ldnc128(gamma + 256 * i + 8 * lane) : make_uint4(0u, 0u, 0u, 0u);
+    gam[i] = (i < ng) ? ldnc128(gamma + 256 * i + 8 * lane) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll 1
-  for (int t = warp; t < p.T; t += kWarps) {
+  for (int t = warp; t < T; t += kWarps) {
     RowRegs x;
-    load_row(p.resid + static_cast<size_t>(t) * p.H, p.H, x);
-    const float r = rstd_fixed(row_sumsq(x, p.H), p.H, p.eps);
-    if (lane == 0) c.rstd[t] = r;
-    uint16_t* xr = c.xs + static_cast<size_t>(t) * c.xs_stride;
+    load_row(resid + static_cast<size_t>(t) * H, H, x);
+    const float r = rstd_fixed(row_sumsq(x, H), H, eps);
+    if (lane == 0) rstd[t] = r;
+    uint16_t* __restrict__ xr = xs + static_cast<size_t>(t) * stride + 8 * lane;
+    float* __restrict__ xf = x32 ? x32 + static_cast<size_t>(t) * H + 8 * lane : nullptr;
 #pragma unroll
     for (int i = 0; i < kHidGroups; ++i) {
-      if (i < p.H / 256) {
+      if (i < ng) {
         const uint4 gv = gam[i];
         const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-        uint32_t o[4];
+        float y[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float g0 = lo_bf(gw[j]), g1 = hi_bf(gw[j]);
           // (x*r)*g or (x*g)*r without duplicating the code path
           const float a0 = gamma_first ? g0 : r, b0 = gamma_first ? r : g0;
           const float a1 = gamma_first ? g1 : r, b1 = gamma_first ? r : g1;
-          const float y0 = __fmul_rn(__fmul_rn(x.v[i][2 * j], a0), b0);
-          const float y1 = __fmul_rn(__fmul_rn(x.v[i][2 * j + 1], a1), b1);
-          o[j] = pack_bf2(y0, y1);
-          if (x32) *reinterpret_cast<float2*>(x32 + static_cast<size_t>(t) * p.H + 256 * i + 8 * lane + 2 * j) =
-              make_float2(y0, y1);
+          y[2 * j] = __fmul_rn(__fmul_rn(x.v[i][2 * j], a0), b0);
+          y[2 * j + 1] = __fmul_rn(__fmul_rn(x.v[i][2 * j + 1], a1), b1);
         }
-        *reinterpret_cast<uint4*>(xr + 256 * i + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(xr + 256 * i) =
+            make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]), pack_bf2(y[4], y[5]), pack_bf2(y[6], y[7]));
+        if (xf) {
+          *reinterpret_cast<float4*>(xf + 256 * i) = make_float4(y[0], y[1], y[2], y[3]);
+          *reinterpret_cast<float4*>(xf + 256 * i + 4) = make_float4(y[4], y[5], y[6], y[7]);
+        }
       }
     }
   }
@@ -1663,9 +1674,18 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
 // ------------------------------------------------------------------ the kernel
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1)
-    qwen3_decode_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap kmap,
+    qwen3_decode_kernel(const __grid_constant__ Params pk, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ uint8_t smem_raw[];
+  // The stage functions read the launch parameters through a reference: a shared-memory copy
+  // answers in tens of cycles, the kernel-parameter space behind a generic pointer in
+  // hundreds.
+  __shared__ __align__(16) Params sp;
+  static_assert(sizeof(Params) % 4 == 0 && sizeof(Params) / 4 <= kThreads, "Params copy");
+  if (threadIdx.x < sizeof(Params) / 4)
+    reinterpret_cast<uint32_t*>(&sp)[threadIdx.x] = reinterpret_cast<const uint32_t*>(&pk)[threadIdx.x];
+  __syncthreads();
+  const Params& p = sp;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const SmemLayout lay(p.H, NT);
   const int warp = threadIdx.x >> 5, lane = lane_id();
