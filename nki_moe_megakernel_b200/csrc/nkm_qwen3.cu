@@ -58,7 +58,7 @@ WsLayout layout_ws(const nkm_qwen3_desc& d, int num_sms) {
   size_t o = 0;
   w.ctrl = o;
   w.bar = o;
-  w.status = o + 16;  // bar[0] = arrival count, bar[1] = generation
+  w.status = o + 16;  // bar[0] = barrier arrival count, bar[2] = CTAs that left the launch
   w.strip_cnt = o + 256;
   w.attn_cnt = w.strip_cnt + kMaxStrips * 4;
   w.row_cnt = w.attn_cnt + align_up(Tm * d.n_kv_heads * 4);

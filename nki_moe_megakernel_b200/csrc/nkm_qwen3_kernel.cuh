@@ -161,6 +161,7 @@ struct Ctx {
   const LayerPtrs* lt;  // pointer table of layers first_layer .. first_layer + num_layers - 1
   int* flag;
   int stage_idx;
+  unsigned bar_k;  // grid barriers passed in this launch
   int primed;  // the next GEMV stage's first chunks are already in flight
 };
 
@@ -212,35 +213,55 @@ __device__ __forceinline__ void slot_wait(const Params& p, Ctx& c, int slot) {
 // bumps the generation word the others spin on, so the counter is zero again when the kernel
 // ends (no per-launch reset needed).  Co-residency is guaranteed by the cooperative launch.
 // Returns false if any CTA recorded a fatal status or the wait timed out.
+// Grid barrier on one monotonic arrival counter (bar[0]): barrier k of a launch is passed
+// when the counter reaches (k + 1) * gridDim.x, so arrivals need no reply and nothing is reset
+// on the way; the last CTA to leave the launch zeroes the counter (launch_exit).  The status
+// word is read with every poll: a fatal error anywhere releases every waiter.
 __device__ __noinline__ bool grid_barrier(const Params& p, Ctx& c) {
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned* count = p.bar;
-    unsigned* gen = p.bar + 1;
-    const unsigned g0 = ld_acquire_u32(gen);
-    __threadfence();
-    const unsigned old = atom_acqrel_add_u32(count, 1u);
+    const unsigned target = (c.bar_k + 1u) * gridDim.x;
+    red_release_add_u32(count, 1u);
     int ok = 1;
-    if (old == gridDim.x - 1) {
-      *reinterpret_cast<volatile unsigned*>(count) = 0u;
-      st_release_u32(gen, g0 + 1u);
-    } else if (ld_acquire_u32(gen) == g0) {
-      const uint64_t t0 = globaltimer_ns();
-      while (ld_acquire_u32(gen) == g0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          set_status(p, kStatusFatal);
-          ok = 0;
-          break;
-        }
-        __nanosleep(32);
+    uint64_t t0 = 0;
+#pragma unroll 1
+    for (unsigned it = 0;; ++it) {
+      const unsigned v = ld_acquire_u32(count);
+      const int st = ld_volatile_i32(p.status);
+      if (st & kStatusFatal) {
+        ok = 0;
+        break;
       }
+      if (static_cast<int>(v - target) >= 0) break;
+      if (it == 0) {
+        t0 = globaltimer_ns();
+      } else if ((it & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_status(p, kStatusFatal);
+        ok = 0;
+        break;
+      }
+      __nanosleep(20);
     }
-    if (ld_volatile_i32(p.status) & kStatusFatal) ok = 0;
     *c.flag = ok;
   }
+  ++c.bar_k;
   __syncthreads();
   stamp(p, c);
   return *c.flag != 0;
+}
+
+// End of a launch: the last CTA out zeroes the barrier counter for the next launch on this
+// workspace (launches on one workspace are stream-ordered).
+__device__ __forceinline__ void launch_exit(const Params& p) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atom_acqrel_add_u32(p.bar + 2, 1u);
+    if (old == gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned*>(p.bar) = 0u;
+      *reinterpret_cast<volatile unsigned*>(p.bar + 2) = 0u;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ fixed-order reductions
@@ -1707,6 +1728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.rt = reinterpret_cast<Route*>(smem + lay.route_off);
   c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
   c.stage_idx = 0;
+  c.bar_k = 0;
   c.primed = 0;
   {
     // the layer pointer table, once per launch: every stage reads its pointers from shared memory
@@ -1729,6 +1751,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncwarp();
 
+  [&]() {  // the launch body; a fatal error returns from here to launch_exit
   // stage 0: residual (fp32) <- embeddings / hidden input (bf16)
   {
     const int nvec = p.T * p.H / 8;
@@ -1835,6 +1858,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     stamp(p, c);
   }
+  }();
+  launch_exit(p);
 }
 
 }  // namespace nkm
