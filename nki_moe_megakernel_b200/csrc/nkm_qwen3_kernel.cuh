@@ -110,6 +110,17 @@ struct Route {
   float pair_w[kMaxPairs];
 };
 
+// The attention items of one CTA are the same for every layer of a launch (they depend on the
+// positions only): planned once per launch.  n < 0: more items than the plan holds (the stage
+// then plans on the fly).
+constexpr int kMaxAttItems = 2;
+struct AttPlan {
+  int n, CT;
+  int b[kMaxAttItems], h[kMaxAttItems], ch[kMaxAttItems], nch[kMaxAttItems], pos[kMaxAttItems],
+      item[kMaxAttItems];
+  int blk[kMaxAttItems][32];  // block ids of the item's context chunk (lane j: block tok_beg/128 + j)
+};
+
 // Shared-memory layout, identical on host (sizing) and device.  Each warp owns a ring of
 // ring_bytes: the GEMV stages use it as 2 slots of (chunk units x 1 KB), the attention stage
 // as 4 KB slots.
@@ -124,7 +135,7 @@ struct RingGeom {
 
 struct SmemLayout {
   uint32_t ring_bytes;
-  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, flag_off, total;
+  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, flag_off, total;
   __host__ __device__ SmemLayout(int H, int NT) {
     ring_bytes = NT == 4 ? 8192u : 16384u;
     ring_off = 0;
@@ -137,7 +148,8 @@ struct SmemLayout {
     rstd_off = bars_off + static_cast<uint32_t>(kWarps * kMaxBars * 8);
     route_off = rstd_off + 32 * 4;
     lt_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
-    flag_off = lt_off + static_cast<uint32_t>(kMaxLaunchLayers * sizeof(LayerPtrs));
+    plan_off = lt_off + static_cast<uint32_t>(kMaxLaunchLayers * sizeof(LayerPtrs));
+    flag_off = plan_off + static_cast<uint32_t>((sizeof(AttPlan) + 15) & ~size_t(15));
     total = flag_off + 16 + 1024;  // + alignment slack for the ring base
   }
 };
@@ -159,6 +171,8 @@ struct Ctx {
   float* rstd;
   Route* rt;
   const LayerPtrs* lt;  // pointer table of layers first_layer .. first_layer + num_layers - 1
+  AttPlan* plan;        // this CTA's attention items
+  int att_pb;           // K/V boxes of the first attention item already issued (-1: none)
   int* flag;
   int stage_idx;
   unsigned bar_k;  // grid barriers passed in this launch
@@ -416,34 +430,11 @@ __device__ __forceinline__ uint4 load_bfrag(const Params& p, const uint16_t* xs,
   const int k = kt * 32 + 8 * (lane & 3);
   if (col >= ncols) return make_uint4(0, 0, 0, 0);
   if (kind == GK_OPROJ) return ldcg128(p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + k);
-  if (kind == GK_DOWN) return ldcg128(p.hbuf + static_cast<size_t>(rt->act_off[seg] + col) * p.I + k);
   const int row = kind == GK_GATEUP ? rt->pair_tok[rt->act_off[seg] + col] : col;
   return lds128(smem_addr(xs + static_cast<size_t>(row) * xs_stride + k));
 }
 
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-
-// Level-2 combine of the MoE output for one 16-row strip: sum the top-k slots of every token
-// in slot order (moe_fused_nki.py:542-568) and add into the residual.
-__device__ __noinline__ void moe_row_combine(const Params& p, const Route* rt, int strip, int layer) {
-  const int lane = lane_id();
-  const int n = 16 * p.T;
-#pragma unroll 1
-  for (int idx = lane; idx < n; idx += 32) {
-    const int t = idx >> 4, row = strip * 16 + (idx & 15);
-    float v[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      v[k] = k < p.K ? ldcg_f(p.ypair + static_cast<size_t>(rt->pmap[t * p.K + k]) * p.H + row) : 0.f;
-    float a = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) a += v[k];
-    float* x = p.resid + static_cast<size_t>(t) * p.H + row;
-    const float nv = (p.residual ? *x : 0.f) + rbf(a);
-    *x = nv;
-    if (p.tr_out) p.tr_out[(static_cast<size_t>(layer - p.first_layer) * p.T + t) * p.H + row] = nv;
-  }
-}
 
 // Final write of one strip's accumulators (all of K reduced): element (row r, column col).
 __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, const GemvGeom& G, int kind, int seg,
@@ -475,12 +466,6 @@ __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, con
     const int pair = rt->act_off[seg] + col;
     const float h = rbf(rbf(silu_f(rbf(v0))) * rbf(v1));
     p.hbuf[static_cast<size_t>(pair) * p.I + strip * 8 + g] = f2bf(h);
-  } else if (kind == GK_DOWN) {
-    const int pair = rt->act_off[seg] + col;
-    const float w = rt->pair_w[pair];
-    float* y = p.ypair + static_cast<size_t>(pair) * p.H + strip * 16 + g;
-    y[0] = v0 * w;
-    y[8] = v1 * w;
   } else {  // GK_LMHEAD
     float* lo = p.logits_out + static_cast<size_t>(col) * p.V + strip * 16 + g;
     lo[0] = v0;
@@ -499,19 +484,6 @@ __device__ __noinline__ void gemv_epilogue(const Params& p, const Route* rt, con
     for (int e = 0; e < 2; ++e) {
       const int col = nt * 8 + 2 * t4 + e;
       if (col < ncols) gemv_store(p, rt, G, kind, seg, strip, g, col, acc.v[nt][e], acc.v[nt][2 + e]);
-    }
-  }
-  if (kind == GK_DOWN) {
-    // when every active expert has finished this row strip, combine it into the residual
-    __threadfence();
-    __syncwarp();
-    unsigned old = 0;
-    if (lane == 0) old = atom_acqrel_add_u32(&p.row_cnt[strip], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == static_cast<unsigned>(rt->nA - 1)) {
-      __threadfence();
-      moe_row_combine(p, rt, strip, G.layer);
-      if (lane == 0) p.row_cnt[strip] = 0u;
     }
   }
 }
@@ -547,7 +519,9 @@ __device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const 
   for (int nt = 0; nt < NT; ++nt)
     *reinterpret_cast<float4*>(dst + nt * 128) =
         make_float4(acc.v[nt][0], acc.v[nt][1], acc.v[nt][2], acc.v[nt][3]);
-  __threadfence();
+  // the warp's partial stores are ordered before lane 0's release by the warp barrier; the
+  // acq_rel counter update makes them visible to the last contributor, whose acquire (and
+  // the warp barrier of the shuffle) orders its reads of the partials after it
   __syncwarp();
   const int wf = worker_of(s0, NU, NWe), wl = worker_of(s1 - 1, NU, NWe);
   const int gstrip = seg * G.sps + strip;
@@ -555,7 +529,6 @@ __device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const 
   if (lane == 0) old = atom_acqrel_add_u32(&p.strip_cnt[gstrip], 1u);
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != static_cast<unsigned>(wl - wf)) return false;
-  __threadfence();
   const int slot_f = range_lo(NU, wf, NWe) == s0 ? 0 : 1;
   Acc<NT> sum;
 #pragma unroll
@@ -837,8 +810,7 @@ __device__ __noinline__ void down_flush(const Params& p, float* tile, int layer,
     float4* dst = reinterpret_cast<float4*>(p.gpart + (static_cast<size_t>(worker) * 2 + slot) * n);
 #pragma unroll 1
     for (int q = lane; q < n4; q += 32) dst[q] = tile4[q];
-    __threadfence();
-    __syncwarp();
+    __syncwarp();  // ordered before lane 0's release (as in gemv_flush)
     const int wf = worker_of(s_lo, NI, NWe), wl = worker_of(s_hi - 1, NI, NWe);
     unsigned old = 0;
     if (lane == 0) old = atom_acqrel_add_u32(&p.strip_cnt[s], 1u);
@@ -849,7 +821,6 @@ __device__ __noinline__ void down_flush(const Params& p, float* tile, int layer,
       __syncwarp();
       return;
     }
-    __threadfence();
     const int slot_f = (range_lo(NI, wf, NWe) >= s_lo) ? 0 : 1;
 #pragma unroll 1
     for (int q = lane; q < n4; q += 32) {
@@ -1073,6 +1044,8 @@ __device__ __forceinline__ uint2 head_finish(const HeadIn& in, float eps) {
 
 // Per-warp flash-decode over the 32-token tiles tile_first, tile_first+step, ... of
 // [tok_beg, tok_end).  Leaves the unnormalised (m, l, o) of rows g and g+8 in registers.
+constexpr int kNoBlocks = -2;  // "block ids not preloaded"
+
 // Block ids of the K/V blocks a context chunk [tok_beg, tok_end) touches: lane j holds the
 // id of block tok_beg/128 + j (j < 32; -1 past the chunk).  One coalesced load per warp.
 __device__ __forceinline__ int att_chunk_blocks(const Params& p, int b, int tok_beg, int tok_end) {
@@ -1247,7 +1220,7 @@ __device__ __forceinline__ void attention_tiles(const Params& p, Ctx& c, int lay
 
 // One (sequence b, kv head h, context chunk ch) item, processed by the whole CTA.
 __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int layer, int b, int h, int ch, int nch,
-                                                  int CT, int item, int pos, const CUtensorMap* kmap,
+                                                  int CT, int item, int pos, int blk_pre, const CUtensorMap* kmap,
                                                   const CUtensorMap* vmap) {
   const int warp = threadIdx.x >> 5, lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int tok_beg = ch * CT;
@@ -1263,8 +1236,9 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   const uint16_t* sinr = p.rope_sin + static_cast<size_t>(prow) * kHeadDim;
   const LayerPtrs& lw = c.lt[layer - p.first_layer];
   const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
-  const int blk_lane = att_chunk_blocks(p, b, tok_beg, tok_end);
-  const int pb = att_prime(p, c, layer, b, h, tok_beg, tok_end, warp, kWarps, blk_lane, kmap, vmap);
+  const int blk_lane = blk_pre != kNoBlocks ? blk_pre : att_chunk_blocks(p, b, tok_beg, tok_end);
+  const int pb = c.att_pb >= 0 ? c.att_pb : att_prime(p, c, layer, b, h, tok_beg, tok_end, warp, kWarps, blk_lane, kmap, vmap);
+  c.att_pb = -1;
 
   // --- stage the q heads (rows warp, warp + 8) and, in the last chunk, the new token's K
   // (warp 7) and V (warp 6); every load is issued before the first one is used
@@ -1403,8 +1377,9 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
     __syncthreads();  // the rings are reused by the next item
     return;
   }
-  // --- split context: the last CTA of (b, h) combines the chunk partials in chunk order
-  __threadfence();
+  // --- split context: the last CTA of (b, h) combines the chunk partials in chunk order.
+  // The CTA barrier orders every thread's partial stores before thread 0's acq_rel update;
+  // the second barrier orders the last CTA's partial reads after thread 0's acquire.
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned old = atom_acqrel_add_u32(&p.attn_cnt[b * p.nkv + h], 1u);
@@ -1412,7 +1387,6 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   }
   __syncthreads();
   if (!*cflag) return;
-  __threadfence();
   const int item0 = item - ch;  // items of one (b, h) are consecutive, chunk-major
   for (int r = warp; r < p.grp; r += kWarps) {
     // lane k holds chunk k's (m, l) (chunks beyond 32 are folded in a loop)
@@ -1457,17 +1431,20 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
 }
 
 __device__ __noinline__ void attention_cta_item(const Params& p, Ctx& cref, int layer, int b, int h, int ch, int nch,
-                                                int CT, int item, int pos, const CUtensorMap* kmap,
+                                                int CT, int item, int pos, int blk_pre, const CUtensorMap* kmap,
                                                 const CUtensorMap* vmap) {
   Ctx c = cref;  // register-resident copy
-  attention_cta_body(p, c, layer, b, h, ch, nch, CT, item, pos, kmap, vmap);
+  attention_cta_body(p, c, layer, b, h, ch, nch, CT, item, pos, blk_pre, kmap, vmap);
   cref.head = c.head;
   cref.phase = c.phase;
+  cref.att_pb = -1;
 }
 
-__device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
-  // chunk length CT (multiple of 32) such that the (b, h, chunk) items fill the grid once.
-  // Lane b holds sequence b's position (batch <= 32), so one load serves the whole plan.
+// Chunk length CT (multiple of 32) such that the (b, h, chunk) items fill the grid once, and
+// the items of this CTA.  Lane b holds sequence b's position (batch <= 32).  Calls fn(b, h, ch,
+// nch, CT, item, pos) for each item of this CTA, in order.
+template <class Fn>
+__device__ __forceinline__ void att_items(const Params& p, Fn&& fn) {
   const int G = gridDim.x, lane = lane_id();
   const int mypos = lane < p.T ? seq_pos(p, lane) : 0;
   const int mytiles = lane < p.T ? (mypos + kAttTile - 1) / kAttTile : 0;
@@ -1502,8 +1479,55 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
     const int nch = __shfl_sync(0xffffffffu, mynch, b);
     const int pos = __shfl_sync(0xffffffffu, mypos, b);
     const int r = it - base;
-    attention_cta_item(p, c, layer, b, r / nch, r % nch, nch, CT, it, pos, kmap, vmap);
+    fn(b, r / nch, r % nch, nch, CT, it, pos);
   }
+}
+
+// Plan this CTA's attention items for the launch (all threads call it; warp 0 writes).
+__device__ __noinline__ void att_plan_build(const Params& p, Ctx& c) {
+  AttPlan* pl = c.plan;
+  const bool w0 = (threadIdx.x >> 5) == 0;
+  int n = 0;
+  att_items(p, [&](int b, int h, int ch, int nch, int CT, int item, int pos) {
+    if (n < kMaxAttItems && w0) {
+      pl->b[n] = b;
+      pl->h[n] = h;
+      pl->ch[n] = ch;
+      pl->nch[n] = nch;
+      pl->pos[n] = pos;
+      pl->item[n] = item;
+      pl->CT = CT;
+      pl->blk[n][lane_id()] = att_chunk_blocks(p, b, ch * CT, min(pos, (ch + 1) * CT));
+    }
+    ++n;
+  });
+  if (w0 && lane_id() == 0) pl->n = n <= kMaxAttItems ? n : -1;
+}
+
+// Issue the first K/V boxes of this CTA's first attention item of `layer` into the warp's
+// (drained) ring, so that they stream while the grid barrier before the attention completes.
+__device__ __noinline__ void att_prime_layer(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap,
+                                             const CUtensorMap* vmap) {
+  const AttPlan* pl = c.plan;
+  if (pl->n <= 0) return;
+  const int warp = threadIdx.x >> 5;
+  const int tok_beg = pl->ch[0] * pl->CT, tok_end = min(pl->pos[0], (pl->ch[0] + 1) * pl->CT);
+  c.att_pb = att_prime(p, c, layer, pl->b[0], pl->h[0], tok_beg, tok_end, warp, kWarps, pl->blk[0][lane_id()], kmap,
+                       vmap);
+}
+
+__device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  const AttPlan* pl = c.plan;
+  if (pl->n >= 0) {
+#pragma unroll 1
+    for (int k = 0; k < pl->n; ++k)
+      attention_cta_item(p, c, layer, pl->b[k], pl->h[k], pl->ch[k], pl->nch[k], pl->CT, pl->item[k], pl->pos[k],
+                         pl->blk[k][lane_id()], kmap, vmap);
+    return;
+  }
+  att_items(p, [&](int b, int h, int ch, int nch, int CT, int item, int pos) {
+    attention_cta_item(p, c, layer, b, h, ch, nch, CT, item, pos, kNoBlocks, kmap, vmap);
+  });
 }
 
 // ------------------------------------------------------------------ router (stage D)
@@ -1729,6 +1753,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
   c.stage_idx = 0;
   c.bar_k = 0;
+  c.plan = reinterpret_cast<AttPlan*>(smem + lay.plan_off);
+  c.att_pb = -1;
   c.primed = 0;
   {
     // the layer pointer table, once per launch: every stage reads its pointers from shared memory
@@ -1738,6 +1764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n16 = p.num_layers * static_cast<int>(sizeof(LayerPtrs) / 16);
     for (int i = threadIdx.x; i < n16; i += kThreads) reinterpret_cast<uint4*>(lt)[i] = src[i];
     c.lt = lt;
+    if (p.stages & 1) att_plan_build(p, c);
     __syncthreads();
   }
   stamp(p, c);
@@ -1804,6 +1831,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
       gemv_stage<NT>(p, c, ga, GK_QKV);
+      att_prime_layer(p, c, layer, &kmap, &vmap);  // this layer's first K/V boxes stream during the barrier
       if (!grid_barrier(p, c)) return;
       // B: attention (+ KV write); the O-proj weights start streaming before the barrier
       attention_stage(p, c, layer, &kmap, &vmap);
