@@ -289,7 +289,8 @@ __device__ __forceinline__ float warp_max(float s) {
   for (int off = 16; off >= 1; off >>= 1) s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, off));
   return s;
 }
-__device__ __forceinline__ float rstd_fixed(float sumsq, int n, float eps) {
+// Out of line: one copy of the correctly rounded square root and division for every caller.
+__device__ __noinline__ float rstd_fixed(float sumsq, int n, float eps) {
   const float v = __fadd_rn(__fmul_rn(sumsq, 1.0f / static_cast<float>(n)), eps);
   return __fdiv_rn(1.0f, __fsqrt_rn(v));
 }
@@ -1035,7 +1036,7 @@ __device__ __forceinline__ HeadIn head_load(const uint16_t* src, const uint16_t*
   in.s = *reinterpret_cast<const uint2*>(sn + 4 * lane);
   return in;
 }
-__device__ __forceinline__ uint2 head_finish(const HeadIn& in, float eps) {
+__device__ __noinline__ uint2 head_finish(HeadIn in, float eps) {
   float x[4];
   unpack4(in.raw, x);
   head_norm_rope(x, in.w, in.c, in.s, eps);
@@ -1057,7 +1058,7 @@ __device__ __forceinline__ int att_chunk_blocks(const Params& p, int b, int tok_
 // TMA box bi of this warp's tiles (tile bi/4; boxes K d0-63, K d64-127, V d0-63, V d64-127)
 // into ring slot `slot`.  All lanes call it (the block id is shuffled from blk_lane); lane 0
 // issues the copy.
-__device__ __forceinline__ void att_issue_box(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg,
+__device__ __noinline__ void att_issue_box(const Params& p, Ctx& c, int layer, int b, int h, int tok_beg,
                                               int tile_first, int tile_step, int blk_lane, int bi, int slot,
                                               const CUtensorMap* kmap, const CUtensorMap* vmap) {
   const int tile = tile_first + (bi >> 2) * tile_step, kind = bi & 3;
@@ -1628,37 +1629,32 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
     uint32_t key[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) key[q] = (q < per && ids[q] < E) ? order_key(v[q]) : 0u;
-    float vals[8];
+    // lane k keeps pick k's softmax value (K <= 8 < 32)
+    float myval = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < K; ++k) {
+      uint32_t lb = 0u;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (k < K) {
-        uint32_t lb = 0u;
+      for (int q = 0; q < 8; ++q) lb = max(lb, key[q]);
+      const uint32_t wmax = __reduce_max_sync(0xffffffffu, lb);
+      int bi = 0x7fffffff;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) lb = max(lb, key[q]);
-        const uint32_t wmax = __reduce_max_sync(0xffffffffu, lb);
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int q = 7; q >= 0; --q) {
-          const unsigned m = __ballot_sync(0xffffffffu, key[q] == wmax);
-          if (m) bi = q * 32 + __ffs(m) - 1;
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (ids[q] == bi) key[q] = 0u;
-        vals[k] = rbf(__expf(key_value(wmax) - mx) * inv);
-        if (lane == 0) rt->topk_idx[t * K + k] = bi;
+      for (int q = 7; q >= 0; --q) {
+        const unsigned m = __ballot_sync(0xffffffffu, key[q] == wmax);
+        if (m) bi = q * 32 + __ffs(m) - 1;
       }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (ids[q] == bi) key[q] = 0u;
+      if (lane == k) myval = rbf(__expf(key_value(wmax) - mx) * inv);
+      if (lane == 0) rt->topk_idx[t * K + k] = bi;
     }
+    // renormalise in pick order (sum over lanes 0..K-1 sequentially)
     float sk = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (k < K) sk += vals[k];
+#pragma unroll 1
+    for (int k = 0; k < K; ++k) sk += __shfl_sync(0xffffffffu, myval, k);
     const float inv2 = 1.f / sk;
-    if (lane == 0) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (k < K) rt->topk_w[t * K + k] = rbf(vals[k] * inv2);
-    }
+    if (lane < K) rt->topk_w[t * K + lane] = rbf(myval * inv2);
   }
   __syncthreads();
   // entry i = threadIdx.x (NP <= kMaxPairs == kThreads): its expert and its rank among the
