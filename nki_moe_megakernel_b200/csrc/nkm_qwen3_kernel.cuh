@@ -110,6 +110,10 @@ struct Route {
   float pair_w[kMaxPairs];
 };
 
+// Dense GEMVs with few strips (QKV, O-proj) at batch <= 8 give every CTA whole strips and
+// reduce them in shared memory: at most this many strips per CTA.
+constexpr int kCtaStripsMax = 4;
+
 // The attention items of one CTA are the same for every layer of a launch (they depend on the
 // positions only): planned once per launch.  n < 0: more items than the plan holds (the stage
 // then plans on the fly).
@@ -135,7 +139,7 @@ struct RingGeom {
 
 struct SmemLayout {
   uint32_t ring_bytes;
-  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, flag_off, total;
+  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, red_off, flag_off, total;
   __host__ __device__ SmemLayout(int H, int NT) {
     ring_bytes = NT == 4 ? 8192u : 16384u;
     ring_off = 0;
@@ -149,7 +153,8 @@ struct SmemLayout {
     route_off = rstd_off + 32 * 4;
     lt_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
     plan_off = lt_off + static_cast<uint32_t>(kMaxLaunchLayers * sizeof(LayerPtrs));
-    flag_off = plan_off + static_cast<uint32_t>((sizeof(AttPlan) + 15) & ~size_t(15));
+    red_off = plan_off + static_cast<uint32_t>((sizeof(AttPlan) + 15) & ~size_t(15));
+    flag_off = red_off + (NT == 1 ? static_cast<uint32_t>(kCtaStripsMax * kWarps * 32 * 4 * 4) : 0u);
     total = flag_off + 16 + 1024;  // + alignment slack for the ring base
   }
 };
@@ -172,6 +177,7 @@ struct Ctx {
   Route* rt;
   const LayerPtrs* lt;  // pointer table of layers first_layer .. first_layer + num_layers - 1
   AttPlan* plan;        // this CTA's attention items
+  float* red;           // per-strip partial tiles of the whole-strip GEMV mode (batch <= 8)
   int att_pb;           // K/V boxes of the first attention item already issued (-1: none)
   int* flag;
   int stage_idx;
@@ -231,12 +237,16 @@ __device__ __forceinline__ void slot_wait(const Params& p, Ctx& c, int slot) {
 // when the counter reaches (k + 1) * gridDim.x, so arrivals need no reply and nothing is reset
 // on the way; the last CTA to leave the launch zeroes the counter (launch_exit).  The status
 // word is read with every poll: a fatal error anywhere releases every waiter.
-__device__ __noinline__ bool grid_barrier(const Params& p, Ctx& c) {
+// Split form: grid_arrive, then work that does not depend on the other CTAs (issuing the next
+// stage's weight copies), then grid_wait.
+__device__ __forceinline__ void grid_arrive(const Params& p) {
   __syncthreads();
+  if (threadIdx.x == 0) red_release_add_u32(p.bar, 1u);
+}
+__device__ __noinline__ bool grid_wait(const Params& p, Ctx& c) {
   if (threadIdx.x == 0) {
     unsigned* count = p.bar;
     const unsigned target = (c.bar_k + 1u) * gridDim.x;
-    red_release_add_u32(count, 1u);
     int ok = 1;
     uint64_t t0 = 0;
 #pragma unroll 1
@@ -263,6 +273,10 @@ __device__ __noinline__ bool grid_barrier(const Params& p, Ctx& c) {
   __syncthreads();
   stamp(p, c);
   return *c.flag != 0;
+}
+__device__ __forceinline__ bool grid_barrier(const Params& p, Ctx& c) {
+  grid_arrive(p);
+  return grid_wait(p, c);
 }
 
 // End of a launch: the last CTA out zeroes the barrier counter for the next launch on this
@@ -569,8 +583,150 @@ __device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const 
 // that the mma dependency chains stay short.
 // Issue the first ring chunks of a GEMV stage early (before the grid barrier that precedes
 // it): the weights do not depend on the barrier, so their latency overlaps the barrier.
+// Whole-strip mode: strip s of a dense GEMV belongs to CTA s % gridDim.x; warp w of the CTA
+// takes K-units [KT w / 8, KT (w + 1) / 8) of each of the CTA's strips.
+template <int NT>
+__device__ __forceinline__ bool cta_strip_mode(const GemvGeom& G, int kind) {
+  return NT == 1 && (kind == GK_QKV || kind == GK_OPROJ) && G.nseg == 1 && G.kt >= kWarps &&
+         (G.sps + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) <= kCtaStripsMax;
+}
+
+template <int NT>
+__device__ __noinline__ void cta_strips_prime(const Params& p, Ctx& c, const GemvGeom& G) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
+  const int lane = lane_id(), warp = threadIdx.x >> 5;
+  const int Gd = gridDim.x, KT = G.kt;
+  const int ns = static_cast<int>(blockIdx.x) < G.sps ? (G.sps - static_cast<int>(blockIdx.x) + Gd - 1) / Gd : 0;
+  const int k0 = KT * warp / kWarps, nk = KT * (warp + 1) / kWarps - k0;
+  int pj = 0, pk = 0;
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    if (pj >= ns) break;
+    const int n = min(CU, nk - pk);
+    if (lane == 0) {
+      const int strip = static_cast<int>(blockIdx.x) + pj * Gd;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[i], static_cast<uint32_t>(n * kUnitBytes));
+      bulk_g2s(c.ring + i * (CU * kUnitBytes), G.base + static_cast<uint64_t>(strip * KT + k0 + pk) * kUnitBytes,
+               static_cast<uint32_t>(n * kUnitBytes), &c.bars[i], c.pol);
+    }
+    pk += n;
+    if (pk == nk) {
+      pk = 0;
+      ++pj;
+    }
+  }
+}
+
+// All warps of the CTA call it (one CTA barrier inside).
+template <int NT>
+__device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const GemvGeom& G, int kind) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
+  Ctx c = cref;
+  const bool primed = c.primed != 0;
+  cref.primed = 0;
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3, warp = threadIdx.x >> 5;
+  const int Gd = gridDim.x, KT = G.kt;
+  const int ns = static_cast<int>(blockIdx.x) < G.sps ? (G.sps - static_cast<int>(blockIdx.x) + Gd - 1) / Gd : 0;
+  const int k0 = KT * warp / kWarps, nk = KT * (warp + 1) / kWarps - k0;
+  const int ncols = p.T;
+  const int ntiles = (ncols + 7) >> 3;
+  // B rows of this lane (column g of each n-tile): shared X (QKV) or the attention output (O-proj)
+  const bool smem_b = kind == GK_QKV;
+  const int col = g;
+  const uint4* brow_s = (smem_b && col < ncols)
+                            ? reinterpret_cast<const uint4*>(c.xs + static_cast<size_t>(col) * c.xs_stride + 8 * t4)
+                            : nullptr;
+  const uint16_t* brow_g = (!smem_b && col < ncols)
+                               ? p.attn_out + static_cast<size_t>(col) * (p.nq * kHeadDim) + 8 * t4
+                               : nullptr;
+  int pj = 0, pk = 0;
+  auto issue = [&](int slot, bool dry) {
+    const int n = min(CU, nk - pk);
+    if (lane == 0 && !dry) {
+      const int strip = static_cast<int>(blockIdx.x) + pj * Gd;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
+      bulk_g2s(c.ring + slot * (CU * kUnitBytes), G.base + static_cast<uint64_t>(strip * KT + k0 + pk) * kUnitBytes,
+               static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
+    }
+    pk += n;
+    if (pk == nk) {
+      pk = 0;
+      ++pj;
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < NS; ++i)
+    if (pj < ns) issue(i, primed);
+  int cs = 0;
+#pragma unroll 1
+  for (int j = 0; j < ns; ++j) {
+    float acc[NA][4];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
+#pragma unroll 1
+    for (int ck = 0; ck < nk; ck += CU) {
+      const int n = min(CU, nk - ck);
+      uint4 bf[CU];
+#pragma unroll
+      for (int i = 0; i < CU; ++i) {
+        const int kt = k0 + ck + i;
+        bf[i] = (i >= n) ? make_uint4(0u, 0u, 0u, 0u)
+                         : (brow_s ? brow_s[kt * 4] : (brow_g ? ldcg128(brow_g + kt * 32) : make_uint4(0u, 0u, 0u, 0u)));
+      }
+      slot_wait(p, c, cs);
+      const uint4* sa = reinterpret_cast<const uint4*>(c.ring + cs * (CU * kUnitBytes)) + lane;
+#pragma unroll
+      for (int i = 0; i < CU; ++i) {
+        if (i < n && ntiles > 0) {
+          const uint4 a0 = sa[i * (kUnitBytes / 16)];
+          const uint4 a1 = sa[i * (kUnitBytes / 16) + 32];
+          mma_bf16(acc[i % NA], a0.x, a1.x, a0.y, a1.y, bf[i].x, bf[i].y);
+          mma_bf16(acc[i % NA], a0.z, a1.z, a0.w, a1.w, bf[i].z, bf[i].w);
+        }
+      }
+      __syncwarp();
+      if (pj < ns) issue(cs, false);
+      cs = (cs + 1 == NS) ? 0 : cs + 1;
+    }
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      v.x += acc[a][0];
+      v.y += acc[a][1];
+      v.z += acc[a][2];
+      v.w += acc[a][3];
+    }
+    reinterpret_cast<float4*>(c.red)[(j * kWarps + warp) * 32 + lane] = v;
+  }
+  cref.phase = c.phase;
+  __syncthreads();
+  if (warp < ns) {
+    // strip `warp` of this CTA: the 8 K-slices summed in warp order
+    Acc<NT> sum;
+    sum.v[0][0] = sum.v[0][1] = sum.v[0][2] = sum.v[0][3] = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float4 v = reinterpret_cast<const float4*>(c.red)[(warp * kWarps + w) * 32 + lane];
+      sum.v[0][0] += v.x;
+      sum.v[0][1] += v.y;
+      sum.v[0][2] += v.z;
+      sum.v[0][3] += v.w;
+    }
+    gemv_epilogue<NT>(p, c.rt, G, kind, 0, static_cast<int>(blockIdx.x) + warp * Gd, sum);
+  }
+}
+
 template <int NT>
 __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom& G, int kind) {
+  if (cta_strip_mode<NT>(G, kind)) {
+    c.primed = 1;
+    cta_strips_prime<NT>(p, c, G);
+    return;
+  }
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
   const int lane = lane_id();
@@ -1750,6 +1906,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.stage_idx = 0;
   c.bar_k = 0;
   c.plan = reinterpret_cast<AttPlan*>(smem + lay.plan_off);
+  c.red = reinterpret_cast<float*>(smem + lay.red_off);
   c.att_pb = -1;
   c.primed = 0;
   {
@@ -1797,12 +1954,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<float4*>(dst + 4) = make_float4(lo_bf(v.z), hi_bf(v.z), lo_bf(v.w), hi_bf(v.w));
     }
   }
+  grid_arrive(p);
   if ((p.stages & 1) && p.num_layers > 0) {  // the first QKV weights stream during the barrier
     const LayerPtrs& l0 = c.lt[0];
     GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
     gemv_prime<NT>(p, c, ga, GK_QKV);
   }
-  if (!grid_barrier(p, c)) return;
+  if (!grid_wait(p, c)) return;
 
   const int layer_end = p.first_layer + p.num_layers;
   const bool want_lm = (p.stages & 4) && p.logits_out;
@@ -1826,18 +1984,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       norm_rows_to_smem(p, c, lw.ln1, false);
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
-      gemv_stage<NT>(p, c, ga, GK_QKV);
+      if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
+      else gemv_stage<NT>(p, c, ga, GK_QKV);
+      grid_arrive(p);
       att_prime_layer(p, c, layer, &kmap, &vmap);  // this layer's first K/V boxes stream during the barrier
-      if (!grid_barrier(p, c)) return;
+      if (!grid_wait(p, c)) return;
       // B: attention (+ KV write); the O-proj weights start streaming before the barrier
       attention_stage(p, c, layer, &kmap, &vmap);
       GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
+      grid_arrive(p);
       gemv_prime<NT>(p, c, gc, GK_OPROJ);
-      if (!grid_barrier(p, c)) return;
+      if (!grid_wait(p, c)) return;
       // C: O-proj + residual
-      gemv_stage<NT>(p, c, gc, GK_OPROJ);
+      if (cta_strip_mode<NT>(gc, GK_OPROJ)) gemv_cta_strips<NT>(p, c, gc, GK_OPROJ);
+      else gemv_stage<NT>(p, c, gc, GK_OPROJ);
+      grid_arrive(p);
       if (!(p.stages & 2)) prime_after(layer);
-      if (!grid_barrier(p, c)) return;
+      if (!grid_wait(p, c)) return;
     }
     if (p.stages & 2) {
       // D: RMSNorm(ln2) once per CTA (fp32 rows into the idle rings, bf16 rows into X for the
@@ -1854,12 +2017,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
       gemv_stage<NT>(p, c, ge, GK_GATEUP);
       GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
+      grid_arrive(p);
       down_prime<NT>(p, c, gf);
-      if (!grid_barrier(p, c)) return;
+      if (!grid_wait(p, c)) return;
       // F: down + affinity + combine + residual
       down_stage<NT>(p, c, gf);
+      grid_arrive(p);
       prime_after(layer);
-      if (!grid_barrier(p, c)) return;
+      if (!grid_wait(p, c)) return;
     }
   }
   // outputs
