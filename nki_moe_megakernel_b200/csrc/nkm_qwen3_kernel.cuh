@@ -488,9 +488,10 @@ __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, con
   }
 }
 
-template <int NT>
-__device__ __noinline__ void gemv_epilogue(const Params& p, const Route* rt, const GemvGeom& G, int kind, int seg,
-                                              int strip, Acc<NT> acc) {
+template <int NT, int KIND>
+__device__ __noinline__ void gemv_epilogue(const Params& p, const Route* rt, const GemvGeom& G, int seg, int strip,
+                                              Acc<NT> acc) {
+  constexpr int kind = KIND;
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int ncols = seg_cols(p, rt, kind, seg);
 #pragma unroll
@@ -518,11 +519,12 @@ __device__ __forceinline__ int worker_of(int u, int NU, int NW) {
 // partial is stored and the last contributor sums all partials in worker order (split-K
 // fix-up, deterministic) and runs the epilogue.  Partial slot: 0 if the strip is the
 // contributor's first strip, else 1 (only the first contributor can start before it).
-template <int NT>
-__device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const GemvGeom& G, int kind, int worker,
-                                        int seg, int strip, bool full, int u0, int NU, int NWe, Acc<NT> acc) {
+template <int NT, int KIND>
+__device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const GemvGeom& G, int worker, int seg,
+                                        int strip, bool full, int u0, int NU, int NWe, Acc<NT> acc) {
+  constexpr int kind = KIND;
   if (full) {
-    gemv_epilogue<NT>(p, rt, G, kind, seg, strip, acc);
+    gemv_epilogue<NT, KIND>(p, rt, G, seg, strip, acc);
     return true;
   }
   const int lane = lane_id();
@@ -572,7 +574,7 @@ __device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const 
     }
   }
   if (lane == 0) p.strip_cnt[gstrip] = 0u;
-  gemv_epilogue<NT>(p, rt, G, kind, seg, strip, sum);
+  gemv_epilogue<NT, KIND>(p, rt, G, seg, strip, sum);
   return true;
 }
 
@@ -716,12 +718,14 @@ __device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const G
       sum.v[0][2] += v.z;
       sum.v[0][3] += v.w;
     }
-    gemv_epilogue<NT>(p, c.rt, G, kind, 0, static_cast<int>(blockIdx.x) + warp * Gd, sum);
+    if (kind == GK_QKV) gemv_epilogue<NT, GK_QKV>(p, c.rt, G, 0, static_cast<int>(blockIdx.x) + warp * Gd, sum);
+    else gemv_epilogue<NT, GK_OPROJ>(p, c.rt, G, 0, static_cast<int>(blockIdx.x) + warp * Gd, sum);
   }
 }
 
-template <int NT>
-__device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom& G, int kind) {
+template <int NT, int KIND>
+__device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom& G) {
+  constexpr int kind = KIND;
   if (cta_strip_mode<NT>(G, kind)) {
     c.primed = 1;
     cta_strips_prime<NT>(p, c, G);
@@ -759,8 +763,9 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
   }
 }
 
-template <int NT>
-__device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGeom& G, int kind) {
+template <int NT, int KIND>
+__device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGeom& G) {
+  constexpr int kind = KIND;
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
   Ctx c = cref;  // register-resident copy for the streaming loop
@@ -886,7 +891,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
           for (int a = 0; a < NA; ++a) v += acc[a][nt][e];
           sum.v[nt][e] = v;
         }
-      gemv_flush<NT>(p, rt, G, kind, c.worker, cseg, cstrip, strip_kt0 == 0 && ckt == KT, u0, NU, NWe, sum);
+      gemv_flush<NT, KIND>(p, rt, G, c.worker, cseg, cstrip, strip_kt0 == 0 && ckt == KT, u0, NU, NWe, sum);
 #pragma unroll
       for (int a = 0; a < NA; ++a)
 #pragma unroll
@@ -1673,18 +1678,24 @@ __device__ __noinline__ void att_prime_layer(const Params& p, Ctx& c, int layer,
                        vmap);
 }
 
-__device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
-  const AttPlan* pl = c.plan;
-  if (pl->n >= 0) {
-#pragma unroll 1
-    for (int k = 0; k < pl->n; ++k)
-      attention_cta_item(p, c, layer, pl->b[k], pl->h[k], pl->ch[k], pl->nch[k], pl->CT, pl->item[k], pl->pos[k],
-                         pl->blk[k][lane_id()], kmap, vmap);
-    return;
-  }
+// More items per CTA than the plan holds: plan them again at every layer.
+__device__ __noinline__ void attention_unplanned(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap,
+                                                 const CUtensorMap* vmap) {
   att_items(p, [&](int b, int h, int ch, int nch, int CT, int item, int pos) {
     attention_cta_item(p, c, layer, b, h, ch, nch, CT, item, pos, kNoBlocks, kmap, vmap);
   });
+}
+
+__device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
+  const AttPlan* pl = c.plan;
+  if (pl->n < 0) {
+    attention_unplanned(p, c, layer, kmap, vmap);
+    return;
+  }
+#pragma unroll 1
+  for (int k = 0; k < pl->n; ++k)
+    attention_cta_item(p, c, layer, pl->b[k], pl->h[k], pl->ch[k], pl->nch[k], pl->CT, pl->item[k], pl->pos[k],
+                       pl->blk[k][lane_id()], kmap, vmap);
 }
 
 // ------------------------------------------------------------------ router (stage D)
@@ -1692,6 +1703,7 @@ __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer,
 // (moe_fused_nki.py:186-218).
 // x32: fp32 normalised rows in shared memory (row stride H), or nullptr to normalise on the
 // fly from the residual with the per-CTA rstd (large batches whose rows do not fit).
+template <bool kX32>
 __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer, const float* x32) {
   const int lane = lane_id();
   const LayerPtrs& lw = c.lt[layer - p.first_layer];
@@ -1713,7 +1725,7 @@ __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer, co
         const int k0 = 256 * i + 8 * lane;
         const uint4 w4 = wv[i];
         float xv[8];
-        if (x32) {
+        if (kX32) {
           const float4 x0 = *reinterpret_cast<const float4*>(x32 + static_cast<size_t>(t) * p.H + k0);
           const float4 x1 = *reinterpret_cast<const float4*>(x32 + static_cast<size_t>(t) * p.H + k0 + 4);
           xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
@@ -1958,7 +1970,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if ((p.stages & 1) && p.num_layers > 0) {  // the first QKV weights stream during the barrier
     const LayerPtrs& l0 = c.lt[0];
     GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
-    gemv_prime<NT>(p, c, ga, GK_QKV);
+    gemv_prime<NT, GK_QKV>(p, c, ga);
   }
   if (!grid_wait(p, c)) return;
 
@@ -1970,11 +1982,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.stages & 1) {
         const LayerPtrs& nl = c.lt[layer + 1 - p.first_layer];
         GemvGeom ga{nl.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer + 1};
-        gemv_prime<NT>(p, c, ga, GK_QKV);
+        gemv_prime<NT, GK_QKV>(p, c, ga);
       }
     } else if (want_lm) {
       GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer};
-      gemv_prime<NT>(p, c, gl, GK_LMHEAD);
+      gemv_prime<NT, GK_LMHEAD>(p, c, gl);
     }
   };
   for (int layer = p.first_layer; layer < layer_end; ++layer) {
@@ -1985,7 +1997,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
       if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
-      else gemv_stage<NT>(p, c, ga, GK_QKV);
+      else gemv_stage<NT, GK_QKV>(p, c, ga);
       grid_arrive(p);
       att_prime_layer(p, c, layer, &kmap, &vmap);  // this layer's first K/V boxes stream during the barrier
       if (!grid_wait(p, c)) return;
@@ -1993,11 +2005,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       attention_stage(p, c, layer, &kmap, &vmap);
       GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
       grid_arrive(p);
-      gemv_prime<NT>(p, c, gc, GK_OPROJ);
+      gemv_prime<NT, GK_OPROJ>(p, c, gc);
       if (!grid_wait(p, c)) return;
       // C: O-proj + residual
       if (cta_strip_mode<NT>(gc, GK_OPROJ)) gemv_cta_strips<NT>(p, c, gc, GK_OPROJ);
-      else gemv_stage<NT>(p, c, gc, GK_OPROJ);
+      else gemv_stage<NT, GK_OPROJ>(p, c, gc);
       grid_arrive(p);
       if (!(p.stages & 2)) prime_after(layer);
       if (!grid_wait(p, c)) return;
@@ -2010,12 +2022,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                        : nullptr;
       norm_rows_to_smem(p, c, lw.ln2, true, x32);
       __syncthreads();
-      router_stage(p, c, layer, x32);
+      if (x32) router_stage<true>(p, c, layer, x32);
+      else router_stage<false>(p, c, layer, nullptr);
       if (!grid_barrier(p, c)) return;
       // E: routing tables + gate/up (X from stage D); the down weights start streaming early
       routing_prologue(p, c, layer);
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
-      gemv_stage<NT>(p, c, ge, GK_GATEUP);
+      gemv_stage<NT, GK_GATEUP>(p, c, ge);
       GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
       grid_arrive(p);
       down_prime<NT>(p, c, gf);
@@ -2041,7 +2054,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
     GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer_end - 1};
-    gemv_stage<NT>(p, c, gl, GK_LMHEAD);
+    gemv_stage<NT, GK_LMHEAD>(p, c, gl);
   }
   if (p.tr_stage) {
     __syncthreads();
