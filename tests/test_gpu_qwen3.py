@@ -198,6 +198,32 @@ def test_out_of_range_token_id_and_position_flagged(dev):
     assert eng.status() == 0
 
 
+def test_grid_wait_timeout_reports_status(dev):
+    """Failure detection without a fault: the grid barrier counter is set so that the first
+    barrier can never be reached; every CTA gives up after the bounded wait (2 s), the step
+    ends, the status reads NKM_ERR_TIMEOUT, and the next step on the same handle succeeds."""
+    import time
+
+    from nki_moe_megakernel_b200 import _lib
+
+    cfg = qwen_cfg(n_layers=1)
+    lw = make_layers(cfg, 1, seed=16)[0]
+    x = torch.randn(4, cfg.hidden, generator=torch.Generator().manual_seed(17)).to(BF16).to(dev)
+    eng = _engine(cfg, gpu_layers([lw], dev, attention=False), 1, 4, 0, kv=False)
+    want = eng.moe_block(0, x)["hidden"]
+    assert eng.status() == 0
+    eng.workspace[0:4].view(torch.int32).fill_(-(1 << 30))  # arrival count far below any target
+    t0 = time.time()
+    eng.moe_block(0, x)
+    st = eng.status()
+    elapsed = time.time() - t0
+    assert st & _lib.NKM_ERR_TIMEOUT, st
+    assert 1.0 < elapsed < 30.0, elapsed
+    got = eng.moe_block(0, x)["hidden"]  # status() cleared the control words
+    assert eng.status() == 0
+    assert torch.equal(got, want)
+
+
 # ----------------------------------------------------------------------------- layers / step
 def test_decoder_layer_config0(dev):
     """Config 0: one layer, B=4, ctx 1024 (attention + MoE + residuals)."""
