@@ -71,6 +71,20 @@ typedef struct nkm_qwen3_desc {
   int32_t num_blocks;
   int32_t block_size;  /* must be 128 */
   int32_t max_batch;   /* largest batch any step will use (<= 32)                         */
+  /* Tensor + expert parallelism across GPUs (one process per GPU).  n_ranks == 1: the whole
+   * model on this GPU.  n_ranks > 1: this GPU holds its attention heads (n_q_heads and
+   * n_kv_heads above are the local counts) and experts [expert_begin, expert_begin +
+   * n_local_experts) of n_experts (router, norms, embedding and LM head replicated); w13_ft /
+   * w2_ft point at the local experts.  After the O-projection and after the experts, every
+   * rank stores its partial sums into the exchange region of every rank (xchg[q], mapped in
+   * this process; nkm_qwen3_xchg_bytes each) and all ranks sum them in rank order, so every
+   * rank keeps the same residual stream.  Replaces the TP/EP sharding of the NxDI model
+   * (qwen_with_megakernel.py:102-132, replica groups at :360-362). */
+  int32_t n_ranks;
+  int32_t rank;
+  int32_t expert_begin;
+  int32_t n_local_experts;
+  void* xchg[8];
 } nkm_qwen3_desc;
 
 typedef struct nkm_qwen3 nkm_qwen3; /* opaque handle (host memory only) */
@@ -114,6 +128,11 @@ typedef struct nkm_qwen3_step {
 
 /* Bytes of device workspace a handle needs (caller allocates, 256-byte aligned). */
 size_t nkm_qwen3_workspace_bytes(const nkm_qwen3_desc* desc);
+
+/* Bytes of the exchange region every rank allocates for n_ranks > 1 (zeroed, 256-byte aligned,
+ * shared with the other ranks by CUDA IPC).  Replaces the collective buffers of the reference's
+ * all-reduce (transformer_qwen.py:331-333, 370-372 with replica_groups). */
+size_t nkm_qwen3_xchg_bytes(const nkm_qwen3_desc* desc);
 
 /* Validate the description, lay out the workspace, copy the layer pointer table into it
  * and encode the K/V tensor maps.  Replaces compile()/load() of the NxDI model

@@ -38,7 +38,8 @@ class nkm_qwen3_desc(ctypes.Structure):
                 ("final_norm", c_void_p), ("lm_head_ft", c_void_p), ("embed", c_void_p),
                 ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("rope_max_pos", c_int32),
                 ("k_pool", c_void_p), ("v_pool", c_void_p), ("num_blocks", c_int32),
-                ("block_size", c_int32), ("max_batch", c_int32)]
+                ("block_size", c_int32), ("max_batch", c_int32), ("n_ranks", c_int32), ("rank", c_int32),
+                ("expert_begin", c_int32), ("n_local_experts", c_int32), ("xchg", c_void_p * 8)]
 
 
 class nkm_qwen3_step(ctypes.Structure):
@@ -53,6 +54,7 @@ class nkm_qwen3_step(ctypes.Structure):
 # name -> (restype, argtypes); every symbol declared in include/nkimoe.h
 SIGNATURES = {
     "nkm_qwen3_workspace_bytes": (c_size_t, [POINTER(nkm_qwen3_desc)]),
+    "nkm_qwen3_xchg_bytes": (c_size_t, [POINTER(nkm_qwen3_desc)]),
     "nkm_qwen3_create": (c_int, [POINTER(nkm_qwen3_desc), c_void_p, c_size_t, POINTER(c_void_p)]),
     "nkm_qwen3_destroy": (None, [c_void_p]),
     "nkm_qwen3_decode_step": (c_int, [c_void_p, POINTER(nkm_qwen3_step), c_void_p]),

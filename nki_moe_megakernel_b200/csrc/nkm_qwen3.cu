@@ -43,7 +43,7 @@ size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 // Workspace layout (offsets in bytes from the workspace base).
 struct WsLayout {
   size_t ctrl, ctrl_bytes;  // bar, status, strip/attn/row counters (zeroed every step)
-  size_t bar, status, strip_cnt, attn_cnt, row_cnt;
+  size_t bar, status, gbase, strip_cnt, attn_cnt, row_cnt;
   size_t layers, resid, qkv, attn_out, att_part, rlogits, hbuf, ypair, gpart;
   size_t total;
 };
@@ -59,6 +59,7 @@ WsLayout layout_ws(const nkm_qwen3_desc& d, int num_sms) {
   w.ctrl = o;
   w.bar = o;
   w.status = o + 16;  // bar[0] = barrier arrival count, bar[2] = CTAs that left the launch
+  w.gbase = o + 24;   // u64: cross-GPU barrier count before the next launch
   w.strip_cnt = o + 256;
   w.attn_cnt = w.strip_cnt + kMaxStrips * 4;
   w.row_cnt = w.attn_cnt + align_up(Tm * d.n_kv_heads * 4);
@@ -105,6 +106,18 @@ int check_desc(const nkm_qwen3_desc* d) {
   if (d->max_batch <= 0 || d->max_batch > 32) return fail(NKM_ERR_ARG, "max_batch must be in 1..32");
   if (d->max_batch * d->top_k > nkm::kMaxPairs) return fail(NKM_ERR_ARG, "max_batch*top_k too large");
   if (d->block_size != nkm::kKvBlock) return fail(NKM_ERR_ARG, "block_size must be 128");
+  const int nr = d->n_ranks > 0 ? d->n_ranks : 1;
+  if (nr > nkm::kMaxRanks) return fail(NKM_ERR_ARG, "n_ranks must be in 1..%d", nkm::kMaxRanks);
+  if (d->rank < 0 || d->rank >= nr) return fail(NKM_ERR_ARG, "rank %d outside 0..%d", d->rank, nr - 1);
+  const int nle = d->n_local_experts > 0 ? d->n_local_experts : d->n_experts;
+  if (d->expert_begin < 0 || d->expert_begin + nle > d->n_experts)
+    return fail(NKM_ERR_ARG, "local experts [%d, %d) outside 0..%d", d->expert_begin, d->expert_begin + nle, d->n_experts);
+  if (nr == 1 && (d->expert_begin != 0 || nle != d->n_experts))
+    return fail(NKM_ERR_ARG, "a single rank holds every expert");
+  if (nr > 1)
+    for (int q = 0; q < nr; ++q)
+      if (!d->xchg[q] || (reinterpret_cast<uintptr_t>(d->xchg[q]) & 255))
+        return fail(NKM_ERR_ARG, "xchg[%d] must be a 256-byte aligned device pointer", q);
   // every GEMV stage indexes one split-K counter per 16-row strip
   const int64_t na_max = std::min<int64_t>(d->n_experts, static_cast<int64_t>(d->max_batch) * d->top_k);
   const int64_t strips[] = {na_max * (2 * d->moe_inter / 16), na_max * (d->hidden / 16), d->vocab / 16,
@@ -177,6 +190,13 @@ size_t nkm_qwen3_workspace_bytes(const nkm_qwen3_desc* desc) {
   int sms = 0, dev = 0;
   if (current_sms(&sms, &dev) != NKM_OK) return 0;
   return layout_ws(*desc, sms).total;
+}
+
+size_t nkm_qwen3_xchg_bytes(const nkm_qwen3_desc* desc) {
+  if (check_desc(desc) != NKM_OK) return 0;
+  const size_t nr = desc->n_ranks > 0 ? static_cast<size_t>(desc->n_ranks) : 1;
+  return align_up(static_cast<size_t>(nkm::kXchgHeader) +
+                  2 * nr * static_cast<size_t>(desc->max_batch) * static_cast<size_t>(desc->hidden) * 4);
 }
 
 int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspace_bytes, nkm_qwen3** out) {
@@ -294,6 +314,12 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.L = d.n_layers;
   p.V = d.vocab;
   p.eps = d.rms_eps;
+  p.n_ranks = d.n_ranks > 0 ? d.n_ranks : 1;
+  p.rank = d.rank;
+  p.expert_begin = d.expert_begin;
+  p.n_local = d.n_local_experts > 0 ? d.n_local_experts : d.n_experts;
+  for (int q = 0; q < nkm::kMaxRanks; ++q) p.xchg[q] = q < p.n_ranks ? static_cast<uint8_t*>(d.xchg[q]) : nullptr;
+  p.gbase = reinterpret_cast<unsigned long long*>(h->ws + h->lay.gbase);
   p.first_layer = first;
   p.num_layers = nl;
   p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | (lm ? NKM_STAGE_LMHEAD : 0));
@@ -376,7 +402,9 @@ int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream) {
     fail(st, "device status 0x%x%s%s", st, (st & NKM_ERR_TIMEOUT) ? " (wait timeout)" : "",
          (st & NKM_ERR_INDEX) ? " (index out of range)" : "");
     // the status is sticky until read; after a fault the barrier and counters may be mid-way
+    // (with several ranks, every rank calls this before the group continues)
     NKM_CUDA(cudaMemset(h->ws + h->lay.ctrl, 0, h->lay.ctrl_bytes));
+    if (h->desc.n_ranks > 1) NKM_CUDA(cudaMemset(h->desc.xchg[h->desc.rank], 0, nkm::kXchgHeader));
   }
   return st;
 }
@@ -480,6 +508,7 @@ extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t l
   } else if (!s->x_in || !aligned16(s->x_in)) {
     return fail(NKM_ERR_ARG, "x_in must be a 16-byte aligned device pointer");
   }
+  if (d.n_ranks > 1) return fail(NKM_ERR_ARG, "the allocation-free MoE block runs on one GPU (n_ranks == 1)");
   const nkm_qwen3_layer& L = d.layers[layer];
   if (!L.router || !L.w13_ft || !L.w2_ft || !L.ln2) return fail(NKM_ERR_ARG, "layer %d: MoE weights missing", layer);
   const void* ps[] = {L.w13_ft, L.w2_ft, L.router, L.ln2};
@@ -516,6 +545,10 @@ extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t l
   p.L = d.n_layers;
   p.V = d.vocab;
   p.eps = d.rms_eps;
+  p.n_ranks = 1;
+  p.rank = 0;
+  p.expert_begin = 0;
+  p.n_local = d.n_experts;
   p.first_layer = layer;
   p.num_layers = 1;
   p.stages = NKM_STAGE_MOE;

@@ -33,6 +33,8 @@ constexpr int kMaxPairs = 256;             // max batch * top_k
 constexpr int kMaxHidden = 2048;           // register-resident row loads: 8 groups of 256
 constexpr int kHidGroups = kMaxHidden / 256;
 constexpr int kMaxLaunchLayers = 128;       // layer pointer table held in shared memory
+constexpr int kMaxRanks = 8;                // GPUs of one tensor/expert-parallel group
+constexpr int kXchgHeader = 256;            // exchange region: barrier counter, then partials
 constexpr int kAttRows = 16;               // q heads per kv head handled by one mma (<= 16)
 constexpr int kAttQStride = kHeadDim + 8;  // bf16 elements per staged q row
 constexpr int kAttShared = kAttRows * kAttQStride * 2 + 2 * kHeadDim * 2 + kWarps * 2 * kAttRows * 4 + 16;
@@ -57,6 +59,10 @@ struct LayerPtrs {
 struct Params {
   int T, H, nq, nkv, grp, R, E, K, I, L, V;
   float eps;
+  // tensor + expert parallelism: this rank's experts [expert_begin, expert_begin + n_local)
+  int n_ranks, rank, expert_begin, n_local;
+  uint8_t* xchg[kMaxRanks];       // exchange region of every rank (kXchgHeader bytes + partials)
+  unsigned long long* gbase;      // workspace: cross-GPU barrier count before this launch
   int first_layer, num_layers, stages, residual;
   const LayerPtrs* layers;
   const uint16_t* final_norm;
@@ -102,10 +108,10 @@ struct Route {
   int act_e[kMaxExperts];
   int act_off[kMaxExperts];
   int act_cnt[kMaxExperts];
-  int cnt[kMaxExperts];
+  unsigned emask[kMaxExperts];  // tokens that picked each expert (routing scratch)
   int topk_idx[kMaxPairs];
   float topk_w[kMaxPairs];
-  int pmap[kMaxPairs];
+  int eoff[kMaxExperts];  // pair offset of each expert (routing scratch)
   int pair_tok[kMaxPairs];
   float pair_w[kMaxPairs];
 };
@@ -182,6 +188,8 @@ struct Ctx {
   int* flag;
   int stage_idx;
   unsigned bar_k;  // grid barriers passed in this launch
+  unsigned gbar_k;           // cross-GPU barriers passed in this launch
+  unsigned long long gbase;  // cross-GPU barrier count before this launch
   int primed;  // the next GEMV stage's first chunks are already in flight
 };
 
@@ -279,13 +287,96 @@ __device__ __forceinline__ bool grid_barrier(const Params& p, Ctx& c) {
   return grid_wait(p, c);
 }
 
+// ------------------------------------------------------------------ ranks (TP + EP)
+// Partial tile `which` (0: O-projection, 1: experts) stored by rank `src` in rank q's region:
+// [2][n_ranks][T][H] fp32 after the header.
+__device__ __forceinline__ float* xchg_part(const Params& p, int q, int which, int src) {
+  return reinterpret_cast<float*>(p.xchg[q] + kXchgHeader) +
+         static_cast<size_t>(which * p.n_ranks + src) * p.T * p.H;
+}
+
+// Barrier over every CTA of every rank: each CTA adds 1 to the counter of every rank (system
+// scope release: its partial stores into the other ranks' regions become visible first) and
+// waits until its own rank's counter reaches the launch base + (k + 1) * CTAs * ranks.  The
+// counters never reset; every rank adds the same count per launch to its base (launch_exit).
+__device__ __noinline__ bool grid_sync_ranks(const Params& p, Ctx& c) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+#pragma unroll 1
+    for (int q = 0; q < p.n_ranks; ++q) red_release_sys_add_u64(reinterpret_cast<unsigned long long*>(p.xchg[q]), 1ull);
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(p.xchg[p.rank]);
+    const unsigned long long target =
+        c.gbase + (static_cast<unsigned long long>(c.gbar_k) + 1ull) * gridDim.x * static_cast<unsigned>(p.n_ranks);
+    int ok = 1;
+    uint64_t t0 = 0;
+#pragma unroll 1
+    for (unsigned it = 0;; ++it) {
+      const unsigned long long v = ld_acquire_sys_u64(mine);
+      const int st = ld_volatile_i32(p.status);
+      if (st & kStatusFatal) {
+        ok = 0;
+        break;
+      }
+      if (v >= target) break;
+      if (it == 0) {
+        t0 = globaltimer_ns();
+      } else if ((it & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_status(p, kStatusFatal);
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    *c.flag = ok;
+  }
+  ++c.gbar_k;
+  __syncthreads();
+  return *c.flag != 0;
+}
+
+// After grid_sync_ranks: resid[t][row] += bf16(sum over ranks, in rank order, of partial
+// `which`), for the 16-row strips s = blockIdx.x, blockIdx.x + gridDim.x, ...  Every rank
+// computes the same sums, so the residual streams stay identical.
+__device__ __noinline__ void rank_reduce(const Params& p, int which, int layer) {
+  const int S = p.H / 16, n = p.T * 16;
+  float* trace = which == 0 ? p.tr_mid : p.tr_out;
+#pragma unroll 1
+  for (int s = blockIdx.x; s < S; s += gridDim.x) {
+#pragma unroll 1
+    for (int e = threadIdx.x; e < n; e += kThreads) {
+      const int t = e >> 4, row = s * 16 + (e & 15);
+      const size_t off = static_cast<size_t>(t) * p.H + row;
+      float v[kMaxRanks];
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q) v[q] = q < p.n_ranks ? ldcg_f(xchg_part(p, p.rank, which, q) + off) : 0.f;
+      float a = 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q)
+        if (q < p.n_ranks) a += v[q];
+      float* x = p.resid + off;
+      const float nv = (p.residual ? *x : 0.f) + rbf(a);
+      *x = nv;
+      if (trace) trace[static_cast<size_t>(layer - p.first_layer) * p.T * p.H + off] = nv;
+    }
+  }
+}
+
+// Rank-partial exchange: cross-GPU barrier, reduction into the residual, grid barrier.
+__device__ __forceinline__ bool rank_exchange(const Params& p, Ctx& c, int which, int layer) {
+  if (!grid_sync_ranks(p, c)) return false;
+  rank_reduce(p, which, layer);
+  return grid_barrier(p, c);
+}
+
 // End of a launch: the last CTA out zeroes the barrier counter for the next launch on this
 // workspace (launches on one workspace are stream-ordered).
-__device__ __forceinline__ void launch_exit(const Params& p) {
+__device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c) {
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned old = atom_acqrel_add_u32(p.bar + 2, 1u);
     if (old == gridDim.x - 1) {
+      if (p.n_ranks > 1)
+        *p.gbase = c.gbase + static_cast<unsigned long long>(c.gbar_k) * gridDim.x * static_cast<unsigned>(p.n_ranks);
       *reinterpret_cast<volatile unsigned*>(p.bar) = 0u;
       *reinterpret_cast<volatile unsigned*>(p.bar + 2) = 0u;
     }
@@ -463,6 +554,15 @@ __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, con
       uint16_t* tq = p.tr_qkv + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.R;
       tq[r0] = f2bf(v0);
       tq[r0 + 8] = f2bf(v1);
+    }
+  } else if (kind == GK_OPROJ && p.n_ranks > 1) {
+    // tensor parallel: this rank's partial sum over its heads, stored in every rank's region
+    const size_t off = static_cast<size_t>(col) * p.H + strip * 16 + g;
+#pragma unroll 1
+    for (int q = 0; q < p.n_ranks; ++q) {
+      float* d = xchg_part(p, q, 0, p.rank) + off;
+      d[0] = v0;
+      d[8] = v1;
     }
   } else if (kind == GK_OPROJ) {
     const int r0 = strip * 16 + g;
@@ -1007,6 +1107,20 @@ __device__ __noinline__ void down_flush(const Params& p, float* tile, int layer,
       tile4[q] = a;
     }
     if (lane == 0) p.strip_cnt[s] = 0u;
+  }
+  if (p.n_ranks > 1) {
+    // expert parallel: this rank's experts' sum for the strip, stored in every rank's region
+#pragma unroll 1
+    for (int q = lane; q < n4; q += 32) {
+      const int t = q >> 2, row = s * 16 + 4 * (q & 3);
+      const size_t off = static_cast<size_t>(t) * p.H + row;
+      const float4 tv = tile4[q];
+#pragma unroll 1
+      for (int r = 0; r < p.n_ranks; ++r) *reinterpret_cast<float4*>(xchg_part(p, r, 1, p.rank) + off) = tv;
+      tile4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncwarp();
+    return;
   }
 #pragma unroll 1
   for (int q = lane; q < n4; q += 32) {
@@ -1825,28 +1939,31 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
     if (lane < K) rt->topk_w[t * K + lane] = rbf(myval * inv2);
   }
   __syncthreads();
-  // entry i = threadIdx.x (NP <= kMaxPairs == kThreads): its expert and its rank among the
-  // entries of that expert in entry order (token-major), computed by every thread at once
+  // Every (token, slot) entry i = threadIdx.x (NP <= kMaxPairs == kThreads) marks its token in
+  // its expert's mask (a token picks an expert at most once).  Counts are popcounts; an
+  // entry's rank among the entries of its expert (token order) is the popcount of the lower
+  // token bits.
   static_assert(kMaxPairs <= kThreads, "one thread per (token, slot) entry");
+  // (batch <= 32, checked on the host: a token mask fits 32 bits)
+  // Only this rank's experts [expert_begin, expert_begin + n_local) enter the tables (all of
+  // them on one GPU); the tables use local expert indices.
   const int NP = p.T * K;
   const int ie = threadIdx.x;
-  const int e_i = (ie < NP) ? rt->topk_idx[ie] : -1;
-  const bool valid = e_i >= 0 && e_i < E;
-  int rank = 0;
-#pragma unroll 8
-  for (int j = 0; j < ie && j < NP; ++j) rank += (rt->topk_idx[j] == e_i);
-#pragma unroll 1
-  for (int e = threadIdx.x; e < E; e += kThreads) rt->cnt[e] = 0;
+  const int EL = p.n_local;
+  for (int e = threadIdx.x; e < EL; e += kThreads) rt->emask[e] = 0u;
   __syncthreads();
-  if (valid) atomicAdd(&rt->cnt[e_i], 1);
+  const int e_i = (ie < NP) ? rt->topk_idx[ie] - p.expert_begin : -1;
+  const bool valid = e_i >= 0 && e_i < EL;
+  const int t_i = ie / K;
+  if (valid) atomicOr(&rt->emask[e_i], 1u << t_i);
   __syncthreads();
   if (warp == 0) {
     // active experts in ascending id order, with pair offsets
     int nA = 0, off = 0;
 #pragma unroll 1
-    for (int e0 = 0; e0 < E; e0 += 32) {
+    for (int e0 = 0; e0 < EL; e0 += 32) {
       const int e = e0 + lane;
-      const int cnt = (e < E) ? rt->cnt[e] : 0;
+      const int cnt = (e < EL) ? __popc(rt->emask[e]) : 0;
       const unsigned act = __ballot_sync(0xffffffffu, cnt > 0);
       int incl = cnt;
 #pragma unroll
@@ -1859,7 +1976,7 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
         rt->act_e[j] = e;
         rt->act_cnt[j] = cnt;
         rt->act_off[j] = off + incl - cnt;
-        rt->cnt[e] = off + incl - cnt;  // reuse as the expert's pair offset
+        rt->eoff[e] = off + incl - cnt;
       }
       nA += __popc(act);
       off += __shfl_sync(0xffffffffu, incl, 31);
@@ -1868,14 +1985,13 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
   }
   __syncthreads();
   if (valid) {
-    const int pr = rt->cnt[e_i] + rank;
-    rt->pmap[ie] = pr;
-    rt->pair_tok[pr] = ie / K;
+    const int pr = rt->eoff[e_i] + __popc(rt->emask[e_i] & ((1u << t_i) - 1u));
+    rt->pair_tok[pr] = t_i;
     rt->pair_w[pr] = rt->topk_w[ie];
-    if (blockIdx.x == 0 && p.tr_topk_idx) {
-      p.tr_topk_idx[static_cast<size_t>(layer - p.first_layer) * NP + ie] = e_i;
-      p.tr_topk_w[static_cast<size_t>(layer - p.first_layer) * NP + ie] = rt->topk_w[ie];
-    }
+  }
+  if (blockIdx.x == 0 && p.tr_topk_idx && ie < NP) {
+    p.tr_topk_idx[static_cast<size_t>(layer - p.first_layer) * NP + ie] = rt->topk_idx[ie];
+    p.tr_topk_w[static_cast<size_t>(layer - p.first_layer) * NP + ie] = rt->topk_w[ie];
   }
   __syncthreads();
 }
@@ -1917,6 +2033,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.flag = reinterpret_cast<int*>(smem + lay.flag_off);
   c.stage_idx = 0;
   c.bar_k = 0;
+  c.gbar_k = 0;
+  c.gbase = p.n_ranks > 1 ? *p.gbase : 0ull;
   c.plan = reinterpret_cast<AttPlan*>(smem + lay.plan_off);
   c.red = reinterpret_cast<float*>(smem + lay.red_off);
   c.att_pb = -1;
@@ -2010,9 +2128,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // C: O-proj + residual
       if (cta_strip_mode<NT>(gc, GK_OPROJ)) gemv_cta_strips<NT>(p, c, gc, GK_OPROJ);
       else gemv_stage<NT, GK_OPROJ>(p, c, gc);
-      grid_arrive(p);
-      if (!(p.stages & 2)) prime_after(layer);
-      if (!grid_wait(p, c)) return;
+      if (p.n_ranks > 1) {
+        // tensor parallel: sum the ranks' O-projection partials into the residual
+        if (!(p.stages & 2)) prime_after(layer);
+        if (!rank_exchange(p, c, 0, layer)) return;
+      } else {
+        grid_arrive(p);
+        if (!(p.stages & 2)) prime_after(layer);
+        if (!grid_wait(p, c)) return;
+      }
     }
     if (p.stages & 2) {
       // D: RMSNorm(ln2) once per CTA (fp32 rows into the idle rings, bf16 rows into X for the
@@ -2035,9 +2159,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!grid_wait(p, c)) return;
       // F: down + affinity + combine + residual
       down_stage<NT>(p, c, gf);
-      grid_arrive(p);
-      prime_after(layer);
-      if (!grid_wait(p, c)) return;
+      if (p.n_ranks > 1) {
+        // expert parallel: sum the ranks' expert partials into the residual (a rank without
+        // active experts contributes zeros)
+        if (c.rt->nA == 0) {
+          const int n = p.T * p.H;
+#pragma unroll 1
+          for (int r = 0; r < p.n_ranks; ++r)
+            for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads)
+              xchg_part(p, r, 1, p.rank)[i] = 0.f;
+        }
+        prime_after(layer);
+        if (!rank_exchange(p, c, 1, layer)) return;
+      } else {
+        grid_arrive(p);
+        prime_after(layer);
+        if (!grid_wait(p, c)) return;
+      }
     }
   }
   // outputs
@@ -2061,7 +2199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     stamp(p, c);
   }
   }();
-  launch_exit(p);
+  launch_exit(p, c);
 }
 
 }  // namespace nkm

@@ -100,7 +100,10 @@ class Qwen3MoeMegakernel:
     def __init__(self, shape: Qwen3MoeShape, layers: Sequence[GpuLayer], *, max_batch: int, num_blocks: int,
                  final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
                  embed: Optional[torch.Tensor] = None, rope_max_pos: int = 40960, device=None,
-                 kv_pools: bool = True):
+                 kv_pools: bool = True, shard=None, xchg=None):
+        """``shard`` (``sharding.RankShard``) and ``xchg`` (``sharding.XchgRegion``) make this
+        instance one rank of a tensor + expert parallel group: ``shape`` then carries the local
+        head counts, ``layers`` the local heads and experts, and ``num_experts`` stays global."""
         self.shape = shape
         self.device = torch.device(device if device is not None else "cuda")
         self.layers = list(layers)
@@ -126,6 +129,22 @@ class Qwen3MoeMegakernel:
             _ptr(self.final_norm), _ptr(self.lm_head_ft), _ptr(self.embed), _ptr(self.rope_cos),
             _ptr(self.rope_sin), rope_max_pos, _ptr(self.k_pool), _ptr(self.v_pool), num_blocks,
             shape.block_size, max_batch)
+        self.shard = shard
+        if shard is not None and shard.world > 1:
+            if xchg is None:
+                raise ValueError("a rank of a parallel group needs its exchange region")
+            self._desc.n_ranks = shard.world
+            self._desc.rank = shard.rank
+            self._desc.expert_begin = shard.expert_begin
+            self._desc.n_local_experts = shard.n_local_experts
+            for q, ptr in enumerate(xchg.ptrs):
+                self._desc.xchg[q] = ptr
+            need = lib().nkm_qwen3_xchg_bytes(ctypes.byref(self._desc))
+            if need == 0 or need > xchg.nbytes:
+                raise _lib.NkmError(_lib.NKM_ERR_ARG, f"exchange region of {xchg.nbytes} bytes, need {need}")
+        else:
+            self._desc.n_ranks = 1
+            self._desc.n_local_experts = shape.num_experts
         nbytes = lib().nkm_qwen3_workspace_bytes(ctypes.byref(self._desc))
         if nbytes == 0:
             raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_qwen3_workspace_bytes")
@@ -135,13 +154,17 @@ class Qwen3MoeMegakernel:
               "nkm_qwen3_create")
         self._h = h
 
-    def __del__(self):
+    def close(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
-            try:
-                lib().nkm_qwen3_destroy(h)
-            except Exception:
-                pass
+            lib().nkm_qwen3_destroy(h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     # ------------------------------------------------------------------ calls
     def _step_struct(self, batch, *, x=None, input_ids=None, positions=None, block_table=None, y=None,

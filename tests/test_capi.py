@@ -61,6 +61,7 @@ int main(void) {
   printf("nkm_qwen3_desc %zu\n", sizeof(nkm_qwen3_desc));
   printf("nkm_qwen3_step %zu\n", sizeof(nkm_qwen3_step));
   P(nkm_qwen3_desc, layers) P(nkm_qwen3_desc, rope_max_pos) P(nkm_qwen3_desc, max_batch)
+  P(nkm_qwen3_desc, n_ranks) P(nkm_qwen3_desc, n_local_experts) P(nkm_qwen3_desc, xchg)
   P(nkm_qwen3_step, max_blocks_per_seq) P(nkm_qwen3_step, trace_resid_out) P(nkm_qwen3_step, trace_stage_ns) P(nkm_qwen3_layer, router_bias)
   return 0;
 }
@@ -78,6 +79,9 @@ int main(void) {
     assert int(got["nkm_qwen3_desc.layers"]) == L.nkm_qwen3_desc.layers.offset
     assert int(got["nkm_qwen3_desc.rope_max_pos"]) == L.nkm_qwen3_desc.rope_max_pos.offset
     assert int(got["nkm_qwen3_desc.max_batch"]) == L.nkm_qwen3_desc.max_batch.offset
+    assert int(got["nkm_qwen3_desc.n_ranks"]) == L.nkm_qwen3_desc.n_ranks.offset
+    assert int(got["nkm_qwen3_desc.n_local_experts"]) == L.nkm_qwen3_desc.n_local_experts.offset
+    assert int(got["nkm_qwen3_desc.xchg"]) == L.nkm_qwen3_desc.xchg.offset
     assert int(got["nkm_qwen3_step.max_blocks_per_seq"]) == L.nkm_qwen3_step.max_blocks_per_seq.offset
     assert int(got["nkm_qwen3_step.trace_resid_out"]) == L.nkm_qwen3_step.trace_resid_out.offset
     assert int(got["nkm_qwen3_step.trace_stage_ns"]) == L.nkm_qwen3_step.trace_stage_ns.offset
