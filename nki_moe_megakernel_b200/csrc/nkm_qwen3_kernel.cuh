@@ -295,15 +295,19 @@ __device__ __forceinline__ float* xchg_part(const Params& p, int q, int which, i
          static_cast<size_t>(which * p.n_ranks + src) * p.T * p.H;
 }
 
-// Barrier over every CTA of every rank: each CTA adds 1 to the counter of every rank (system
-// scope release: its partial stores into the other ranks' regions become visible first) and
+// Barrier over every CTA of every rank: each CTA adds 1 to the counter of every rank (after a
+// system-scope fence: its partial stores into the other ranks' regions become visible first) and
 // waits until its own rank's counter reaches the launch base + (k + 1) * CTAs * ranks.  The
 // counters never reset; every rank adds the same count per launch to its base (launch_exit).
 __device__ __noinline__ bool grid_sync_ranks(const Params& p, Ctx& c) {
   __syncthreads();
+  // lane q of warp 0 arrives at rank q, after a system-scope fence that orders the CTA's
+  // partial stores (made visible to it by the CTA barrier) before the arrival
+  if (threadIdx.x < p.n_ranks) {
+    fence_acq_rel_sys();
+    red_relaxed_sys_add_u64(reinterpret_cast<unsigned long long*>(p.xchg[threadIdx.x]), 1ull);
+  }
   if (threadIdx.x == 0) {
-#pragma unroll 1
-    for (int q = 0; q < p.n_ranks; ++q) red_release_sys_add_u64(reinterpret_cast<unsigned long long*>(p.xchg[q]), 1ull);
     const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(p.xchg[p.rank]);
     const unsigned long long target =
         c.gbase + (static_cast<unsigned long long>(c.gbar_k) + 1ull) * gridDim.x * static_cast<unsigned>(p.n_ranks);
