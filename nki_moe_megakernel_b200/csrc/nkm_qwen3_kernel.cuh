@@ -118,7 +118,7 @@ struct Route {
 
 // Dense GEMVs with few strips (QKV, O-proj) at batch <= 8 give every CTA whole strips and
 // reduce them in shared memory: at most this many strips per CTA.
-constexpr int kCtaStripsMax = 4;
+constexpr int kCtaStripsMax = 3;
 
 // The attention items of one CTA are the same for every layer of a launch (they depend on the
 // positions only): planned once per launch.  n < 0: more items than the plan holds (the stage
@@ -145,7 +145,7 @@ struct RingGeom {
 
 struct SmemLayout {
   uint32_t ring_bytes;
-  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, red_off, flag_off, total;
+  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, red_off, flag_off, cbar_off, total;
   __host__ __device__ SmemLayout(int H, int NT) {
     ring_bytes = NT == 4 ? 8192u : 16384u;
     ring_off = 0;
@@ -161,7 +161,8 @@ struct SmemLayout {
     plan_off = lt_off + static_cast<uint32_t>(kMaxLaunchLayers * sizeof(LayerPtrs));
     red_off = plan_off + static_cast<uint32_t>((sizeof(AttPlan) + 15) & ~size_t(15));
     flag_off = red_off + (NT == 1 ? static_cast<uint32_t>(kCtaStripsMax * kWarps * 32 * 4 * 4) : 0u);
-    total = flag_off + 16 + 1024;  // + alignment slack for the ring base
+    cbar_off = flag_off + 16;
+    total = cbar_off + 16 + 1024;  // + alignment slack for the ring base
   }
 };
 
@@ -190,7 +191,10 @@ struct Ctx {
   unsigned bar_k;  // grid barriers passed in this launch
   unsigned gbar_k;           // cross-GPU barriers passed in this launch
   unsigned long long gbase;  // cross-GPU barrier count before this launch
-  int primed;  // the next GEMV stage's first chunks are already in flight
+  int primed;  // ring slots of the next GEMV stage already in flight
+  uint64_t* cbar;   // CTA mbarrier of the staged norms' prefetch (thread 0 issues, all wait)
+  uint32_t cphase;  // its phase (tracked by every thread)
+  int npref;        // the next staged norm's prefetch is in flight
 };
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
@@ -216,24 +220,26 @@ __device__ __forceinline__ void stamp(const Params& p, Ctx& c) {
 
 // Bounded wait on a slot's mbarrier.  On timeout the fatal status bit is set and the caller
 // continues (the next grid barrier then aborts every CTA).
-__device__ __forceinline__ void slot_wait(const Params& p, Ctx& c, int slot) {
-  const uint32_t par = (c.phase >> slot) & 1u;
-  if (!mbar_try_wait(&c.bars[slot], par)) {
-    // try_wait itself suspends for a while; read the (slow) global timer only every 64 tries
-    uint64_t t0 = 0;
-    for (uint32_t it = 1;; ++it) {
-      if (mbar_try_wait(&c.bars[slot], par)) break;
-      if ((it & 63u) == 0) {
-        const uint64_t now = globaltimer_ns();
-        if (t0 == 0) {
-          t0 = now;
-        } else if (now - t0 > kWaitLimitNs) {
-          if (lane_id() == 0) set_status(p, kStatusFatal);
-          break;
-        }
+// Bounded wait for phase `par` of an mbarrier; on timeout the status records a fatal error.
+__device__ __noinline__ void mbar_wait_slow(const Params& p, uint64_t* bar, uint32_t par) {
+  // try_wait itself suspends for a while; read the (slow) global timer only every 64 tries
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, par)) break;
+    if ((it & 63u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        if (lane_id() == 0) set_status(p, kStatusFatal);
+        break;
       }
     }
   }
+}
+__device__ __forceinline__ void slot_wait(const Params& p, Ctx& c, int slot) {
+  const uint32_t par = (c.phase >> slot) & 1u;
+  if (!mbar_try_wait(&c.bars[slot], par)) mbar_wait_slow(p, &c.bars[slot], par);
   c.phase ^= (1u << slot);
 }
 
@@ -375,7 +381,14 @@ __device__ __forceinline__ bool rank_exchange(const Params& p, Ctx& c, int which
 // End of a launch: the last CTA out zeroes the barrier counter for the next launch on this
 // workspace (launches on one workspace are stream-ordered).
 __device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c) {
+  if (ld_volatile_i32(p.status) & kStatusFatal) {
+    // a failed wait ends the launch early: give bulk copies this CTA still has in flight
+    // (at most a few ring slots and the broadcast buffer) time to land before it exits
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 50000ull) __nanosleep(1000);
+  }
   __syncthreads();
+
   if (threadIdx.x == 0) {
     const unsigned old = atom_acqrel_add_u32(p.bar + 2, 1u);
     if (old == gridDim.x - 1) {
@@ -698,7 +711,7 @@ __device__ __forceinline__ bool cta_strip_mode(const GemvGeom& G, int kind) {
 }
 
 template <int NT>
-__device__ __noinline__ void cta_strips_prime(const Params& p, Ctx& c, const GemvGeom& G) {
+__device__ __noinline__ void cta_strips_prime(const Params& p, Ctx& c, const GemvGeom& G, int nprime) {
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
   const int lane = lane_id(), warp = threadIdx.x >> 5;
@@ -708,7 +721,7 @@ __device__ __noinline__ void cta_strips_prime(const Params& p, Ctx& c, const Gem
   int pj = 0, pk = 0;
 #pragma unroll
   for (int i = 0; i < NS; ++i) {
-    if (pj >= ns) break;
+    if (pj >= ns || i >= nprime) break;
     const int n = min(CU, nk - pk);
     if (lane == 0) {
       const int strip = static_cast<int>(blockIdx.x) + pj * Gd;
@@ -731,7 +744,7 @@ __device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const G
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
   Ctx c = cref;
-  const bool primed = c.primed != 0;
+  const int primed = c.primed;  // ring slots already filled
   cref.primed = 0;
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3, warp = threadIdx.x >> 5;
   const int Gd = gridDim.x, KT = G.kt;
@@ -766,7 +779,7 @@ __device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const G
   };
 #pragma unroll
   for (int i = 0; i < NS; ++i)
-    if (pj < ns) issue(i, primed);
+    if (pj < ns) issue(i, i < primed);
   int cs = 0;
 #pragma unroll 1
   for (int j = 0; j < ns; ++j) {
@@ -827,19 +840,21 @@ __device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const G
   }
 }
 
+// nprime: ring slots to fill (1 when a staged norm uses slot 1 first)
 template <int NT, int KIND>
-__device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom& G) {
+__device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom& G,
+                                        int nprime = RingGeom<NT>::kGemvSlots) {
   constexpr int kind = KIND;
   if (cta_strip_mode<NT>(G, kind)) {
-    c.primed = 1;
-    cta_strips_prime<NT>(p, c, G);
+    c.primed = nprime;
+    cta_strips_prime<NT>(p, c, G, nprime);
     return;
   }
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
   const int lane = lane_id();
   const int KT = G.kt, SPS = G.sps, upseg = SPS * KT, NU = upseg * G.nseg;
-  c.primed = 1;
+  c.primed = nprime;
   if (NU <= 0) return;
   const int NWe = max(1, min(c.nworkers, NU / 2));
   if (c.worker >= NWe) return;
@@ -847,7 +862,7 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
   int pu = u0, pseg = u0 / upseg, pstrip = (u0 - pseg * upseg) / KT, pkt = u0 - pseg * upseg - pstrip * KT;
 #pragma unroll
   for (int i = 0; i < NS; ++i) {
-    if (pu >= u1) break;
+    if (pu >= u1 || i >= nprime) break;
     const int n = min(CU, min(KT - pkt, u1 - pu));
     if (lane == 0) {
       const uint8_t* src = seg_base(G, c.rt, kind, pseg) + static_cast<uint64_t>(pstrip * KT + pkt) * kUnitBytes;
@@ -873,7 +888,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
   Ctx c = cref;  // register-resident copy for the streaming loop
-  const bool primed = c.primed != 0;
+  const int primed = c.primed;  // ring slots already filled
   cref.primed = 0;
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int KT = G.kt, SPS = G.sps;
@@ -910,7 +925,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
   };
 #pragma unroll
   for (int i = 0; i < NS; ++i)
-    if (pu < u1) issue(i, primed);
+    if (pu < u1) issue(i, i < primed);
   // consumer cursor and per-segment B-fragment rows
   int cu = u0, cseg = u0 / upseg, cstrip = (u0 - cseg * upseg) / KT, ckt = u0 - cseg * upseg - cstrip * KT;
   const uint4* brow_s[NT];    // this lane's B row in shared memory (smem sources)
@@ -1036,7 +1051,7 @@ __device__ __noinline__ void down_prime(const Params& p, Ctx& c, const GemvGeom&
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots;
   const int lane = lane_id();
   const int NI = G.sps * G.nseg, KT = G.kt;
-  c.primed = 1;
+  c.primed = NS;
   if (NI <= 0) return;
   const int NWe = max(1, min(c.nworkers, NI));
   if (c.worker >= NWe) return;
@@ -1146,7 +1161,7 @@ __device__ __noinline__ void down_stage(const Params& p, Ctx& cref, const GemvGe
   using RG = RingGeom<NT>;
   constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
   Ctx c = cref;
-  const bool primed = c.primed != 0;
+  const int primed = c.primed;  // ring slots already filled
   cref.primed = 0;
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3, warp = threadIdx.x >> 5;
   const int nA = G.nseg, KT = G.kt, NI = G.sps * nA;
@@ -1177,7 +1192,7 @@ __device__ __noinline__ void down_stage(const Params& p, Ctx& cref, const GemvGe
   };
 #pragma unroll
   for (int k = 0; k < NS; ++k)
-    if (pi < i1) issue(k, primed);
+    if (pi < i1) issue(k, k < primed);
   float acc[NA][NT][4];
 #pragma unroll
   for (int a = 0; a < NA; ++a)
@@ -1875,6 +1890,128 @@ __device__ __noinline__ void router_stage(const Params& p, Ctx& c, int layer, co
   }
 }
 
+// ------------------------------------------------------------------ staged norms (batch <= 8)
+// RMSNorm of stage A and fused RMSNorm + router logits of stage D for batches of at most kWarps
+// tokens whose residual row fits one GEMV ring slot.  Warp t copies token t's residual row into
+// slot 1 of its ring with one bulk copy (when every SM reads the same rows right after a grid
+// barrier, one bulk copy per row lands several times sooner than per-thread loads of it),
+// normalises it into X and, in stage D, replaces the staged row by its fp32 normalised values
+// and scores them against the router rows of this CTA's experts (e = blockIdx.x, blockIdx.x + G,
+// ...), so the stage needs no CTA barrier.  The norm's gamma (and in stage D the router row of
+// expert blockIdx.x) are copied into the strip-reduction area while the grid barrier before the
+// stage completes (norm_prefetch).  Both stages run the same code: it executes cold in the
+// instruction cache once per layer, so the loops stay rolled.  Products and summation orders are
+// those of norm_rows_to_smem and router_stage: X and the logits are bit-identical to theirs.
+template <int NT>
+__device__ __forceinline__ bool norm_staged_ok(const Params& p) {
+  return NT == 1 && p.T <= kWarps && p.H * 4 <= RingGeom<NT>::kChunk * kUnitBytes;
+}
+// Call with every thread, after a CTA barrier that ends the strip-reduction area's previous use.
+// d: stage D (gamma ln2 and the router row), else stage A (gamma ln1).
+__device__ __noinline__ void norm_prefetch(const Params& p, Ctx& c, int layer, bool d) {
+  if (threadIdx.x == 0) {
+    const LayerPtrs& lw = c.lt[layer - p.first_layer];
+    const uint32_t hb = static_cast<uint32_t>(p.H) * 2u;
+    const bool has_e = d && static_cast<int>(blockIdx.x) < p.E;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(c.cbar, has_e ? 2u * hb : hb);
+    bulk_g2s_plain(c.red, d ? lw.ln2 : lw.ln1, hb, c.cbar);
+    if (has_e)
+      bulk_g2s_plain(reinterpret_cast<uint8_t*>(c.red) + hb, lw.router + static_cast<size_t>(blockIdx.x) * p.H, hb,
+                     c.cbar);
+  }
+  c.npref = 1;
+}
+
+__device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, bool d) {
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  const int H = p.H, ng = H / 256, E = p.E;
+  const LayerPtrs& lw = c.lt[layer - p.first_layer];
+  float* stage = reinterpret_cast<float*>(c.ring + RingGeom<1>::kChunk * kUnitBytes);
+  const bool mine = warp < p.T;
+  if (mine && lane == 0) {
+    fence_proxy_async_smem();    // earlier generic accesses of the staging slot
+    fence_proxy_async_global();  // the residual was written by other CTAs during this launch
+    mbar_arrive_expect_tx(&c.bars[1], static_cast<uint32_t>(H) * 4u);
+    bulk_g2s_plain(stage, p.resid + static_cast<size_t>(warp) * H, static_cast<uint32_t>(H) * 4u, &c.bars[1]);
+  }
+  if (!c.npref) {  // not prefetched during the barrier (a stage launched on its own)
+    __syncthreads();
+    norm_prefetch(p, c, layer, d);
+  }
+  c.npref = 0;
+  {
+    const uint32_t par = c.cphase & 1u;
+    if (!mbar_try_wait(c.cbar, par)) mbar_wait_slow(p, c.cbar, par);
+    c.cphase ^= 1u;
+  }
+  if (!mine) return;
+  slot_wait(p, c, 1);
+  // RMSNorm ((x*r)*g in stage A, (x*g)*r in stage D) into X; in stage D the fp32 normalised row
+  // also replaces the staged one
+  float* row = stage + 8 * lane;
+  float ss = 0.f;
+#pragma unroll 2
+  for (int i = 0; i < ng; ++i) {
+    const float4 a = *reinterpret_cast<const float4*>(row + 256 * i);
+    const float4 b = *reinterpret_cast<const float4*>(row + 256 * i + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+  }
+  const float r = rstd_fixed(warp_sum_fixed(ss), H, p.eps);
+  if (lane == 0) c.rstd[warp] = r;
+  const uint16_t* gs = reinterpret_cast<const uint16_t*>(c.red) + 8 * lane;
+  uint16_t* xr = c.xs + static_cast<size_t>(warp) * c.xs_stride + 8 * lane;
+#pragma unroll 2
+  for (int i = 0; i < ng; ++i) {
+    const float4 a = *reinterpret_cast<const float4*>(row + 256 * i);
+    const float4 b = *reinterpret_cast<const float4*>(row + 256 * i + 4);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gs + 256 * i);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float g = (j & 1) ? hi_bf(gw[j >> 1]) : lo_bf(gw[j >> 1]);
+      y[j] = __fmul_rn(__fmul_rn(v[j], d ? g : r), d ? r : g);
+    }
+    *reinterpret_cast<uint4*>(xr + 256 * i) =
+        make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]), pack_bf2(y[4], y[5]), pack_bf2(y[6], y[7]));
+    if (d) {
+      *reinterpret_cast<float4*>(row + 256 * i) = make_float4(y[0], y[1], y[2], y[3]);
+      *reinterpret_cast<float4*>(row + 256 * i + 4) = make_float4(y[4], y[5], y[6], y[7]);
+    }
+  }
+  if (!d) return;
+  // router logits (token warp, expert e); the row of expert blockIdx.x is in shared memory
+  const int nitems = p.T * E;
+#pragma unroll 1
+  for (int e = blockIdx.x; e < E; e += gridDim.x) {
+    const bool sm = e == static_cast<int>(blockIdx.x);
+    const uint16_t* wr = (sm ? reinterpret_cast<const uint16_t*>(c.red) + H : lw.router + static_cast<size_t>(e) * H) +
+                         8 * lane;
+    float acc = 0.f;
+#pragma unroll 2
+    for (int i = 0; i < ng; ++i) {
+      const uint4 w4 = sm ? *reinterpret_cast<const uint4*>(wr + 256 * i) : ldnc128(wr + 256 * i);
+      const float4 a = *reinterpret_cast<const float4*>(row + 256 * i);
+      const float4 b = *reinterpret_cast<const float4*>(row + 256 * i + 4);
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn((j & 1) ? hi_bf(ww[j >> 1]) : lo_bf(ww[j >> 1]), v[j]));
+    }
+    acc = warp_sum_fixed(acc);
+    if (lw.router_bias) acc = __fadd_rn(acc, __ldg(lw.router_bias + e));
+    if (lane == 0) {
+      const int it = warp * E + e;
+      p.rlogits[it] = acc;
+      if (p.tr_rlogits) p.tr_rlogits[static_cast<size_t>(layer - p.first_layer) * nitems + it] = acc;
+    }
+  }
+}
+
 // Softmax / top-k / renorm per token (one warp per token) and the expert tables, in every CTA
 // (moe_fused_nki.py:224-272, 404-418).
 // Order-preserving key of a float (larger float -> larger key; -0 and +0 map to one key) and
@@ -2043,6 +2180,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.red = reinterpret_cast<float*>(smem + lay.red_off);
   c.att_pb = -1;
   c.primed = 0;
+  c.cbar = reinterpret_cast<uint64_t*>(smem + lay.cbar_off);
+  c.cphase = 0;
+  c.npref = 0;
   {
     // the layer pointer table, once per launch: every stage reads its pointers from shared memory
     static_assert(sizeof(LayerPtrs) % 16 == 0, "LayerPtrs is copied as uint4");
@@ -2057,6 +2197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   stamp(p, c);
   if (lane == 0) {
     for (int s = 0; s < kMaxBars; ++s) mbar_init(&c.bars[s], 1);
+    if (threadIdx.x == 0) mbar_init(c.cbar, 1);
     fence_mbar_init();
   }
   if (threadIdx.x == 0 && (p.stages & 1)) {
@@ -2088,15 +2229,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<float4*>(dst + 4) = make_float4(lo_bf(v.z), hi_bf(v.z), lo_bf(v.w), hi_bf(v.w));
     }
   }
+  const bool staged = norm_staged_ok<NT>(p);
   grid_arrive(p);
   if ((p.stages & 1) && p.num_layers > 0) {  // the first QKV weights stream during the barrier
     const LayerPtrs& l0 = c.lt[0];
     GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
-    gemv_prime<NT, GK_QKV>(p, c, ga);
+    gemv_prime<NT, GK_QKV>(p, c, ga, staged ? 1 : RingGeom<NT>::kGemvSlots);
+    if (staged) norm_prefetch(p, c, p.first_layer, false);
   }
   if (!grid_wait(p, c)) return;
 
   const int layer_end = p.first_layer + p.num_layers;
+
   const bool want_lm = (p.stages & 4) && p.logits_out;
   // prime whatever GEMV follows the last stage of `layer` (next layer's QKV, or the LM head)
   auto prime_after = [&](int layer) {
@@ -2104,7 +2248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.stages & 1) {
         const LayerPtrs& nl = c.lt[layer + 1 - p.first_layer];
         GemvGeom ga{nl.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer + 1};
-        gemv_prime<NT, GK_QKV>(p, c, ga);
+        gemv_prime<NT, GK_QKV>(p, c, ga, staged ? 1 : RingGeom<NT>::kGemvSlots);
+        if (staged) norm_prefetch(p, c, layer + 1, false);
       }
     } else if (want_lm) {
       GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer};
@@ -2115,7 +2260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const LayerPtrs& lw = c.lt[layer - p.first_layer];
     if (p.stages & 1) {
       // A: RMSNorm(ln1) + QKV
-      norm_rows_to_smem(p, c, lw.ln1, false);
+      if (staged) norm_staged(p, c, layer, false);
+      else norm_rows_to_smem(p, c, lw.ln1, false);
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
       if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
@@ -2132,26 +2278,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       // C: O-proj + residual
       if (cta_strip_mode<NT>(gc, GK_OPROJ)) gemv_cta_strips<NT>(p, c, gc, GK_OPROJ);
       else gemv_stage<NT, GK_OPROJ>(p, c, gc);
+      // stage D's gamma and router row stream during the barrier
+      const bool pre_d = (p.stages & 2) && staged;
       if (p.n_ranks > 1) {
         // tensor parallel: sum the ranks' O-projection partials into the residual
+        __syncthreads();  // the rings and the strip-reduction area are free
         if (!(p.stages & 2)) prime_after(layer);
+        if (pre_d) norm_prefetch(p, c, layer, true);
         if (!rank_exchange(p, c, 0, layer)) return;
       } else {
         grid_arrive(p);
         if (!(p.stages & 2)) prime_after(layer);
+        if (pre_d) norm_prefetch(p, c, layer, true);
         if (!grid_wait(p, c)) return;
       }
     }
     if (p.stages & 2) {
       // D: RMSNorm(ln2) once per CTA (fp32 rows into the idle rings, bf16 rows into X for the
       // experts), then the router logits (fp32, fixed order)
-      float* x32 = (static_cast<uint32_t>(p.T * p.H * 4) <= static_cast<uint32_t>(kWarps * c.ring_bytes))
-                       ? reinterpret_cast<float*>(c.ring_all)
-                       : nullptr;
-      norm_rows_to_smem(p, c, lw.ln2, true, x32);
-      __syncthreads();
-      if (x32) router_stage<true>(p, c, layer, x32);
-      else router_stage<false>(p, c, layer, nullptr);
+      if (staged) {
+        norm_staged(p, c, layer, true);
+      } else {
+        float* x32 = (static_cast<uint32_t>(p.T * p.H * 4) <= static_cast<uint32_t>(kWarps * c.ring_bytes))
+                         ? reinterpret_cast<float*>(c.ring_all)
+                         : nullptr;
+        norm_rows_to_smem(p, c, lw.ln2, true, x32);
+        __syncthreads();
+        if (x32) router_stage<true>(p, c, layer, x32);
+        else router_stage<false>(p, c, layer, nullptr);
+      }
       if (!grid_barrier(p, c)) return;
       // E: routing tables + gate/up (X from stage D); the down weights start streaming early
       routing_prologue(p, c, layer);
