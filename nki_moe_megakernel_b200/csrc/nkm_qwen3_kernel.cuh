@@ -1907,23 +1907,23 @@ __device__ __forceinline__ bool norm_staged_ok(const Params& p) {
   return NT == 1 && p.T <= kWarps && p.H * 4 <= RingGeom<NT>::kChunk * kUnitBytes;
 }
 // Call with every thread, after a CTA barrier that ends the strip-reduction area's previous use.
-// d: stage D (gamma ln2 and the router row), else stage A (gamma ln1).
-__device__ __noinline__ void norm_prefetch(const Params& p, Ctx& c, int layer, bool d) {
+// router: the layer's router weights in stage D (the row of expert blockIdx.x is copied too).
+__device__ __noinline__ void norm_prefetch(const Params& p, Ctx& c, const uint16_t* gamma, const uint16_t* router) {
   if (threadIdx.x == 0) {
-    const LayerPtrs& lw = c.lt[layer - p.first_layer];
     const uint32_t hb = static_cast<uint32_t>(p.H) * 2u;
-    const bool has_e = d && static_cast<int>(blockIdx.x) < p.E;
+    const bool has_e = router && static_cast<int>(blockIdx.x) < p.E;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(c.cbar, has_e ? 2u * hb : hb);
-    bulk_g2s_plain(c.red, d ? lw.ln2 : lw.ln1, hb, c.cbar);
+    bulk_g2s_plain(c.red, gamma, hb, c.cbar);
     if (has_e)
-      bulk_g2s_plain(reinterpret_cast<uint8_t*>(c.red) + hb, lw.router + static_cast<size_t>(blockIdx.x) * p.H, hb,
+      bulk_g2s_plain(reinterpret_cast<uint8_t*>(c.red) + hb, router + static_cast<size_t>(blockIdx.x) * p.H, hb,
                      c.cbar);
   }
   c.npref = 1;
 }
 
-__device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, bool d) {
+// gamma: the norm's weights (ln1, ln2 or the final norm); d: stage D (router logits of `layer`).
+__device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, bool d, const uint16_t* gamma) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
   const int H = p.H, ng = H / 256, E = p.E;
   const LayerPtrs& lw = c.lt[layer - p.first_layer];
@@ -1937,7 +1937,7 @@ __device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, boo
   }
   if (!c.npref) {  // not prefetched during the barrier (a stage launched on its own)
     __syncthreads();
-    norm_prefetch(p, c, layer, d);
+    norm_prefetch(p, c, gamma, d ? lw.router : nullptr);
   }
   c.npref = 0;
   {
@@ -2030,48 +2030,66 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
   const int E = p.E, K = p.K;
 #pragma unroll 1
   for (int t = warp; t < p.T; t += kWarps) {
-    float v[8];
-    int ids[8];
+    // lane l holds experts e = 32 q + l (q < 8); keys order the logits, ties by lower index
     const int per = (E + 31) / 32;
-    float mx = -INFINITY;
+    float v[8];
+    uint32_t key[8];
+    int qq[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int e = q * 32 + lane;
-      ids[q] = e;
-      v[q] = (q < per && e < E) ? ldcg_f(p.rlogits + static_cast<size_t>(t) * E + e) : -INFINITY;
-      mx = fmaxf(mx, v[q]);
+      const bool ok = q < per && e < E;
+      v[q] = ok ? ldcg_f(p.rlogits + static_cast<size_t>(t) * E + e) : -INFINITY;
+      key[q] = ok ? order_key(v[q]) : 0u;
+      qq[q] = q;
     }
-    mx = warp_max(mx);
-    float se = 0.f;
+    // sort the lane's candidates by key, descending: odd-even transposition sort swapping only
+    // strictly smaller neighbours, so equal keys keep their (ascending index) order
 #pragma unroll
-    for (int q = 0; q < 8; ++q) se += (q < per && ids[q] < E) ? __expf(v[q] - mx) : 0.f;
-    se = warp_sum_fixed(se);
-    const float inv = 1.f / se;
-    // top-K by (value desc, index asc): order-preserving uint32 keys (-0 folded into +0),
-    // one warp max-reduction per pick; the lowest index wins among equal keys
-    uint32_t key[8];
+    for (int r = 0; r < 8; ++r) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) key[q] = (q < per && ids[q] < E) ? order_key(v[q]) : 0u;
-    // lane k keeps pick k's softmax value (K <= 8 < 32)
-    float myval = 0.f;
+      for (int a = r & 1; a + 1 < 8; a += 2) {
+        const bool sw = key[a + 1] > key[a];
+        const uint32_t k0 = key[a], k1 = key[a + 1];
+        const int q0 = qq[a], q1 = qq[a + 1];
+        key[a] = sw ? k1 : k0;
+        key[a + 1] = sw ? k0 : k1;
+        qq[a] = sw ? q1 : q0;
+        qq[a + 1] = sw ? q0 : q1;
+      }
+    }
+    // top-K picks: the largest head key over the warp, the lowest index among equal ones; its
+    // lane pops its head.  Lane k keeps pick k.
+    uint32_t wmax0 = 0u, mykey = 0u;
+    int mybi = 0;
 #pragma unroll 1
     for (int k = 0; k < K; ++k) {
-      uint32_t lb = 0u;
+      const uint32_t wmax = __reduce_max_sync(0xffffffffu, key[0]);
+      const int bi = static_cast<int>(__reduce_min_sync(
+          0xffffffffu, key[0] == wmax ? static_cast<uint32_t>(qq[0] * 32 + lane) : 0xffffffffu));
+      const bool own = lane == (bi & 31);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) lb = max(lb, key[q]);
-      const uint32_t wmax = __reduce_max_sync(0xffffffffu, lb);
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int q = 7; q >= 0; --q) {
-        const unsigned m = __ballot_sync(0xffffffffu, key[q] == wmax);
-        if (m) bi = q * 32 + __ffs(m) - 1;
+      for (int a = 0; a < 7; ++a) {
+        key[a] = own ? key[a + 1] : key[a];
+        qq[a] = own ? qq[a + 1] : qq[a];
       }
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (ids[q] == bi) key[q] = 0u;
-      if (lane == k) myval = rbf(__expf(key_value(wmax) - mx) * inv);
-      if (lane == 0) rt->topk_idx[t * K + k] = bi;
+      key[7] = own ? 0u : key[7];
+      if (k == 0) wmax0 = wmax;
+      if (lane == k) {
+        mykey = wmax;
+        mybi = bi;
+      }
     }
+    // softmax over all E logits (lane-sequential over q, then the xor butterfly); its maximum is
+    // the first pick
+    const float mx = key_value(wmax0);
+    float se = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) se += (q < per && q * 32 + lane < E) ? __expf(v[q] - mx) : 0.f;
+    se = warp_sum_fixed(se);
+    const float inv = 1.f / se;
+    const float myval = lane < K ? rbf(__expf(key_value(mykey) - mx) * inv) : 0.f;
+    if (lane < K) rt->topk_idx[t * K + lane] = mybi;
     // renormalise in pick order (sum over lanes 0..K-1 sequentially)
     float sk = 0.f;
 #pragma unroll 1
@@ -2099,30 +2117,42 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
   if (valid) atomicOr(&rt->emask[e_i], 1u << t_i);
   __syncthreads();
   if (warp == 0) {
-    // active experts in ascending id order, with pair offsets
-    int nA = 0, off = 0;
+    // active experts in ascending id order, with pair offsets: lane l takes the contiguous
+    // experts [l * pe, (l + 1) * pe); one warp scan of (pairs, active experts) per lane
+    const int pe = (EL + 31) / 32;
+    const int e0 = lane * pe;
+    int cs = 0, ns = 0;
 #pragma unroll 1
-    for (int e0 = 0; e0 < EL; e0 += 32) {
-      const int e = e0 + lane;
-      const int cnt = (e < EL) ? __popc(rt->emask[e]) : 0;
-      const unsigned act = __ballot_sync(0xffffffffu, cnt > 0);
-      int incl = cnt;
+    for (int a = 0; a < pe; ++a) {
+      const int cnt = (e0 + a < EL) ? __popc(rt->emask[e0 + a]) : 0;
+      cs += cnt;
+      ns += cnt > 0;
+    }
+    int ci = cs, ni = ns;
 #pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += y;
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, ci, d);
+      const int z = __shfl_up_sync(0xffffffffu, ni, d);
+      if (lane >= d) {
+        ci += y;
+        ni += z;
       }
+    }
+    int off = ci - cs, j = ni - ns;
+#pragma unroll 1
+    for (int a = 0; a < pe; ++a) {
+      const int e = e0 + a;
+      const int cnt = (e < EL) ? __popc(rt->emask[e]) : 0;
       if (cnt > 0) {
-        const int j = nA + __popc(act & ((1u << lane) - 1u));
         rt->act_e[j] = e;
         rt->act_cnt[j] = cnt;
-        rt->act_off[j] = off + incl - cnt;
-        rt->eoff[e] = off + incl - cnt;
+        rt->act_off[j] = off;
+        rt->eoff[e] = off;
+        ++j;
       }
-      nA += __popc(act);
-      off += __shfl_sync(0xffffffffu, incl, 31);
+      off += cnt;
     }
-    if (lane == 0) rt->nA = nA;
+    if (lane == 31) rt->nA = ni;
   }
   __syncthreads();
   if (valid) {
@@ -2235,7 +2265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const LayerPtrs& l0 = c.lt[0];
     GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
     gemv_prime<NT, GK_QKV>(p, c, ga, staged ? 1 : RingGeom<NT>::kGemvSlots);
-    if (staged) norm_prefetch(p, c, p.first_layer, false);
+    if (staged) norm_prefetch(p, c, l0.ln1, nullptr);
   }
   if (!grid_wait(p, c)) return;
 
@@ -2249,18 +2279,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const LayerPtrs& nl = c.lt[layer + 1 - p.first_layer];
         GemvGeom ga{nl.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer + 1};
         gemv_prime<NT, GK_QKV>(p, c, ga, staged ? 1 : RingGeom<NT>::kGemvSlots);
-        if (staged) norm_prefetch(p, c, layer + 1, false);
+        if (staged) norm_prefetch(p, c, nl.ln1, nullptr);
       }
     } else if (want_lm) {
       GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer};
-      gemv_prime<NT, GK_LMHEAD>(p, c, gl);
+      gemv_prime<NT, GK_LMHEAD>(p, c, gl, staged ? 1 : RingGeom<NT>::kGemvSlots);
+      if (staged) norm_prefetch(p, c, p.final_norm, nullptr);
     }
   };
   for (int layer = p.first_layer; layer < layer_end; ++layer) {
     const LayerPtrs& lw = c.lt[layer - p.first_layer];
     if (p.stages & 1) {
       // A: RMSNorm(ln1) + QKV
-      if (staged) norm_staged(p, c, layer, false);
+      if (staged) norm_staged(p, c, layer, false, lw.ln1);
       else norm_rows_to_smem(p, c, lw.ln1, false);
       __syncthreads();
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
@@ -2284,12 +2315,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tensor parallel: sum the ranks' O-projection partials into the residual
         __syncthreads();  // the rings and the strip-reduction area are free
         if (!(p.stages & 2)) prime_after(layer);
-        if (pre_d) norm_prefetch(p, c, layer, true);
+        if (pre_d) norm_prefetch(p, c, lw.ln2, lw.router);
         if (!rank_exchange(p, c, 0, layer)) return;
       } else {
         grid_arrive(p);
         if (!(p.stages & 2)) prime_after(layer);
-        if (pre_d) norm_prefetch(p, c, layer, true);
+        if (pre_d) norm_prefetch(p, c, lw.ln2, lw.router);
         if (!grid_wait(p, c)) return;
       }
     }
@@ -2297,7 +2328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // D: RMSNorm(ln2) once per CTA (fp32 rows into the idle rings, bf16 rows into X for the
       // experts), then the router logits (fp32, fixed order)
       if (staged) {
-        norm_staged(p, c, layer, true);
+        norm_staged(p, c, layer, true, lw.ln2);
       } else {
         float* x32 = (static_cast<uint32_t>(p.T * p.H * 4) <= static_cast<uint32_t>(kWarps * c.ring_bytes))
                          ? reinterpret_cast<float*>(c.ring_all)
@@ -2348,7 +2379,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (want_lm) {
-    norm_rows_to_smem(p, c, p.final_norm, false);
+    if (staged) norm_staged(p, c, max(layer_end - 1, p.first_layer), false, p.final_norm);
+    else norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
     GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer_end - 1};
     gemv_stage<NT, GK_LMHEAD>(p, c, gl);
