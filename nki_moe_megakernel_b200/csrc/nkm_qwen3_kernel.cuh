@@ -42,6 +42,9 @@ constexpr int kPartFloats = 2 * kAttRows + kAttRows * kHeadDim;  // m, l, o of o
 constexpr int kStatusFatal = 4;            // NKM_ERR_TIMEOUT
 constexpr int kStatusIndex = 8;            // NKM_ERR_INDEX
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
+// Router-logit slot not written yet (a NaN bit pattern the arithmetic never produces: results
+// that are NaN are stored as the canonical NaN instead).
+constexpr uint32_t kLogitEmpty = 0xffffffffu;
 
 struct LayerPtrs {
   const uint8_t* wqkv;
@@ -2006,9 +2009,23 @@ __device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, boo
     if (lw.router_bias) acc = __fadd_rn(acc, __ldg(lw.router_bias + e));
     if (lane == 0) {
       const int it = warp * E + e;
+      if (__float_as_uint(acc) == kLogitEmpty) acc = __uint_as_float(0x7fffffffu);
       p.rlogits[it] = acc;
       if (p.tr_rlogits) p.tr_rlogits[static_cast<size_t>(layer - p.first_layer) * nitems + it] = acc;
     }
+  }
+}
+
+// Mark this CTA's router-logit slots (tokens x experts blockIdx.x, blockIdx.x + G, ...) as not
+// written.  Called at launch start and after the grid barrier that ends stage E, so that the next
+// stage D's writes are the only values a reader can see after that barrier.
+__device__ __forceinline__ void logits_rearm(const Params& p) {
+#pragma unroll 1
+  for (int i = threadIdx.x;; i += kThreads) {
+    const int ej = i / p.T, t = i - ej * p.T;
+    const int e = static_cast<int>(blockIdx.x) + ej * static_cast<int>(gridDim.x);
+    if (e >= p.E) break;
+    p.rlogits[t * p.E + e] = __uint_as_float(kLogitEmpty);
   }
 }
 
@@ -2024,7 +2041,9 @@ __device__ __forceinline__ float key_value(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-__device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer) {
+// wait_logits: stage D published the logits without a grid barrier; every slot is read until it
+// no longer holds kLogitEmpty (bounded wait; a fatal status from another CTA ends it).
+__device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer, bool wait_logits) {
   const int warp = threadIdx.x >> 5, lane = lane_id();
   Route* rt = c.rt;
   const int E = p.E, K = p.K;
@@ -2040,7 +2059,32 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
       const int e = q * 32 + lane;
       const bool ok = q < per && e < E;
       v[q] = ok ? ldcg_f(p.rlogits + static_cast<size_t>(t) * E + e) : -INFINITY;
-      key[q] = ok ? order_key(v[q]) : 0u;
+    }
+    if (wait_logits) {
+      uint64_t t0 = 0;
+#pragma unroll 1
+      for (uint32_t it = 0;; ++it) {
+        bool pend = false;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) pend |= __float_as_uint(v[q]) == kLogitEmpty;
+        if (!__any_sync(0xffffffffu, pend)) break;
+        if ((it & 15u) == 0) {
+          const uint64_t now = globaltimer_ns();
+          if (it == 0) t0 = now;
+          if ((ld_volatile_i32(p.status) & kStatusFatal) || now - t0 > kWaitLimitNs) {
+            if (lane == 0) set_status(p, kStatusFatal);
+            break;
+          }
+        }
+        __nanosleep(200);  // back off: the polls share L2 with the last producers
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (__float_as_uint(v[q]) == kLogitEmpty) v[q] = ldcg_f(p.rlogits + static_cast<size_t>(t) * E + q * 32 + lane);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      key[q] = (q < per && q * 32 + lane < E) ? order_key(v[q]) : 0u;
       qq[q] = q;
     }
     // sort the lane's candidates by key, descending: odd-even transposition sort swapping only
@@ -2237,7 +2281,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   [&]() {  // the launch body; a fatal error returns from here to launch_exit
-  // stage 0: residual (fp32) <- embeddings / hidden input (bf16)
+  // stage 0: residual (fp32) <- embeddings / hidden input (bf16); the router-logit slots of the
+  // staged path start unwritten
+  if (norm_staged_ok<NT>(p) && (p.stages & 2)) logits_rearm(p);
   {
     const int nvec = p.T * p.H / 8;
     for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads) {
@@ -2338,9 +2384,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (x32) router_stage<true>(p, c, layer, x32);
         else router_stage<false>(p, c, layer, nullptr);
       }
-      if (!grid_barrier(p, c)) return;
-      // E: routing tables + gate/up (X from stage D); the down weights start streaming early
-      routing_prologue(p, c, layer);
+      // E: routing tables + gate/up (X from stage D); the down weights start streaming early.  On
+      // the staged path the logits are the only data stage E takes from other CTAs: routing waits
+      // for them slot by slot instead of a grid barrier.
+      if (staged) stamp(p, c);  // (stage-time probes: stage D ends here)
+      else if (!grid_barrier(p, c)) return;
+      routing_prologue(p, c, layer, staged);
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
       gemv_stage<NT, GK_GATEUP>(p, c, ge);
       GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
@@ -2349,6 +2398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!grid_wait(p, c)) return;
       // F: down + affinity + combine + residual
       down_stage<NT>(p, c, gf);
+      if (staged) logits_rearm(p);  // every CTA read this layer's logits before the last barrier
       if (p.n_ranks > 1) {
         // expert parallel: sum the ranks' expert partials into the residual (a rank without
         // active experts contributes zeros)
