@@ -148,7 +148,7 @@ struct RingGeom {
 
 struct SmemLayout {
   uint32_t ring_bytes;
-  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, red_off, flag_off, cbar_off, total;
+  uint32_t ring_off, xs_off, bars_off, rstd_off, route_off, lt_off, plan_off, red_off, flag_off, cbar_off, dyn_off, total;
   __host__ __device__ SmemLayout(int H, int NT) {
     ring_bytes = NT == 4 ? 8192u : 16384u;
     ring_off = 0;
@@ -165,7 +165,8 @@ struct SmemLayout {
     red_off = plan_off + static_cast<uint32_t>((sizeof(AttPlan) + 15) & ~size_t(15));
     flag_off = red_off + (NT == 1 ? static_cast<uint32_t>(kCtaStripsMax * kWarps * 32 * 4 * 4) : 0u);
     cbar_off = flag_off + 16;
-    total = cbar_off + 16 + 1024;  // + alignment slack for the ring base
+    dyn_off = cbar_off + 16;
+    total = dyn_off + 64 + 1024;  // + alignment slack for the ring base
   }
 };
 
@@ -197,6 +198,7 @@ struct Ctx {
   int primed;  // ring slots of the next GEMV stage already in flight
   uint64_t* cbar;   // CTA mbarrier of the staged norms' prefetch (thread 0 issues, all wait)
   uint32_t cphase;  // its phase (tracked by every thread)
+  int* dyn;         // chunk scheduling words of the expert gate/up stage (shared memory)
   int npref;        // the next staged norm's prefetch is in flight
 };
 
@@ -883,6 +885,150 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
       }
     }
   }
+}
+
+// Expert gate/up projection for batches of at most 8 (NT = 1) with the work of each CTA shared
+// by its warps.  CTA b owns the contiguous range of whole 16-row strips [NS b / G, NS (b+1) / G)
+// of the nA x (2I / 16) strips; a strip's K is split into KB chunks of kChunk units (one ring
+// slot).  Warps claim the CTA's chunks in order from a shared-memory counter, so a warp that
+// streams faster takes more of them.  Each chunk's partial tile goes to the strip's slot in the
+// strip-reduction area; the warp that completes a strip's KB chunks sums the partials in chunk
+// order (fixed order: the result does not depend on which warp took which chunk) and writes
+// SiLU(gate) * up.  Strips never straddle CTAs, so no partial leaves the SM.  All warps of the CTA
+// call it (one CTA barrier at the start).
+constexpr int kDynSlots = 3;  // strips in reduction at once (strip s uses slot (s - s0) % kDynSlots)
+template <int NT>
+__device__ __forceinline__ bool gateup_dyn_ok(const GemvGeom& G) {
+  return NT == 1 && G.kt % RingGeom<NT>::kChunk == 0 &&
+         (G.kt / RingGeom<NT>::kChunk) * 32 * 16 * kDynSlots <= kCtaStripsMax * kWarps * 32 * 16;
+}
+template <int NT>
+__device__ __noinline__ void gateup_dyn(const Params& p, Ctx& cref, const GemvGeom& G) {
+  using RG = RingGeom<NT>;
+  constexpr int CU = RG::kChunk, NS = RG::kGemvSlots, NA = RG::kAccSets;
+  Ctx c = cref;
+  cref.primed = 0;
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
+  const Route* rt = c.rt;
+  const int SPS = G.sps, KT = G.kt, KB = KT / CU, Gd = gridDim.x;
+  const int NSt = G.nseg * SPS;
+  const int s0 = static_cast<int>(static_cast<long long>(NSt) * blockIdx.x / Gd);
+  const int s1 = static_cast<int>(static_cast<long long>(NSt) * (blockIdx.x + 1) / Gd);
+  const int c1 = s1 * KB;
+  volatile int* next = c.dyn;       // next chunk to claim
+  volatile int* gen = c.dyn + 1;    // [kDynSlots] strip each slot currently collects
+  int* cnt = c.dyn + 1 + kDynSlots; // [kDynSlots] chunks deposited
+  float4* part = reinterpret_cast<float4*>(c.red);  // [kDynSlots][KB][32]
+  if (threadIdx.x == 0) {
+    *next = s0 * KB;
+    for (int j = 0; j < kDynSlots; ++j) {
+      gen[j] = s0 + j;
+      cnt[j] = 0;
+    }
+  }
+  __syncthreads();
+  auto claim = [&]() {
+    int id = 0;
+    if (lane == 0) id = atomicAdd(const_cast<int*>(next), 1);
+    return __shfl_sync(0xffffffffu, id, 0);
+  };
+  auto issue = [&](int slot, int id) {
+    if (lane == 0) {
+      const int strip = id / KB, kb = id - strip * KB;
+      const int seg = strip / SPS, ss = strip - seg * SPS;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(CU * kUnitBytes));
+      bulk_g2s(c.ring + slot * (CU * kUnitBytes),
+               G.base + static_cast<uint64_t>(rt->act_e[seg]) * G.seg_bytes +
+                   static_cast<uint64_t>(ss * KT + kb * CU) * kUnitBytes,
+               static_cast<uint32_t>(CU * kUnitBytes), &c.bars[slot], c.pol);
+    }
+  };
+  int ids[NS];
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    ids[i] = claim();
+    if (ids[i] < c1) issue(i, ids[i]);
+  }
+  int cs = 0;
+#pragma unroll 1
+  while (ids[cs] < c1) {
+    const int id = ids[cs];
+    const int strip = id / KB, kb = id - strip * KB;
+    const int seg = strip / SPS, ss = strip - seg * SPS;
+    const int ncols = rt->act_cnt[seg];
+    const uint4* brow = g < ncols ? reinterpret_cast<const uint4*>(c.xs + static_cast<size_t>(rt->pair_tok[rt->act_off[seg] + g]) *
+                                                                            c.xs_stride + 8 * t4)
+                                  : nullptr;
+    uint4 bf[CU];
+#pragma unroll
+    for (int i = 0; i < CU; ++i) bf[i] = brow ? brow[(kb * CU + i) * 4] : make_uint4(0u, 0u, 0u, 0u);
+    slot_wait(p, c, cs);
+    float acc[NA][4];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
+    const uint4* sa = reinterpret_cast<const uint4*>(c.ring + cs * (CU * kUnitBytes)) + lane;
+#pragma unroll
+    for (int i = 0; i < CU; ++i) {
+      const uint4 a0 = sa[i * (kUnitBytes / 16)];
+      const uint4 a1 = sa[i * (kUnitBytes / 16) + 32];
+      mma_bf16(acc[i % NA], a0.x, a1.x, a0.y, a1.y, bf[i].x, bf[i].y);
+      mma_bf16(acc[i % NA], a0.z, a1.z, a0.w, a1.w, bf[i].z, bf[i].w);
+    }
+    __syncwarp();
+    ids[cs] = claim();  // the slot's next chunk streams while this one is reduced
+    if (ids[cs] < c1) issue(cs, ids[cs]);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      v.x += acc[a][0];
+      v.y += acc[a][1];
+      v.z += acc[a][2];
+      v.w += acc[a][3];
+    }
+    // deposit the partial into the strip's slot (once the slot's previous strip is reduced)
+    const int sl = (strip - s0) % kDynSlots;
+    if (gen[sl] != strip) {
+      const uint64_t t0 = globaltimer_ns();
+      while (gen[sl] != strip) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (lane == 0) set_status(p, kStatusFatal);
+          break;
+        }
+      }
+    }
+    part[(sl * KB + kb) * 32 + lane] = v;
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      old = atomicAdd(&cnt[sl], 1);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == KB - 1) {
+      // the strip's last chunk: sum the KB partials in chunk order, release the slot, epilogue
+      __threadfence_block();
+      Acc<NT> sum;
+      sum.v[0][0] = sum.v[0][1] = sum.v[0][2] = sum.v[0][3] = 0.f;
+#pragma unroll 1
+      for (int k = 0; k < KB; ++k) {
+        const float4 u = part[(sl * KB + k) * 32 + lane];
+        sum.v[0][0] += u.x;
+        sum.v[0][1] += u.y;
+        sum.v[0][2] += u.z;
+        sum.v[0][3] += u.w;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        cnt[sl] = 0;
+        __threadfence_block();
+        gen[sl] = strip + kDynSlots;
+      }
+      gemv_epilogue<NT, GK_GATEUP>(p, rt, G, seg, ss, sum);
+    }
+    cs = (cs + 1 == NS) ? 0 : cs + 1;
+  }
+  cref.phase = c.phase;
 }
 
 template <int NT, int KIND>
@@ -2255,6 +2401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.att_pb = -1;
   c.primed = 0;
   c.cbar = reinterpret_cast<uint64_t*>(smem + lay.cbar_off);
+  c.dyn = reinterpret_cast<int*>(smem + lay.dyn_off);
   c.cphase = 0;
   c.npref = 0;
   {
@@ -2391,7 +2538,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       else if (!grid_barrier(p, c)) return;
       routing_prologue(p, c, layer, staged);
       GemvGeom ge{lw.w13, static_cast<uint64_t>(2) * p.I * p.H * 2, c.rt->nA, (2 * p.I) / 16, p.H / 32, p.H, layer};
-      gemv_stage<NT, GK_GATEUP>(p, c, ge);
+      if (gateup_dyn_ok<NT>(ge)) gateup_dyn<NT>(p, c, ge);
+      else gemv_stage<NT, GK_GATEUP>(p, c, ge);
       GemvGeom gf{lw.w2, static_cast<uint64_t>(p.H) * p.I * 2, c.rt->nA, p.H / 16, p.I / 32, p.I, layer};
       grid_arrive(p);
       down_prime<NT>(p, c, gf);
