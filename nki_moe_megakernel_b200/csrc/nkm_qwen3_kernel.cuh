@@ -45,6 +45,9 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any wait
 // Router-logit slot not written yet (a NaN bit pattern the arithmetic never produces: results
 // that are NaN are stored as the canonical NaN instead).
 constexpr uint32_t kLogitEmpty = 0xffffffffu;
+// QKV output element not written yet (bf16 NaN pattern never produced by rounding; a computed
+// NaN is stored as the canonical 0x7fff).
+constexpr uint16_t kBf16Empty = 0xffffu;
 
 struct LayerPtrs {
   const uint8_t* wqkv;
@@ -199,6 +202,7 @@ struct Ctx {
   uint64_t* cbar;   // CTA mbarrier of the staged norms' prefetch (thread 0 issues, all wait)
   uint32_t cphase;  // its phase (tracked by every thread)
   int* dyn;         // chunk scheduling words of the expert gate/up stage (shared memory)
+  int awaitq;       // attention waits for its q/k/v element by element (no grid barrier before it)
   int npref;        // the next staged norm's prefetch is in flight
 };
 
@@ -570,8 +574,9 @@ __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, con
   if (kind == GK_QKV) {
     const int r0 = strip * 16 + g;
     uint16_t* q = p.qkv + static_cast<size_t>(col) * p.R;
-    q[r0] = f2bf(v0);
-    q[r0 + 8] = f2bf(v1);
+    const uint16_t h0 = f2bf(v0), h1 = f2bf(v1);
+    q[r0] = h0 == kBf16Empty ? 0x7fffu : h0;
+    q[r0 + 8] = h1 == kBf16Empty ? 0x7fffu : h1;
     if (p.tr_qkv) {
       uint16_t* tq = p.tr_qkv + (static_cast<size_t>(G.layer - p.first_layer) * p.T + col) * p.R;
       tq[r0] = f2bf(v0);
@@ -1492,6 +1497,11 @@ constexpr int kNoBlocks = -2;  // "block ids not preloaded"
 
 // Block ids of the K/V blocks a context chunk [tok_beg, tok_end) touches: lane j holds the
 // id of block tok_beg/128 + j (j < 32; -1 past the chunk).  One coalesced load per warp.
+__device__ __forceinline__ bool bf16x4_empty(uint2 v) {
+  return (v.x & 0xffffu) == kBf16Empty || (v.x >> 16) == kBf16Empty || (v.y & 0xffffu) == kBf16Empty ||
+         (v.y >> 16) == kBf16Empty;
+}
+
 __device__ __forceinline__ int att_chunk_blocks(const Params& p, int b, int tok_beg, int tok_end) {
   const int j = tok_beg / kKvBlock + lane_id();
   const int jend = tok_end > tok_beg ? (tok_end - 1) / kKvBlock : -1;
@@ -1700,6 +1710,30 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   if (do_k) kin = head_load(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim, lw.kn, cosr, sinr);
   if (do_v) vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
   if (do_k || do_v) wblk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
+  if (c.awaitq) {
+    // no grid barrier before this stage: re-read the elements still unwritten (bounded wait)
+    uint64_t t0 = 0;
+#pragma unroll 1
+    for (uint32_t it = 0;; ++it) {
+      const bool q0 = warp < p.grp && bf16x4_empty(qin[0].raw);
+      const bool q1 = warp + kWarps < p.grp && bf16x4_empty(qin[1].raw);
+      const bool kk = do_k && bf16x4_empty(kin.raw), vq = do_v && bf16x4_empty(vv);
+      if (!__any_sync(0xffffffffu, q0 || q1 || kk || vq)) break;
+      if ((it & 15u) == 0) {
+        const uint64_t now = globaltimer_ns();
+        if (it == 0) t0 = now;
+        if ((ld_volatile_i32(p.status) & kStatusFatal) || now - t0 > kWaitLimitNs) {
+          if (lane == 0) set_status(p, kStatusFatal);
+          break;
+        }
+      }
+      __nanosleep(100);
+      if (q0) qin[0].raw = ldcg64(qkv_b + static_cast<size_t>(h * p.grp + warp) * kHeadDim + 4 * lane);
+      if (q1) qin[1].raw = ldcg64(qkv_b + static_cast<size_t>(h * p.grp + warp + kWarps) * kHeadDim + 4 * lane);
+      if (kk) kin.raw = ldcg64(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim + 4 * lane);
+      if (vq) vv = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int r = warp + i * kWarps;
@@ -2162,6 +2196,13 @@ __device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, boo
   }
 }
 
+// Fill a bf16 buffer of n elements (n % 8 == 0) with kBf16Empty, spread over the grid.
+__device__ __forceinline__ void bf16_rearm(uint16_t* buf, int n) {
+  const uint4 e = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+  for (int i = blockIdx.x * kThreads + threadIdx.x; i < n / 8; i += gridDim.x * kThreads)
+    reinterpret_cast<uint4*>(buf)[i] = e;
+}
+
 // Mark this CTA's router-logit slots (tokens x experts blockIdx.x, blockIdx.x + G, ...) as not
 // written.  Called at launch start and after the grid barrier that ends stage E, so that the next
 // stage D's writes are the only values a reader can see after that barrier.
@@ -2402,6 +2443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.primed = 0;
   c.cbar = reinterpret_cast<uint64_t*>(smem + lay.cbar_off);
   c.dyn = reinterpret_cast<int*>(smem + lay.dyn_off);
+  c.awaitq = 0;
   c.cphase = 0;
   c.npref = 0;
   {
@@ -2431,6 +2473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // stage 0: residual (fp32) <- embeddings / hidden input (bf16); the router-logit slots of the
   // staged path start unwritten
   if (norm_staged_ok<NT>(p) && (p.stages & 2)) logits_rearm(p);
+  if (norm_staged_ok<NT>(p) && (p.stages & 1)) bf16_rearm(p.qkv, p.T * p.R);
   {
     const int nvec = p.T * p.H / 8;
     for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads) {
@@ -2490,9 +2533,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
       if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
       else gemv_stage<NT, GK_QKV>(p, c, ga);
-      grid_arrive(p);
-      att_prime_layer(p, c, layer, &kmap, &vmap);  // this layer's first K/V boxes stream during the barrier
-      if (!grid_wait(p, c)) return;
+      if (staged) {
+        // stage B takes only q/k/v from other CTAs and waits for them element by element
+        c.awaitq = 1;
+        att_prime_layer(p, c, layer, &kmap, &vmap);
+        stamp(p, c);  // (stage-time probes: stage A ends here)
+      } else {
+        grid_arrive(p);
+        att_prime_layer(p, c, layer, &kmap, &vmap);  // this layer's first K/V boxes stream during the barrier
+        if (!grid_wait(p, c)) return;
+      }
       // B: attention (+ KV write); the O-proj weights start streaming before the barrier
       attention_stage(p, c, layer, &kmap, &vmap);
       GemvGeom gc{lw.wo, 0, 1, p.H / 16, (p.nq * kHeadDim) / 32, p.nq * kHeadDim, layer};
@@ -2502,6 +2552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // C: O-proj + residual
       if (cta_strip_mode<NT>(gc, GK_OPROJ)) gemv_cta_strips<NT>(p, c, gc, GK_OPROJ);
       else gemv_stage<NT, GK_OPROJ>(p, c, gc);
+      if (staged) bf16_rearm(p.qkv, p.T * p.R);  // every CTA read this layer's q/k/v before barrier B
       // stage D's gamma and router row stream during the barrier
       const bool pre_d = (p.stages & 2) && staged;
       if (p.n_ranks > 1) {
