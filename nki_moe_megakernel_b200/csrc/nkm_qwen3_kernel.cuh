@@ -2552,7 +2552,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // C: O-proj + residual
       if (cta_strip_mode<NT>(gc, GK_OPROJ)) gemv_cta_strips<NT>(p, c, gc, GK_OPROJ);
       else gemv_stage<NT, GK_OPROJ>(p, c, gc);
-      if (staged) bf16_rearm(p.qkv, p.T * p.R);  // every CTA read this layer's q/k/v before barrier B
+      // every CTA read this layer's q/k/v before barrier B; with stage D the re-arm waits for it
+      // (it then overlaps the router-logit wait instead of delaying this stage's barrier)
+      if (staged && !(p.stages & 2)) bf16_rearm(p.qkv, p.T * p.R);
       // stage D's gamma and router row stream during the barrier
       const bool pre_d = (p.stages & 2) && staged;
       if (p.n_ranks > 1) {
@@ -2573,6 +2575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // experts), then the router logits (fp32, fixed order)
       if (staged) {
         norm_staged(p, c, layer, true, lw.ln2);
+        if (p.stages & 1) bf16_rearm(p.qkv, p.T * p.R);
       } else {
         float* x32 = (static_cast<uint32_t>(p.T * p.H * 4) <= static_cast<uint32_t>(kWarps * c.ring_bytes))
                          ? reinterpret_cast<float*>(c.ring_all)
