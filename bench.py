@@ -118,36 +118,65 @@ def algorithmic_bytes(shape, args, distinct_per_layer):
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """``nvidia-smi`` clock/throttle samples of this process's GPU during the timed region.
+
+    The GPU is named by its UUID (the local rank's index need not be nvidia-smi's index when
+    CUDA_VISIBLE_DEVICES is set), and ``__enter__`` returns only once the first sample has
+    arrived (several ranks starting nvidia-smi at once can take a second), so a short timed
+    region still has samples."""
+
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        self.gpu = str(gpu_index)
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+            if uuid:
+                self.gpu = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            pass
         self.proc = None
+        self.lines = []
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.QUERY}",
                                           "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._reader, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 10 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
-        time.sleep(0.15)
+        self.skip = len(self.lines)  # samples taken before the timed region
         return self
 
     def __exit__(self, *a):
-        self.out = ""
         if self.proc is not None:
+            time.sleep(0.06)  # one more sample period
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            self.thread.join(timeout=5)
 
     def summary(self):
         rows = []
-        for line in (self.out or "").splitlines():
+        lines = self.lines[self.skip:] or self.lines
+        for line in lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) >= 9:
                 rows.append(f)
@@ -162,58 +191,70 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_layer_sample(args, repeats: int):
-    """Time the oracle (faithful mode) for one decoder layer at the bench shape plus the LM head.
+def config_of(args, world):
+    """The ``config`` object of both arms (same keys, so the driver can match the lines)."""
+    return {"workload": "qwen3-30b-a3b decode step (48 layers + final norm + LM head)",
+            "global_batch": args.batch, "ctx": args.ctx, "kv_block": 128, "layers": args.layers,
+            "parallelism": "single GPU" if world == 1 else
+            f"tp{world} over KV-head groups + ep{world} over experts, in-kernel exchange over NVLink",
+            "l2": "no flush: ~27 GB of weights streamed per step >> 126 MB L2"}
 
-    Returns (seconds per layer list, seconds for the LM head, threads)."""
+
+def cpu_steps(args, warmup: int, steps: int):
+    """Time the oracle (the faithful CPU restatement of the reference's decode path) over whole
+    decode steps of the bench shape: all ``args.layers`` layers, each with its own paged K/V
+    cache, the final norm and the LM head.  The layers share one layer's weight tensors (48
+    distinct bf16 layers, ~61 GB, do not fit host memory; one layer's 1.2 GB of experts exceeds
+    the last-level cache, so the sharing gives no cache advantage).
+
+    Returns (seconds of every timed step, threads)."""
     import torch
 
     from oracle import qwen3_moe_oracle as O
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = O.QwenConfig()
+    cfg = O.QwenConfig(n_layers=args.layers)
     gen = torch.Generator().manual_seed(args.seed)
     lw = O.random_layer(cfg, gen)
     B, ctx = args.batch, args.ctx
     nb = ctx // 128 + 1
     NB = B * nb
-    kc = torch.randn(NB, cfg.n_kv_heads, 128, cfg.head_dim, generator=gen).to(torch.bfloat16)
-    vc = torch.randn(NB, cfg.n_kv_heads, 128, cfg.head_dim, generator=gen).to(torch.bfloat16)
+    kcs = [torch.randn(NB, cfg.n_kv_heads, 128, cfg.head_dim, generator=gen).to(torch.bfloat16)
+           for _ in range(args.layers)]
+    vcs = [torch.randn(NB, cfg.n_kv_heads, 128, cfg.head_dim, generator=gen).to(torch.bfloat16)
+           for _ in range(args.layers)]
     table = torch.arange(NB, dtype=torch.int32).view(B, nb)
     pos = torch.full((B,), ctx, dtype=torch.int32)
     cos, sin = O.rope_tables(ctx + 1, cfg.head_dim, cfg.rope_theta)
+    lm = (torch.randn(cfg.vocab, cfg.hidden, generator=gen) * 0.02).to(torch.bfloat16)
+    fn = (1.0 + torch.randn(cfg.hidden, generator=gen) * 0.02).to(torch.bfloat16)
     x = torch.randn(B, cfg.hidden, generator=gen).to(torch.bfloat16)
     times = []
-    for _ in range(repeats):
+    for i in range(warmup + steps):
         t0 = time.perf_counter()
-        O.decoder_layer(x, lw, cfg, kc, vc, pos, table, cos, sin, "faithful")
-        times.append(time.perf_counter() - t0)
-    lm = (torch.randn(cfg.vocab, cfg.hidden, generator=gen) * 0.02).to(torch.bfloat16)
-    fn = torch.ones(cfg.hidden, dtype=torch.bfloat16)
-    t0 = time.perf_counter()
-    xn = O.rbf(O.rmsnorm_hidden_faithful(x, fn, cfg.rms_eps, gamma_first=False))
-    _ = xn @ lm.float().t()
-    t_head = time.perf_counter() - t0
-    return times, t_head, threads
+        O.decode_step(x, [lw], cfg, kcs, vcs, pos, table, cos, sin, fn, lm, "faithful")
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return times, threads
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    times, t_head, threads = cpu_layer_sample(args, args.warmup + args.steps)
-    timed = times[args.warmup:] if len(times) > args.warmup else times
-    step_s = [t * args.layers + t_head for t in timed]
-    value = args.batch / statistics.median(step_s)
-    sample = (f"oracle (faithful PyTorch CPU restatement) of 1 of {args.layers} decoder layers per step at B="
-              f"{args.batch} ctx {args.ctx}, extrapolated x{args.layers}, plus the LM head timed once")
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(step_s) * 1e3,
-            "p50_ms": statistics.median(step_s) * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
-            "config": {"workload": "qwen3-30b-a3b decode step (48 layers + LM head)", "batch": args.batch,
-                       "ctx": args.ctx, "kv_block": 128},
+    times, threads = cpu_steps(args, args.warmup, args.steps)
+    p50 = statistics.median(times)
+    value = args.batch / p50
+    sample = (f"oracle (faithful PyTorch CPU restatement of the reference's decode path): {args.steps} whole "
+              f"{args.layers}-layer decode steps at B={args.batch} ctx {args.ctx} (layers share one layer's weights, "
+              f"distinct KV caches) + final norm + LM head, after {args.warmup} warm-up steps; p50")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(times) * 1e3,
+            "p50_ms": p50 * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, KV prefix ~N(0,1))",
+            "config": config_of(args, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -253,6 +294,107 @@ def _nvtx(torch, name):
         pass
 
 
+def multi_gpu_parity(rank, world, local, device):
+    """Parity of the tensor + expert parallel step, run before the timing at N > 1.
+
+    A small seeded case of the bench model (2 layers, B=4, positions crossing K/V pages, vocab
+    4096, every rank building the same full weights from one seed and keeping its shard) runs
+    through the sharded engine; rank 0 also runs the single-GPU kernel on the full weights (the
+    path the GPU tests pin against the fp32 oracle) and compares hidden states and logits.  Every
+    rank hashes its outputs; the hashes are all-gathered to check that the ranks agree bit for
+    bit.  Returns the ``parity`` object of the bench line (rank 0) or None."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+
+    from nki_moe_megakernel_b200.engine import GpuLayer, Qwen3MoeMegakernel, Qwen3MoeShape
+    from nki_moe_megakernel_b200.sharding import XchgRegion, plan_shard, shard_attention, shard_experts, xchg_bytes
+
+    L, B, V = 2, 4, 4096
+    positions = [600, 33, 1025, 128]
+    full = Qwen3MoeShape(num_hidden_layers=L, vocab_size=V)
+    H, D, E, I = full.hidden_size, full.head_dim, full.num_experts, full.moe_intermediate_size
+    nq, nkv = full.num_attention_heads, full.num_key_value_heads
+    g = torch.Generator(device=device).manual_seed(1234)
+
+    def n(*sz):
+        return (torch.randn(*sz, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    def one(*sz):
+        return (1.0 + torch.randn(*sz, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    raw = [dict(wq=n(nq * D, H), wk=n(nkv * D, H), wv=n(nkv * D, H), wo=n(H, nq * D), qn=one(D), kn=one(D),
+                ln1=one(H), ln2=one(H), router=n(E, H), gu=n(E, 2 * I, H), dn=n(E, H, I)) for _ in range(L)]
+    fnorm, lm = one(H), n(V, H)
+    embed = torch.randn(V, H, generator=g, device=device).to(torch.bfloat16)
+    need = [p // 128 + 1 for p in positions]
+    NB = sum(need) + 2
+    k0 = torch.randn(L, NB, nkv, 128, D, generator=g, device=device).to(torch.bfloat16)
+    v0 = torch.randn(L, NB, nkv, 128, D, generator=g, device=device).to(torch.bfloat16)
+    perm = torch.randperm(NB, generator=torch.Generator().manual_seed(7)).tolist()
+    table = torch.full((B, max(need)), -1, dtype=torch.int32)
+    nxt = 0
+    for b in range(B):
+        for j in range(need[b]):
+            table[b, j] = perm[nxt]
+            nxt += 1
+    tab_d = table.to(device)
+    pos_d = torch.tensor(positions, dtype=torch.int32, device=device)
+    ids_d = torch.randint(0, V, (B,), generator=torch.Generator().manual_seed(8), dtype=torch.int32).to(device)
+
+    shard = plan_shard(rank, world, nq, nkv, E)
+    layers = []
+    for r in raw:
+        wq, wk, wv, wo = shard_attention(r["wq"], r["wk"], r["wv"], r["wo"], shard, D)
+        gu, dn = shard_experts(r["gu"], r["dn"], shard)
+        layers.append(GpuLayer(wq, wk, wv, wo, r["qn"], r["kn"], r["ln1"], r["ln2"], r["router"], gu, dn))
+    lshape = Qwen3MoeShape(num_hidden_layers=L, vocab_size=V, num_attention_heads=len(shard.q_heads),
+                           num_key_value_heads=len(shard.kv_heads))
+    xchg = XchgRegion(xchg_bytes(H, B, world), rank, world, local)
+    eng = Qwen3MoeMegakernel(lshape, layers, max_batch=B, num_blocks=NB, final_norm=fnorm, lm_head=lm, embed=embed,
+                             device=device, shard=shard, xchg=xchg)
+    eng.k_pool.copy_(k0[:, :, shard.kv_heads])
+    eng.v_pool.copy_(v0[:, :, shard.kv_heads])
+    dist.barrier()
+    res = eng.decode_step(pos_d, tab_d, input_ids=ids_d)
+    st = eng.status()
+    hid, lg = res["hidden"].cpu(), res["logits"].cpu()
+    digest = hashlib.sha256(hid.view(torch.int16).numpy().tobytes() + lg.numpy().tobytes()).hexdigest()
+    got = [None] * world
+    dist.all_gather_object(got, (digest, st))
+    out = None
+    if rank == 0:
+        ref = Qwen3MoeMegakernel(full, [GpuLayer(r["wq"], r["wk"], r["wv"], r["wo"], r["qn"], r["kn"], r["ln1"],
+                                                 r["ln2"], r["router"], r["gu"], r["dn"]) for r in raw],
+                                 max_batch=B, num_blocks=NB, final_norm=fnorm, lm_head=lm, embed=embed, device=device)
+        ref.k_pool.copy_(k0)
+        ref.v_pool.copy_(v0)
+        rr = ref.decode_step(pos_d, tab_d, input_ids=ids_d)
+        ref_st = ref.status()
+
+        def cmp(a, b):
+            a, b = a.float().flatten(), b.float().flatten()
+            return (a - b).abs().max().item(), torch.nn.functional.cosine_similarity(a, b, dim=0).item()
+
+        mh, ch = cmp(hid, rr["hidden"].cpu())
+        ml, cl = cmp(lg, rr["logits"].cpu())
+        ref.close()
+        out = {"case": "2 layers, B=4, positions [600, 33, 1025, 128], vocab 4096",
+               "against": "single-GPU kernel on the full weights (oracle-pinned by the GPU tests)",
+               "hidden": {"max_abs": mh, "cosine": ch}, "logits": {"max_abs": ml, "cosine": cl},
+               "max_abs": max(mh, ml), "cosine": min(ch, cl),
+               "ranks_identical": len({d for d, _ in got}) == 1,
+               "status": [s for _, s in got] + [ref_st],
+               "within_tolerance": max(mh, ml) <= 2e-2 and min(ch, cl) >= 0.999}
+    dist.barrier()
+    eng.close()
+    xchg.close()
+    del eng, layers, raw
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -274,6 +416,7 @@ def run_ours(args):
         shard = plan_shard(rank, world, full.num_attention_heads, full.num_key_value_heads, full.num_experts)
         xchg = XchgRegion(xchg_bytes(full.hidden_size, args.batch, world), rank, world, local)
         dist.barrier()
+    parity = multi_gpu_parity(rank, world, local, device) if world > 1 else None
     eng, shape, table, positions, ids = build_engine(args, device, args.seed, shard, xchg)
     table_d, pos_d, ids_d = table.to(device), positions.to(device), ids.to(device)
     out = {"hidden": torch.empty(args.batch, shape.hidden_size, dtype=torch.bfloat16, device=device),
@@ -369,24 +512,20 @@ def run_ours(args):
             traffic = None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        times, t_head, threads = cpu_layer_sample(args, 2)
-        step_s = min(times) * args.layers + t_head
+        times, threads = cpu_steps(args, 1, 3)
+        step_s = statistics.median(times)
         cpu = {"value": args.batch / step_s, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"oracle (faithful PyTorch CPU restatement), 1 of {args.layers} layers at B={args.batch} "
-                         f"ctx {args.ctx} timed (best of 2) and extrapolated x{args.layers}, plus the LM head"}
+               "sample": f"oracle (faithful PyTorch CPU restatement): 3 whole {args.layers}-layer decode steps at "
+                         f"B={args.batch} ctx {args.ctx} (shared layer weights, distinct KV caches) + final norm + "
+                         f"LM head after 1 warm-up step; p50"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "p50_ms": statistics.median(per),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights of the Qwen3-30B-A3B architecture, KV prefix ~N(0,1))",
-            "config": {"workload": "qwen3-30b-a3b decode step (48 layers + final norm + LM head)",
-                       "global_batch": args.batch, "ctx": args.ctx,
-                       "kv_block": 128, "layers": args.layers,
-                       "parallelism": "single GPU" if world == 1 else
-                       f"tp{world} over KV-head groups + ep{world} over experts, in-kernel exchange over NVLink",
-                       "l2": "no flush: ~27 GB of weights streamed per step >> 126 MB L2",
-                       "distinct_experts_per_layer_mean": sum(distinct) / len(distinct)},
+            "config": config_of(args, world),
+            "distinct_experts_per_layer_mean": sum(distinct) / len(distinct),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_step": nbytes,
@@ -394,6 +533,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": args.steps,
+            "parity": parity,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

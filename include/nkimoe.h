@@ -93,6 +93,9 @@ typedef struct nkm_qwen3 nkm_qwen3; /* opaque handle (host memory only) */
 #define NKM_STAGE_ATTN 1    /* RMSNorm(ln1)+QKV+q/k-norm+RoPE+KV write+attention+O-proj */
 #define NKM_STAGE_MOE 2     /* RMSNorm(ln2)+router top-k+expert SwiGLU                  */
 #define NKM_STAGE_LMHEAD 4  /* final RMSNorm + LM head (after the last layer run)       */
+#define NKM_STAGE_QKV_IN 8  /* with NKM_STAGE_ATTN, one layer: the attention takes the raw q/k/v
+                               projections the caller wrote into the QKV buffer
+                               (nkm_qwen3_qkv_buffer) instead of RMSNorm(ln1) + QKV GEMV     */
 
 /* One decode step.  Replaces the kernel call
  *   get_multilayer_kernel_jit(L)[2](X, *W..., *K_caches, *V_caches, cos, sin, position_ids)
@@ -157,6 +160,18 @@ int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream);
 int nkm_qwen3_attention_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* step,
                               nkm_stream_t stream);
 
+/* The handle's QKV buffer: raw (pre-norm, pre-RoPE) bf16 projections [max_batch][R], R =
+ * (n_q_heads + 2 n_kv_heads) * 128, row b = sequence b, columns q heads, k heads, v heads.
+ * An attention block called with step->stages containing NKM_STAGE_QKV_IN consumes the rows
+ * the caller wrote here instead of projecting the hidden input: the attention core on given
+ * projections, as attention_tkg takes projected Q/K/V (nki_kernels/attention/attention_tkg.py:56).
+ * At batch <= 8 the attention starts without waiting for the whole buffer: an element still
+ * holding 0xffff (the "not written" mark every launch leaves in the buffer after reading it) is
+ * re-read until it changes, bounded by the 2 s wait limit (then NKM_ERR_TIMEOUT), so the rows may
+ * be produced by work that overlaps the launch.  *ptr receives the device address, *bytes (may
+ * be NULL) the size. */
+int nkm_qwen3_qkv_buffer(nkm_qwen3* h, void** ptr, size_t* bytes);
+
 /* Single fused MoE block (RMSNorm(ln2) + router top-k + selective-expert SwiGLU) on layer
  * `layer`.  Replaces _qwen3_moe_sbuf_in_sbuf_out_hoisted / qwen3_moe_fused_tkg_sbuf_io
  * (megakernels/qwen3_moe/moe_fused_nki.py:769-997) and the primitive pair router_topk +
@@ -175,8 +190,9 @@ int nkm_qwen3_moe_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* step,
  * nothing: its scratch (barrier, counters, residual rows, router logits, expert activations,
  * split-K partials) lives in a static device array of NKM_NOALLOC_SCRATCH_BYTES; a shape
  * whose scratch does not fit (hidden, top_k, moe_inter and batch set the size) is rejected
- * with NKM_ERR_ARG.  The first call on a device looks up that device's array address and
- * must come before any stream capture on that device.  Each call clears the part of the
+ * with NKM_ERR_ARG.  The first call on a device looks up that device's array address (again
+ * if the device's context was replaced, e.g. after cudaDeviceReset) and must come before any
+ * stream capture on that device.  Each call clears the part of the
  * scratch that must start at zero; all calls share the one array per device, so calls that
  * overlap on the GPU (other streams, other host threads) race: serialise them.  K/V pools,
  * RoPE tables and the LM head of `desc` are not used (they may be NULL).  `status_out`

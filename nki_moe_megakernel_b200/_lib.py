@@ -20,6 +20,7 @@ NKM_ERR_INDEX = 8
 NKM_STAGE_ATTN = 1
 NKM_STAGE_MOE = 2
 NKM_STAGE_LMHEAD = 4
+NKM_STAGE_QKV_IN = 8
 
 NKM_PACK_PLAIN = 0
 NKM_PACK_GATE_UP = 1
@@ -61,6 +62,7 @@ SIGNATURES = {
     "nkm_qwen3_status": (c_int, [c_void_p, c_void_p]),
     "nkm_qwen3_attention_block": (c_int, [c_void_p, c_int32, POINTER(nkm_qwen3_step), c_void_p]),
     "nkm_qwen3_moe_block": (c_int, [c_void_p, c_int32, POINTER(nkm_qwen3_step), c_void_p]),
+    "nkm_qwen3_qkv_buffer": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_size_t)]),
     "nkm_qwen3_moe_block_noalloc": (c_int, [POINTER(nkm_qwen3_desc), c_int32, POINTER(nkm_qwen3_step), c_void_p,
                                             c_void_p]),
     "nkm_pack_ft": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),

@@ -167,6 +167,39 @@ int encode_kv_map(CUtensorMap* map, void* pool, const nkm_qwen3_desc& d) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The three instantiations of the decode kernel (column tiles NT = 1, 2, 4).
+void* decode_kernel_fn(int i) {
+  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
+                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
+  return kfn[i];
+}
+constexpr int kNts[3] = {1, 2, 4};
+constexpr int kMaxDevices = 64;
+
+// Once per device, with that device current: the decode kernel's dynamic shared-memory limit.
+// The attribute belongs to the kernel for the whole process, so it is set to what the largest
+// accepted hidden size needs (not to one handle's size: a handle with a smaller hidden size would
+// otherwise lower it under the launches of a handle with a larger one); every launch still
+// requests only its own size.
+int ensure_smem_limits() {
+  static std::mutex mu;
+  static bool done[kMaxDevices] = {};
+  int dev = 0;
+  NKM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(NKM_ERR_ARG, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return NKM_OK;
+  for (int i = 0; i < 3; ++i) {
+    const nkm::SmemLayout sl(nkm::kMaxHidden, kNts[i]);
+    if (sl.total > 232448 - 1024) return fail(NKM_ERR_ARG, "decode kernel shared memory exceeds the per-CTA limit");
+    NKM_CUDA(cudaFuncSetAttribute(decode_kernel_fn(i), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(sl.total)));
+  }
+  done[dev] = true;
+  return NKM_OK;
+}
+
 }  // namespace
 
 struct nkm_qwen3 {
@@ -246,19 +279,14 @@ int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspa
     return cleanup(fail(NKM_ERR_CUDA, "clearing the workspace failed"));
   if ((rc = encode_kv_map(&h->kmap, desc->k_pool, *desc))) return cleanup(rc);
   if ((rc = encode_kv_map(&h->vmap, desc->v_pool, *desc))) return cleanup(rc);
-  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
-  const int nts[3] = {1, 2, 4};
+  if ((rc = ensure_smem_limits())) return cleanup(rc);
   for (int i = 0; i < 3; ++i) {
-    nkm::SmemLayout sl(desc->hidden, nts[i]);
+    nkm::SmemLayout sl(desc->hidden, kNts[i]);
     h->smem[i] = sl.total;
     if (sl.total > 232448 - 1024) return cleanup(fail(NKM_ERR_ARG, "hidden too large for shared memory"));
-    if (cudaFuncSetAttribute(kfn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sl.total)) !=
-        cudaSuccess)
-      return cleanup(fail(NKM_ERR_CUDA, "cudaFuncSetAttribute failed"));
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn[i], nkm::kThreads, sl.total) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel_fn(i), nkm::kThreads, sl.total) !=
+            cudaSuccess ||
         occ < 1)
       return cleanup(fail(NKM_ERR_CUDA, "decode kernel does not fit on an SM"));
   }
@@ -300,6 +328,8 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   }
   const bool lm = (stages & NKM_STAGE_LMHEAD) && s->logits_out;
   if (lm && (d.vocab <= 0 || !d.lm_head_ft || !d.final_norm)) return fail(NKM_ERR_ARG, "LM head requested but missing");
+  if ((stages & NKM_STAGE_QKV_IN) && (!(stages & NKM_STAGE_ATTN) || nl != 1))
+    return fail(NKM_ERR_ARG, "NKM_STAGE_QKV_IN needs the attention stage and exactly one layer");
 
   nkm::Params p{};
   p.T = s->batch;
@@ -322,7 +352,7 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.gbase = reinterpret_cast<unsigned long long*>(h->ws + h->lay.gbase);
   p.first_layer = first;
   p.num_layers = nl;
-  p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | (lm ? NKM_STAGE_LMHEAD : 0));
+  p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_QKV_IN | (lm ? NKM_STAGE_LMHEAD : 0));
   p.residual = residual;
   p.layers = reinterpret_cast<const nkm::LayerPtrs*>(h->ws + h->lay.layers);
   p.final_norm = static_cast<const uint16_t*>(d.final_norm);
@@ -365,11 +395,9 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
 
   const int nt = nt_for_batch(p.T);
   const int ki = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
-  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
   void* args[3] = {&p, &h->kmap, &h->vmap};
-  NKM_CUDA(cudaLaunchCooperativeKernel(kfn[ki], dim3(h->num_sms), dim3(nkm::kThreads), args, h->smem[ki], stream));
+  NKM_CUDA(cudaLaunchCooperativeKernel(decode_kernel_fn(ki), dim3(h->num_sms), dim3(nkm::kThreads), args, h->smem[ki],
+                                       stream));
   return NKM_OK;
 }
 
@@ -384,7 +412,16 @@ int nkm_qwen3_decode_step(nkm_qwen3* h, const nkm_qwen3_step* s, nkm_stream_t st
 int nkm_qwen3_attention_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* s, nkm_stream_t stream) {
   if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
   if (!s) return fail(NKM_ERR_ARG, "step is NULL");
-  return launch_step(h, s, layer, 1, NKM_STAGE_ATTN, s->residual ? 1 : 0, reinterpret_cast<cudaStream_t>(stream));
+  return launch_step(h, s, layer, 1, NKM_STAGE_ATTN | (s->stages & NKM_STAGE_QKV_IN), s->residual ? 1 : 0,
+                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+int nkm_qwen3_qkv_buffer(nkm_qwen3* h, void** ptr, size_t* bytes) {
+  if (!h || !ptr) return fail(NKM_ERR_ARG, "handle or ptr is NULL");
+  *ptr = h->ws + h->lay.qkv;
+  if (bytes)
+    *bytes = static_cast<size_t>(h->desc.max_batch) * (h->desc.n_q_heads + 2 * h->desc.n_kv_heads) * h->desc.head_dim * 2;
+  return NKM_OK;
 }
 
 int nkm_qwen3_moe_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* s, nkm_stream_t stream) {
@@ -425,7 +462,24 @@ constexpr int kMaxNoAllocDevices = 64;
 struct NoAllocDevice {
   uint8_t* scratch;  // device address of this device's g_noalloc_scratch
   int num_sms;
+  CUcontext ctx;     // the context the address was looked up in
 };
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links no libcuda).
+CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(p);
+  }
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
 
 std::mutex g_noalloc_mu;
 NoAllocDevice g_noalloc_dev[kMaxNoAllocDevices];
@@ -465,20 +519,24 @@ NoAllocLayout layout_noalloc(const nkm_qwen3_desc& d, int T, int num_sms) {
   return w;
 }
 
-// Once per device, with that device current: the address of its scratch array.
+// Once per device (and again if the device's context was replaced, e.g. after a device reset),
+// with that device current: the address of its scratch array.
 int noalloc_device(NoAllocDevice* out) {
   int dev = 0;
   NKM_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxNoAllocDevices) return fail(NKM_ERR_ARG, "device %d out of range", dev);
+  NKM_CUDA(cudaFree(nullptr));  // makes the device's primary context current (allocates nothing)
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   NoAllocDevice& s = g_noalloc_dev[dev];
-  if (!s.scratch) {
+  if (!s.scratch || s.ctx != ctx) {
     void* ptr = nullptr;
     NKM_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
     int sms = 0;
     NKM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     s.num_sms = sms;
     s.scratch = static_cast<uint8_t*>(ptr);
+    s.ctx = ctx;
   }
   *out = s;
   return NKM_OK;
@@ -524,12 +582,9 @@ extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t l
 
   const int nt = nt_for_batch(s->batch);
   const int ki = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
-  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
   const nkm::SmemLayout sl(d.hidden, nt);
   if (sl.total > 232448 - 1024) return fail(NKM_ERR_ARG, "hidden too large for shared memory");
-  NKM_CUDA(cudaFuncSetAttribute(kfn[ki], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sl.total)));
+  if ((rc = ensure_smem_limits())) return rc;
 
   uint8_t* ws = dv.scratch;
   nkm::Params p{};
@@ -586,7 +641,8 @@ extern "C" int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t l
   CUtensorMap nomap;
   memset(&nomap, 0, sizeof(nomap));
   void* args[3] = {&p, &nomap, &nomap};
-  NKM_CUDA(cudaLaunchCooperativeKernel(kfn[ki], dim3(dv.num_sms), dim3(nkm::kThreads), args, sl.total, stream));
+  NKM_CUDA(cudaLaunchCooperativeKernel(decode_kernel_fn(ki), dim3(dv.num_sms), dim3(nkm::kThreads), args, sl.total,
+                                       stream));
   if (status_out)
     NKM_CUDA(cudaMemcpyAsync(status_out, ws + lay.status, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream));
   return NKM_OK;

@@ -204,6 +204,11 @@ struct Ctx {
   int* dyn;         // chunk scheduling words of the expert gate/up stage (shared memory)
   int awaitq;       // attention waits for its q/k/v element by element (no grid barrier before it)
   int npref;        // the next staged norm's prefetch is in flight
+  // This warp's copies in flight (shared memory, written by lane 0): bit s flips when a copy
+  // into ring slot s is issued, bit 4 when the norm prefetch (warp 0) is issued.  Compared with
+  // the waited parities (phase, cphase) it tells which copies have not been waited for, so a
+  // launch that ends early waits for exactly those before its CTA exits.
+  uint32_t* issued;
 };
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
@@ -230,12 +235,17 @@ __device__ __forceinline__ void stamp(const Params& p, Ctx& c) {
 // Bounded wait on a slot's mbarrier.  On timeout the fatal status bit is set and the caller
 // continues (the next grid barrier then aborts every CTA).
 // Bounded wait for phase `par` of an mbarrier; on timeout the status records a fatal error.
+// The status word is polled too: once any wait of the launch has given up, every other wait
+// ends at its next poll instead of spending its own full bound (the launch then ends at the next
+// grid barrier), so the whole launch is bounded by one wait limit plus the polls.
 __device__ __noinline__ void mbar_wait_slow(const Params& p, uint64_t* bar, uint32_t par) {
-  // try_wait itself suspends for a while; read the (slow) global timer only every 64 tries
+  // try_wait itself suspends for a while; read the (slow) global timer and the status word only
+  // every 64 tries (a short wait never pays for them)
   uint64_t t0 = 0;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, par)) break;
     if ((it & 63u) == 0) {
+      if (ld_volatile_i32(p.status) & kStatusFatal) break;
       const uint64_t now = globaltimer_ns();
       if (t0 == 0) {
         t0 = now;
@@ -390,11 +400,19 @@ __device__ __forceinline__ bool rank_exchange(const Params& p, Ctx& c, int which
 // End of a launch: the last CTA out zeroes the barrier counter for the next launch on this
 // workspace (launches on one workspace are stream-ordered).
 __device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c) {
-  if (ld_volatile_i32(p.status) & kStatusFatal) {
-    // a failed wait ends the launch early: give bulk copies this CTA still has in flight
-    // (at most a few ring slots and the broadcast buffer) time to land before it exits
-    const uint64_t t0 = globaltimer_ns();
-    while (globaltimer_ns() - t0 < 50000ull) __nanosleep(1000);
+  if ((ld_volatile_i32(p.status) & kStatusFatal) && lane_id() == 0) {
+    // a failed wait ends the launch early: wait for the copies this warp issued and has not
+    // waited for (they write into this CTA's shared memory), each wait bounded by 1 ms
+    const uint32_t pend = (*c.issued ^ (c.phase & 15u) ^ ((threadIdx.x == 0 ? (c.cphase & 1u) : 0u) << 4)) & 31u;
+#pragma unroll 1
+    for (int s = 0; s < 5; ++s) {
+      if (!((pend >> s) & 1u)) continue;
+      uint64_t* bar = s < 4 ? &c.bars[s] : c.cbar;
+      const uint32_t par = s < 4 ? ((c.phase >> s) & 1u) : (c.cphase & 1u);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(bar, par) && globaltimer_ns() - t0 < 1000000ull) {
+      }
+    }
   }
   __syncthreads();
 
@@ -739,6 +757,7 @@ __device__ __noinline__ void cta_strips_prime(const Params& p, Ctx& c, const Gem
       mbar_arrive_expect_tx(&c.bars[i], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + i * (CU * kUnitBytes), G.base + static_cast<uint64_t>(strip * KT + k0 + pk) * kUnitBytes,
                static_cast<uint32_t>(n * kUnitBytes), &c.bars[i], c.pol);
+      *c.issued ^= 1u << i;
     }
     pk += n;
     if (pk == nk) {
@@ -780,6 +799,7 @@ __device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const G
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + slot * (CU * kUnitBytes), G.base + static_cast<uint64_t>(strip * KT + k0 + pk) * kUnitBytes,
                static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
+      *c.issued ^= 1u << slot;
     }
     pk += n;
     if (pk == nk) {
@@ -879,6 +899,7 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&c.bars[i], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + i * (CU * kUnitBytes), src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[i], c.pol);
+      *c.issued ^= 1u << i;
     }
     pu += n;
     pkt += n;
@@ -902,6 +923,7 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
 // SiLU(gate) * up.  Strips never straddle CTAs, so no partial leaves the SM.  All warps of the CTA
 // call it (one CTA barrier at the start).
 constexpr int kDynSlots = 3;  // strips in reduction at once (strip s uses slot (s - s0) % kDynSlots)
+static_assert((1 + 2 * kDynSlots) * 4 <= 32, "the chunk words end where the per-warp issue words start");
 template <int NT>
 __device__ __forceinline__ bool gateup_dyn_ok(const GemvGeom& G) {
   return NT == 1 && G.kt % RingGeom<NT>::kChunk == 0 &&
@@ -947,6 +969,7 @@ __device__ __noinline__ void gateup_dyn(const Params& p, Ctx& cref, const GemvGe
                G.base + static_cast<uint64_t>(rt->act_e[seg]) * G.seg_bytes +
                    static_cast<uint64_t>(ss * KT + kb * CU) * kUnitBytes,
                static_cast<uint32_t>(CU * kUnitBytes), &c.bars[slot], c.pol);
+      *c.issued ^= 1u << slot;
     }
   };
   int ids[NS];
@@ -996,7 +1019,7 @@ __device__ __noinline__ void gateup_dyn(const Params& p, Ctx& cref, const GemvGe
     if (gen[sl] != strip) {
       const uint64_t t0 = globaltimer_ns();
       while (gen[sl] != strip) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if ((ld_volatile_i32(p.status) & kStatusFatal) || globaltimer_ns() - t0 > kWaitLimitNs) {
           if (lane == 0) set_status(p, kStatusFatal);
           break;
         }
@@ -1065,6 +1088,7 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + slot * (CU * kUnitBytes), src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
+      *c.issued ^= 1u << slot;
     }
     pu += n;
     pkt += n;
@@ -1220,6 +1244,7 @@ __device__ __noinline__ void down_prime(const Params& p, Ctx& c, const GemvGeom&
       mbar_arrive_expect_tx(&c.bars[k], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + k * (CU * kUnitBytes), down_item_src(G, c.rt, pi, pkt), static_cast<uint32_t>(n * kUnitBytes),
                &c.bars[k], c.pol);
+      *c.issued ^= 1u << k;
     }
     pkt += n;
     if (pkt == KT) {
@@ -1337,6 +1362,7 @@ __device__ __noinline__ void down_stage(const Params& p, Ctx& cref, const GemvGe
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + slot * (CU * kUnitBytes), down_item_src(G, rt, pi, pkt), static_cast<uint32_t>(n * kUnitBytes),
                &c.bars[slot], c.pol);
+      *c.issued ^= 1u << slot;
     }
     pkt += n;
     if (pkt == KT) {
@@ -1529,6 +1555,7 @@ __device__ __noinline__ void att_issue_box(const Params& p, Ctx& c, int layer, i
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&c.bars[slot], kSlotBytes);
     tma_load_2d(c.ring + slot * kSlotBytes, kind < 2 ? kmap : vmap, (kind & 1) * 64, row, &c.bars[slot]);
+    *c.issued ^= 1u << slot;
   }
 }
 
@@ -2101,6 +2128,7 @@ __device__ __noinline__ void norm_prefetch(const Params& p, Ctx& c, const uint16
     if (has_e)
       bulk_g2s_plain(reinterpret_cast<uint8_t*>(c.red) + hb, router + static_cast<size_t>(blockIdx.x) * p.H, hb,
                      c.cbar);
+    *c.issued ^= 16u;
   }
   c.npref = 1;
 }
@@ -2117,6 +2145,7 @@ __device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, boo
     fence_proxy_async_global();  // the residual was written by other CTAs during this launch
     mbar_arrive_expect_tx(&c.bars[1], static_cast<uint32_t>(H) * 4u);
     bulk_g2s_plain(stage, p.resid + static_cast<size_t>(warp) * H, static_cast<uint32_t>(H) * 4u, &c.bars[1]);
+    *c.issued ^= 2u;
   }
   if (!c.npref) {  // not prefetched during the barrier (a stage launched on its own)
     __syncthreads();
@@ -2446,6 +2475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.awaitq = 0;
   c.cphase = 0;
   c.npref = 0;
+  c.issued = reinterpret_cast<uint32_t*>(smem + lay.dyn_off + 32) + warp;
+  if (lane == 0) *c.issued = 0u;
   {
     // the layer pointer table, once per launch: every stage reads its pointers from shared memory
     static_assert(sizeof(LayerPtrs) % 16 == 0, "LayerPtrs is copied as uint4");
@@ -2470,10 +2501,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   [&]() {  // the launch body; a fatal error returns from here to launch_exit
+  // stages bit 8: the attention takes the q/k/v projections the caller wrote into the QKV buffer
+  // (no RMSNorm(ln1) + QKV GEMV; one layer per launch, checked on the host)
+  const bool qkv_in = (p.stages & 8) != 0;
   // stage 0: residual (fp32) <- embeddings / hidden input (bf16); the router-logit slots of the
   // staged path start unwritten
   if (norm_staged_ok<NT>(p) && (p.stages & 2)) logits_rearm(p);
-  if (norm_staged_ok<NT>(p) && (p.stages & 1)) bf16_rearm(p.qkv, p.T * p.R);
+  if (norm_staged_ok<NT>(p) && (p.stages & 1) && !qkv_in) bf16_rearm(p.qkv, p.T * p.R);
   {
     const int nvec = p.T * p.H / 8;
     for (int i = blockIdx.x * kThreads + threadIdx.x; i < nvec; i += gridDim.x * kThreads) {
@@ -2497,7 +2531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const bool staged = norm_staged_ok<NT>(p);
   grid_arrive(p);
-  if ((p.stages & 1) && p.num_layers > 0) {  // the first QKV weights stream during the barrier
+  if ((p.stages & 1) && p.num_layers > 0 && !qkv_in) {  // the first QKV weights stream during the barrier
     const LayerPtrs& l0 = c.lt[0];
     GemvGeom ga{l0.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, p.first_layer};
     gemv_prime<NT, GK_QKV>(p, c, ga, staged ? 1 : RingGeom<NT>::kGemvSlots);
@@ -2527,12 +2561,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const LayerPtrs& lw = c.lt[layer - p.first_layer];
     if (p.stages & 1) {
       // A: RMSNorm(ln1) + QKV
-      if (staged) norm_staged(p, c, layer, false, lw.ln1);
-      else norm_rows_to_smem(p, c, lw.ln1, false);
-      __syncthreads();
-      GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
-      if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
-      else gemv_stage<NT, GK_QKV>(p, c, ga);
+      if (!qkv_in) {
+        if (staged) norm_staged(p, c, layer, false, lw.ln1);
+        else norm_rows_to_smem(p, c, lw.ln1, false);
+        __syncthreads();
+        GemvGeom ga{lw.wqkv, 0, 1, p.R / 16, p.H / 32, p.H, layer};
+        if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
+        else gemv_stage<NT, GK_QKV>(p, c, ga);
+      }
       if (staged) {
         // stage B takes only q/k/v from other CTAs and waits for them element by element
         c.awaitq = 1;

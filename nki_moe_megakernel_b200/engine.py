@@ -219,12 +219,16 @@ class Qwen3MoeMegakernel:
         return res
 
     def attention_block(self, layer: int, x: torch.Tensor, positions: torch.Tensor, block_table: torch.Tensor,
-                        residual: bool = False, trace: bool = False, stream=None) -> Dict[str, torch.Tensor]:
+                        residual: bool = False, trace: bool = False, qkv_in: bool = False,
+                        stream=None) -> Dict[str, torch.Tensor]:
+        """One attention block.  ``qkv_in``: take the q/k/v projections from ``qkv_buffer()``
+        (written by the caller) instead of RMSNorm(ln1) + QKV GEMV of ``x``."""
         B = int(x.shape[0])
         y = torch.empty(B, self.shape.hidden_size, dtype=BF16, device=self.device)
         traces = self._alloc_traces(B, 1) if trace else None
         st = self._step_struct(B, x=x, positions=positions, block_table=block_table, y=y, residual=int(residual),
-                               first_layer=layer, num_layers=1, traces=traces)
+                               first_layer=layer, num_layers=1, traces=traces,
+                               stages=_lib.NKM_STAGE_QKV_IN if qkv_in else 0)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         check(lib().nkm_qwen3_attention_block(self._h, layer, ctypes.byref(st), s.cuda_stream),
               "nkm_qwen3_attention_block")
@@ -232,6 +236,17 @@ class Qwen3MoeMegakernel:
         if traces:
             res.update(traces)
         return res
+
+    def qkv_buffer(self) -> torch.Tensor:
+        """The handle's QKV buffer as a bf16 tensor ``[max_batch, (nq + 2 nkv) * head_dim]`` (a view
+        of the workspace): raw q/k/v projections that ``attention_block(..., qkv_in=True)`` consumes
+        (``nkm_qwen3_qkv_buffer``)."""
+        ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+        check(lib().nkm_qwen3_qkv_buffer(self._h, ctypes.byref(ptr), ctypes.byref(nbytes)), "nkm_qwen3_qkv_buffer")
+        off = ptr.value - self.workspace.data_ptr()
+        s = self.shape
+        R = (s.num_attention_heads + 2 * s.num_key_value_heads) * s.head_dim
+        return self.workspace[off:off + nbytes.value].view(BF16).view(self.max_batch, R)
 
     def moe_block(self, layer: int, x: torch.Tensor, residual: bool = False, trace: bool = False,
                   stream=None) -> Dict[str, torch.Tensor]:

@@ -10,12 +10,18 @@ Without ``--model-path`` the weights are seeded random-init of the configured sh
 prompts are turned into token ids deterministically (no tokenizer or checkpoint needed).
 
 Run: ``python -m nki_moe_megakernel_b200.main --mode generate --enable-nki [--num-layers 2]``.
+Several GPUs (tensor + expert parallel, reference ``--tp-degree`` / ``--moe-ep-degree``,
+``main.py:224-231``): ``torchrun --nproc-per-node 2 -m nki_moe_megakernel_b200.main --mode validate
+--enable-nki --tp-degree 2 --moe-ep-degree 2 --num-layers 2``; every rank steps the kernel, rank 0
+prints.
 """
 from __future__ import annotations
 
 import argparse
 import ast
+import contextlib
 import importlib
+import io
 import os
 import time
 from typing import Dict, List, Optional
@@ -51,7 +57,35 @@ def parse_args(argv=None):
     p.add_argument("--num-layers", type=int, default=None, help="override num_hidden_layers (random-init only)")
     p.add_argument("--benchmark-iters", type=int, default=5)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--tp-degree", type=int, default=None,
+                   help="GPUs of the tensor + expert parallel group (default: WORLD_SIZE, 1 without torchrun)")
+    p.add_argument("--moe-ep-degree", type=int, default=None, help="1 or tp-degree (experts split over the TP ranks)")
+    p.add_argument("--moe-tp-degree", type=int, default=1)
     return p.parse_args(argv)
+
+
+def init_distributed(args):
+    """One process per GPU under torchrun: NCCL process group, this rank's GPU.  Returns
+    (rank, world, device)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    tp = args.tp_degree or world
+    if tp != world:
+        raise SystemExit(f"--tp-degree {tp} needs {tp} processes (got WORLD_SIZE={world})")
+    args.tp_degree = tp
+    args.moe_ep_degree = args.moe_ep_degree or tp
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist  # noqa: PLC0415
+
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    return rank, world, device
 
 
 # ---------------------------------------------------------------------------
@@ -77,12 +111,16 @@ def prepare_inference(model_cls, args):
     mod = importlib.import_module(model_cls.__module__)
     ncfg = ncfg_cls(batch_size=args.batch_size, max_batch_size=args.batch_size, seq_len=args.seq_len,
                     max_length=args.seq_len, pa_block_size=args.pa_block_size, pa_num_blocks=args.pa_num_blocks,
-                    top_k=args.top_k, do_sample=args.do_sample, temperature=args.temperature)
+                    top_k=args.top_k, do_sample=args.do_sample, temperature=args.temperature,
+                    tp_degree=getattr(args, "tp_degree", None) or 1,
+                    moe_ep_degree=getattr(args, "moe_ep_degree", None) or 1,
+                    moe_tp_degree=getattr(args, "moe_tp_degree", 1))
     overrides = {}
     if args.num_layers is not None and not args.model_path:
         overrides["num_hidden_layers"] = args.num_layers
     cfg = cfg_cls(ncfg, load_config=mod.load_pretrained_config(args.model_path), **overrides)
-    model = model_cls(args.model_path, cfg, seed=args.seed, state_dict=getattr(args, "_state_dict", None))
+    model = model_cls(args.model_path, cfg, device=getattr(args, "_device", None), seed=args.seed,
+                      state_dict=getattr(args, "_state_dict", None))
     model.compile(args.compiled_model_path)
     model.load(args.compiled_model_path)
     return model, _tokenizer(args.model_path)
@@ -182,28 +220,42 @@ def main(argv=None):
     args.batch_size = args.batch_size or len(args.prompts)
     if args.batch_size != len(args.prompts):
         raise SystemExit("--batch-size must equal the number of prompts")
+    rank, world, args._device = init_distributed(args)
     mod_name, cls_name = _MODEL_REGISTRY[args.model]
     model_cls = getattr(importlib.import_module(mod_name), cls_name)
     torch.manual_seed(args.seed)
-    model, tokenizer = prepare_inference(model_cls, args)
-    ids = encode_prompts(args.prompts, tokenizer, model.config.vocab_size)
-    max_new = args.max_new_tokens or max(1, args.seq_len - max(len(i) for i in ids) - 1)
-    n_check = args.num_tokens_to_check or min(max_new, 16)
+    # every rank steps the kernel (the ranks exchange partial sums inside each step); rank 0 prints
+    quiet = contextlib.redirect_stdout(io.StringIO()) if rank != 0 else contextlib.nullcontext()
+    rc = 0
+    with quiet:
+        model, tokenizer = prepare_inference(model_cls, args)
+        ids = encode_prompts(args.prompts, tokenizer, model.config.vocab_size)
+        max_new = args.max_new_tokens or max(1, args.seq_len - max(len(i) for i in ids) - 1)
+        n_check = args.num_tokens_to_check or min(max_new, 16)
 
-    if args.mode == "generate":
-        run_generation(model, tokenizer, args.prompts, max_new)
-    elif args.mode == "validate":
-        passed = run_accuracy_check(model, tokenizer, args.prompts, args.tol_map, n_check)
-        return 0 if passed else 1
-    elif args.mode == "evaluate_single":
-        accuracy = 1 if run_accuracy_check(model, tokenizer, args.prompts, args.tol_map, n_check) else 0
-        report = benchmark_sampling(model, ids, max_new, args.benchmark_iters)
-        print(f"Prompt: {args.prompts[0]}\n"
-              f"\tAccuracy: {accuracy}\n"
-              f"\tLatency: {report['e2e_model']['latency_ms_p99']}\n"
-              f"\tThroughput: {report['e2e_model']['throughput']}\n"
-              f"\tCustom-kernel FLOPs ratio: 1.0 (every decode-step op runs inside the megakernel)")
-    return 0
+        if args.mode == "generate":
+            run_generation(model, tokenizer, args.prompts, max_new)
+        elif args.mode == "validate":
+            passed = run_accuracy_check(model, tokenizer, args.prompts, args.tol_map, n_check)
+            rc = 0 if passed else 1
+        elif args.mode == "evaluate_single":
+            accuracy = 1 if run_accuracy_check(model, tokenizer, args.prompts, args.tol_map, n_check) else 0
+            report = benchmark_sampling(model, ids, max_new, args.benchmark_iters)
+            print(f"Prompt: {args.prompts[0]}\n"
+                  f"\tAccuracy: {accuracy}\n"
+                  f"\tLatency: {report['e2e_model']['latency_ms_p99']}\n"
+                  f"\tThroughput: {report['e2e_model']['throughput']}\n"
+                  f"\tCustom-kernel FLOPs ratio: 1.0 (every decode-step op runs inside the megakernel)")
+    if world > 1:
+        import torch.distributed as dist  # noqa: PLC0415
+
+        flag = torch.tensor([rc], device=args._device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)  # a failure on any rank fails every rank
+        rc = int(flag.item())
+        model.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    return rc
 
 
 if __name__ == "__main__":

@@ -9,7 +9,10 @@ Same public names as the reference: ``Qwen3MoEV3MultilayerNeuronConfig`` (refere
 
 Token generation (TKG) runs every decoder layer, the final norm and the LM head in ONE
 persistent sm_100a kernel per step (``libnkimoe.so``, C ABI ``include/nkimoe.h``), writing
-each layer's K/V in place into a paged cache (block 128).  Prompt tokens are fed through the
+each layer's K/V in place into a paged cache (block 128).  With ``tp_degree`` = N > 1 (one
+process per GPU, ``torch.distributed`` initialised by the caller, e.g. ``torchrun``) every rank
+holds its KV-head group and 1/N of the experts and the kernels exchange partial sums over
+NVLink inside each step (the reference's TP replica groups, ``qwen_with_megakernel.py:360-362``).  Prompt tokens are fed through the
 same decode kernel one position per step (per-sequence positions), so a batch can mix
 sequences that are still reading their prompt with sequences that are generating.
 """
@@ -23,6 +26,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from ...engine import GpuLayer, Qwen3MoeMegakernel, Qwen3MoeShape
+from ...sharding import XchgRegion, plan_shard, shard_attention, shard_experts, xchg_bytes
 
 BF16 = torch.bfloat16
 
@@ -58,9 +62,14 @@ class Qwen3MoEV3MultilayerNeuronConfig:
             setattr(self, k, v)
         if torch_dtype not in (BF16, "bfloat16"):
             raise ValueError("the decode megakernel computes in bf16")
-        if tp_degree != 1 or moe_ep_degree != 1:
-            # one GPU per model instance; TP/EP sharding is described by the desc of each rank
-            self.per_rank = True
+        if tp_degree < 1 or tp_degree > 8:
+            raise ValueError("tp_degree must be in 1..8 (GPUs of one node)")
+        # experts are always expert-parallel over the tensor-parallel ranks (128/N per GPU); an
+        # expert-parallel degree other than 1 or tp_degree has no layout here
+        if moe_ep_degree not in (1, tp_degree):
+            raise ValueError("moe_ep_degree must be 1 or equal to tp_degree (experts are split over the TP ranks)")
+        if moe_tp_degree != 1:
+            raise ValueError("expert tensor parallelism is not used: experts are expert-parallel over the TP ranks")
 
 
 def load_pretrained_config(model_path: Optional[str]):
@@ -204,6 +213,21 @@ class NeuronQwen3MoeForCausalLMV3:
         self._layers: List[GpuLayer] = []
         self._head: Dict[str, torch.Tensor] = {}
         self.kernel: Optional[Qwen3MoeMegakernel] = None
+        self.shard = self._plan_shard()
+        self.xchg = None
+
+    def _plan_shard(self):
+        """This process's heads and experts when ``tp_degree`` > 1 (None on one GPU)."""
+        tp = self.neuron_config.tp_degree
+        if tp == 1:
+            return None
+        import torch.distributed as dist  # noqa: PLC0415
+
+        if not dist.is_initialized() or dist.get_world_size() != tp:
+            raise RuntimeError(f"tp_degree={tp} needs torch.distributed initialised with {tp} processes "
+                               "(one per GPU, e.g. torchrun --nproc-per-node {tp})")
+        c = self.config
+        return plan_shard(dist.get_rank(), tp, c.num_attention_heads, c.num_key_value_heads, c.num_experts)
 
     @classmethod
     def get_neuron_config_cls(cls):
@@ -262,6 +286,10 @@ class NeuronQwen3MoeForCausalLMV3:
         for l in range(self.config.num_hidden_layers):
             t = {k: sd.pop(f"layers.{l}.{k}").to(dev) for k in ("wq", "wk", "wv", "wo", "q_norm", "k_norm", "ln1",
                                                                "ln2", "router", "gate_up", "down")}
+            if self.shard is not None:  # this rank's heads and experts
+                t["wq"], t["wk"], t["wv"], t["wo"] = shard_attention(t["wq"], t["wk"], t["wv"], t["wo"], self.shard,
+                                                                     self.config.head_dim)
+                t["gate_up"], t["down"] = shard_experts(t["gate_up"], t["down"], self.shard)
             self._layers.append(GpuLayer(t["wq"], t["wk"], t["wv"], t["wo"], t["q_norm"], t["k_norm"], t["ln1"],
                                          t["ln2"], t["router"], t["gate_up"], t["down"]))
         self._head = {k: sd[k].to(dev) for k in ("embed", "final_norm", "lm_head")}
@@ -277,12 +305,30 @@ class NeuronQwen3MoeForCausalLMV3:
         if not self._layers:
             self.compile(compiled_model_path)
         nc = self.neuron_config
-        self.kernel = Qwen3MoeMegakernel(self.config.shape(), self._layers, max_batch=nc.max_batch_size,
+        shape = self.config.shape()
+        if self.shard is not None:
+            shape.num_attention_heads = len(self.shard.q_heads)
+            shape.num_key_value_heads = len(self.shard.kv_heads)
+            dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+            self.xchg = XchgRegion(xchg_bytes(shape.hidden_size, nc.max_batch_size, self.shard.world),
+                                   self.shard.rank, self.shard.world, dev_index)
+        self.kernel = Qwen3MoeMegakernel(shape, self._layers, max_batch=nc.max_batch_size,
                                          num_blocks=nc.pa_num_blocks, final_norm=self._head["final_norm"],
                                          lm_head=self._head["lm_head"], embed=self._head["embed"],
                                          rope_max_pos=max(self.config.max_position_embeddings, nc.max_length + 1),
-                                         device=self.device)
+                                         device=self.device, shard=self.shard, xchg=self.xchg)
         self.reset()
+
+    def close(self):
+        """Release the kernel instance and, on several GPUs, the exchange region (every rank
+        calls it, after its last step)."""
+        if self.kernel is not None:
+            torch.cuda.synchronize(self.device)
+            self.kernel.close()
+            self.kernel = None
+        if self.xchg is not None:
+            self.xchg.close()
+            self.xchg = None
 
     # -- KV cache bookkeeping ----------------------------------------------
     def reset(self):

@@ -1,0 +1,176 @@
+"""Parity at the benchmarked configuration, and the router's top-k against the reference order.
+
+* The full decode step of the bench (48 layers, B=8, context 2048 in a paged KV cache, vocab
+  151936, final norm and LM head) against the fp32 oracle run free (no teacher forcing): the
+  final hidden state and the logits within max-abs 2e-2 and cosine >= 0.999, and at every layer
+  the kernel's top-k expert indices equal the oracle's selection on the kernel's own residual
+  (bit-exact router logits in the kernel's summation order).  The weights cycle through two
+  distinct seeded layers (distinct K/V caches per layer), as in the CPU baseline.
+* Top-k flips against the reference's router order: the kernel's expert sets compared with
+  ``topk_select(xn @ W_router.T)`` computed in plain fp32 (RMSNorm and matmul in torch's order,
+  the NxDI / Hugging Face computation, reference ``moe_fused_nki.py:186-218, 241-250``), at
+  the shapes of configs 0, 1 and 2 over several seeds.  A flip is allowed only between experts
+  whose plain-fp32 logits differ by less than ``FLIP_GAP`` (the two summation orders differ by
+  a few fp32 ulps of the logit magnitude); the flip count and the largest flipped gap are printed.
+"""
+import pytest
+import torch
+
+from oracle import qwen3_moe_oracle as O
+from tests.qwen_cases import BF16, gpu_layers, make_kv, make_layers, qwen_cfg, shape_of, skew_bias
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+COS = 0.999
+FLIP_GAP = 1e-4   # largest plain-fp32 logit gap at which a top-k set may differ
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+def _plain_router_logits(mid: torch.Tensor, lw: O.LayerWeights, cfg: O.QwenConfig) -> torch.Tensor:
+    xn = O.rmsnorm_fp32(mid, lw.ln2, cfg.rms_eps)
+    logits = xn @ lw.router.float().t()
+    if lw.router_bias is not None:
+        logits = logits + lw.router_bias.float()
+    return logits
+
+
+def _flips(idx_gpu: torch.Tensor, logits_ref: torch.Tensor, k: int):
+    """(rows compared, rows whose top-k set differs, largest plain-fp32 logit gap among them)."""
+    ref = O.topk_select(logits_ref, k)
+    n = flips = 0
+    worst = 0.0
+    for r in range(idx_gpu.shape[0]):
+        a, b = set(idx_gpu[r].tolist()), set(ref[r].tolist())
+        n += 1
+        if a == b:
+            continue
+        flips += 1
+        for ea in a - b:
+            for eb in b - a:
+                worst = max(worst, abs(float(logits_ref[r, ea]) - float(logits_ref[r, eb])))
+    return n, flips, worst
+
+
+FLIP_TOTAL = {"rows": 0, "flips": 0, "worst_gap": 0.0}
+
+
+def _record(tag, n, f, w):
+    FLIP_TOTAL["rows"] += n
+    FLIP_TOTAL["flips"] += f
+    FLIP_TOTAL["worst_gap"] = max(FLIP_TOTAL["worst_gap"], w)
+    print(f"[topk-vs-fp32] {tag}: {f} of {n} rows differ, largest flipped gap {w:.3g} "
+          f"(running total {FLIP_TOTAL})", flush=True)
+    assert w <= FLIP_GAP, (tag, w)
+
+
+def test_bench_shape_48_layers_free_running(dev):
+    from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
+
+    L, B, ctx = 48, 8, 2048
+    cfg = qwen_cfg(n_layers=L)
+    distinct = make_layers(cfg, 2, seed=41)
+    layers = [distinct[i % 2] for i in range(L)]
+    g = torch.Generator().manual_seed(42)
+    positions = [ctx, ctx, ctx - 1, ctx, 1900, ctx, 2047, ctx]
+    NB = sum(p // 128 + 1 for p in positions) + 2
+    k0, v0, table = make_kv(cfg, L, positions, NB, seed=43, nan_fill=False)
+    final_norm = (1 + 0.02 * torch.randn(cfg.hidden, generator=g)).to(BF16)
+    lm_head = (0.02 * torch.randn(cfg.vocab, cfg.hidden, generator=g)).to(BF16)
+    embed = torch.randn(cfg.vocab, cfg.hidden, generator=g).to(BF16)
+    ids = torch.randint(0, cfg.vocab, (B,), generator=g, dtype=torch.int32)
+    gl = gpu_layers(distinct, dev)
+    eng = Qwen3MoeMegakernel(shape_of(cfg, L, cfg.vocab), [gl[i % 2] for i in range(L)], max_batch=B,
+                             num_blocks=NB, final_norm=final_norm.to(dev), lm_head=lm_head.to(dev),
+                             embed=embed.to(dev), rope_max_pos=4096, device=dev)
+    eng.k_pool.copy_(k0.to(dev))
+    eng.v_pool.copy_(v0.to(dev))
+    pos = torch.tensor(positions, dtype=torch.int32)
+    res = eng.decode_step(pos.to(dev), table.to(dev), input_ids=ids.to(dev), trace=True)
+    torch.cuda.synchronize()
+    assert eng.status() == 0
+    hidden, logits = res["hidden"].cpu(), res["logits"].cpu()
+    mids, outs = res["resid_mid"].cpu(), res["resid_out"].cpu()
+    idx_all = res["topk_idx"].cpu().long()
+    rlog = res["router_logits"].cpu()
+    eng.close()
+    del eng, gl, res
+    torch.cuda.empty_cache()
+
+    # layer by layer: the router on the kernel's own residual is bit-exact, and the top-k set
+    # against the plain-fp32 (reference-order) logits differs only at near ties
+    n = f = 0
+    worst = 0.0
+    for li in range(L):
+        lw = layers[li]
+        lg = O.router_logits_fixed(O.rmsnorm_hidden_faithful(mids[li], lw.ln2, cfg.rms_eps, True), lw.router)
+        assert torch.equal(rlog[li], lg), li
+        assert torch.equal(idx_all[li], O.topk_select(lg, cfg.top_k)), li
+        a, b, c = _flips(idx_all[li], _plain_router_logits(mids[li], lw, cfg), cfg.top_k)
+        n, f, worst = n + a, f + b, max(worst, c)
+    _record("config 2 (48 layers x B=8)", n, f, worst)
+
+    # free-running fp32 oracle of the whole step
+    x = embed[ids.long()]
+    cos32, sin32 = O.rope_tables(4096, cfg.head_dim, cfg.rope_theta, torch.float32)
+    traces = []
+    ref_hidden, ref_logits = O.decode_step(x, distinct, cfg, [k0[i].clone() for i in range(L)],
+                                           [v0[i].clone() for i in range(L)], pos, table, cos32, sin32,
+                                           final_norm, lm_head, "fp32", traces)
+    growth = []
+    for li in (0, 11, 23, 35, 47):
+        r = O.compare(outs[li], traces[li].resid_out)
+        growth.append((li + 1, round(r["max_abs"], 5), round(r["cosine"], 7)))
+    print(f"[48-layer] per-layer residual vs fp32 (layer, max_abs, cosine): {growth}", flush=True)
+    rh = O.compare(hidden.float(), ref_hidden)
+    rl = O.compare(logits, ref_logits)
+    print(f"[48-layer] final hidden {rh}, logits {rl}", flush=True)
+    assert rh["max_abs"] <= ATOL and rh["cosine"] >= COS, rh
+    assert rl["max_abs"] <= ATOL and rl["cosine"] >= COS, rl
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2, 3])
+def test_topk_vs_plain_fp32_router_config0(dev, seed):
+    """Config 0 (one layer, B=4, ctx 1024): the kernel's expert sets on its own residual."""
+    from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
+
+    cfg = qwen_cfg(n_layers=1)
+    lw = make_layers(cfg, 1, seed=500 + seed)[0]
+    positions = [1024] * 4
+    NB = 4 * 9 + 1
+    k0, v0, table = make_kv(cfg, 1, positions, NB, seed=600 + seed)
+    x = torch.randn(4, cfg.hidden, generator=torch.Generator().manual_seed(700 + seed)).to(BF16)
+    eng = Qwen3MoeMegakernel(shape_of(cfg, 1, 0), gpu_layers([lw], dev), max_batch=4, num_blocks=NB, device=dev)
+    eng.k_pool.copy_(k0.to(dev))
+    eng.v_pool.copy_(v0.to(dev))
+    res = eng.decode_step(torch.tensor(positions, dtype=torch.int32, device=dev), table.to(dev), x=x.to(dev),
+                          want_logits=False, trace=True)
+    torch.cuda.synchronize()
+    assert eng.status() == 0
+    mid = res["resid_mid"][0].cpu()
+    _record(f"config 0 seed {seed}", *_flips(res["topk_idx"][0].cpu().long(), _plain_router_logits(mid, lw, cfg),
+                                             cfg.top_k))
+
+
+@pytest.mark.parametrize("seed,skewed", [(0, False), (1, False), (2, True), (3, True)])
+def test_topk_vs_plain_fp32_router_config1(dev, seed, skewed):
+    """Config 1 (MoE block, T=32, uniform and skewed routing)."""
+    from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
+
+    cfg = qwen_cfg(n_layers=1)
+    lw = make_layers(cfg, 1, seed=800 + seed)[0]
+    if skewed:
+        lw.router_bias = skew_bias(cfg)
+    x = torch.randn(32, cfg.hidden, generator=torch.Generator().manual_seed(900 + seed)).to(BF16)
+    eng = Qwen3MoeMegakernel(shape_of(cfg, 1, 0), gpu_layers([lw], dev, attention=False, router_bias=lw.router_bias),
+                             max_batch=32, num_blocks=0, kv_pools=False, device=dev)
+    res = eng.moe_block(0, x.to(dev), trace=True)
+    torch.cuda.synchronize()
+    assert eng.status() == 0
+    _record(f"config 1 seed {seed} skewed={skewed}",
+            *_flips(res["topk_idx"][0].cpu().long(), _plain_router_logits(x.float(), lw, cfg), cfg.top_k))

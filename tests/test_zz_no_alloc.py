@@ -79,3 +79,38 @@ def test_noalloc_rejects_oversized_scratch():
                                                 torch.cuda.current_stream(dev).cuda_stream)
     assert rc == _lib.NKM_ERR_ARG
     assert "scratch" in _lib.last_error()
+
+
+def test_handles_and_noalloc_with_different_hidden_sizes():
+    """The decode kernel's shared-memory limit is a per-process attribute of the kernel.  A
+    handle for hidden 2048 keeps working after a handle for hidden 256 is created and after an
+    allocation-free call on that smaller model (neither lowers the limit under the larger
+    handle's launches), and the small model's two entry points agree."""
+    from nki_moe_megakernel_b200 import _lib
+    from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
+
+    dev = torch.device("cuda:0")
+    big = qwen_cfg(n_layers=1)
+    small = qwen_cfg(n_layers=1, hidden=256, n_experts=16, top_k=4, moe_inter=128)
+    eb = Qwen3MoeMegakernel(shape_of(big, 1, 0), gpu_layers(make_layers(big, 1, seed=7), dev, attention=False),
+                            max_batch=8, num_blocks=0, kv_pools=False)
+    es = Qwen3MoeMegakernel(shape_of(small, 1, 0), gpu_layers(make_layers(small, 1, seed=8), dev, attention=False),
+                            max_batch=8, num_blocks=0, kv_pools=False)
+    xb = torch.randn(8, big.hidden, generator=torch.Generator().manual_seed(9)).to(BF16).to(dev)
+    xs = torch.randn(8, small.hidden, generator=torch.Generator().manual_seed(10)).to(BF16).to(dev)
+    want_b = eb.moe_block(0, xb)["hidden"]
+    assert eb.status() == 0
+    want_s = es.moe_block(0, xs)["hidden"]
+    assert es.status() == 0
+    got_s = torch.empty_like(xs)
+    step = es._step_struct(8, x=xs, y=got_s, residual=0, first_layer=0, num_layers=1)
+    status = torch.full((1,), -1, dtype=torch.int32, device=dev)
+    rc = _lib.lib().nkm_qwen3_moe_block_noalloc(ctypes.byref(es._desc), 0, ctypes.byref(step), status.data_ptr(),
+                                                torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    _close(got_s, want_s)
+    again = eb.moe_block(0, xb)["hidden"]
+    assert eb.status() == 0
+    assert torch.equal(again, want_b)
