@@ -71,3 +71,29 @@ def test_main_validate_random_init():
     rc = drv.main(["--mode", "validate", "--enable-nki", "--num-layers", "2", "--seq-len", "96",
                    "--num-tokens-to-check", "8", "--prompt", "I believe the meaning of life is"])
     assert rc == 0
+
+
+def test_model_from_safetensors_checkpoint_vs_hf_from_pretrained(tmp_path):
+    """The checkpoint route of the reference: a Hugging Face directory (config.json +
+    safetensors) loaded by the model class from ``model_path``, against the same directory
+    loaded with ``Qwen3MoeForCausalLM.from_pretrained`` (fp32), teacher-forced logits."""
+    from transformers import Qwen3MoeForCausalLM
+
+    from nki_moe_megakernel_b200.megakernels.qwen3_moe import qwen_with_megakernel as qm
+    from tests.test_host_mirror import _save_tiny_checkpoint
+
+    _save_tiny_checkpoint(tmp_path)
+    nc = qm.Qwen3MoEV3MultilayerNeuronConfig(batch_size=1, seq_len=200)
+    cfg = qm.Qwen3MoeInferenceConfig(nc, load_config=qm.load_pretrained_config(str(tmp_path)))
+    model = qm.NeuronQwen3MoeForCausalLM(str(tmp_path), cfg, device="cuda")
+    model.compile()
+    model.load()
+    g = torch.Generator().manual_seed(11)
+    toks = torch.randint(0, cfg.vocab_size, (135,), generator=g).tolist()
+    ours = model.teacher_forced_logits(toks)
+    hf = Qwen3MoeForCausalLM.from_pretrained(str(tmp_path), torch_dtype=torch.float32).cuda().eval()
+    with torch.no_grad():
+        ref = hf(torch.tensor([toks], device="cuda")).logits[0].float()
+    err = (ours - ref).abs().max().item()
+    assert err < 2e-2, err
+    assert _cos(ours, ref) > 0.999

@@ -86,3 +86,36 @@ def test_encode_prompts_and_args():
     assert a.mode == "validate" and a.enable_nki and a.prompts == ["x"] and a.num_layers == 2
     tm = drv._parse_tol_map(drv.DEFAULT_TOL_MAP)
     assert tm[None] == (1e-5, 0.05) and tm[5] == (1e-5, 0.03)
+
+
+def _save_tiny_checkpoint(path):
+    """The golden tiny model written as a Hugging Face checkpoint (config.json + safetensors)."""
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+
+    d = torch.load(os.path.join(os.path.dirname(__file__), "golden", "qwen3_moe_tiny.pt"), weights_only=False)
+    cfg = Qwen3MoeConfig(**{k: v for k, v in d["config"].items() if not k.startswith("_")})
+    model = Qwen3MoeForCausalLM(cfg)
+    missing, _ = model.load_state_dict(d["state_dict"], strict=False)
+    assert not missing, missing
+    model.save_pretrained(str(path), safe_serialization=True)
+    return d
+
+
+def test_safetensors_checkpoint_loads_like_the_in_memory_state_dict(tmp_path):
+    """A Hugging Face checkpoint directory (``save_pretrained``: config.json + *.safetensors, the
+    files the reference loads with ``from_pretrained``, ``qwen_with_megakernel.py:606-608``) read
+    by the model class gives the same config and, after conversion, the same tensors as the
+    in-memory state dict."""
+    d = _save_tiny_checkpoint(tmp_path)
+    assert list(tmp_path.glob("*.safetensors")), "no safetensors written"
+    nc = qm.Qwen3MoEV3MultilayerNeuronConfig(batch_size=1, seq_len=64)
+    cfg = qm.Qwen3MoeInferenceConfig(nc, load_config=qm.load_pretrained_config(str(tmp_path)))
+    c = d["config"]
+    assert (cfg.hidden_size, cfg.num_experts, cfg.num_hidden_layers, cfg.vocab_size) == (
+        c["hidden_size"], c.get("num_experts") or c["num_local_experts"], c["num_hidden_layers"], c["vocab_size"])
+    model = qm.NeuronQwen3MoeForCausalLM(str(tmp_path), cfg, device="cpu")
+    from_disk = qm.convert_qwen3_moe_hf_to_neuron_state_dict(model.hf_state_dict(), cfg)
+    in_mem = qm.convert_qwen3_moe_hf_to_neuron_state_dict(d["state_dict"], cfg)
+    assert from_disk.keys() == in_mem.keys()
+    for k in in_mem:
+        assert torch.equal(from_disk[k].to(in_mem[k].dtype), in_mem[k]), k
