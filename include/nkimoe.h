@@ -96,6 +96,12 @@ typedef struct nkm_qwen3 nkm_qwen3; /* opaque handle (host memory only) */
 #define NKM_STAGE_QKV_IN 8  /* with NKM_STAGE_ATTN, one layer: the attention takes the raw q/k/v
                                projections the caller wrote into the QKV buffer
                                (nkm_qwen3_qkv_buffer) instead of RMSNorm(ln1) + QKV GEMV     */
+#define NKM_STAGE_KV_FIRST 16 /* with NKM_STAGE_ATTN: every row's new K/V is written to the cache
+                               before any row's attention reads it, so rows of ONE sequence at
+                               consecutive positions (same block-table row) attend causally to
+                               each other: multi-token decode and chunked prefill (reference
+                               S_tkg > 1, nki_kernels/attention/attention_block_tkg.py:144-146).
+                               Costs two grid barriers per layer.                             */
 
 /* One decode step.  Replaces the kernel call
  *   get_multilayer_kernel_jit(L)[2](X, *W..., *K_caches, *V_caches, cos, sin, position_ids)
@@ -115,7 +121,8 @@ typedef struct nkm_qwen3_step {
   float* logits_out;           /* device fp32 [B, V] or NULL (LM head skipped)              */
   int32_t first_layer;         /* layer range to run: [first_layer, first_layer+num_layers) */
   int32_t num_layers;          /* 0 = all layers                                            */
-  int32_t stages;              /* NKM_STAGE_* bits; 0 = ATTN|MOE|LMHEAD                      */
+  int32_t stages;              /* NKM_STAGE_* bits; no ATTN/MOE/LMHEAD bit = all three; QKV_IN
+                                  and KV_FIRST are added to the selected stages             */
   int32_t residual;            /* 1 = blocks add into the residual stream (decoder layer);
                                   0 = a single-block call returns the block output only    */
   /* optional traces (device, NULL to skip), indexed [layer - first_layer] */

@@ -21,6 +21,7 @@ NKM_STAGE_ATTN = 1
 NKM_STAGE_MOE = 2
 NKM_STAGE_LMHEAD = 4
 NKM_STAGE_QKV_IN = 8
+NKM_STAGE_KV_FIRST = 16
 
 NKM_PACK_PLAIN = 0
 NKM_PACK_GATE_UP = 1

@@ -330,6 +330,8 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   if (lm && (d.vocab <= 0 || !d.lm_head_ft || !d.final_norm)) return fail(NKM_ERR_ARG, "LM head requested but missing");
   if ((stages & NKM_STAGE_QKV_IN) && (!(stages & NKM_STAGE_ATTN) || nl != 1))
     return fail(NKM_ERR_ARG, "NKM_STAGE_QKV_IN needs the attention stage and exactly one layer");
+  if ((stages & NKM_STAGE_KV_FIRST) && s->trace_stage_ns)
+    return fail(NKM_ERR_ARG, "stage timestamps are not recorded with NKM_STAGE_KV_FIRST");
 
   nkm::Params p{};
   p.T = s->batch;
@@ -352,7 +354,8 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.gbase = reinterpret_cast<unsigned long long*>(h->ws + h->lay.gbase);
   p.first_layer = first;
   p.num_layers = nl;
-  p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_QKV_IN | (lm ? NKM_STAGE_LMHEAD : 0));
+  p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST |
+                       (lm ? NKM_STAGE_LMHEAD : 0));
   p.residual = residual;
   p.layers = reinterpret_cast<const nkm::LayerPtrs*>(h->ws + h->lay.layers);
   p.final_norm = static_cast<const uint16_t*>(d.final_norm);
@@ -405,15 +408,18 @@ int nkm_qwen3_decode_step(nkm_qwen3* h, const nkm_qwen3_step* s, nkm_stream_t st
   if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
   if (!s) return fail(NKM_ERR_ARG, "step is NULL");
   const int nl = s->num_layers > 0 ? s->num_layers : h->desc.n_layers - s->first_layer;
-  const int stages = s->stages ? s->stages : (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_LMHEAD);
+  // stage bits 1, 2, 4 select stages (none: all three); bits 8, 16 modify the attention stage
+  const int sel = s->stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_LMHEAD);
+  const int stages = (sel ? sel : (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_LMHEAD)) |
+                     (s->stages & (NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST));
   return launch_step(h, s, s->first_layer, nl, stages, 1, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int nkm_qwen3_attention_block(nkm_qwen3* h, int32_t layer, const nkm_qwen3_step* s, nkm_stream_t stream) {
   if (!h) return fail(NKM_ERR_ARG, "handle is NULL");
   if (!s) return fail(NKM_ERR_ARG, "step is NULL");
-  return launch_step(h, s, layer, 1, NKM_STAGE_ATTN | (s->stages & NKM_STAGE_QKV_IN), s->residual ? 1 : 0,
-                     reinterpret_cast<cudaStream_t>(stream));
+  return launch_step(h, s, layer, 1, NKM_STAGE_ATTN | (s->stages & (NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST)),
+                     s->residual ? 1 : 0, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int nkm_qwen3_qkv_buffer(nkm_qwen3* h, void** ptr, size_t* bytes) {

@@ -1770,7 +1770,9 @@ __device__ __forceinline__ void attention_cta_body(const Params& p, Ctx& c, int 
   if (do_k || do_v) {
     const uint2 val = do_k ? head_finish(kin, p.eps) : vv;
     *reinterpret_cast<uint2*>((do_k ? kn : vn) + 4 * lane) = val;
-    if (wblk >= 0 && wblk < p.num_blocks) {
+    if (p.stages & 16) {
+      // written by kv_prewrite before this stage
+    } else if (wblk >= 0 && wblk < p.num_blocks) {
       const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + wblk) * p.nkv + h) * kKvBlock * kHeadDim +
                          static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
       *reinterpret_cast<uint2*>((do_k ? p.k_pool : p.v_pool) + off) = val;
@@ -2027,6 +2029,41 @@ __device__ __noinline__ void attention_unplanned(const Params& p, Ctx& c, int la
   att_items(p, [&](int b, int h, int ch, int nch, int CT, int item, int pos) {
     attention_cta_item(p, c, layer, b, h, ch, nch, CT, item, pos, kNoBlocks, kmap, vmap);
   });
+}
+
+// Rows of one sequence at consecutive positions in one launch (multi-token decode, chunked
+// prefill; stages bit 16): every row's new K (q/k-norm + RoPE, the values stage B computes) and V
+// are stored into the cache before any attention reads it, so a row's context includes the rows
+// at earlier positions.  One warp per (row, kv head, K or V).
+__device__ __noinline__ void kv_prewrite(const Params& p, Ctx& c, int layer) {
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  const LayerPtrs& lw = c.lt[layer - p.first_layer];
+  const int n = p.T * p.nkv;
+#pragma unroll 1
+  for (int it = blockIdx.x * kWarps + warp; it < 2 * n; it += gridDim.x * kWarps) {
+    const int kind = it / n;
+    const int r = it - kind * n, b = r / p.nkv, h = r - b * p.nkv;
+    const int pos = seq_pos(p, b);
+    const int wblk = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + pos / kKvBlock);
+    const uint16_t* qkv_b = p.qkv + static_cast<size_t>(b) * p.R;
+    uint2 val;
+    if (kind == 0) {
+      const int prow = min(pos, p.rope_max - 1);
+      const HeadIn kin = head_load(qkv_b + static_cast<size_t>(p.nq + h) * kHeadDim, lw.kn,
+                                   p.rope_cos + static_cast<size_t>(prow) * kHeadDim,
+                                   p.rope_sin + static_cast<size_t>(prow) * kHeadDim);
+      val = head_finish(kin, p.eps);
+    } else {
+      val = ldcg64(qkv_b + static_cast<size_t>(p.nq + p.nkv + h) * kHeadDim + 4 * lane);
+    }
+    if (wblk >= 0 && wblk < p.num_blocks) {
+      const size_t off = ((static_cast<size_t>(layer) * p.num_blocks + wblk) * p.nkv + h) * kKvBlock * kHeadDim +
+                         static_cast<size_t>(pos % kKvBlock) * kHeadDim + 4 * lane;
+      *reinterpret_cast<uint2*>((kind == 0 ? p.k_pool : p.v_pool) + off) = val;
+    } else if (wblk >= p.num_blocks && lane == 0) {
+      set_status(p, kStatusIndex);
+    }
+  }
 }
 
 __device__ __noinline__ void attention_stage(const Params& p, Ctx& c, int layer, const CUtensorMap* kmap, const CUtensorMap* vmap) {
@@ -2569,7 +2606,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
         else gemv_stage<NT, GK_QKV>(p, c, ga);
       }
-      if (staged) {
+      if (p.stages & 16) {
+        // K/V of every row first (a grid barrier on each side), then the attention reads them
+        if (!grid_barrier(p, c)) return;
+        kv_prewrite(p, c, layer);
+        grid_arrive(p);
+        if (!grid_wait(p, c)) return;
+        fence_proxy_async_global();  // this launch's K/V stores, before the TMA reads of them
+        att_prime_layer(p, c, layer, &kmap, &vmap);
+      } else if (staged) {
         // stage B takes only q/k/v from other CTAs and waits for them element by element
         c.awaitq = 1;
         att_prime_layer(p, c, layer, &kmap, &vmap);

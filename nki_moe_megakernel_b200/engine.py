@@ -192,12 +192,14 @@ class Qwen3MoeMegakernel:
     def decode_step(self, positions: torch.Tensor, block_table: torch.Tensor, *, x: Optional[torch.Tensor] = None,
                     input_ids: Optional[torch.Tensor] = None, want_logits: bool = True, trace: bool = False,
                     first_layer: int = 0, num_layers: int = 0, out: Optional[Dict[str, torch.Tensor]] = None,
-                    stage_times: bool = False, stream=None) -> Dict[str, torch.Tensor]:
+                    stage_times: bool = False, kv_first: bool = False, stream=None) -> Dict[str, torch.Tensor]:
         """Run one decode step (all layers by default).  K/V pools are updated in place.
 
         Returns ``{"hidden": [B,H] bf16, "logits": [B,V] fp32 (if requested), traces...}``;
         ``stage_times`` adds ``stage_ns``: globaltimer stamps of CTA 0 at kernel start, after
-        every grid barrier and at kernel end.
+        every grid barrier and at kernel end.  ``kv_first``: rows may be consecutive positions of
+        one sequence (same block-table row); every row's K/V is written before the attention
+        reads the cache (``NKM_STAGE_KV_FIRST``: multi-token decode, chunked prefill).
         """
         B = int(positions.shape[0])
         nl = num_layers or (self.shape.num_hidden_layers - first_layer)
@@ -209,9 +211,12 @@ class Qwen3MoeMegakernel:
         traces = self._alloc_traces(B, nl) if trace else None
         if stage_times and not trace:
             traces = {"stage_ns": torch.zeros(3 + 6 * nl, dtype=torch.int64, device=self.device)}
+        if kv_first and traces:
+            traces.pop("stage_ns", None)  # the extra barriers of this mode are not stamped
         st = self._step_struct(B, x=x, input_ids=input_ids, positions=positions, block_table=block_table,
                                y=res["hidden"], logits=res.get("logits") if want_logits else None,
-                               first_layer=first_layer, num_layers=nl, traces=traces)
+                               first_layer=first_layer, num_layers=nl, traces=traces,
+                               stages=_lib.NKM_STAGE_KV_FIRST if kv_first else 0)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         check(lib().nkm_qwen3_decode_step(self._h, ctypes.byref(st), s.cuda_stream), "nkm_qwen3_decode_step")
         if traces:

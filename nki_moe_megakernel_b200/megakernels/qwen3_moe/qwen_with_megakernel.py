@@ -42,7 +42,8 @@ class Qwen3MoEV3MultilayerNeuronConfig:
                  max_context_length: Optional[int] = None, max_length: Optional[int] = None,
                  tp_degree: int = 1, moe_ep_degree: int = 1, moe_tp_degree: int = 1,
                  torch_dtype=BF16, pa_block_size: int = 128, pa_num_blocks: Optional[int] = None,
-                 top_k: int = 1, do_sample: bool = False, temperature: float = 1.0, **kwargs):
+                 top_k: int = 1, do_sample: bool = False, temperature: float = 1.0,
+                 prefill_chunk_size: int = 32, **kwargs):
         self.batch_size = batch_size
         self.max_batch_size = max_batch_size or batch_size
         self.seq_len = seq_len
@@ -58,6 +59,11 @@ class Qwen3MoEV3MultilayerNeuronConfig:
         self.top_k = top_k
         self.do_sample = do_sample
         self.temperature = temperature
+        # prompt tokens processed per launch (rows of one launch, at most 32): the kernel instance
+        # is sized for max(max_batch_size, prefill_chunk_size) rows
+        if not 1 <= prefill_chunk_size <= 32:
+            raise ValueError("prefill_chunk_size must be in 1..32")
+        self.prefill_chunk_size = prefill_chunk_size
         for k, v in kwargs.items():
             setattr(self, k, v)
         if torch_dtype not in (BF16, "bfloat16"):
@@ -310,14 +316,18 @@ class NeuronQwen3MoeForCausalLMV3:
             shape.num_attention_heads = len(self.shard.q_heads)
             shape.num_key_value_heads = len(self.shard.kv_heads)
             dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
-            self.xchg = XchgRegion(xchg_bytes(shape.hidden_size, nc.max_batch_size, self.shard.world),
+            self.xchg = XchgRegion(xchg_bytes(shape.hidden_size, self._rows(), self.shard.world),
                                    self.shard.rank, self.shard.world, dev_index)
-        self.kernel = Qwen3MoeMegakernel(shape, self._layers, max_batch=nc.max_batch_size,
+        self.kernel = Qwen3MoeMegakernel(shape, self._layers, max_batch=self._rows(),
                                          num_blocks=nc.pa_num_blocks, final_norm=self._head["final_norm"],
                                          lm_head=self._head["lm_head"], embed=self._head["embed"],
                                          rope_max_pos=max(self.config.max_position_embeddings, nc.max_length + 1),
                                          device=self.device, shard=self.shard, xchg=self.xchg)
         self.reset()
+
+    def _rows(self) -> int:
+        nc = self.neuron_config
+        return max(nc.max_batch_size, nc.prefill_chunk_size)
 
     def close(self):
         """Release the kernel instance and, on several GPUs, the exchange region (every rank
@@ -352,15 +362,35 @@ class NeuronQwen3MoeForCausalLMV3:
         res = self.kernel.decode_step(pos, self.block_table[:B], input_ids=ids)
         return res["logits"]
 
-    def teacher_forced_logits(self, tokens: Sequence[int]) -> torch.Tensor:
-        """Feed ``tokens`` one position per step (sequence 0) and return every step's logits
-        ``[len(tokens), vocab]`` fp32."""
-        self.reset()
+    def prefill(self, rows: Sequence[tuple], want_logits: bool = False) -> Optional[torch.Tensor]:
+        """Context encoding through the decode kernel: ``rows`` = (sequence, position, token id)
+        triples, processed ``prefill_chunk_size`` rows per launch.  Rows of one sequence at
+        consecutive positions share a launch: every row's K/V is written before the attention
+        reads the cache (``NKM_STAGE_KV_FIRST``), so each row attends causally to the rows
+        before it.  Returns the logits of every row ``[len(rows), vocab]`` if ``want_logits``.
+        (The reference keeps context encoding on the per-layer NxDI path,
+        ``qwen_with_megakernel.py:496-526``.)"""
+        if self.kernel is None:
+            raise RuntimeError("call load() first")
+        n = self.neuron_config.prefill_chunk_size
         out = []
-        for t, tok in enumerate(tokens):
-            out.append(self.forward(torch.tensor([tok], dtype=torch.int32), torch.tensor([t], dtype=torch.int32)))
+        for c0 in range(0, len(rows), n):
+            chunk = rows[c0:c0 + n]
+            ids = torch.tensor([r[2] for r in chunk], dtype=torch.int32, device=self.device)
+            pos = torch.tensor([r[1] for r in chunk], dtype=torch.int32, device=self.device)
+            table = self.block_table[torch.tensor([r[0] for r in chunk], device=self.device)].contiguous()
+            res = self.kernel.decode_step(pos, table, input_ids=ids, want_logits=want_logits, kv_first=True)
+            if want_logits:
+                out.append(res["logits"])
+        return torch.cat(out, 0) if want_logits and out else None
+
+    def teacher_forced_logits(self, tokens: Sequence[int]) -> torch.Tensor:
+        """Feed ``tokens`` (sequence 0, positions 0, 1, ...) through the chunked prefill and return
+        every position's logits ``[len(tokens), vocab]`` fp32."""
+        self.reset()
+        logits = self.prefill([(0, t, tok) for t, tok in enumerate(tokens)], want_logits=True)
         self.kernel.check_status()
-        return torch.cat(out, 0)
+        return logits
 
     def sample(self, logits: torch.Tensor, generator: Optional[torch.Generator] = None) -> torch.Tensor:
         nc = self.neuron_config
@@ -372,29 +402,30 @@ class NeuronQwen3MoeForCausalLMV3:
         return i.gather(-1, pick[:, None]).squeeze(-1)
 
     def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int) -> List[List[int]]:
-        """Greedy (or top-k) generation for a batch of token-id prompts.  Every step feeds each
-        sequence one token at its own position: prompt tokens first, then sampled tokens."""
+        """Greedy (or top-k) generation for a batch of token-id prompts: every prompt but its last
+        token through the chunked prefill, then one decode step per new token for the whole
+        batch (each sequence at its own position)."""
         self.reset()
         B = len(prompts)
         lens = [len(p) for p in prompts]
         if min(lens) == 0:
             raise ValueError("empty prompt")
+        if B > self.neuron_config.max_batch_size:
+            raise ValueError("more prompts than max_batch_size")
         total = max(lens) + max_new_tokens
         if total > self.neuron_config.max_length:
             raise ValueError("prompt + new tokens exceed max_length")
+        self.prefill([(b, t, int(tok)) for b, p in enumerate(prompts) for t, tok in enumerate(p[:-1])])
         outs: List[List[int]] = [[] for _ in range(B)]
-        cur = [p[0] for p in prompts]
-        pos = [0] * B
-        while any(len(o) < max_new_tokens for o in outs):
+        cur = [int(p[-1]) for p in prompts]
+        pos = [n - 1 for n in lens]
+        for _ in range(max_new_tokens):
             logits = self.forward(torch.tensor(cur, dtype=torch.int32), torch.tensor(pos, dtype=torch.int32))
             nxt = self.sample(logits).tolist()
             for b in range(B):
+                outs[b].append(int(nxt[b]))
+                cur[b] = int(nxt[b])
                 pos[b] += 1
-                if pos[b] < lens[b]:
-                    cur[b] = prompts[b][pos[b]]
-                elif len(outs[b]) < max_new_tokens:
-                    outs[b].append(int(nxt[b]))
-                    cur[b] = int(nxt[b])
         self.kernel.check_status()
         return outs
 

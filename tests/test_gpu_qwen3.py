@@ -342,3 +342,55 @@ def test_multilayer_step_teacher_forced(dev, B, ctx, n_layers):
                                   final_norm, lm_head, "fp32")
     r = O.compare(res["logits"].cpu(), ref_logits)
     assert r["max_abs"] <= ATOL and r["cosine"] >= COS, r
+
+
+def test_multi_token_rows_kv_first(dev):
+    """Rows of one sequence at consecutive positions in one launch (NKM_STAGE_KV_FIRST: chunked
+    prefill / multi-token decode): two sequences with 4 and 3 new tokens.  Every row's logits and
+    hidden state match the fp32 oracle run token by token (each token seeing the K/V of the
+    earlier ones), and the layer-0 K/V slots of all 7 tokens are bit-exact."""
+    from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
+
+    L = 2
+    cfg = qwen_cfg(n_layers=L, vocab=4096)
+    distinct = make_layers(cfg, 2, seed=61)
+    starts, counts = [300, 127], [4, 3]
+    NB = sum((s0 + n) // 128 + 1 for s0, n in zip(starts, counts)) + 2
+    k0, v0, table = make_kv(cfg, L, [s0 + n for s0, n in zip(starts, counts)], NB, seed=62)
+    g = torch.Generator().manual_seed(63)
+    final_norm = (1 + 0.02 * torch.randn(cfg.hidden, generator=g)).to(BF16)
+    lm_head = (0.02 * torch.randn(cfg.vocab, cfg.hidden, generator=g)).to(BF16)
+    rows = [(b, s0 + i) for b, (s0, n) in enumerate(zip(starts, counts)) for i in range(n)]
+    B = len(rows)
+    x = torch.randn(B, cfg.hidden, generator=g).to(BF16)
+    pos = torch.tensor([p for _, p in rows], dtype=torch.int32)
+    row_table = torch.stack([table[b] for b, _ in rows]).contiguous()
+    eng = Qwen3MoeMegakernel(shape_of(cfg, L, cfg.vocab), gpu_layers(distinct, dev), max_batch=B, num_blocks=NB,
+                             final_norm=final_norm.to(dev), lm_head=lm_head.to(dev))
+    eng.k_pool.copy_(k0.to(dev))
+    eng.v_pool.copy_(v0.to(dev))
+    res = eng.decode_step(pos.to(dev), row_table.to(dev), x=x.to(dev), trace=True, kv_first=True)
+    torch.cuda.synchronize()
+    assert eng.status() == 0
+    # token by token through the fp32 oracle (its caches are updated in place)
+    kc = [k0[i].clone() for i in range(L)]
+    vc = [v0[i].clone() for i in range(L)]
+    cos32, sin32 = O.rope_tables(4096, cfg.head_dim, cfg.rope_theta, torch.float32)
+    order = sorted(range(B), key=lambda r: rows[r][1])
+    for r in order:
+        b, p_ = rows[r]
+        h, lg = O.decode_step(x[r:r + 1], distinct, cfg, kc, vc, pos[r:r + 1], table[b:b + 1], cos32, sin32,
+                              final_norm, lm_head, "fp32")
+        _close(res["hidden"][r], h[0], what=f"hidden row {r}")
+        _close(res["logits"][r], lg[0], what=f"logits row {r}")
+    # layer 0 K/V slots: bit-exact from the kernel's own raw projections
+    cos, sin = O.rope_tables(4096, cfg.head_dim, cfg.rope_theta)
+    nq, nkv, D = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
+    kg, vg = eng.k_pool.cpu(), eng.v_pool.cpu()
+    for r, (b, p_) in enumerate(rows):
+        qkv = res["qkv"][0, r].cpu()
+        knew = O.head_norm_rope_faithful(qkv[nq * D:(nq + nkv) * D].view(nkv, D), distinct[0].k_norm, cos[p_],
+                                         sin[p_], cfg.rms_eps).to(BF16)
+        blk, off = int(table[b, p_ // 128]), p_ % 128
+        assert bits_equal(kg[0, blk, :, off], knew), r
+        assert bits_equal(vg[0, blk, :, off], qkv[(nq + nkv) * D:].view(nkv, D)), r
