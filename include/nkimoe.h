@@ -219,6 +219,29 @@ int nkm_qwen3_moe_block_noalloc(const nkm_qwen3_desc* desc, int32_t layer, const
 int nkm_pack_ft(const void* src, void* dst, int64_t rows, int64_t cols, int64_t count,
                 int32_t mode, nkm_stream_t stream);
 
+/* On-device sampling of the next token from LM-head logits (the on-device sampler the
+ * reference configures with OnDeviceSamplingConfig, global_topk capped to top_k:
+ * megakernels/qwen3_moe/qwen_with_megakernel.py:123-127, main.py:390-398). */
+typedef struct nkm_sample_params {
+  int32_t top_k;       /* 1: greedy (argmax; equal logits -> lowest token id); 2..64: sample   */
+  float top_p;         /* (0, 1]: keep the shortest prefix of the top-k (by probability, after
+                          temperature) whose mass reaches top_p                               */
+  float temperature;   /* > 0: logits are multiplied by 1/temperature before the softmax      */
+  uint64_t seed;       /* uniform draw u = SplitMix64(seed ^ position << 32 ^ row) top 24 bits */
+} nkm_sample_params;
+
+/* Bytes of device scratch nkm_sample_logits needs (8-byte aligned; 0 for invalid sizes). */
+size_t nkm_sample_workspace_bytes(int32_t batch, int32_t vocab, int32_t top_k);
+
+/* tokens_out[b] (device int32) <- a token drawn from row b of logits (device fp32 [batch, vocab]):
+ * the top_k largest logits (ties -> lower token id), softmax at temperature, top-p prefix,
+ * inverse-CDF draw with the row's uniform (positions: device int32 [batch] or NULL = 0).  Two
+ * kernel launches on `stream`; workspace of nkm_sample_workspace_bytes.  Returns NKM_ERR_ARG for
+ * bad parameters. */
+int nkm_sample_logits(const float* logits, int32_t batch, int32_t vocab, const nkm_sample_params* params,
+                      const int32_t* positions, int32_t* tokens_out, void* workspace, size_t workspace_bytes,
+                      nkm_stream_t stream);
+
 /* Message for the last error returned on this thread ("" if none). */
 const char* nkm_last_error(void);
 

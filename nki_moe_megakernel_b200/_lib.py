@@ -53,6 +53,10 @@ class nkm_qwen3_step(ctypes.Structure):
                 ("trace_resid_mid", c_void_p), ("trace_resid_out", c_void_p), ("trace_stage_ns", c_void_p)]
 
 
+class nkm_sample_params(ctypes.Structure):
+    _fields_ = [("top_k", c_int32), ("top_p", c_float), ("temperature", c_float), ("seed", ctypes.c_uint64)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/nkimoe.h
 SIGNATURES = {
     "nkm_qwen3_workspace_bytes": (c_size_t, [POINTER(nkm_qwen3_desc)]),
@@ -67,6 +71,9 @@ SIGNATURES = {
     "nkm_qwen3_moe_block_noalloc": (c_int, [POINTER(nkm_qwen3_desc), c_int32, POINTER(nkm_qwen3_step), c_void_p,
                                             c_void_p]),
     "nkm_pack_ft": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
+    "nkm_sample_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "nkm_sample_logits": (c_int, [c_void_p, c_int32, c_int32, POINTER(nkm_sample_params), c_void_p, c_void_p,
+                                  c_void_p, c_size_t, c_void_p]),
     "nkm_last_error": (c_char_p, []),
     "nkm_version": (c_char_p, []),
 }

@@ -202,6 +202,10 @@ int ensure_smem_limits() {
 
 }  // namespace
 
+namespace nkm {
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace nkm
+
 struct nkm_qwen3 {
   nkm_qwen3_desc desc;
   std::vector<nkm_qwen3_layer> layers;

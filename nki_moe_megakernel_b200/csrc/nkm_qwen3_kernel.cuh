@@ -667,7 +667,6 @@ __device__ __forceinline__ int worker_of(int u, int NU, int NW) {
 template <int NT, int KIND>
 __device__ __noinline__ bool gemv_flush(const Params& p, const Route* rt, const GemvGeom& G, int worker, int seg,
                                         int strip, bool full, int u0, int NU, int NWe, Acc<NT> acc) {
-  constexpr int kind = KIND;
   if (full) {
     gemv_epilogue<NT, KIND>(p, rt, G, seg, strip, acc);
     return true;

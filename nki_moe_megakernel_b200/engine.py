@@ -62,6 +62,27 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, device) -> tuple:
     return emb.cos().to(BF16).to(device), emb.sin().to(BF16).to(device)
 
 
+def sample_tokens(logits: torch.Tensor, positions: Optional[torch.Tensor] = None, *, top_k: int = 1,
+                  top_p: float = 1.0, temperature: float = 1.0, seed: int = 0,
+                  workspace: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                  stream=None) -> torch.Tensor:
+    """Next tokens ``[B]`` int32 drawn on the device from ``logits [B, V]`` fp32
+    (``nkm_sample_logits``): the top_k largest logits, temperature, top_p prefix, a SplitMix64
+    uniform per (seed, row, position); ``top_k`` = 1 is greedy."""
+    B, V = int(logits.shape[0]), int(logits.shape[1])
+    need = lib().nkm_sample_workspace_bytes(B, V, top_k)
+    if need == 0:
+        raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_sample_workspace_bytes")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=logits.device)
+    tokens = out if out is not None else torch.empty(B, dtype=torch.int32, device=logits.device)
+    params = _lib.nkm_sample_params(top_k, top_p, temperature, seed)
+    s = stream if stream is not None else torch.cuda.current_stream(logits.device)
+    check(lib().nkm_sample_logits(logits.data_ptr(), B, V, ctypes.byref(params), _ptr(positions), tokens.data_ptr(),
+                                  workspace.data_ptr(), workspace.numel(), s.cuda_stream), "nkm_sample_logits")
+    return tokens
+
+
 class GpuLayer:
     """One decoder layer's weights in the kernel layouts (device tensors)."""
 
@@ -241,6 +262,18 @@ class Qwen3MoeMegakernel:
         if traces:
             res.update(traces)
         return res
+
+    def sample(self, logits: torch.Tensor, positions: Optional[torch.Tensor] = None, *, top_k: int = 1,
+               top_p: float = 1.0, temperature: float = 1.0, seed: int = 0, out: Optional[torch.Tensor] = None,
+               stream=None) -> torch.Tensor:
+        """Next tokens ``[B]`` int32 drawn on the device from ``logits [B, V]`` fp32 (see
+        ``sample_tokens``); the sampler's scratch is kept with the instance."""
+        need = lib().nkm_sample_workspace_bytes(int(logits.shape[0]), int(logits.shape[1]), top_k)
+        ws = getattr(self, "_sample_ws", None)
+        if ws is None or ws.numel() < need:
+            ws = self._sample_ws = torch.empty(max(need, 8), dtype=torch.uint8, device=self.device)
+        return sample_tokens(logits, positions, top_k=top_k, top_p=top_p, temperature=temperature, seed=seed,
+                             workspace=ws, out=out, stream=stream)
 
     def qkv_buffer(self) -> torch.Tensor:
         """The handle's QKV buffer as a bf16 tensor ``[max_batch, (nq + 2 nkv) * head_dim]`` (a view

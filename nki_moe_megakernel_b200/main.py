@@ -49,6 +49,9 @@ def parse_args(argv=None):
     p.add_argument("--top-k", type=int, default=1)
     p.add_argument("--do-sample", action="store_true")
     p.add_argument("--temperature", type=float, default=1.0)
+    p.add_argument("--top-p", type=float, default=1.0)
+    p.add_argument("--on-device-sampling", action="store_true",
+                   help="accepted for command-line compatibility; tokens are always sampled on the device")
     p.add_argument("--tol-map", default=DEFAULT_TOL_MAP)
     p.add_argument("--num-tokens-to-check", type=int, default=None)
     p.add_argument("--divergence-difference-tol", type=float, default=0.001)
@@ -111,7 +114,7 @@ def prepare_inference(model_cls, args):
     mod = importlib.import_module(model_cls.__module__)
     ncfg = ncfg_cls(batch_size=args.batch_size, max_batch_size=args.batch_size, seq_len=args.seq_len,
                     max_length=args.seq_len, pa_block_size=args.pa_block_size, pa_num_blocks=args.pa_num_blocks,
-                    top_k=args.top_k, do_sample=args.do_sample, temperature=args.temperature,
+                    top_k=args.top_k, do_sample=args.do_sample, temperature=args.temperature, top_p=args.top_p,
                     tp_degree=getattr(args, "tp_degree", None) or 1,
                     moe_ep_degree=getattr(args, "moe_ep_degree", None) or 1,
                     moe_tp_degree=getattr(args, "moe_tp_degree", 1))

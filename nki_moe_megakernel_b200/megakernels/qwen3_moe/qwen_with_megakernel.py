@@ -392,14 +392,15 @@ class NeuronQwen3MoeForCausalLMV3:
         self.kernel.check_status()
         return logits
 
-    def sample(self, logits: torch.Tensor, generator: Optional[torch.Generator] = None) -> torch.Tensor:
+    def sample(self, logits: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        """Next tokens on the device (``nkm_sample_logits``): greedy unless ``do_sample``, else
+        top-k (capped to 64, as the reference caps ``global_topk`` to ``top_k``,
+        ``qwen_with_megakernel.py:123-127``), temperature and ``top_p``."""
         nc = self.neuron_config
-        if not nc.do_sample or nc.top_k <= 1:
-            return logits.argmax(-1)
-        v, i = torch.topk(logits / max(nc.temperature, 1e-5), nc.top_k, dim=-1)
-        probs = torch.softmax(v, -1)
-        pick = torch.multinomial(probs, 1, generator=generator).squeeze(-1)
-        return i.gather(-1, pick[:, None]).squeeze(-1)
+        greedy = not nc.do_sample or nc.top_k <= 1
+        return self.kernel.sample(logits, positions.to(self.device, torch.int32),
+                                  top_k=1 if greedy else min(nc.top_k, 64), top_p=float(getattr(nc, "top_p", 1.0)),
+                                  temperature=float(nc.temperature), seed=self.seed)
 
     def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int) -> List[List[int]]:
         """Greedy (or top-k) generation for a batch of token-id prompts: every prompt but its last
@@ -420,8 +421,9 @@ class NeuronQwen3MoeForCausalLMV3:
         cur = [int(p[-1]) for p in prompts]
         pos = [n - 1 for n in lens]
         for _ in range(max_new_tokens):
-            logits = self.forward(torch.tensor(cur, dtype=torch.int32), torch.tensor(pos, dtype=torch.int32))
-            nxt = self.sample(logits).tolist()
+            pos_t = torch.tensor(pos, dtype=torch.int32)
+            logits = self.forward(torch.tensor(cur, dtype=torch.int32), pos_t)
+            nxt = self.sample(logits, pos_t).tolist()
             for b in range(B):
                 outs[b].append(int(nxt[b]))
                 cur[b] = int(nxt[b])
