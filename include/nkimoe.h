@@ -242,6 +242,105 @@ int nkm_sample_logits(const float* logits, int32_t batch, int32_t vocab, const n
                       const int32_t* positions, int32_t* tokens_out, void* workspace, size_t workspace_bytes,
                       nkm_stream_t stream);
 
+/* ======================================================================================
+ * GPT-OSS decode step (the reference's second megakernel,
+ * megakernels/gpt_oss/transformer_gpt_oss.py:240-530, model class
+ * megakernels/gpt_oss/gpt_oss_with_megakernel.py): sliding-window / full attention with
+ * learned sinks, QKV and O-projection biases, YaRN RoPE, top-k softmax router with bias,
+ * MXFP4 experts with biases and the clamped SwiGLU.  Head dim 64, batch <= 16.
+ * ====================================================================================== */
+typedef struct nkm_gptoss_layer {
+  const void* wqkv_ft;     /* bf16 FT [(nq+2nkv)*64, H]: q heads, k heads, v heads          */
+  const void* bqkv;        /* bf16 [(nq+2nkv)*64]                                           */
+  const void* wo_ft;       /* bf16 FT [H, nq*64]                                            */
+  const void* bo;          /* bf16 [H]                                                      */
+  const void* sinks;       /* bf16 [nq] learned sink logits                                 */
+  const void* ln1;         /* bf16 [H]                                                      */
+  const void* ln2;         /* bf16 [H]                                                      */
+  const void* router;      /* bf16 [E, H] row-major                                         */
+  const void* router_bias; /* bf16 [E]                                                      */
+  const void* w13_fp4;     /* nkm_pack_mxfp4 weights of gate/up [E][2I, H] (row 2i gate i,
+                              row 2i+1 up i: Hugging Face's interleaved gate_up_proj)       */
+  const void* s13;         /* nkm_pack_mxfp4 scales of gate/up                              */
+  const void* b13;         /* bf16 [E][2I]                                                  */
+  const void* w2_fp4;      /* nkm_pack_mxfp4 weights of down [E][H, I]                      */
+  const void* s2;          /* nkm_pack_mxfp4 scales of down                                 */
+  const void* b2;          /* bf16 [E][H]                                                   */
+  int32_t sliding;         /* 1: sliding-window attention (window sliding_window)           */
+} nkm_gptoss_layer;
+
+typedef struct nkm_gptoss_desc {
+  int32_t hidden;          /* H: multiple of 32, <= 4096 (2880)                              */
+  int32_t hidden_actual;   /* RMSNorm mean over this many elements (rows padded with zeros
+                              beyond it, rmsnorm_tkg.py:49-147 hidden_actual); 0 = hidden   */
+  int32_t n_q_heads;       /* 64 */
+  int32_t n_kv_heads;      /* 8  */
+  int32_t head_dim;        /* must be 64 */
+  int32_t n_experts;       /* <= 128 (32) */
+  int32_t top_k;           /* <= 8 (4) */
+  int32_t inter;           /* I: multiple of 32, <= 4096 (2880) */
+  int32_t n_layers;
+  int32_t vocab;           /* multiple of 16 (201088) */
+  float rms_eps;           /* 1e-5 */
+  float swiglu_limit;      /* 7.0: gate <= limit, up in [-limit, limit] */
+  float swiglu_alpha;      /* 1.702 */
+  int32_t sliding_window;  /* W (128): a sliding layer sees the last W-1 tokens and the new one */
+  const nkm_gptoss_layer* layers;
+  const void* final_norm;  /* bf16 [H] */
+  const void* lm_head_ft;  /* bf16 FT [V, H] */
+  const void* embed;       /* bf16 [V, H] */
+  const float* rope_cos;   /* fp32 [rope_max_pos, 32] (YaRN, attention factor applied) */
+  const float* rope_sin;
+  int32_t rope_max_pos;
+  void* k_pool;            /* bf16 [L][num_blocks][nkv][128 tokens][64]                     */
+  void* v_pool;            /* bf16 [L][num_blocks][nkv][64][128 tokens] (blocks transposed) */
+  int32_t num_blocks;
+  int32_t block_size;      /* must be 128 */
+  int32_t max_batch;       /* <= 16 */
+  int32_t max_context;     /* longest context (tokens) any step will attend to */
+} nkm_gptoss_desc;
+
+typedef struct nkm_gptoss_step {
+  int32_t batch;
+  const int32_t* input_ids;    /* device [B] or NULL (then x_in) */
+  const void* x_in;            /* device bf16 [B, H] */
+  const int32_t* positions;    /* device [B] */
+  const int32_t* block_table;  /* device [B, max_blocks_per_seq]; -1 at the write slot skips the write */
+  int32_t max_blocks_per_seq;
+  void* y_out;                 /* device bf16 [B, H] hidden after the last layer (pre final norm) */
+  float* logits_out;           /* device fp32 [B, V] or NULL */
+  int32_t first_layer;
+  int32_t num_layers;          /* 0 = all */
+  float* trace_qkv;            /* fp32 [nl, B, (nq+2nkv)*64] projections + bias, before RoPE */
+  float* trace_resid_mid;      /* fp32 [nl, B, H] */
+  float* trace_resid_out;      /* fp32 [nl, B, H] */
+  float* trace_router_logits;  /* fp32 [nl, B, E] */
+  int32_t* trace_topk_idx;     /* [nl, B, K] */
+  float* trace_topk_w;         /* [nl, B, K] */
+} nkm_gptoss_step;
+
+typedef struct nkm_gptoss nkm_gptoss;
+
+/* Workspace bytes of a GPT-OSS handle (caller allocates, 256-byte aligned). */
+size_t nkm_gptoss_workspace_bytes(const nkm_gptoss_desc* desc);
+/* Replaces compile()/load() of the reference's GPT-OSS model (gpt_oss_with_megakernel.py). */
+int nkm_gptoss_create(const nkm_gptoss_desc* desc, void* workspace, size_t workspace_bytes, nkm_gptoss** out);
+void nkm_gptoss_destroy(nkm_gptoss* h);
+/* One decode step, one cooperative launch.  Replaces
+ * get_multilayer_kernel_jit(L, mxfp4)(X, Wqkv_*, bqkv_*, Wo_*, bo_*, Sink_*, ..., K_*, V_*, cos, sin,
+ * position_ids, position_ids_window) (transformer_gpt_oss.py:540-636). */
+int nkm_gptoss_decode_step(nkm_gptoss* h, const nkm_gptoss_step* step, nkm_stream_t stream);
+/* Synchronise and return (and clear) the device status word. */
+int nkm_gptoss_status(nkm_gptoss* h, nkm_stream_t stream);
+
+/* MXFP4 weight packer (load time).  codes: uint8 [count][rows][cols] e2m1 codes 0..15 (bit 3 sign;
+ * Hugging Face's *_blocks unpacked low nibble first), scales: uint8 [count][rows][cols/32] e8m0.
+ * dst_w receives count*rows*cols/2 bytes, dst_s count*rows*cols/32 bytes, in the kernel's tiled
+ * order.  rows % 16 == 0, cols % 32 == 0.  Replaces the MX layout conversion of
+ * gpt_oss_with_megakernel.py:290-327 / selective_expert_mx_impl.py:60. */
+int nkm_pack_mxfp4(const void* codes, const void* scales, void* dst_w, void* dst_s, int64_t rows, int64_t cols,
+                   int64_t count, nkm_stream_t stream);
+
 /* Message for the last error returned on this thread ("" if none). */
 const char* nkm_last_error(void);
 

@@ -53,6 +53,31 @@ class nkm_qwen3_step(ctypes.Structure):
                 ("trace_resid_mid", c_void_p), ("trace_resid_out", c_void_p), ("trace_stage_ns", c_void_p)]
 
 
+class nkm_gptoss_layer(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("wqkv_ft", "bqkv", "wo_ft", "bo", "sinks", "ln1", "ln2", "router",
+                                        "router_bias", "w13_fp4", "s13", "b13", "w2_fp4", "s2", "b2")] + \
+        [("sliding", c_int32)]
+
+
+class nkm_gptoss_desc(ctypes.Structure):
+    _fields_ = [("hidden", c_int32), ("hidden_actual", c_int32), ("n_q_heads", c_int32), ("n_kv_heads", c_int32),
+                ("head_dim", c_int32), ("n_experts", c_int32), ("top_k", c_int32), ("inter", c_int32),
+                ("n_layers", c_int32), ("vocab", c_int32), ("rms_eps", c_float), ("swiglu_limit", c_float),
+                ("swiglu_alpha", c_float), ("sliding_window", c_int32), ("layers", POINTER(nkm_gptoss_layer)),
+                ("final_norm", c_void_p), ("lm_head_ft", c_void_p), ("embed", c_void_p),
+                ("rope_cos", POINTER(c_float)), ("rope_sin", POINTER(c_float)), ("rope_max_pos", c_int32),
+                ("k_pool", c_void_p), ("v_pool", c_void_p), ("num_blocks", c_int32), ("block_size", c_int32),
+                ("max_batch", c_int32), ("max_context", c_int32)]
+
+
+class nkm_gptoss_step(ctypes.Structure):
+    _fields_ = [("batch", c_int32), ("input_ids", c_void_p), ("x_in", c_void_p), ("positions", c_void_p),
+                ("block_table", c_void_p), ("max_blocks_per_seq", c_int32), ("y_out", c_void_p),
+                ("logits_out", c_void_p), ("first_layer", c_int32), ("num_layers", c_int32),
+                ("trace_qkv", c_void_p), ("trace_resid_mid", c_void_p), ("trace_resid_out", c_void_p),
+                ("trace_router_logits", c_void_p), ("trace_topk_idx", c_void_p), ("trace_topk_w", c_void_p)]
+
+
 class nkm_sample_params(ctypes.Structure):
     _fields_ = [("top_k", c_int32), ("top_p", c_float), ("temperature", c_float), ("seed", ctypes.c_uint64)]
 
@@ -74,6 +99,12 @@ SIGNATURES = {
     "nkm_sample_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "nkm_sample_logits": (c_int, [c_void_p, c_int32, c_int32, POINTER(nkm_sample_params), c_void_p, c_void_p,
                                   c_void_p, c_size_t, c_void_p]),
+    "nkm_gptoss_workspace_bytes": (c_size_t, [POINTER(nkm_gptoss_desc)]),
+    "nkm_gptoss_create": (c_int, [POINTER(nkm_gptoss_desc), c_void_p, c_size_t, POINTER(c_void_p)]),
+    "nkm_gptoss_destroy": (None, [c_void_p]),
+    "nkm_gptoss_decode_step": (c_int, [c_void_p, POINTER(nkm_gptoss_step), c_void_p]),
+    "nkm_gptoss_status": (c_int, [c_void_p, c_void_p]),
+    "nkm_pack_mxfp4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "nkm_last_error": (c_char_p, []),
     "nkm_version": (c_char_p, []),
 }

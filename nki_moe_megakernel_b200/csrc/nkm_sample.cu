@@ -129,7 +129,10 @@ __global__ void __launch_bounds__(kThreads) sample_candidates_kernel(const float
   const uint64_t kth = radix_kth(n, K, get, hist, scan, sel);
   for (int i = threadIdx.x; i < n; i += kThreads) {
     const uint64_t c = get(i);
-    if (c >= kth) out[atomicAdd(&nout, 1u)] = c;  // exactly K entries (the composites are distinct)
+    if (c >= kth) {  // exactly K entries (the composites are distinct); the guard only bounds the store
+      const unsigned j = atomicAdd(&nout, 1u);
+      if (j < static_cast<unsigned>(K)) out[j] = c;
+    }
   }
 }
 
@@ -152,7 +155,10 @@ __global__ void __launch_bounds__(kThreads) sample_pick_kernel(const uint64_t* _
   auto get = [&](int i) { return c[i]; };
   const uint64_t kth = radix_kth(M, kk, get, hist, scan, sel);
   for (int i = threadIdx.x; i < M; i += kThreads)
-    if (c[i] >= kth && c[i] != 0ull) top[atomicAdd(&nout, 1u)] = c[i];
+    if (c[i] >= kth && c[i] != 0ull) {
+      const unsigned j = atomicAdd(&nout, 1u);
+      if (j < static_cast<unsigned>(kk)) top[j] = c[i];
+    }
   __syncthreads();
   // rank sort of the kk winners (descending)
   uint64_t mine = 0ull;

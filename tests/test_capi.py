@@ -118,3 +118,53 @@ def test_pack_rejects_bad_shapes(L):
     assert f(16, 16, 15, 32, 1, 0, None) == L.NKM_ERR_ARG
     assert f(16, 16, 16, 30, 1, 0, None) == L.NKM_ERR_ARG
     assert f(16, 16, 16, 32, 1, 7, None) == L.NKM_ERR_ARG
+
+
+def test_gptoss_structs_match_c_layout(L):
+    prog = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "nkimoe.h"
+int main(void) {
+  printf("layer %zu\n", sizeof(nkm_gptoss_layer));
+  printf("desc %zu\n", sizeof(nkm_gptoss_desc));
+  printf("step %zu\n", sizeof(nkm_gptoss_step));
+  printf("sample %zu\n", sizeof(nkm_sample_params));
+  printf("desc.layers %zu\n", offsetof(nkm_gptoss_desc, layers));
+  printf("desc.max_context %zu\n", offsetof(nkm_gptoss_desc, max_context));
+  printf("step.trace_topk_w %zu\n", offsetof(nkm_gptoss_step, trace_topk_w));
+  printf("layer.sliding %zu\n", offsetof(nkm_gptoss_layer, sliding));
+  return 0;
+}
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        open(c, "w").write(prog)
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = dict(line.rsplit(" ", 1) for line in out if line)
+    assert int(got["layer"]) == ctypes.sizeof(L.nkm_gptoss_layer)
+    assert int(got["desc"]) == ctypes.sizeof(L.nkm_gptoss_desc)
+    assert int(got["step"]) == ctypes.sizeof(L.nkm_gptoss_step)
+    assert int(got["sample"]) == ctypes.sizeof(L.nkm_sample_params)
+    assert int(got["desc.layers"]) == L.nkm_gptoss_desc.layers.offset
+    assert int(got["desc.max_context"]) == L.nkm_gptoss_desc.max_context.offset
+    assert int(got["step.trace_topk_w"]) == L.nkm_gptoss_step.trace_topk_w.offset
+    assert int(got["layer.sliding"]) == L.nkm_gptoss_layer.sliding.offset
+
+
+def test_gptoss_create_rejects_bad_descriptions(L):
+    for bad in (dict(head_dim=128), dict(hidden=2000), dict(max_batch=17), dict(top_k=9), dict(inter=100)):
+        base = dict(hidden=2880, hidden_actual=0, n_q_heads=64, n_kv_heads=8, head_dim=64, n_experts=32, top_k=4,
+                    inter=2880, n_layers=1, vocab=0, rms_eps=1e-5, swiglu_limit=7.0, swiglu_alpha=1.702,
+                    sliding_window=128, block_size=128, max_batch=16, max_context=4096)
+        base.update(bad)
+        d = L.nkm_gptoss_desc()
+        for k, v in base.items():
+            setattr(d, k, v)
+        layer = (L.nkm_gptoss_layer * 1)()
+        d.layers = layer
+        h = ctypes.c_void_p()
+        assert L.lib().nkm_gptoss_create(ctypes.byref(d), None, 0, ctypes.byref(h)) == L.NKM_ERR_ARG, bad
+        assert L.lib().nkm_gptoss_workspace_bytes(ctypes.byref(d)) == 0
