@@ -30,6 +30,7 @@ import torch
 
 _MODEL_REGISTRY = {
     "qwen3_moe": ("nki_moe_megakernel_b200.megakernels.qwen3_moe.qwen_with_megakernel", "NeuronQwen3MoeForCausalLM"),
+    "gpt_oss": ("nki_moe_megakernel_b200.megakernels.gpt_oss.gpt_oss_with_megakernel", "NeuronGptOssForCausalLM"),
 }
 DEFAULT_TOL_MAP = "{None: (1e-5, 0.05), 1000: (1e-5, 0.03), 50: (1e-5, 0.03), 5: (1e-5, 0.03)}"
 
@@ -139,8 +140,44 @@ def run_generation(model, tokenizer, prompts: List[str], max_new_tokens: int):
 
 
 # ---------------------------------------------------------------------------
+def hf_baseline_gpt_oss(model):
+    """HF GptOssForCausalLM (fp32) with exactly the megakernel's weights (MXFP4 experts
+    dequantised)."""
+    from transformers import GptOssConfig, GptOssForCausalLM  # noqa: PLC0415
+
+    from .megakernels.gpt_oss.gpt_oss_with_megakernel import mxfp4_dequant, unpack_mxfp4_blocks  # noqa: PLC0415
+
+    c = model.config
+    hc = GptOssConfig(vocab_size=c.vocab_size, hidden_size=c.hidden_size, intermediate_size=c.intermediate_size,
+                      num_hidden_layers=c.num_hidden_layers, num_attention_heads=c.num_attention_heads,
+                      num_key_value_heads=c.num_key_value_heads, head_dim=c.head_dim,
+                      num_local_experts=c.num_local_experts, num_experts_per_tok=c.num_experts_per_tok,
+                      sliding_window=c.sliding_window, rms_norm_eps=c.rms_norm_eps, tie_word_embeddings=False,
+                      max_position_embeddings=c.max_position_embeddings, rope_parameters=dict(c.rope_parameters),
+                      layer_types=list(c.layer_types))
+    hc._attn_implementation = "eager"
+    with torch.device(model.device):
+        hf = GptOssForCausalLM(hc).to(torch.float32).eval()
+    sd = {}
+    raw = model.hf_state_dict()
+    for k, v in raw.items():
+        if k.endswith("_blocks"):
+            base = k[: -len("_blocks")]
+            w = mxfp4_dequant(unpack_mxfp4_blocks(v), raw[base + "_scales"])
+            sd[base] = w.transpose(-1, -2).float()
+        elif not k.endswith("_scales"):
+            sd[k] = v.float()
+    missing, _ = hf.load_state_dict(sd, strict=False)
+    if missing:
+        raise RuntimeError(f"baseline weights missing: {missing[:4]}")
+    return hf
+
+
 def hf_baseline(model):
-    """HF Qwen3MoeForCausalLM (fp32) with exactly the megakernel's weights."""
+    """HF Qwen3MoeForCausalLM (fp32) with exactly the megakernel's weights (GPT-OSS models:
+    ``hf_baseline_gpt_oss``)."""
+    if type(model).__name__ == "NeuronGptOssForCausalLM":
+        return hf_baseline_gpt_oss(model)
     from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM  # noqa: PLC0415
 
     c = model.config

@@ -214,3 +214,14 @@ def test_padded_hidden_matches_unpadded(dev):
     r = G.compare(outs[1][1], outs[0][1])
     assert r["max_abs"] <= 2e-3 and r["cosine"] >= 0.99999, r
     assert bool((torch.zeros(1) == 0).all())
+
+
+def test_model_class_validate_against_hf():
+    """``main.py --model gpt_oss --mode validate`` on a 2-layer random-init GPT-OSS-20B-shaped
+    model (MXFP4 experts): the megakernel's teacher-forced logits pass the reference's tolerance
+    map against Hugging Face ``GptOssForCausalLM`` (fp32) with the same weights."""
+    from nki_moe_megakernel_b200 import main as drv
+
+    rc = drv.main(["--model", "gpt_oss", "--mode", "validate", "--enable-nki", "--num-layers", "2", "--seq-len", "160",
+                   "--num-tokens-to-check", "6", "--prompt", "I believe the meaning of life is"])
+    assert rc == 0
