@@ -243,6 +243,39 @@ int nkm_sample_logits(const float* logits, int32_t batch, int32_t vocab, const n
                       nkm_stream_t stream);
 
 /* ======================================================================================
+ * MoE block on the 5th-generation tensor cores (tcgen05 + TMEM grouped GEMM), for batches
+ * whose tokens give the experts several columns each (config 3: 64 tokens x top-8 over 128
+ * experts).  Same arithmetic as nkm_qwen3_moe_block (RMSNorm(ln2), fp32 router logits in the
+ * same fixed order, top-k on the logits, softmax at the top-k, bf16 renormalisation, bf16
+ * SwiGLU, fp32 down projection times the routing weight); the expert outputs of a token are
+ * summed in slot order.  Replaces moe_tkg's selective-expert path for dense token counts
+ * (nki_kernels/moe/moe_tkg.py:56-293, selective_expert_impl.py:84-520).
+ * ====================================================================================== */
+typedef struct nkm_moe_tc_desc {
+  int32_t hidden;             /* H: multiple of 256 */
+  int32_t n_experts;          /* <= 256 */
+  int32_t top_k;              /* <= 8 */
+  int32_t moe_inter;          /* I: multiple of 64 */
+  float rms_eps;
+  const void* ln2;            /* bf16 [H] */
+  const void* router;         /* bf16 [E, H] */
+  const float* router_bias;   /* fp32 [E] or NULL */
+  const void* w13;            /* bf16 [E][2I][H] row-major: gate rows then up rows (HF gate_up_proj) */
+  const void* w2;             /* bf16 [E][H][I] row-major (HF down_proj) */
+  int32_t max_tokens;         /* <= 512 */
+} nkm_moe_tc_desc;
+
+/* Workspace bytes (256-byte aligned; the first 4 bytes are the call's status word). */
+size_t nkm_moe_tc_workspace_bytes(const nkm_moe_tc_desc* desc);
+/* y_out = MoE(x_in) (+ x_in if residual) for `tokens` rows; topk_idx_out / topk_w_out (device
+ * [tokens, top_k], may be NULL) receive the routing.  Six launches on `stream`. */
+int nkm_moe_block_tc(const nkm_moe_tc_desc* desc, int32_t tokens, const void* x_in, void* y_out, int32_t residual,
+                     int32_t* topk_idx_out, float* topk_w_out, void* workspace, size_t workspace_bytes,
+                     nkm_stream_t stream);
+/* Synchronise and return the status word of the last call on this workspace (0 = ok). */
+int nkm_moe_tc_status(void* workspace, nkm_stream_t stream);
+
+/* ======================================================================================
  * GPT-OSS decode step (the reference's second megakernel,
  * megakernels/gpt_oss/transformer_gpt_oss.py:240-530, model class
  * megakernels/gpt_oss/gpt_oss_with_megakernel.py): sliding-window / full attention with

@@ -78,6 +78,12 @@ class nkm_gptoss_step(ctypes.Structure):
                 ("trace_router_logits", c_void_p), ("trace_topk_idx", c_void_p), ("trace_topk_w", c_void_p)]
 
 
+class nkm_moe_tc_desc(ctypes.Structure):
+    _fields_ = [("hidden", c_int32), ("n_experts", c_int32), ("top_k", c_int32), ("moe_inter", c_int32),
+                ("rms_eps", c_float), ("ln2", c_void_p), ("router", c_void_p), ("router_bias", c_void_p),
+                ("w13", c_void_p), ("w2", c_void_p), ("max_tokens", c_int32)]
+
+
 class nkm_sample_params(ctypes.Structure):
     _fields_ = [("top_k", c_int32), ("top_p", c_float), ("temperature", c_float), ("seed", ctypes.c_uint64)]
 
@@ -105,6 +111,10 @@ SIGNATURES = {
     "nkm_gptoss_decode_step": (c_int, [c_void_p, POINTER(nkm_gptoss_step), c_void_p]),
     "nkm_gptoss_status": (c_int, [c_void_p, c_void_p]),
     "nkm_pack_mxfp4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "nkm_moe_tc_workspace_bytes": (c_size_t, [POINTER(nkm_moe_tc_desc)]),
+    "nkm_moe_block_tc": (c_int, [POINTER(nkm_moe_tc_desc), c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
+                                 c_void_p, c_size_t, c_void_p]),
+    "nkm_moe_tc_status": (c_int, [c_void_p, c_void_p]),
     "nkm_last_error": (c_char_p, []),
     "nkm_version": (c_char_p, []),
 }

@@ -307,3 +307,41 @@ class Qwen3MoeMegakernel:
         st = self.status(stream)
         if st != 0:
             raise _lib.NkmError(st, "decode kernel")
+
+
+class MoeTcBlock:
+    """The MoE block on tcgen05/TMEM grouped GEMMs (``nkm_moe_block_tc``) for token counts that
+    give the experts several columns each (config 3 and larger batches).  Weights in the plain
+    Hugging Face layouts: gate_up ``[E, 2I, H]`` (gate rows then up rows), down ``[E, H, I]``."""
+
+    def __init__(self, ln2: torch.Tensor, router: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, *,
+                 eps: float, top_k: int, max_tokens: int, router_bias: Optional[torch.Tensor] = None, device=None):
+        self.device = torch.device(device if device is not None else "cuda")
+        self.ln2 = ln2.to(self.device, BF16).contiguous()
+        self.router = router.to(self.device, BF16).contiguous()
+        self.w13 = gate_up.to(self.device, BF16).contiguous()
+        self.w2 = down.to(self.device, BF16).contiguous()
+        self.router_bias = None if router_bias is None else router_bias.to(self.device, torch.float32).contiguous()
+        E, I2, H = self.w13.shape
+        self.H, self.E, self.K, self.I = H, E, top_k, I2 // 2
+        self._desc = _lib.nkm_moe_tc_desc(H, E, top_k, self.I, eps, self.ln2.data_ptr(), self.router.data_ptr(),
+                                          _ptr(self.router_bias), self.w13.data_ptr(), self.w2.data_ptr(), max_tokens)
+        n = lib().nkm_moe_tc_workspace_bytes(ctypes.byref(self._desc))
+        if n == 0:
+            raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_moe_tc_workspace_bytes")
+        self.workspace = torch.empty(n, dtype=torch.uint8, device=self.device)
+
+    def __call__(self, x: torch.Tensor, residual: bool = False, stream=None):
+        T = int(x.shape[0])
+        y = torch.empty_like(x)
+        idx = torch.empty(T, self.K, dtype=torch.int32, device=self.device)
+        w = torch.empty(T, self.K, dtype=torch.float32, device=self.device)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        check(lib().nkm_moe_block_tc(ctypes.byref(self._desc), T, x.data_ptr(), y.data_ptr(), int(residual),
+                                     idx.data_ptr(), w.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(),
+                                     s.cuda_stream), "nkm_moe_block_tc")
+        return y, idx, w
+
+    def status(self, stream=None) -> int:
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return lib().nkm_moe_tc_status(self.workspace.data_ptr(), s.cuda_stream)
