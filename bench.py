@@ -39,6 +39,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stage-times", action="store_true", help="print a per-stage time breakdown to stderr")
+    ap.add_argument("--workload", choices=["qwen3", "gpt-oss", "moe-tc"], default="qwen3",
+                    help="qwen3: the headline (config 2); gpt-oss: GPT-OSS-20B decode (config 4, B=16 ctx 4096); "
+                         "moe-tc: the tcgen05 MoE block at config 3's 64 tokens")
     return ap.parse_args()
 
 
@@ -550,8 +553,130 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def _events_time(torch, stream, fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record(stream)
+    for i in range(steps):
+        fn()
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+    return evs[0].elapsed_time(evs[-1]) / steps, per
+
+
+def run_gpt_oss(args):
+    """GPT-OSS-20B decode step (config 4): 24 layers (sliding/full alternating), B=16, context
+    4096, MXFP4 experts, vocab 201088, seeded random weights, one GPU."""
+    import torch
+
+    from nki_moe_megakernel_b200.gpt_oss_engine import GptOssGpuLayer, GptOssMegakernel, GptOssShape
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, ctx = 16, 4096
+    shape = GptOssShape()
+    H, D, E, I, V = shape.hidden_size, shape.head_dim, shape.num_local_experts, shape.intermediate_size, shape.vocab_size
+    nq, nkv, L = shape.num_attention_heads, shape.num_key_value_heads, shape.num_hidden_layers
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+
+    def n(*sz, std=0.02):
+        return (torch.randn(*sz, generator=g, device=dev) * std).to(torch.bfloat16)
+
+    layers = []
+    for l in range(L):
+        t = dict(wq=n(nq * D, H), bq=n(nq * D), wk=n(nkv * D, H), bk=n(nkv * D), wv=n(nkv * D, H), bv=n(nkv * D),
+                 wo=n(H, nq * D), bo=n(H), sinks=n(nq, std=1.0), ln1=1 + n(H), ln2=1 + n(H), router=n(E, H),
+                 router_b=n(E), gu_b=n(E, 2 * I), dn_b=n(E, H),
+                 gu_codes=torch.randint(0, 16, (E, 2 * I, H), generator=g, device=dev, dtype=torch.uint8),
+                 gu_scales=torch.randint(119, 122, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8),
+                 dn_codes=torch.randint(0, 16, (E, H, I), generator=g, device=dev, dtype=torch.uint8),
+                 dn_scales=torch.randint(119, 122, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8))
+        layers.append(GptOssGpuLayer(t, shape.is_sliding(l)))
+        del t
+        torch.cuda.empty_cache()
+    nb = ctx // 128 + 1
+    NB = B * nb
+    eng = GptOssMegakernel(shape, layers, max_batch=B, num_blocks=NB, max_context=ctx + 128, final_norm=1 + n(H),
+                           lm_head=n(V, H), embed=torch.randn(V, H, generator=g, device=dev).to(torch.bfloat16),
+                           device=dev)
+    eng.k_pool.normal_(generator=g)
+    eng.v_pool.normal_(generator=g)
+    table = torch.randperm(NB, generator=torch.Generator().manual_seed(args.seed)).view(B, nb).to(torch.int32).to(dev)
+    pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    ids = torch.randint(0, V, (B,), generator=torch.Generator().manual_seed(1), dtype=torch.int32).to(dev)
+    out = {"hidden": torch.empty(B, H, dtype=torch.bfloat16, device=dev),
+           "logits": torch.empty(B, V, dtype=torch.float32, device=dev)}
+    tr = eng.decode_step(pos, table, input_ids=ids, trace=True)
+    eng.check_status()
+    distinct = [len(torch.unique(tr["topk_idx"][l])) for l in range(L)]
+    del tr
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(0) as clk:
+        ms, per = _events_time(torch, stream, lambda: eng.decode_step(pos, table, input_ids=ids, out=out), args.steps,
+                               args.warmup)
+    eng.check_status()
+    attn_w = ((nq + 2 * nkv) * D * H + H * nq * D) * 2 + ((nq + 2 * nkv) * D + H + nq + 2 * H + E) * 2 + E * H * 2
+    expert = (2 * I * H) // 2 + 2 * I * (H // 32) + 2 * I * 2 + (H * I) // 2 + H * (I // 32) + H * 2
+    kv = sum(B * (min(ctx, shape.sliding_window - 1) if shape.is_sliding(l) else ctx) * nkv * D * 2 * 2 for l in range(L))
+    nbytes = L * attn_w + sum(distinct) * expert + kv + L * B * nkv * D * 2 * 2 + V * H * 2
+    peak, peak_kind = measured_peaks()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "GPT-OSS-20B decode tokens/s at B=16 ctx 4096 (config 4)", "value": B / (ms / 1e3), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "p50_ms": statistics.median(per),
+        "higher_is_better": True, "dtype": "bf16 activations, MXFP4 experts", "data": "synthetic (seeded random)",
+        "config": {"workload": "gpt-oss-20b decode step (24 layers + LM head)", "global_batch": B, "ctx": ctx,
+                   "distinct_experts_per_layer_mean": sum(distinct) / L},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "algorithmic_bytes_per_step": nbytes,
+                     "kernel": "gptoss_decode_kernel (one launch per step)"},
+        "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+
+
+def run_moe_tc(args):
+    """The tcgen05 MoE block at config 3's expert stage: 64 tokens, top-8 of 128 Qwen3-30B-A3B
+    experts (one layer), seeded random weights."""
+    import torch
+
+    from nki_moe_megakernel_b200.engine import MoeTcBlock
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T, H, E, K, I = 64, 2048, 128, 8, 768
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    n = lambda *sz: (torch.randn(*sz, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
+    blk = MoeTcBlock(1 + n(H), n(E, H), n(E, 2 * I, H), n(E, H, I), eps=1e-6, top_k=K, max_tokens=T, device=dev)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    _, idx, _ = blk(x)
+    assert blk.status() == 0
+    distinct = len(torch.unique(idx))
+    stream = torch.cuda.current_stream(dev)
+    ms, per = _events_time(torch, stream, lambda: blk(x), args.steps, args.warmup)
+    assert blk.status() == 0
+    nbytes = distinct * 3 * I * H * 2 + E * H * 2 + 2 * T * H * 2
+    flops = 2 * T * K * 3 * I * H
+    peak, peak_kind = measured_peaks()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "tcgen05 MoE block (config 3 expert stage) tokens/s", "value": T / (ms / 1e3), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_call": ms, "p50_ms": statistics.median(per),
+        "dtype": "bf16", "config": {"workload": "qwen3-30b-a3b MoE block, 64 tokens", "distinct_experts": distinct},
+        "tflops": flops / (ms / 1e3) / 1e12,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "algorithmic_bytes_per_call": nbytes}}), flush=True)
+
+
 if __name__ == "__main__":
     a = parse()
+    if a.workload == "gpt-oss":
+        run_gpt_oss(a)
+        raise SystemExit(0)
+    if a.workload == "moe-tc":
+        run_moe_tc(a)
+        raise SystemExit(0)
     if a.impl == "reference":
         run_reference(a)
     else:
