@@ -331,6 +331,10 @@ typedef struct nkm_gptoss_desc {
   int32_t block_size;      /* must be 128 */
   int32_t max_batch;       /* <= 16 */
   int32_t max_context;     /* longest context (tokens) any step will attend to */
+  int32_t kv_fp8;          /* 1: K/V pools hold e4m3 bytes (same shapes): stored = e4m3(clip(x * scale,
+                              +-240)), read = stored / scale (attention_block_tkg.py:213-218, 1694) */
+  float k_scale;           /* used when kv_fp8 */
+  float v_scale;
 } nkm_gptoss_desc;
 
 typedef struct nkm_gptoss_step {

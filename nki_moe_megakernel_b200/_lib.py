@@ -67,7 +67,8 @@ class nkm_gptoss_desc(ctypes.Structure):
                 ("final_norm", c_void_p), ("lm_head_ft", c_void_p), ("embed", c_void_p),
                 ("rope_cos", POINTER(c_float)), ("rope_sin", POINTER(c_float)), ("rope_max_pos", c_int32),
                 ("k_pool", c_void_p), ("v_pool", c_void_p), ("num_blocks", c_int32), ("block_size", c_int32),
-                ("max_batch", c_int32), ("max_context", c_int32)]
+                ("max_batch", c_int32), ("max_context", c_int32), ("kv_fp8", c_int32), ("k_scale", c_float),
+                ("v_scale", c_float)]
 
 
 class nkm_gptoss_step(ctypes.Structure):

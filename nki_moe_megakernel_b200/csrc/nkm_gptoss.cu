@@ -94,6 +94,7 @@ int gcheck(const nkm_gptoss_desc* d) {
   if (d->block_size != nkg::kBlk) return gfail(NKM_ERR_ARG, "block_size must be 128");
   if (d->max_context <= 0) return gfail(NKM_ERR_ARG, "max_context must be positive");
   if (d->sliding_window <= 0) return gfail(NKM_ERR_ARG, "sliding_window must be positive");
+  if (d->kv_fp8 && !(d->k_scale > 0.f && d->v_scale > 0.f)) return gfail(NKM_ERR_ARG, "FP8 K/V needs positive scales");
   return NKM_OK;
 }
 
@@ -248,6 +249,9 @@ int nkm_gptoss_decode_step(nkm_gptoss* h, const nkm_gptoss_step* s, nkm_stream_t
   p.V = d.vocab;
   p.window = d.sliding_window;
   p.eps = d.rms_eps;
+  p.kv_fp8 = d.kv_fp8 ? 1 : 0;
+  p.k_scale = d.k_scale;
+  p.v_scale = d.v_scale;
   p.limit = d.swiglu_limit;
   p.alpha = d.swiglu_alpha;
   p.kc_qkv = h->kc_qkv;

@@ -18,6 +18,7 @@
 // then the final RMSNorm and the LM head GEMV.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "nkm_ptx.cuh"
 
@@ -72,6 +73,10 @@ struct Layer {
 struct Params {
   int B, H, Hact, nq, nkv, grp, R, E, K, I, L, V, window;
   float eps, limit, alpha;
+  // FP8 K/V cache (e4m3): stored = e4m3(clip(x * k_scale, +-240)), read = stored / k_scale
+  // (attention_block_tkg.py:213-218, 1694); 0: bf16 cache
+  int kv_fp8;
+  float k_scale, v_scale;
   int kc_qkv, kc_o;
   int first_layer, num_layers, want_lm;
   const Layer* layers;
@@ -81,8 +86,8 @@ struct Params {
   const float* rope_cos;  // [rope_max][32]
   const float* rope_sin;
   int rope_max;
-  uint16_t* k_pool;       // [L][NB][nkv][128][64]
-  uint16_t* v_pool;       // [L][NB][nkv][64][128]  (transposed blocks)
+  uint16_t* k_pool;       // [L][NB][nkv][128][64]            (bf16, or e4m3 bytes when kv_fp8)
+  uint16_t* v_pool;       // [L][NB][nkv][64][128]  transposed blocks (bf16, or e4m3 bytes)
   int num_blocks;
   const int* input_ids;
   const uint16_t* x_in;
@@ -203,6 +208,22 @@ __device__ __forceinline__ void e2m1x8(uint32_t w, uint32_t& r0, uint32_t& r1, u
       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
       : "r"(w));
 }
+__device__ __forceinline__ uint32_t ldcg_u32(const void* ptr) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(ptr));
+  return v;
+}
+// two e4m3 bytes (low byte -> low half) to f16x2
+__device__ __forceinline__ uint32_t e4m3x2(uint32_t v16) {
+  uint32_t d;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(d) : "r"(v16));
+  return d;
+}
+__device__ __forceinline__ uint8_t to_e4m3(float x, float scale) {
+  const float y = fminf(fmaxf(x * scale, -240.f), 240.f);
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ uint16_t f2h_bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
 // e8m0 scale 2^(s - 127) as fp32 (s = 0 gives 0: below any weight this format holds in practice)
 __device__ __forceinline__ float e8m0(uint32_t s) { return __uint_as_float(s << 23); }
 
@@ -423,9 +444,9 @@ __device__ __noinline__ void qkv_finalize(const Params& p, const Layer& lw, int 
       x1 = y1;
       x2 = y2;
     }
-    if (h < p.nq) {
-      p.qbuf[static_cast<size_t>(b) * p.nq * kHD + r1] = f2bf(x1);
-      p.qbuf[static_cast<size_t>(b) * p.nq * kHD + r2] = f2bf(x2);
+    if (h < p.nq) {  // f16 q for the f16 products of the FP8 cache, bf16 otherwise
+      p.qbuf[static_cast<size_t>(b) * p.nq * kHD + r1] = p.kv_fp8 ? f2h_bits(x1) : f2bf(x1);
+      p.qbuf[static_cast<size_t>(b) * p.nq * kHD + r2] = p.kv_fp8 ? f2h_bits(x2) : f2bf(x2);
       continue;
     }
     const bool is_k = h < p.nq + p.nkv;
@@ -438,7 +459,17 @@ __device__ __noinline__ void qkv_finalize(const Params& p, const Layer& lw, int 
     }
     const size_t base = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + kh) * (kBlk * kHD);
     const int slot = pos % kBlk;
-    if (is_k) {
+    if (p.kv_fp8) {
+      uint8_t* pool = reinterpret_cast<uint8_t*>(is_k ? p.k_pool : p.v_pool) + base;
+      const float sc = is_k ? p.k_scale : p.v_scale;
+      if (is_k) {
+        pool[static_cast<size_t>(slot) * kHD + i] = to_e4m3(x1, sc);
+        pool[static_cast<size_t>(slot) * kHD + i + 32] = to_e4m3(x2, sc);
+      } else {
+        pool[static_cast<size_t>(i) * kBlk + slot] = to_e4m3(x1, sc);
+        pool[static_cast<size_t>(i + 32) * kBlk + slot] = to_e4m3(x2, sc);
+      }
+    } else if (is_k) {
       p.k_pool[base + static_cast<size_t>(slot) * kHD + i] = f2bf(x1);
       p.k_pool[base + static_cast<size_t>(slot) * kHD + i + 32] = f2bf(x2);
     } else {
@@ -471,6 +502,9 @@ __device__ __forceinline__ int att_base(const Params& p, const Layer& lw, int b)
 // step: S = Q K^T (mma, Q rows = the group's query heads), online softmax, O += P V with V read from
 // the transposed cache.  Token order inside a step is permuted (lane t covers tokens 4t..4t+3 of the
 // V^T row) so that every lane reads 8 contiguous bytes; S uses the same permutation.
+// kFp8: the cache holds e4m3 bytes; q, K, P and V enter f16 products, the 1/scale factors are
+// applied to the scores and to the partial output.
+template <bool kFp8>
 __device__ __noinline__ void attention_unit(const Params& p, const Layer& lw, int layer, int b, int h, int c, int unit) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   int lo, hi;
@@ -485,6 +519,8 @@ __device__ __noinline__ void attention_unit(const Params& p, const Layer& lw, in
   const size_t base = ((static_cast<size_t>(layer) * p.num_blocks + blk) * p.nkv + h) * (kBlk * kHD);
   const uint16_t* kb = p.k_pool + base;
   const uint16_t* vb = p.v_pool + base;
+  const uint8_t* kb8 = reinterpret_cast<const uint8_t*>(p.k_pool) + base;
+  const uint8_t* vb8 = reinterpret_cast<const uint8_t*>(p.v_pool) + base;
   // Q fragments: lane (g, t) holds head rows g and g + 8 of the group, dims 16 t .. 16 t + 15 (four k-steps)
   uint32_t qa[4][4];
   {
@@ -506,7 +542,7 @@ __device__ __noinline__ void attention_unit(const Params& p, const Layer& lw, in
   }
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   float o[8][4] = {};
-  constexpr float kScale = 0.125f;  // 1 / sqrt(64)
+  const float kScale = kFp8 ? 0.125f / p.k_scale : 0.125f;  // 1 / sqrt(64) (and the K dequantisation)
   constexpr float kLog2e = 1.4426950408889634f;
   const int s0 = tb - blk_idx * kBlk, s1 = te - blk_idx * kBlk;  // slot range inside the block
 #pragma unroll 1
@@ -517,11 +553,26 @@ __device__ __noinline__ void attention_unit(const Params& p, const Layer& lw, in
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const int slot = nt ? tbk : ta;
-      const uint16_t* kr = kb + static_cast<size_t>(slot) * kHD + 16 * t4;
-      const uint4 k0 = nkm::ldcg128(kr), k1 = nkm::ldcg128(kr + 8);
-      const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+      uint32_t kw[8];
+      if (kFp8) {
+        const uint4 k8 = nkm::ldcg128(kb8 + static_cast<size_t>(slot) * kHD + 16 * t4);
+        const uint32_t w4[4] = {k8.x, k8.y, k8.z, k8.w};
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) mma_bf16(sc[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kw[2 * ks], kw[2 * ks + 1]);
+        for (int j = 0; j < 4; ++j) {
+          kw[2 * j] = e4m3x2(w4[j] & 0xffffu);
+          kw[2 * j + 1] = e4m3x2(w4[j] >> 16);
+        }
+      } else {
+        const uint16_t* kr = kb + static_cast<size_t>(slot) * kHD + 16 * t4;
+        const uint4 k0 = nkm::ldcg128(kr), k1 = nkm::ldcg128(kr + 8);
+        kw[0] = k0.x; kw[1] = k0.y; kw[2] = k0.z; kw[3] = k0.w;
+        kw[4] = k1.x; kw[5] = k1.y; kw[6] = k1.z; kw[7] = k1.w;
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        if (kFp8) mma_f16(sc[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kw[2 * ks], kw[2 * ks + 1]);
+        else mma_bf16(sc[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kw[2 * ks], kw[2 * ks + 1]);
+      }
     }
     // accumulator (row, col 2t + e) of n-tile nt is token st + 4 t + 2 nt + e
     float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -565,22 +616,42 @@ __device__ __noinline__ void attention_unit(const Params& p, const Layer& lw, in
         l1 += pr[nt][2 + e];
       }
     // P as the A operand (k = the 16 tokens in the permuted order) and V^T rows (dims) as B
-    const uint32_t pa0 = pack_bf2(pr[0][0], pr[0][1]), pa1 = pack_bf2(pr[0][2], pr[0][3]);
-    const uint32_t pa2 = pack_bf2(pr[1][0], pr[1][1]), pa3 = pack_bf2(pr[1][2], pr[1][3]);
+    auto pk = [](float a, float b2) {
+      if (kFp8) {
+        const __half2 hh = __floats2half2_rn(a, b2);
+        return *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      return pack_bf2(a, b2);
+    };
+    const uint32_t pa0 = pk(pr[0][0], pr[0][1]), pa1 = pk(pr[0][2], pr[0][3]);
+    const uint32_t pa2 = pk(pr[1][0], pr[1][1]), pa3 = pk(pr[1][2], pr[1][3]);
     const int vs = st + 4 * t4;  // this lane's 4 tokens
     const bool vfull = vs >= s0 && vs + 3 < s1;
 #pragma unroll
     for (int nd = 0; nd < 8; ++nd) {
-      const uint16_t* vr = vb + static_cast<size_t>(nd * 8 + g) * kBlk + vs;
-      uint2 v = nkm::ldcg64(vr);
+      uint2 v;
+      if (kFp8) {
+        const uint32_t v8 = ldcg_u32(vb8 + static_cast<size_t>(nd * 8 + g) * kBlk + vs);
+        v = make_uint2(e4m3x2(v8 & 0xffffu), e4m3x2(v8 >> 16));
+      } else {
+        v = nkm::ldcg64(vb + static_cast<size_t>(nd * 8 + g) * kBlk + vs);
+      }
       if (!vfull) {  // slots outside the context may hold anything: zero them
         const uint32_t m[4] = {vs >= s0 && vs < s1 ? 0xffffu : 0u, vs + 1 >= s0 && vs + 1 < s1 ? 0xffffu : 0u,
                                vs + 2 >= s0 && vs + 2 < s1 ? 0xffffu : 0u, vs + 3 >= s0 && vs + 3 < s1 ? 0xffffu : 0u};
         v.x &= m[0] | (m[1] << 16);
         v.y &= m[2] | (m[3] << 16);
       }
-      mma_bf16(o[nd], pa0, pa1, pa2, pa3, v.x, v.y);
+      if (kFp8) mma_f16(o[nd], pa0, pa1, pa2, pa3, v.x, v.y);
+      else mma_bf16(o[nd], pa0, pa1, pa2, pa3, v.x, v.y);
     }
+  }
+  if (kFp8) {
+    const float iv = 1.f / p.v_scale;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[nd][e] *= iv;
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -634,7 +705,8 @@ __device__ __noinline__ void attention_stage(const Params& p, const Layer& lw, i
     int lo, hi;
     att_range(p, lw, b, lo, hi);
     const int nb = att_nblocks(lo, hi), r = u - base;
-    attention_unit(p, lw, layer, b, r / nb, r % nb, u);
+    if (p.kv_fp8) attention_unit<true>(p, lw, layer, b, r / nb, r % nb, u);
+    else attention_unit<false>(p, lw, layer, b, r / nb, r % nb, u);
   }
 }
 

@@ -120,15 +120,20 @@ class GptOssMegakernel:
 
     def __init__(self, shape: GptOssShape, layers: Sequence[GptOssGpuLayer], *, max_batch: int, num_blocks: int,
                  max_context: int, final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
-                 embed: Optional[torch.Tensor] = None, device=None):
+                 embed: Optional[torch.Tensor] = None, device=None, kv_fp8: bool = False, k_scale: float = 1.0,
+                 v_scale: float = 1.0):
+        """``kv_fp8``: the K/V pools hold e4m3 bytes (``uint8``): stored = e4m3(clip(x * scale,
+        +-240)), read = stored / scale."""
         self.shape = shape
         self.device = torch.device(device if device is not None else "cuda")
         self.layers = list(layers)
         L, nkv, D = shape.num_hidden_layers, shape.num_key_value_heads, shape.head_dim
         assert len(self.layers) == L
         self.max_batch, self.num_blocks, self.max_context = max_batch, num_blocks, max_context
-        self.k_pool = torch.zeros(L, num_blocks, nkv, shape.block_size, D, dtype=BF16, device=self.device)
-        self.v_pool = torch.zeros(L, num_blocks, nkv, D, shape.block_size, dtype=BF16, device=self.device)
+        pool_dtype = torch.uint8 if kv_fp8 else BF16
+        self.kv_fp8, self.k_scale, self.v_scale = kv_fp8, k_scale, v_scale
+        self.k_pool = torch.zeros(L, num_blocks, nkv, shape.block_size, D, dtype=pool_dtype, device=self.device)
+        self.v_pool = torch.zeros(L, num_blocks, nkv, D, shape.block_size, dtype=pool_dtype, device=self.device)
         self.rope_max = max_context + shape.block_size
         self.rope_cos, self.rope_sin = yarn_tables(shape, self.rope_max, self.device)
         self.final_norm = None if final_norm is None else final_norm.to(BF16).contiguous()
@@ -143,7 +148,8 @@ class GptOssMegakernel:
             shape.swiglu_alpha, shape.sliding_window, self._structs, ptr(self.final_norm), ptr(self.lm_head_ft),
             ptr(self.embed), ctypes.cast(self.rope_cos.data_ptr(), ctypes.POINTER(ctypes.c_float)),
             ctypes.cast(self.rope_sin.data_ptr(), ctypes.POINTER(ctypes.c_float)), self.rope_max,
-            self.k_pool.data_ptr(), self.v_pool.data_ptr(), num_blocks, shape.block_size, max_batch, max_context)
+            self.k_pool.data_ptr(), self.v_pool.data_ptr(), num_blocks, shape.block_size, max_batch, max_context,
+            int(kv_fp8), k_scale, v_scale)
         nbytes = lib().nkm_gptoss_workspace_bytes(ctypes.byref(self._desc))
         if nbytes == 0:
             raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_gptoss_workspace_bytes")

@@ -225,3 +225,50 @@ def test_model_class_validate_against_hf():
     rc = drv.main(["--model", "gpt_oss", "--mode", "validate", "--enable-nki", "--num-layers", "2", "--seq-len", "160",
                    "--num-tokens-to-check", "6", "--prompt", "I believe the meaning of life is"])
     assert rc == 0
+
+
+def test_two_layers_fp8_kv(dev):
+    """FP8 (e4m3) K/V cache (the reference's k_scale / v_scale quantisation,
+    attention_block_tkg.py:213-218, 1694): the new K/V bytes equal e4m3(clip(x * scale, +-240)) of
+    the kernel's own projections (round to nearest even), and the layer outputs stay within the
+    tolerance of the fp32 oracle run on the dequantised cache."""
+    from nki_moe_megakernel_b200.gpt_oss_engine import GptOssMegakernel
+
+    KS, VS = 16.0, 16.0
+    cfg = G.GptOssConfig(n_layers=2)
+    gen = torch.Generator().manual_seed(931)
+    lws = [G.random_layer(cfg, gen) for _ in range(2)]
+    positions = [300, 17, 128, 1000]
+    B = len(positions)
+    NB = sum(p // 128 + 1 for p in positions) + 2
+    k0, v0, table = make_kv(cfg, 2, positions, NB, seed=932, nan_fill=False)
+    q8 = lambda t, s: (t.float() * s).clamp(-240, 240).to(torch.float8_e4m3fn)  # noqa: E731
+    k8, v8 = q8(k0, KS), q8(v0, VS)
+    x = torch.randn(B, cfg.hidden, generator=gen).to(BF16)
+    eng = GptOssMegakernel(_shape(cfg, 2, 0), [_gpu_layer(lws[i], dev, cfg.is_sliding(i)) for i in range(2)],
+                           max_batch=B, num_blocks=NB, max_context=1152, device=dev, kv_fp8=True, k_scale=KS,
+                           v_scale=VS)
+    eng.k_pool.copy_(k8.view(torch.uint8).to(dev))
+    eng.v_pool.copy_(_to_vt(v8.view(torch.uint8)).to(dev))
+    pos = torch.tensor(positions, dtype=torch.int32)
+    res = eng.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=False, trace=True)
+    torch.cuda.synchronize()
+    assert eng.status() == 0
+    cos, sin = eng.rope_cos.cpu(), eng.rope_sin.cpu()
+    kg, vg = eng.k_pool.cpu(), eng.v_pool.cpu().transpose(-1, -2)
+    nq, nkv, D = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
+    inp = x.float()
+    for li in range(2):
+        ref = G.decoder_layer(inp, lws[li], cfg, li, k8[li].float() / KS, v8[li].float() / VS, pos, table, cos, sin)
+        out = res["resid_out"][li].cpu()
+        r = G.compare(out, ref)
+        assert r["max_abs"] <= ATOL and r["cosine"] >= COS, (li, r)
+        qkv = res["qkv"][li].cpu()
+        for b, p in enumerate(positions):
+            kraw = qkv[b, nq * D:(nq + nkv) * D].view(nkv, D)
+            kexp = q8(G.apply_rope(kraw, cos[p], sin[p]), KS).view(torch.uint8)
+            vexp = q8(qkv[b, (nq + nkv) * D:].view(nkv, D), VS).view(torch.uint8)
+            blk, off = int(table[b, p // 128]), p % 128
+            assert torch.equal(kg[li, blk, :, off], kexp), (li, b)
+            assert torch.equal(vg[li, blk, :, off].contiguous(), vexp), (li, b)
+        inp = out
