@@ -227,7 +227,8 @@ typedef struct nkm_sample_params {
   float top_p;         /* (0, 1]: keep the shortest prefix of the top-k (by probability, after
                           temperature) whose mass reaches top_p                               */
   float temperature;   /* > 0: logits are multiplied by 1/temperature before the softmax      */
-  uint64_t seed;       /* uniform draw u = SplitMix64(seed ^ position << 32 ^ row) top 24 bits */
+  uint64_t seed;       /* uniform draw u = top 24 bits of SplitMix64(SplitMix64(seed) ^
+                          (position << 32 | row))                                              */
 } nkm_sample_params;
 
 /* Bytes of device scratch nkm_sample_logits needs (8-byte aligned; 0 for invalid sizes). */

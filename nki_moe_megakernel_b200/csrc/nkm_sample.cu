@@ -196,8 +196,10 @@ __global__ void __launch_bounds__(kThreads) sample_pick_kernel(const uint64_t* _
     float mass = 0.f;
     for (int j = 0; j < keep; ++j) mass += z[j];
     const int pos = positions ? positions[b] : 0;
-    const uint64_t r = splitmix64(seed ^ (static_cast<uint64_t>(static_cast<uint32_t>(pos)) << 32) ^
-                                  static_cast<uint64_t>(b));
+    // one stream per seed (SplitMix64 of the seed), one draw per (position, row): the two fields
+    // occupy disjoint bits, so no two (seed, position, row) triples share an input
+    const uint64_t r = splitmix64(splitmix64(seed) ^ ((static_cast<uint64_t>(static_cast<uint32_t>(pos)) << 32) |
+                                                      static_cast<uint64_t>(static_cast<uint32_t>(b))));
     const float u = static_cast<float>(r >> 40) * (1.0f / 16777216.0f);  // [0, 1), 24 bits
     const float target = u * mass;
     float cum = 0.f;

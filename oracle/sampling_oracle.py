@@ -6,7 +6,7 @@ Restates the sampler's semantics in plain Python / torch: the ``top_k`` largest 
 (descending; equal logits ordered by lower token id, -0 equal to +0), logits times
 ``fp32(1 / temperature)``, a softmax over the k relative to the largest, the shortest prefix
 whose probability mass reaches ``top_p``, and an inverse-CDF draw with the row's uniform
-``u = top 24 bits of SplitMix64(seed ^ position << 32 ^ row) / 2^24``.  SplitMix64 is the
+``u = top 24 bits of SplitMix64(SplitMix64(seed) ^ (position << 32 | row)) / 2^24``.  SplitMix64 is the
 published generator of Steele, Lea and Flood (OOPSLA 2014).  The reference's sampler is NxDI's
 on-device sampler configured at ``megakernels/qwen3_moe/qwen_with_megakernel.py:123-127``
 (``global_topk`` capped to ``top_k``) and ``main.py:390-398``; it is not in the reference tree,
@@ -31,7 +31,7 @@ def splitmix64(x: int) -> int:
 
 
 def uniform(seed: int, position: int, row: int) -> float:
-    r = splitmix64((seed ^ ((position & 0xFFFFFFFF) << 32) ^ row) & _M64)
+    r = splitmix64(splitmix64(seed & _M64) ^ (((position & 0xFFFFFFFF) << 32) | (row & 0xFFFFFFFF)))
     return float(np.float32(r >> 40) * np.float32(1.0 / 16777216.0))
 
 
