@@ -235,23 +235,26 @@ __device__ __forceinline__ void stamp(const Params& p, Ctx& c) {
 // Bounded wait on a slot's mbarrier.  On timeout the fatal status bit is set and the caller
 // continues (the next grid barrier then aborts every CTA).
 // Bounded wait for phase `par` of an mbarrier; on timeout the status records a fatal error.
-// The status word is polled too: once any wait of the launch has given up, every other wait
-// ends at its next poll instead of spending its own full bound (the launch then ends at the next
-// grid barrier), so the whole launch is bounded by one wait limit plus the polls.
+// A wait that has lasted longer than any normal one (kPollAfterNs) also polls the status word:
+// once any wait of the launch has given up, every other wait ends at its next poll instead of
+// spending its own full bound (the launch then ends at the next grid barrier), so the whole
+// launch is bounded by one wait limit plus the polls.  Normal waits never load the status word.
+constexpr uint64_t kPollAfterNs = 20000ull;
 __device__ __noinline__ void mbar_wait_slow(const Params& p, uint64_t* bar, uint32_t par) {
-  // try_wait itself suspends for a while; read the (slow) global timer and the status word only
-  // every 64 tries (a short wait never pays for them)
+  // try_wait itself suspends for a while; read the (slow) global timer only every 64 tries
   uint64_t t0 = 0;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, par)) break;
     if ((it & 63u) == 0) {
-      if (ld_volatile_i32(p.status) & kStatusFatal) break;
       const uint64_t now = globaltimer_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
-        if (lane_id() == 0) set_status(p, kStatusFatal);
-        break;
+      } else if (now - t0 > kPollAfterNs) {
+        if (ld_volatile_i32(p.status) & kStatusFatal) break;
+        if (now - t0 > kWaitLimitNs) {
+          if (lane_id() == 0) set_status(p, kStatusFatal);
+          break;
+        }
       }
     }
   }
@@ -1018,7 +1021,8 @@ __device__ __noinline__ void gateup_dyn(const Params& p, Ctx& cref, const GemvGe
     if (gen[sl] != strip) {
       const uint64_t t0 = globaltimer_ns();
       while (gen[sl] != strip) {
-        if ((ld_volatile_i32(p.status) & kStatusFatal) || globaltimer_ns() - t0 > kWaitLimitNs) {
+        const uint64_t dt = globaltimer_ns() - t0;
+        if (dt > kPollAfterNs && ((ld_volatile_i32(p.status) & kStatusFatal) || dt > kWaitLimitNs)) {
           if (lane == 0) set_status(p, kStatusFatal);
           break;
         }
