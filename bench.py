@@ -486,6 +486,7 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _nvtx(torch, "e2e")  # `ncu --nvtx --nvtx-include e2e/` lists the end-to-end launches
         e0.record(stream)
         for _ in range(args.steps):
             ids_d.copy_(ids_h, non_blocking=True)
@@ -496,6 +497,7 @@ def run_ours(args):
             tokens_h.copy_(tokens_d, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize()
+        _nvtx(torch, None)
         e2e_ms = e0.elapsed_time(e1)
         if world > 1:
             t = torch.tensor([e2e_ms], device=device)

@@ -1052,6 +1052,7 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
       oproj_residual(p, lw, layer);  // C2
       if (!grid_sync(p, bar_k, flag)) return;
       norm_rows(p, lw.ln2, xs, rstd, true);  // D (f16 rows stay in shared memory for stage E)
+      __syncthreads();  // every row's rstd (written by its warp) before any warp scores it
       router_logits(p, lw, layer, rstd);
       if (!grid_sync(p, bar_k, flag)) return;
       routing(p, rt, layer);  // E

@@ -204,11 +204,6 @@ struct Ctx {
   int* dyn;         // chunk scheduling words of the expert gate/up stage (shared memory)
   int awaitq;       // attention waits for its q/k/v element by element (no grid barrier before it)
   int npref;        // the next staged norm's prefetch is in flight
-  // This warp's copies in flight (shared memory, written by lane 0): bit s flips when a copy
-  // into ring slot s is issued, bit 4 when the norm prefetch (warp 0) is issued.  Compared with
-  // the waited parities (phase, cphase) it tells which copies have not been waited for, so a
-  // launch that ends early waits for exactly those before its CTA exits.
-  uint32_t* issued;
 };
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
@@ -404,12 +399,13 @@ __device__ __forceinline__ bool rank_exchange(const Params& p, Ctx& c, int which
 // workspace (launches on one workspace are stream-ordered).
 __device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c) {
   if ((ld_volatile_i32(p.status) & kStatusFatal) && lane_id() == 0) {
-    // a failed wait ends the launch early: wait for the copies this warp issued and has not
-    // waited for (they write into this CTA's shared memory), each wait bounded by 1 ms
-    const uint32_t pend = (*c.issued ^ (c.phase & 15u) ^ ((threadIdx.x == 0 ? (c.cphase & 1u) : 0u) << 4)) & 31u;
+    // a failed wait ends the launch early: wait for the next phase of each of this warp's
+    // mbarriers (and the norm-prefetch barrier for thread 0), each wait bounded by 1 ms.  A copy
+    // this warp issued and has not waited for (it writes into this CTA's shared memory) completes
+    // that phase when it lands; a slot with no copy in flight spends the 1 ms bound (only on this
+    // error path; the hot path carries no per-copy bookkeeping for it).
 #pragma unroll 1
-    for (int s = 0; s < 5; ++s) {
-      if (!((pend >> s) & 1u)) continue;
+    for (int s = 0; s < (threadIdx.x == 0 ? 5 : 4); ++s) {
       uint64_t* bar = s < 4 ? &c.bars[s] : c.cbar;
       const uint32_t par = s < 4 ? ((c.phase >> s) & 1u) : (c.cphase & 1u);
       const uint64_t t0 = globaltimer_ns();
@@ -759,7 +755,6 @@ __device__ __noinline__ void cta_strips_prime(const Params& p, Ctx& c, const Gem
       mbar_arrive_expect_tx(&c.bars[i], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + i * (CU * kUnitBytes), G.base + static_cast<uint64_t>(strip * KT + k0 + pk) * kUnitBytes,
                static_cast<uint32_t>(n * kUnitBytes), &c.bars[i], c.pol);
-      *c.issued ^= 1u << i;
     }
     pk += n;
     if (pk == nk) {
@@ -801,7 +796,6 @@ __device__ __noinline__ void gemv_cta_strips(const Params& p, Ctx& cref, const G
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + slot * (CU * kUnitBytes), G.base + static_cast<uint64_t>(strip * KT + k0 + pk) * kUnitBytes,
                static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
-      *c.issued ^= 1u << slot;
     }
     pk += n;
     if (pk == nk) {
@@ -901,7 +895,6 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&c.bars[i], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + i * (CU * kUnitBytes), src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[i], c.pol);
-      *c.issued ^= 1u << i;
     }
     pu += n;
     pkt += n;
@@ -925,7 +918,6 @@ __device__ __noinline__ void gemv_prime(const Params& p, Ctx& c, const GemvGeom&
 // SiLU(gate) * up.  Strips never straddle CTAs, so no partial leaves the SM.  All warps of the CTA
 // call it (one CTA barrier at the start).
 constexpr int kDynSlots = 3;  // strips in reduction at once (strip s uses slot (s - s0) % kDynSlots)
-static_assert((1 + 2 * kDynSlots) * 4 <= 32, "the chunk words end where the per-warp issue words start");
 template <int NT>
 __device__ __forceinline__ bool gateup_dyn_ok(const GemvGeom& G) {
   return NT == 1 && G.kt % RingGeom<NT>::kChunk == 0 &&
@@ -971,7 +963,6 @@ __device__ __noinline__ void gateup_dyn(const Params& p, Ctx& cref, const GemvGe
                G.base + static_cast<uint64_t>(rt->act_e[seg]) * G.seg_bytes +
                    static_cast<uint64_t>(ss * KT + kb * CU) * kUnitBytes,
                static_cast<uint32_t>(CU * kUnitBytes), &c.bars[slot], c.pol);
-      *c.issued ^= 1u << slot;
     }
   };
   int ids[NS];
@@ -1091,7 +1082,6 @@ __device__ __noinline__ void gemv_stage(const Params& p, Ctx& cref, const GemvGe
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + slot * (CU * kUnitBytes), src, static_cast<uint32_t>(n * kUnitBytes), &c.bars[slot], c.pol);
-      *c.issued ^= 1u << slot;
     }
     pu += n;
     pkt += n;
@@ -1247,7 +1237,6 @@ __device__ __noinline__ void down_prime(const Params& p, Ctx& c, const GemvGeom&
       mbar_arrive_expect_tx(&c.bars[k], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + k * (CU * kUnitBytes), down_item_src(G, c.rt, pi, pkt), static_cast<uint32_t>(n * kUnitBytes),
                &c.bars[k], c.pol);
-      *c.issued ^= 1u << k;
     }
     pkt += n;
     if (pkt == KT) {
@@ -1365,7 +1354,6 @@ __device__ __noinline__ void down_stage(const Params& p, Ctx& cref, const GemvGe
       mbar_arrive_expect_tx(&c.bars[slot], static_cast<uint32_t>(n * kUnitBytes));
       bulk_g2s(c.ring + slot * (CU * kUnitBytes), down_item_src(G, rt, pi, pkt), static_cast<uint32_t>(n * kUnitBytes),
                &c.bars[slot], c.pol);
-      *c.issued ^= 1u << slot;
     }
     pkt += n;
     if (pkt == KT) {
@@ -1558,7 +1546,6 @@ __device__ __noinline__ void att_issue_box(const Params& p, Ctx& c, int layer, i
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&c.bars[slot], kSlotBytes);
     tma_load_2d(c.ring + slot * kSlotBytes, kind < 2 ? kmap : vmap, (kind & 1) * 64, row, &c.bars[slot]);
-    *c.issued ^= 1u << slot;
   }
 }
 
@@ -2168,7 +2155,6 @@ __device__ __noinline__ void norm_prefetch(const Params& p, Ctx& c, const uint16
     if (has_e)
       bulk_g2s_plain(reinterpret_cast<uint8_t*>(c.red) + hb, router + static_cast<size_t>(blockIdx.x) * p.H, hb,
                      c.cbar);
-    *c.issued ^= 16u;
   }
   c.npref = 1;
 }
@@ -2185,7 +2171,6 @@ __device__ __noinline__ void norm_staged(const Params& p, Ctx& c, int layer, boo
     fence_proxy_async_global();  // the residual was written by other CTAs during this launch
     mbar_arrive_expect_tx(&c.bars[1], static_cast<uint32_t>(H) * 4u);
     bulk_g2s_plain(stage, p.resid + static_cast<size_t>(warp) * H, static_cast<uint32_t>(H) * 4u, &c.bars[1]);
-    *c.issued ^= 2u;
   }
   if (!c.npref) {  // not prefetched during the barrier (a stage launched on its own)
     __syncthreads();
@@ -2515,8 +2500,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.awaitq = 0;
   c.cphase = 0;
   c.npref = 0;
-  c.issued = reinterpret_cast<uint32_t*>(smem + lay.dyn_off + 32) + warp;
-  if (lane == 0) *c.issued = 0u;
   {
     // the layer pointer table, once per launch: every stage reads its pointers from shared memory
     static_assert(sizeof(LayerPtrs) % 16 == 0, "LayerPtrs is copied as uint4");

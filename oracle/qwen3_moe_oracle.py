@@ -102,10 +102,25 @@ def lane_sum_head(p: torch.Tensor) -> torch.Tensor:
 
 
 def rstd_fixed(sumsq: torch.Tensor, n: int, eps: float) -> torch.Tensor:
-    """``1 / sqrt(sumsq * fp32(1/n) + eps)`` with IEEE-rounded sqrt and divide."""
+    """``1 / sqrt(sumsq * fp32(1/n) + eps)`` with IEEE-rounded sqrt and divide.
+
+    The square root and the reciprocal are taken in fp64 and rounded once to fp32, which is the
+    correctly rounded fp32 result (fp64 carries more than 2 * 24 + 2 bits); torch's fp32 CPU
+    ``sqrt`` is not always correctly rounded (it was 1 ulp low on some inputs here).
+    """
     inv_n = torch.tensor(1.0 / n, dtype=F32)
     v = sumsq * inv_n + torch.tensor(eps, dtype=F32)
-    return torch.tensor(1.0, dtype=F32) / torch.sqrt(v)
+    s = torch.sqrt(v.to(torch.float64)).to(F32)
+    return (1.0 / s.to(torch.float64)).to(F32)
+
+
+def rstd_fixed_div(sumsq: torch.Tensor, n: int, eps: float) -> torch.Tensor:
+    """``1 / sqrt(sumsq / n + eps)`` with an IEEE fp32 divide by ``n`` (for ``n`` whose reciprocal
+    is not exact, as the padded-hidden RMSNorm of the GPT-OSS kernel computes it), then the
+    correctly rounded sqrt and reciprocal as in ``rstd_fixed``."""
+    v = sumsq / torch.tensor(float(n), dtype=F32) + torch.tensor(eps, dtype=F32)
+    s = torch.sqrt(v.to(torch.float64)).to(F32)
+    return (1.0 / s.to(torch.float64)).to(F32)
 
 
 # ---------------------------------------------------------------------------
@@ -158,6 +173,11 @@ class LayerTrace:
     resid_mid: Optional[torch.Tensor] = None
     router_logits: Optional[torch.Tensor] = None
     topk_idx: Optional[torch.Tensor] = None
+    # input: a top-k selection [T, k] to follow where the logits make it a top-k within
+    # ``hint_gap`` (the other side's choice at a near tie); ``hint_rows`` counts the rows that did
+    topk_hint: Optional[torch.Tensor] = None
+    hint_gap: float = 0.0
+    hint_rows: int = 0
     topk_w: Optional[torch.Tensor] = None
     moe_out: Optional[torch.Tensor] = None
     resid_out: Optional[torch.Tensor] = None
@@ -265,7 +285,27 @@ def topk_select(logits: torch.Tensor, k: int):
     return order[..., :k]
 
 
-def router_topk(logits: torch.Tensor, k: int, mode: str):
+def follow_hint(logits: torch.Tensor, idx: torch.Tensor, hint: torch.Tensor, gap: float):
+    """Rows of ``idx`` replaced by ``hint`` where the hinted set is a top-k of ``logits`` up to
+    ``gap`` (its lowest logit is within ``gap`` of the highest logit outside it).  Returns
+    (indices, number of rows replaced)."""
+    out = idx.clone()
+    n = 0
+    for r in range(idx.shape[0]):
+        a, b = set(idx[r].tolist()), set(hint[r].tolist())
+        if a == b:
+            continue
+        inside = logits[r, hint[r].long()].min()
+        mask = torch.ones(logits.shape[-1], dtype=torch.bool)
+        mask[hint[r].long()] = False
+        if float(logits[r, mask].max() - inside) <= gap:
+            out[r] = hint[r].to(out.dtype)
+            n += 1
+    return out, n
+
+
+def router_topk(logits: torch.Tensor, k: int, mode: str, hint: Optional[torch.Tensor] = None,
+                gap: float = 0.0, counter: Optional[list] = None):
     """Softmax at the top-k and L1 renormalisation.
 
     faithful: ``v = bf16(exp(l_k - max) * (1/sum))``, ``w = bf16(v * (1/sum_k v))``
@@ -273,6 +313,10 @@ def router_topk(logits: torch.Tensor, k: int, mode: str):
     Returns ``(idx [T,k] int64, w [T,k] fp32)``.
     """
     idx = topk_select(logits, k)
+    if hint is not None:
+        idx, n = follow_hint(logits, idx, hint, gap)
+        if counter is not None:
+            counter.append(n)
     mx = logits.max(dim=-1, keepdim=True).values
     ex = torch.exp(logits - mx)
     inv = 1.0 / ex.sum(-1, keepdim=True)
@@ -331,7 +375,11 @@ def moe_block(x_bf16: torch.Tensor, lw: LayerWeights, cfg: QwenConfig, mode: str
         logits = xn @ lw.router.to(F32).t()
     if lw.router_bias is not None:
         logits = logits + lw.router_bias.to(F32)
-    idx, w = router_topk(logits, cfg.top_k, mode)
+    used: list = []
+    hint = trace.topk_hint if trace is not None else None
+    idx, w = router_topk(logits, cfg.top_k, mode, hint, trace.hint_gap if trace is not None else 0.0, used)
+    if trace is not None and used:
+        trace.hint_rows = used[0]
     out = experts_forward(xn, idx, w, lw.gate_up, lw.down, mode)
     if trace is not None:
         trace.router_logits, trace.topk_idx, trace.topk_w = logits, idx, w
@@ -464,7 +512,8 @@ def decode_step(x_bf16: torch.Tensor, layers: List[LayerWeights], cfg: QwenConfi
                 k_caches: List[torch.Tensor], v_caches: List[torch.Tensor],
                 positions: torch.Tensor, block_table: torch.Tensor, cos_tab, sin_tab,
                 final_norm: Optional[torch.Tensor], lm_head: Optional[torch.Tensor],
-                mode: str, traces: Optional[List[LayerTrace]] = None):
+                mode: str, traces: Optional[List[LayerTrace]] = None,
+                topk_hints: Optional[List[torch.Tensor]] = None, hint_gap: float = 0.0):
     """Full decode step: ``len(k_caches)`` layers (weights cycle through ``layers``),
     then the final RMSNorm and the LM head (``qwen_with_megakernel.py:20-21,589-594``).
 
@@ -472,7 +521,9 @@ def decode_step(x_bf16: torch.Tensor, layers: List[LayerWeights], cfg: QwenConfi
     """
     x = x_bf16
     for li in range(len(k_caches)):
-        tr = LayerTrace() if traces is not None else None
+        tr = LayerTrace() if (traces is not None or topk_hints is not None) else None
+        if topk_hints is not None:
+            tr.topk_hint, tr.hint_gap = topk_hints[li], hint_gap
         x = decoder_layer(x, layers[li % len(layers)], cfg, k_caches[li], v_caches[li],
                           positions, block_table, cos_tab, sin_tab, mode, tr)
         if traces is not None:

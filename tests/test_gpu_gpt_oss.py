@@ -61,7 +61,7 @@ def _fixed_logits(mid: torch.Tensor, lw: G.GptOssLayer, cfg: G.GptOssConfig) -> 
     pad = (-H) % 256
     x = torch.nn.functional.pad(mid, (0, pad))
     ss = Q.lane_sum_hidden(x * x)
-    r = torch.tensor(1.0) / torch.sqrt(ss / torch.tensor(float(H)) + torch.tensor(cfg.rms_eps, dtype=torch.float32))
+    r = Q.rstd_fixed_div(ss, H, cfg.rms_eps)
     xn = (x * r[:, None]) * torch.nn.functional.pad(lw.ln2.float(), (0, pad))
     w = torch.nn.functional.pad(lw.router.float(), (0, pad))
     return Q.lane_sum_hidden(w[None] * xn[:, None, :]) + lw.router_b.float()
