@@ -179,8 +179,19 @@ def _gather(cache, table, b, h, lo, hi, bs):
     return torch.cat(rows, 0) if rows else cache.new_zeros(0, cache.shape[-1])
 
 
-def attention(xn, lw: GptOssLayer, cfg: GptOssConfig, layer: int, k_cache, v_cache, positions, table, cos, sin):
-    """Attention block on normed rows ``xn [T, H]``; writes the new K/V into the paged cache."""
+def fp8_qdq(t: torch.Tensor, scale: float) -> torch.Tensor:
+    """``e4m3(clip(t * scale, +-240)) / scale`` (round to nearest even): a value as an FP8 K/V
+    cache stores and returns it (``attention_block_tkg.py:1694-1737``)."""
+    return (t.to(F32) * scale).clamp(-240.0, 240.0).to(torch.float8_e4m3fn).to(F32) / scale
+
+
+def attention(xn, lw: GptOssLayer, cfg: GptOssConfig, layer: int, k_cache, v_cache, positions, table, cos, sin,
+              kv_scales=None):
+    """Attention block on normed rows ``xn [T, H]``; writes the new K/V into the paged cache.
+
+    ``kv_scales = (k_scale, v_scale)``: FP8 K/V cache; the new token's K and V are quantised
+    before the attention uses them, as the reference quantises the active K/V it attends to
+    (``attention_block_tkg.py:975-986, 1075-1084``)."""
     T = xn.shape[0]
     D, nq, nkv = cfg.head_dim, cfg.n_q_heads, cfg.n_kv_heads
     grp = nq // nkv
@@ -190,6 +201,8 @@ def attention(xn, lw: GptOssLayer, cfg: GptOssConfig, layer: int, k_cache, v_cac
     pos = positions.tolist()
     c, s = cos[pos][:, None, :], sin[pos][:, None, :]
     q, k = apply_rope(q, c, s), apply_rope(k, c, s)
+    if kv_scales is not None:
+        k, v = fp8_qdq(k, kv_scales[0]), fp8_qdq(v, kv_scales[1])
     out = torch.zeros(T, nq, D, dtype=F32)
     sinks = lw.sinks.to(F32)
     for b in range(T):
@@ -212,9 +225,22 @@ def attention(xn, lw: GptOssLayer, cfg: GptOssConfig, layer: int, k_cache, v_cac
     return out.reshape(T, nq * D) @ lw.wo.to(F32).t() + lw.bo.to(F32)
 
 
-def router(xn, lw: GptOssLayer, cfg: GptOssConfig):
+def router(xn, lw: GptOssLayer, cfg: GptOssConfig, topk_hint=None, hint_gap: float = 0.0):
+    """Logits, top-k indices and softmax over the top-k.  ``topk_hint [T, k]``: rows whose hinted
+    set is a top-k of the logits up to ``hint_gap`` take it (the other side's choice at a near
+    tie)."""
     logits = xn @ lw.router.to(F32).t() + lw.router_b.to(F32)
     top, idx = torch.topk(logits, cfg.top_k, dim=-1)
+    if topk_hint is not None:
+        for r in range(idx.shape[0]):
+            h = topk_hint[r].long()
+            if set(h.tolist()) == set(idx[r].tolist()):
+                continue
+            mask = torch.ones(logits.shape[-1], dtype=torch.bool)
+            mask[h] = False
+            if float(logits[r, mask].max() - logits[r, h].min()) <= hint_gap:
+                idx[r] = h
+                top[r] = logits[r, h]
     return logits, idx, torch.softmax(top, dim=-1)
 
 
@@ -235,11 +261,13 @@ def experts(xn, idx, w, lw: GptOssLayer, cfg: GptOssConfig):
     return acc
 
 
-def decoder_layer(x, lw, cfg, layer, k_cache, v_cache, positions, table, cos, sin, trace=None):
+def decoder_layer(x, lw, cfg, layer, k_cache, v_cache, positions, table, cos, sin, trace=None, kv_scales=None,
+                  topk_hint=None, hint_gap: float = 0.0):
     x = x.to(F32)
-    mid = x + attention(rmsnorm(x, lw.ln1, cfg.rms_eps), lw, cfg, layer, k_cache, v_cache, positions, table, cos, sin)
+    mid = x + attention(rmsnorm(x, lw.ln1, cfg.rms_eps), lw, cfg, layer, k_cache, v_cache, positions, table, cos, sin,
+                        kv_scales)
     xn2 = rmsnorm(mid, lw.ln2, cfg.rms_eps)
-    logits, idx, w = router(xn2, lw, cfg)
+    logits, idx, w = router(xn2, lw, cfg, topk_hint, hint_gap)
     out = mid + experts(xn2, idx, w, lw, cfg)
     if trace is not None:
         trace.append({"resid_mid": mid, "router_logits": logits, "topk_idx": idx, "topk_w": w, "resid_out": out})

@@ -1,11 +1,20 @@
 """Parity at the benchmarked configuration, and the router's top-k against the reference order.
 
 * The full decode step of the bench (48 layers, B=8, context 2048 in a paged KV cache, vocab
-  151936, final norm and LM head) against the fp32 oracle run free (no teacher forcing): the
-  final hidden state and the logits within max-abs 2e-2 and cosine >= 0.999, and at every layer
-  the kernel's top-k expert indices equal the oracle's selection on the kernel's own residual
-  (bit-exact router logits in the kernel's summation order).  The weights cycle through two
-  distinct seeded layers (distinct K/V caches per layer), as in the CPU baseline.
+  151936, final norm and LM head), weights cycling through two distinct seeded layers (distinct
+  K/V caches per layer), as in the CPU baseline:
+  - at every layer the router logits are bit-exact (and so the top-k indices equal the oracle's)
+    on the kernel's own residual, in the kernel's documented summation order;
+  - at every layer the kernel's output is within max-abs 2e-2 and cosine >= 0.999 of the fp32
+    oracle layer applied to the kernel's input of that layer, and the logits within the same
+    bounds of the fp32 final norm + LM head applied to the kernel's final residual;
+  - run free for 48 layers (no teacher forcing), the final hidden state and the logits keep
+    cosine >= 0.999 against the fp32 oracle, and their max-abs error is no larger than that of
+    the reference's own arithmetic (the oracle's bf16-faithful mode, run free the same way)
+    against the same fp32 run.  Both numbers are printed.  A free run of 48 bf16 layers drifts
+    from fp32 by more than 2e-2 (the hidden grows to |x| ~ 10 and near-tie routing decisions
+    diverge once the residuals differ); the kernel keeps its residual in fp32 and drifts less
+    than the reference's bf16 residual does.
 * Top-k flips against the reference's router order: the kernel's expert sets compared with
   ``topk_select(xn @ W_router.T)`` computed in plain fp32 (RMSNorm and matmul in torch's order,
   the NxDI / Hugging Face computation, reference ``moe_fused_nki.py:186-218, 241-250``), at
@@ -24,7 +33,6 @@ pytestmark = pytest.mark.gpu
 ATOL = 2e-2
 COS = 0.999
 FLIP_GAP = 1e-4   # largest plain-fp32 logit gap at which a top-k set may differ
-HINT_GAP = 2e-3   # free-running: logit gap under which the fp32 run follows the kernel's set
 
 
 @pytest.fixture(scope="module")
@@ -70,7 +78,7 @@ def _record(tag, n, f, w):
     assert w <= FLIP_GAP, (tag, w)
 
 
-def test_bench_shape_48_layers_free_running(dev):
+def test_bench_shape_48_layers(dev):
     from nki_moe_megakernel_b200.engine import Qwen3MoeMegakernel
 
     L, B, ctx = 48, 8, 2048
@@ -122,33 +130,39 @@ def test_bench_shape_48_layers_free_running(dev):
     print(f"[48-layer] router mismatches (layer, count, max diff, nan logits, nan mid): {bad}", flush=True)
     _record("config 2 (48 layers x B=8)", n, f, worst)
 
-    # free-running fp32 oracle of the whole step.  Run as is, a near tie in the router (8th and
-    # 9th logit closer than the drift between the two residual streams) can pick a different
-    # expert on the two sides, and one such flip moves that row by the weight of one expert; the
-    # asserted run therefore follows the kernel's expert set where the fp32 logits make it a
-    # top-k within HINT_GAP (the rows that did are counted and printed), and is otherwise free.
     x = embed[ids.long()]
     cos32, sin32 = O.rope_tables(4096, cfg.head_dim, cfg.rope_theta, torch.float32)
     final = outs[L - 1]  # the kernel's fp32 residual after layer 48 (the hidden it normalises)
-    for hinted in (False, True):
-        traces = []
-        ref_hidden, ref_logits = O.decode_step(
-            x, distinct, cfg, [k0[i].clone() for i in range(L)], [v0[i].clone() for i in range(L)], pos, table,
-            cos32, sin32, final_norm, lm_head, "fp32", traces,
-            topk_hints=[idx_all[i] for i in range(L)] if hinted else None, hint_gap=HINT_GAP)
-        growth = []
-        for li in (0, 11, 23, 35, 47):
-            r = O.compare(outs[li], traces[li].resid_out)
-            growth.append((li + 1, round(r["max_abs"], 5), round(r["cosine"], 7)))
-        rh = O.compare(final, ref_hidden)
-        rl = O.compare(logits, ref_logits)
-        tag = f"near-tie rows following the kernel: {sum(t.hint_rows for t in traces)}" if hinted else "unguided"
-        print(f"[48-layer] {tag}; per-layer residual vs fp32 (layer, max_abs, cosine): {growth}", flush=True)
-        print(f"[48-layer] {tag}; final hidden {rh}, logits {rl}, bf16 output hidden "
-              f"{O.compare(hidden.float(), ref_hidden)}", flush=True)
-    assert not bad, bad
-    assert rh["max_abs"] <= ATOL and rh["cosine"] >= COS, rh
-    assert rl["max_abs"] <= ATOL and rl["cosine"] >= COS, rl
+
+    # teacher-forced: every layer from the kernel's own input (near-tie routing follows the kernel)
+    worst = {"max_abs": 0.0, "cosine": 1.0}
+    for li in range(L):
+        inp = x.float() if li == 0 else outs[li - 1]
+        tr = O.LayerTrace(topk_hint=idx_all[li], hint_gap=FLIP_GAP)
+        ref = O.decoder_layer(inp, layers[li], cfg, k0[li].clone(), v0[li].clone(), pos, table, cos32, sin32,
+                              "fp32", tr)
+        r = O.compare(outs[li], ref)
+        worst = {"max_abs": max(worst["max_abs"], r["max_abs"]), "cosine": min(worst["cosine"], r["cosine"])}
+        assert r["max_abs"] <= ATOL and r["cosine"] >= COS, (li, r)
+    ref_logits_tf = O.rmsnorm_fp32(final, final_norm, cfg.rms_eps) @ lm_head.float().t()
+    rl_tf = O.compare(logits, ref_logits_tf)
+    print(f"[48-layer] teacher-forced: worst layer {worst}; logits {rl_tf}", flush=True)
+    assert rl_tf["max_abs"] <= ATOL and rl_tf["cosine"] >= COS, rl_tf
+
+    # free-running: the kernel and the reference's own (bf16-faithful) arithmetic against fp32
+    ref_hidden, ref_logits = O.decode_step(x, distinct, cfg, [k0[i].clone() for i in range(L)],
+                                           [v0[i].clone() for i in range(L)], pos, table, cos32, sin32,
+                                           final_norm, lm_head, "fp32")
+    cos16, sin16 = O.rope_tables(4096, cfg.head_dim, cfg.rope_theta, BF16)
+    fa_hidden, fa_logits = O.decode_step(x, distinct, cfg, [k0[i].clone() for i in range(L)],
+                                         [v0[i].clone() for i in range(L)], pos, table, cos16, sin16,
+                                         final_norm, lm_head, "faithful")
+    rh, rl = O.compare(final, ref_hidden), O.compare(logits, ref_logits)
+    fh, fl = O.compare(fa_hidden.float(), ref_hidden), O.compare(fa_logits, ref_logits)
+    print(f"[48-layer] free-running vs fp32: kernel hidden {rh}, logits {rl}; reference arithmetic "
+          f"(bf16-faithful oracle) hidden {fh}, logits {fl}", flush=True)
+    assert rh["cosine"] >= COS and rl["cosine"] >= COS, (rh, rl)
+    assert rh["max_abs"] <= max(ATOL, fh["max_abs"]) and rl["max_abs"] <= max(ATOL, fl["max_abs"]), (rh, rl, fh, fl)
 
 
 @pytest.mark.parametrize("seed", [0, 1, 2, 3])
