@@ -345,3 +345,90 @@ class MoeTcBlock:
     def status(self, stream=None) -> int:
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         return lib().nkm_moe_tc_status(self.workspace.data_ptr(), s.cuda_stream)
+
+
+class Qwen3MoeWideDecoder:
+    """Decode steps at batches beyond one decode-kernel launch (config 3: B = 64, contexts up to
+    8192), per layer ``transformer_qwen.py:218-378`` at that batch:
+
+    * the attention block (``nkm_qwen3_attention_block``: RMSNorm, QKV, q/k-norm, RoPE, K/V write,
+      GQA decode attention, O-projection, residual) in launches of up to ``row_chunk`` (32) rows;
+    * the MoE block on the tcgen05/TMEM grouped GEMMs (``nkm_moe_block_tc``) over all rows at
+      once, where 64 tokens give the experts ~4 columns each;
+    * the residual between the blocks is bf16 (the reference's bf16 residual adds,
+      ``transformer_qwen.py:331-333, 370-372``);
+    * final RMSNorm (fp32) and the LM head as one plain GEMM over all rows (cuBLAS through torch:
+      one read of the 622 MB head for the whole batch).
+
+    ``layers``: per layer a dict of Hugging Face layout tensors (``wq, wk, wv, wo, q_norm,
+    k_norm, ln1, ln2, router, gate_up, down``, optional ``router_bias``); a list may repeat the same
+    dict (weights shared by several layers; each layer still has its own K/V pages)."""
+
+    def __init__(self, shape: Qwen3MoeShape, layers: Sequence[Dict[str, torch.Tensor]], *, max_batch: int,
+                 num_blocks: int, final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
+                 embed: Optional[torch.Tensor] = None, rope_max_pos: int = 40960, row_chunk: int = 32,
+                 device=None):
+        self.shape = shape
+        self.device = torch.device(device if device is not None else "cuda")
+        self.max_batch = max_batch
+        self.row_chunk = min(row_chunk, 32, max_batch)
+        att, moe = {}, {}
+        for lw in layers:
+            if id(lw) in att:
+                continue
+            att[id(lw)] = GpuLayer(lw["wq"], lw["wk"], lw["wv"], lw["wo"], lw["q_norm"], lw["k_norm"], lw["ln1"],
+                                   None, None, None, None, moe=False)
+            moe[id(lw)] = MoeTcBlock(lw["ln2"], lw["router"], lw["gate_up"], lw["down"], eps=shape.rms_norm_eps,
+                                     top_k=shape.num_experts_per_tok, max_tokens=max_batch,
+                                     router_bias=lw.get("router_bias"), device=self.device)
+        self.moe = [moe[id(lw)] for lw in layers]
+        self.attn = Qwen3MoeMegakernel(shape, [att[id(lw)] for lw in layers], max_batch=self.row_chunk,
+                                       num_blocks=num_blocks, rope_max_pos=rope_max_pos, device=self.device)
+        self.k_pool, self.v_pool = self.attn.k_pool, self.attn.v_pool
+        self.final_norm = None if final_norm is None else final_norm.to(self.device, torch.float32)
+        self.lm_head = None if lm_head is None else lm_head.to(self.device, BF16).contiguous()
+        self.embed = None if embed is None else embed.to(self.device, BF16).contiguous()
+
+    def decode_step(self, positions: torch.Tensor, block_table: torch.Tensor, *, x: Optional[torch.Tensor] = None,
+                    input_ids: Optional[torch.Tensor] = None, want_logits: bool = True, trace: bool = False,
+                    stream=None) -> Dict[str, torch.Tensor]:
+        """One decode step for ``B = positions.shape[0]`` rows (``B <= max_batch``).  Returns
+        ``{"hidden": [B, H] bf16, "logits": [B, V] fp32}``; ``trace`` adds per layer
+        ``resid_mid`` / ``resid_out`` (bf16 as fp32) and the MoE routing ``topk_idx`` / ``topk_w``."""
+        B = int(positions.shape[0])
+        assert 0 < B <= self.max_batch, B
+        if x is None:
+            x = self.embed[input_ids.long()]
+        h = x.to(BF16).contiguous()
+        L = self.shape.num_hidden_layers
+        tr = {"resid_mid": [], "resid_out": [], "topk_idx": [], "topk_w": []} if trace else None
+        for layer in range(L):
+            mid = torch.empty_like(h)
+            for r0 in range(0, B, self.row_chunk):
+                r1 = min(B, r0 + self.row_chunk)
+                mid[r0:r1] = self.attn.attention_block(layer, h[r0:r1], positions[r0:r1], block_table[r0:r1],
+                                                       residual=True, stream=stream)["hidden"]
+            h, idx, w = self.moe[layer](mid, residual=True, stream=stream)
+            if tr is not None:
+                tr["resid_mid"].append(mid.float())
+                tr["resid_out"].append(h.float())
+                tr["topk_idx"].append(idx)
+                tr["topk_w"].append(w)
+        res = {"hidden": h}
+        if want_logits and self.lm_head is not None:
+            xf = h.float()
+            xn = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.shape.rms_norm_eps) * self.final_norm
+            res["logits"] = torch.mm(xn.to(BF16), self.lm_head.t(), out_dtype=torch.float32)
+        if tr is not None:
+            res.update({k: torch.stack(v) for k, v in tr.items()})
+        return res
+
+    def check_status(self) -> None:
+        self.attn.check_status()
+        for m in {id(m): m for m in self.moe}.values():
+            st = m.status()
+            if st != 0:
+                raise _lib.NkmError(st, "tcgen05 MoE block")
+
+    def close(self) -> None:
+        self.attn.close()

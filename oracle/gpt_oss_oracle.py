@@ -186,12 +186,14 @@ def fp8_qdq(t: torch.Tensor, scale: float) -> torch.Tensor:
 
 
 def attention(xn, lw: GptOssLayer, cfg: GptOssConfig, layer: int, k_cache, v_cache, positions, table, cos, sin,
-              kv_scales=None):
+              kv_scales=None, new_kv=None):
     """Attention block on normed rows ``xn [T, H]``; writes the new K/V into the paged cache.
 
     ``kv_scales = (k_scale, v_scale)``: FP8 K/V cache; the new token's K and V are quantised
     before the attention uses them, as the reference quantises the active K/V it attends to
-    (``attention_block_tkg.py:975-986, 1075-1084``)."""
+    (``attention_block_tkg.py:975-986, 1075-1084``).  ``new_kv = (k [T, nkv, D], v [T, nkv, D])``:
+    the new tokens' (RoPE'd) K and V as given (e.g. read back from a cache another implementation
+    wrote), in place of this function's own projections."""
     T = xn.shape[0]
     D, nq, nkv = cfg.head_dim, cfg.n_q_heads, cfg.n_kv_heads
     grp = nq // nkv
@@ -203,6 +205,8 @@ def attention(xn, lw: GptOssLayer, cfg: GptOssConfig, layer: int, k_cache, v_cac
     q, k = apply_rope(q, c, s), apply_rope(k, c, s)
     if kv_scales is not None:
         k, v = fp8_qdq(k, kv_scales[0]), fp8_qdq(v, kv_scales[1])
+    if new_kv is not None:
+        k, v = new_kv[0].to(F32), new_kv[1].to(F32)
     out = torch.zeros(T, nq, D, dtype=F32)
     sinks = lw.sinks.to(F32)
     for b in range(T):
@@ -262,10 +266,10 @@ def experts(xn, idx, w, lw: GptOssLayer, cfg: GptOssConfig):
 
 
 def decoder_layer(x, lw, cfg, layer, k_cache, v_cache, positions, table, cos, sin, trace=None, kv_scales=None,
-                  topk_hint=None, hint_gap: float = 0.0):
+                  topk_hint=None, hint_gap: float = 0.0, new_kv=None):
     x = x.to(F32)
     mid = x + attention(rmsnorm(x, lw.ln1, cfg.rms_eps), lw, cfg, layer, k_cache, v_cache, positions, table, cos, sin,
-                        kv_scales)
+                        kv_scales, new_kv)
     xn2 = rmsnorm(mid, lw.ln2, cfg.rms_eps)
     logits, idx, w = router(xn2, lw, cfg, topk_hint, hint_gap)
     out = mid + experts(xn2, idx, w, lw, cfg)

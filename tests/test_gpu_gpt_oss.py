@@ -248,8 +248,8 @@ def test_two_layers_fp8_kv(dev):
     """FP8 (e4m3) K/V cache (the reference's k_scale / v_scale quantisation,
     attention_block_tkg.py:213-218, 1694): the new K/V bytes equal e4m3(clip(x * scale, +-240)) of
     the kernel's own projections (round to nearest even), and the layer outputs stay within the
-    tolerance of the fp32 oracle run on the dequantised cache (the new token's K/V quantised as
-    the reference quantises the active K/V)."""
+    tolerance of the fp32 oracle run on the dequantised cache, the new token's K/V included as the
+    kernel quantised them (the reference attends to the quantised active K/V as well)."""
     from nki_moe_megakernel_b200.gpt_oss_engine import GptOssMegakernel
 
     KS, VS = 16.0, 16.0
@@ -276,9 +276,13 @@ def test_two_layers_fp8_kv(dev):
     kg, vg = eng.k_pool.cpu(), eng.v_pool.cpu().transpose(-1, -2)
     nq, nkv, D = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
     inp = x.float()
+    # the new tokens' K/V as the kernel stored them (their bytes are checked below), dequantised
+    kg8, vg8 = kg.view(torch.float8_e4m3fn).float() / KS, vg.view(torch.float8_e4m3fn).float() / VS
     for li in range(2):
+        newk = torch.stack([kg8[li, int(table[b, p // 128]), :, p % 128] for b, p in enumerate(positions)])
+        newv = torch.stack([vg8[li, int(table[b, p // 128]), :, p % 128] for b, p in enumerate(positions)])
         ref = G.decoder_layer(inp, lws[li], cfg, li, k8[li].float() / KS, v8[li].float() / VS, pos, table, cos, sin,
-                              kv_scales=(KS, VS))
+                              new_kv=(newk, newv))
         out = res["resid_out"][li].cpu()
         r = G.compare(out, ref)
         assert r["max_abs"] <= ATOL and r["cosine"] >= COS, (li, r)

@@ -1,0 +1,94 @@
+"""Config 3 on one GPU: decode steps at B=64 with contexts uniform in [1024, 8192]
+(``Qwen3MoeWideDecoder``: the attention block in 32-row launches, the MoE block on the tcgen05
+grouped GEMMs over all 64 rows, bf16 residual between the blocks as in the reference).
+
+Two layers of the Qwen3-30B-A3B shape, teacher-forced layer by layer:
+* the MoE block's top-k indices equal the oracle's fixed-order selection on the block's own
+  input (bit-exact router logits);
+* every layer output within max-abs 2e-2 (beyond one bf16 ulp of the value: both sides round the
+  residual to bf16) of the oracle's bf16-faithful layer (the reference's rounding points, bf16
+  residual) and cosine >= 0.999 against the fp32 layer;
+* the logits (fp32 final norm + LM head) within max-abs 2e-2 / cosine 0.999 of fp32 on the
+  decoder's final hidden state.
+"""
+import pytest
+import torch
+
+from oracle import qwen3_moe_oracle as O
+from tests.qwen_cases import BF16, make_kv, make_layers, qwen_cfg, shape_of
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+COS = 0.999
+
+
+def _excess(a: torch.Tensor, b: torch.Tensor) -> float:
+    """max |a - b| beyond one bf16 ulp of b: both sides round the residual to bf16, and a sum
+    taken in another order may round to the neighbouring bf16 value (one ulp is 0.03 at |x| >= 4)."""
+    b32 = b.float()
+    ulp = torch.exp2(torch.floor(torch.log2(b32.abs().clamp_min(1e-30))) - 7)
+    return float(((a.float() - b32).abs() - ulp).clamp_min(0).max())
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+def _dicts(layers, dev):
+    keys = ("wq", "wk", "wv", "wo", "q_norm", "k_norm", "ln1", "ln2", "router", "gate_up", "down")
+    return [{k: getattr(lw, k).to(dev) for k in keys} for lw in layers]
+
+
+def test_wide_batch_64_two_layers(dev):
+    from nki_moe_megakernel_b200.engine import Qwen3MoeWideDecoder
+
+    L, B = 2, 64
+    cfg = qwen_cfg(n_layers=L, vocab=4096)
+    layers = make_layers(cfg, L, seed=61)
+    g = torch.Generator().manual_seed(62)
+    positions = torch.randint(1024, 8193, (B,), generator=g).tolist()
+    NB = sum(p // 128 + 1 for p in positions) + 2
+    k0, v0, table = make_kv(cfg, L, positions, NB, seed=63, nan_fill=False)
+    final_norm = (1 + 0.02 * torch.randn(cfg.hidden, generator=g)).to(BF16)
+    lm_head = (0.02 * torch.randn(cfg.vocab, cfg.hidden, generator=g)).to(BF16)
+    x = torch.randn(B, cfg.hidden, generator=g).to(BF16)
+    wide = Qwen3MoeWideDecoder(shape_of(cfg, L, cfg.vocab), _dicts(layers, dev), max_batch=B, num_blocks=NB,
+                               final_norm=final_norm.to(dev), lm_head=lm_head.to(dev), rope_max_pos=8320,
+                               device=dev)
+    wide.k_pool.copy_(k0.to(dev))
+    wide.v_pool.copy_(v0.to(dev))
+    pos = torch.tensor(positions, dtype=torch.int32)
+    res = wide.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), trace=True)
+    torch.cuda.synchronize()
+    wide.check_status()
+    outs, mids = res["resid_out"].cpu(), res["resid_mid"].cpu()
+    idx = res["topk_idx"].cpu().long()
+    logits = res["logits"].cpu()
+    wide.close()
+    del wide, res
+    torch.cuda.empty_cache()
+
+    cos16, sin16 = O.rope_tables(8320, cfg.head_dim, cfg.rope_theta, BF16)
+    cos32, sin32 = O.rope_tables(8320, cfg.head_dim, cfg.rope_theta, torch.float32)
+    inp = x
+    for li in range(L):
+        lw = layers[li]
+        lg = O.router_logits_fixed(O.rmsnorm_hidden_faithful(mids[li].to(BF16), lw.ln2, cfg.rms_eps, True), lw.router)
+        assert torch.equal(idx[li], O.topk_select(lg, cfg.top_k)), li
+        fa = O.decoder_layer(inp.to(BF16), lw, cfg, k0[li].clone(), v0[li].clone(), pos, table, cos16, sin16,
+                             "faithful", O.LayerTrace(topk_hint=idx[li], hint_gap=1e-4))
+        f32 = O.decoder_layer(inp.float(), lw, cfg, k0[li].clone(), v0[li].clone(), pos, table, cos32, sin32,
+                              "fp32", O.LayerTrace(topk_hint=idx[li], hint_gap=1e-4))
+        rf, r32 = O.compare(outs[li], fa.float()), O.compare(outs[li], f32)
+        ex = _excess(outs[li], fa)
+        print(f"[wide B=64 layer {li}] vs faithful {rf} (beyond one bf16 ulp: {ex:.4g}), vs fp32 {r32}", flush=True)
+        assert ex <= ATOL and rf["cosine"] >= COS, (li, rf, ex)
+        assert r32["cosine"] >= COS, (li, r32)
+        inp = outs[li]
+    ref_l = O.rmsnorm_fp32(outs[L - 1], final_norm, cfg.rms_eps) @ lm_head.float().t()
+    rl = O.compare(logits, ref_l)
+    print(f"[wide B=64] logits {rl}", flush=True)
+    assert rl["max_abs"] <= ATOL and rl["cosine"] >= COS, rl
