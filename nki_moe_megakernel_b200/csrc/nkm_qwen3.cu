@@ -167,14 +167,19 @@ int encode_kv_map(CUtensorMap* map, void* pool, const nkm_qwen3_desc& d) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// The three instantiations of the decode kernel (column tiles NT = 1, 2, 4).
+// The instantiations of the decode kernel: column tiles NT = 1, 2, 4 for the decode step, and
+// NT = 1 and 4 with the caller-q/k/v and K/V-first stage bits (kExt; batches of 9..16 run on the
+// NT = 4 one).
+constexpr int kNumKernels = 5;
 void* decode_kernel_fn(int i) {
-  void* kfn[3] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2>),
-                  reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4>)};
+  void* kfn[kNumKernels] = {reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1, false>),
+                            reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<2, false>),
+                            reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4, false>),
+                            reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<1, true>),
+                            reinterpret_cast<void*>(&nkm::qwen3_decode_kernel<4, true>)};
   return kfn[i];
 }
-constexpr int kNts[3] = {1, 2, 4};
+constexpr int kNts[kNumKernels] = {1, 2, 4, 1, 4};
 constexpr int kMaxDevices = 64;
 
 // Once per device, with that device current: the decode kernel's dynamic shared-memory limit.
@@ -190,7 +195,7 @@ int ensure_smem_limits() {
   if (dev < 0 || dev >= kMaxDevices) return fail(NKM_ERR_ARG, "device %d out of range", dev);
   std::lock_guard<std::mutex> lock(mu);
   if (done[dev]) return NKM_OK;
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < kNumKernels; ++i) {
     const nkm::SmemLayout sl(nkm::kMaxHidden, kNts[i]);
     if (sl.total > 232448 - 1024) return fail(NKM_ERR_ARG, "decode kernel shared memory exceeds the per-CTA limit");
     NKM_CUDA(cudaFuncSetAttribute(decode_kernel_fn(i), cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -214,7 +219,7 @@ struct nkm_qwen3 {
   WsLayout lay;
   CUtensorMap kmap, vmap;
   int device, num_sms;
-  size_t smem[3];
+  size_t smem[kNumKernels];
 };
 
 extern "C" {
@@ -284,7 +289,7 @@ int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspa
   if ((rc = encode_kv_map(&h->kmap, desc->k_pool, *desc))) return cleanup(rc);
   if ((rc = encode_kv_map(&h->vmap, desc->v_pool, *desc))) return cleanup(rc);
   if ((rc = ensure_smem_limits())) return cleanup(rc);
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < kNumKernels; ++i) {
     nkm::SmemLayout sl(desc->hidden, kNts[i]);
     h->smem[i] = sl.total;
     if (sl.total > 232448 - 1024) return cleanup(fail(NKM_ERR_ARG, "hidden too large for shared memory"));
@@ -401,7 +406,8 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.gpart = reinterpret_cast<float*>(ws + h->lay.gpart);
 
   const int nt = nt_for_batch(p.T);
-  const int ki = nt == 1 ? 0 : (nt == 2 ? 1 : 2);
+  const bool ext = (stages & (NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST)) != 0;
+  const int ki = ext ? (nt == 1 ? 3 : 4) : (nt == 1 ? 0 : (nt == 2 ? 1 : 2));
   void* args[3] = {&p, &h->kmap, &h->vmap};
   NKM_CUDA(cudaLaunchCooperativeKernel(decode_kernel_fn(ki), dim3(h->num_sms), dim3(nkm::kThreads), args, h->smem[ki],
                                        stream));

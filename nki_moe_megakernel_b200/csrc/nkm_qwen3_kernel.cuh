@@ -2453,7 +2453,11 @@ __device__ __noinline__ void routing_prologue(const Params& p, Ctx& c, int layer
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int NT>
+// kExt: the instantiation that also serves stages bits 8 (q/k/v from the caller) and 16 (every
+// row's K/V before the attention).  The decode step's instantiations (kExt = false) carry none
+// of that code: the per-layer path is larger than the SM instruction cache, and code added to it
+// costs time even where it never runs.
+template <int NT, bool kExt>
 __global__ void __launch_bounds__(kThreads, 1)
     qwen3_decode_kernel(const __grid_constant__ Params pk, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
@@ -2526,7 +2530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   [&]() {  // the launch body; a fatal error returns from here to launch_exit
   // stages bit 8: the attention takes the q/k/v projections the caller wrote into the QKV buffer
   // (no RMSNorm(ln1) + QKV GEMV; one layer per launch, checked on the host)
-  const bool qkv_in = (p.stages & 8) != 0;
+  const bool qkv_in = kExt && (p.stages & 8) != 0;
   // stage 0: residual (fp32) <- embeddings / hidden input (bf16); the router-logit slots of the
   // staged path start unwritten
   if (norm_staged_ok<NT>(p) && (p.stages & 2)) logits_rearm(p);
@@ -2592,7 +2596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cta_strip_mode<NT>(ga, GK_QKV)) gemv_cta_strips<NT>(p, c, ga, GK_QKV);
         else gemv_stage<NT, GK_QKV>(p, c, ga);
       }
-      if (p.stages & 16) {
+      if (kExt && (p.stages & 16)) {
         // K/V of every row first (a grid barrier on each side), then the attention reads them
         if (!grid_barrier(p, c)) return;
         kv_prewrite(p, c, layer);

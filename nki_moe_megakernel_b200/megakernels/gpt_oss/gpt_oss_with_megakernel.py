@@ -298,11 +298,20 @@ class NeuronGptOssForCausalLM:
         pos = position_ids.to(self.device, torch.int32).view(-1)
         return self.kernel.decode_step(pos, self.block_table[:ids.shape[0]], input_ids=ids)["logits"]
 
-    def teacher_forced_logits(self, tokens: Sequence[int]) -> torch.Tensor:
+    def teacher_forced_logits(self, tokens: Sequence[int], routing: bool = False):
+        """Every position's logits ``[len(tokens), vocab]`` fp32 (one decode step per position);
+        with ``routing`` also the expert indices ``[len(tokens), layers, top_k]``."""
         self.reset()
-        out = [self.forward(torch.tensor([t]), torch.tensor([i])) for i, t in enumerate(tokens)]
+        out, rt = [], []
+        for i, t in enumerate(tokens):
+            ids = torch.tensor([t], dtype=torch.int32, device=self.device)
+            pos = torch.tensor([i], dtype=torch.int32, device=self.device)
+            res = self.kernel.decode_step(pos, self.block_table[:1], input_ids=ids, trace=routing)
+            out.append(res["logits"])
+            if routing:
+                rt.append(res["topk_idx"].transpose(0, 1))
         self.kernel.check_status()
-        return torch.cat(out, 0)
+        return (torch.cat(out, 0), torch.cat(rt, 0)) if routing else torch.cat(out, 0)
 
     def sample(self, logits: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         from ...engine import sample_tokens  # noqa: PLC0415

@@ -362,14 +362,15 @@ class NeuronQwen3MoeForCausalLMV3:
         res = self.kernel.decode_step(pos, self.block_table[:B], input_ids=ids)
         return res["logits"]
 
-    def prefill(self, rows: Sequence[tuple], want_logits: bool = False) -> Optional[torch.Tensor]:
+    def prefill(self, rows: Sequence[tuple], want_logits: bool = False, routing: Optional[list] = None):
         """Context encoding through the decode kernel: ``rows`` = (sequence, position, token id)
         triples, processed ``prefill_chunk_size`` rows per launch.  Rows of one sequence at
         consecutive positions share a launch: every row's K/V is written before the attention
         reads the cache (``NKM_STAGE_KV_FIRST``), so each row attends causally to the rows
         before it.  Returns the logits of every row ``[len(rows), vocab]`` if ``want_logits``.
         (The reference keeps context encoding on the per-layer NxDI path,
-        ``qwen_with_megakernel.py:496-526``.)"""
+        ``qwen_with_megakernel.py:496-526``.)  ``routing``: a list that receives each row's expert
+        indices per layer (``[rows, layers, top_k]`` int32 tensors, one per launch)."""
         if self.kernel is None:
             raise RuntimeError("call load() first")
         n = self.neuron_config.prefill_chunk_size
@@ -379,18 +380,23 @@ class NeuronQwen3MoeForCausalLMV3:
             ids = torch.tensor([r[2] for r in chunk], dtype=torch.int32, device=self.device)
             pos = torch.tensor([r[1] for r in chunk], dtype=torch.int32, device=self.device)
             table = self.block_table[torch.tensor([r[0] for r in chunk], device=self.device)].contiguous()
-            res = self.kernel.decode_step(pos, table, input_ids=ids, want_logits=want_logits, kv_first=True)
+            res = self.kernel.decode_step(pos, table, input_ids=ids, want_logits=want_logits, kv_first=True,
+                                          trace=routing is not None)
+            if routing is not None:
+                routing.append(res["topk_idx"].transpose(0, 1).contiguous())
             if want_logits:
                 out.append(res["logits"])
         return torch.cat(out, 0) if want_logits and out else None
 
-    def teacher_forced_logits(self, tokens: Sequence[int]) -> torch.Tensor:
+    def teacher_forced_logits(self, tokens: Sequence[int], routing: bool = False):
         """Feed ``tokens`` (sequence 0, positions 0, 1, ...) through the chunked prefill and return
-        every position's logits ``[len(tokens), vocab]`` fp32."""
+        every position's logits ``[len(tokens), vocab]`` fp32; with ``routing`` also the expert
+        indices ``[len(tokens), layers, top_k]``."""
         self.reset()
-        logits = self.prefill([(0, t, tok) for t, tok in enumerate(tokens)], want_logits=True)
+        rt: Optional[list] = [] if routing else None
+        logits = self.prefill([(0, t, tok) for t, tok in enumerate(tokens)], want_logits=True, routing=rt)
         self.kernel.check_status()
-        return logits
+        return (logits, torch.cat(rt, 0)) if routing else logits
 
     def sample(self, logits: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         """Next tokens on the device (``nkm_sample_logits``): greedy unless ``do_sample``, else
