@@ -39,6 +39,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stage-times", action="store_true", help="print a per-stage time breakdown to stderr")
+    ap.add_argument("--weights", choices=["bf16", "mxfp8"], default="bf16",
+                    help="expert weights of the tcgen05 workloads (moe-tc, wide): bf16 or MXFP8")
     ap.add_argument("--workload", choices=["qwen3", "gpt-oss", "moe-tc", "wide"], default="qwen3",
                     help="qwen3: the headline (config 2); gpt-oss: GPT-OSS-20B decode (config 4, B=16 ctx 4096); "
                          "moe-tc: the tcgen05 MoE block at config 3's 64 tokens; wide: config 3's whole decode "
@@ -639,6 +641,14 @@ def run_gpt_oss(args):
         "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
 
 
+def _mx_experts(torch, g, dev, E, rows, cols):
+    """Seeded synthetic MXFP8 expert matrices on the device: e4m3 codes of N(0, 32) values
+    (clipped to +-448) with the e8m0 scale 2^-11 in every block (weights ~N(0, 0.016))."""
+    codes = (torch.randn(E, rows, cols, generator=g, device=dev) * 32).clamp(-448, 448).to(torch.float8_e4m3fn)
+    scales = torch.full((E, rows, cols // 32), 127 - 11, dtype=torch.uint8, device=dev)
+    return codes.view(torch.uint8), scales
+
+
 def run_moe_tc(args):
     """The tcgen05 MoE block at config 3's expert stage: 64 tokens, top-8 of 128 Qwen3-30B-A3B
     experts (one layer), seeded random weights."""
@@ -651,7 +661,12 @@ def run_moe_tc(args):
     T, H, E, K, I = 64, 2048, 128, 8, 768
     g = torch.Generator(device=dev).manual_seed(args.seed)
     n = lambda *sz: (torch.randn(*sz, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
-    blk = MoeTcBlock(1 + n(H), n(E, H), n(E, 2 * I, H), n(E, H, I), eps=1e-6, top_k=K, max_tokens=T, device=dev)
+    mx = args.weights == "mxfp8"
+    if mx:
+        blk = MoeTcBlock(1 + n(H), n(E, H), None, None, eps=1e-6, top_k=K, max_tokens=T, device=dev,
+                         mxfp8=(*_mx_experts(torch, g, dev, E, 2 * I, H), *_mx_experts(torch, g, dev, E, H, I)))
+    else:
+        blk = MoeTcBlock(1 + n(H), n(E, H), n(E, 2 * I, H), n(E, H, I), eps=1e-6, top_k=K, max_tokens=T, device=dev)
     x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     _, idx, _ = blk(x)
     assert blk.status() == 0
@@ -659,14 +674,16 @@ def run_moe_tc(args):
     stream = torch.cuda.current_stream(dev)
     ms, per = _events_time(torch, stream, lambda: blk(x), args.steps, args.warmup)
     assert blk.status() == 0
-    nbytes = distinct * 3 * I * H * 2 + E * H * 2 + 2 * T * H * 2
+    wb = (1 + 1 / 32) if mx else 2  # bytes per expert weight
+    nbytes = distinct * 3 * I * H * wb + E * H * 2 + 2 * T * H * 2
     flops = 2 * T * K * 3 * I * H
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (ms / 1e3) / 1e9
     print(json.dumps({
         "metric": "tcgen05 MoE block (config 3 expert stage) tokens/s", "value": T / (ms / 1e3), "unit": UNIT,
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_call": ms, "p50_ms": statistics.median(per),
-        "dtype": "bf16", "config": {"workload": "qwen3-30b-a3b MoE block, 64 tokens", "distinct_experts": distinct},
+        "dtype": "bf16", "config": {"workload": "qwen3-30b-a3b MoE block, 64 tokens", "distinct_experts": distinct,
+                                    "expert_weights": args.weights},
         "tflops": flops / (ms / 1e3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "algorithmic_bytes_per_call": nbytes}}), flush=True)
@@ -690,9 +707,16 @@ def run_wide(args):
     g = torch.Generator(device=dev).manual_seed(args.seed)
     n = lambda *sz: (torch.randn(*sz, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
     one = lambda *sz: (1.0 + torch.randn(*sz, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
-    layers = [{"wq": n(nq * D, H), "wk": n(nkv * D, H), "wv": n(nkv * D, H), "wo": n(H, nq * D), "q_norm": one(D),
-               "k_norm": one(D), "ln1": one(H), "ln2": one(H), "router": n(E, H), "gate_up": n(E, 2 * I, H),
-               "down": n(E, H, I)} for _ in range(L)]
+    mx = args.weights == "mxfp8"
+    layers = []
+    for _ in range(L):
+        lw = {"wq": n(nq * D, H), "wk": n(nkv * D, H), "wv": n(nkv * D, H), "wo": n(H, nq * D), "q_norm": one(D),
+              "k_norm": one(D), "ln1": one(H), "ln2": one(H), "router": n(E, H)}
+        if mx:
+            lw["mxfp8"] = (*_mx_experts(torch, g, dev, E, 2 * I, H), *_mx_experts(torch, g, dev, E, H, I))
+        else:
+            lw["gate_up"], lw["down"] = n(E, 2 * I, H), n(E, H, I)
+        layers.append(lw)
     ctx = torch.randint(1024, 8193, (B,), generator=torch.Generator().manual_seed(args.seed)).tolist()
     need = [c // 128 + 1 for c in ctx]
     NB = sum(need)
@@ -700,8 +724,9 @@ def run_wide(args):
                                embed=torch.randn(V, H, generator=g, device=dev).to(torch.bfloat16),
                                rope_max_pos=8320, device=dev)
     for lw in layers:  # the tcgen05 blocks hold the expert tensors; the FT copies hold attention
-        for k in ("wq", "wk", "wv", "wo"):
-            lw.pop(k)
+        for k in ("wq", "wk", "wv", "wo", "mxfp8"):
+            lw.pop(k, None)
+    torch.cuda.empty_cache()
     wide.k_pool.normal_(generator=g)
     wide.v_pool.normal_(generator=g)
     perm = torch.randperm(NB, generator=torch.Generator().manual_seed(args.seed + 1))
@@ -723,7 +748,8 @@ def run_wide(args):
     wide.check_status()
     att_w = (nq * D * H + 2 * nkv * D * H + H * nq * D) * 2
     kv = sum(ctx) * nkv * D * 2 * 2
-    nbytes = L * (att_w + kv + E * H * 2 + sum(distinct) / L * 3 * I * H * 2) + V * H * 2
+    wb = (1 + 1 / 32) if mx else 2  # bytes per expert weight
+    nbytes = L * (att_w + kv + E * H * 2 + sum(distinct) / L * 3 * I * H * wb) + V * H * 2
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (ms / 1e3) / 1e9
     print(json.dumps({
@@ -732,7 +758,7 @@ def run_wide(args):
         "ms_per_step": ms, "p50_ms": statistics.median(per), "higher_is_better": True, "dtype": "bf16",
         "data": "synthetic (seeded random-init weights, 48 distinct layers; K/V ~N(0,1))",
         "config": {"workload": "qwen3-30b-a3b decode step at B=64 (attention 2 x 32-row launches, tcgen05 experts)",
-                   "global_batch": B, "ctx_mean": sum(ctx) / B, "layers": L,
+                   "global_batch": B, "ctx_mean": sum(ctx) / B, "layers": L, "expert_weights": args.weights,
                    "distinct_experts_per_layer_mean": sum(distinct) / L},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "algorithmic_bytes_per_step": nbytes}}), flush=True)

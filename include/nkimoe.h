@@ -261,10 +261,27 @@ typedef struct nkm_moe_tc_desc {
   const void* ln2;            /* bf16 [H] */
   const void* router;         /* bf16 [E, H] */
   const float* router_bias;   /* fp32 [E] or NULL */
-  const void* w13;            /* bf16 [E][2I][H] row-major: gate rows then up rows (HF gate_up_proj) */
-  const void* w2;             /* bf16 [E][H][I] row-major (HF down_proj) */
+  const void* w13;            /* bf16 [E][2I][H] row-major: gate rows then up rows (HF gate_up_proj),
+                                 or (MXFP8) nkm_pack_mxfp8_experts(..., rows = 2I, cols = H, gate_up = 1) */
+  const void* w2;             /* bf16 [E][H][I] row-major (HF down_proj), or (MXFP8)
+                                 nkm_pack_mxfp8_experts(..., rows = H, cols = I, gate_up = 0) */
   int32_t max_tokens;         /* <= 512 */
+  int32_t weight_format;      /* NKM_MOE_WEIGHTS_BF16 or NKM_MOE_WEIGHTS_MXFP8 (e4m3 values, e8m0
+                                 scale per 32 along K; expanded exactly to bf16 in shared memory) */
 } nkm_moe_tc_desc;
+
+#define NKM_MOE_WEIGHTS_BF16 0
+#define NKM_MOE_WEIGHTS_MXFP8 1
+
+/* Bytes of nkm_pack_mxfp8_experts' output for `count` matrices of [rows, cols] (rows % 128,
+ * cols % 64; 0 if invalid). */
+size_t nkm_mxfp8_experts_bytes(int32_t count, int32_t rows, int32_t cols);
+/* MXFP8 expert matrices (OCP MX: e4m3 codes [count][rows][cols] and e8m0 scales
+ * [count][rows][cols/32], device) into the units the MXFP8 grouped GEMM streams.  gate_up = 1
+ * for [E][2I][H] gate-then-up matrices.  Replaces the reference's MX weight layout
+ * (nki_kernels/moe/down_projection_mx_shard_H.py:43-110, mxfp_x4 [128, n_I512_tile, H]). */
+int nkm_pack_mxfp8_experts(const void* codes, const void* scales, void* dst, int32_t count, int32_t rows,
+                           int32_t cols, int32_t gate_up, nkm_stream_t stream);
 
 /* Workspace bytes (256-byte aligned; the first 4 bytes are the call's status word). */
 size_t nkm_moe_tc_workspace_bytes(const nkm_moe_tc_desc* desc);

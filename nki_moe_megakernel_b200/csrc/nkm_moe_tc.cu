@@ -21,6 +21,7 @@
 // NKM_ERR_TIMEOUT, all roles leave their loops, outstanding copies and MMAs are waited for
 // (bounded) and TMEM is freed before the CTA exits.  No load uses cluster multicast.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -39,7 +40,11 @@ namespace {
 using nkm::smem_addr;
 
 constexpr int kTcThreads = 192;
+constexpr int kTcThreadsMx = 320;         // + 4 converter warps (MXFP8 weights)
 constexpr int kStages = 4;
+constexpr int kStagesMx = 3;              // bf16 operand stages with MXFP8 weights
+constexpr int kRawMx = 8;                 // MXFP8 weight units in flight per CTA
+constexpr int kMxUnit = 128 * 64 + 128 * 2;  // 128 rows x 64 e4m3 codes, then 128 rows x 2 e8m0 scales
 constexpr int kBK = 64;                   // K elements per stage (128 bytes: one swizzle atom row)
 constexpr int kMaxN = 256;                // columns of one tile
 constexpr int kABytes = 128 * 128;        // A stage: 128 rows x 128 bytes
@@ -47,6 +52,9 @@ constexpr int kBBytes = kMaxN * 128;      // B stage: up to 256 rows x 128 bytes
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kXchBytes = 64 * 16 * 4;    // gate/up epilogue exchange (64 rows x 16 columns fp32)
 constexpr int kTcSmem = kStages * kStageBytes + kXchBytes + 256 + 1024;
+constexpr int kTcSmemMx = kStagesMx * kStageBytes + kRawMx * kMxUnit + kXchBytes + 256 + 1024;
+static_assert(kTcSmemMx <= 232448, "MXFP8 GEMM shared memory");
+static_assert(kMxUnit % 16 == 0, "bulk copy size");
 constexpr int kMaxTokens = 512;
 constexpr int kMaxE = 256;
 constexpr int kMaxK = 8;
@@ -76,6 +84,8 @@ struct TcParams {
   uint16_t* hbuf;           // [P, I]
   float* ypair;             // [P, H]
   int P;                    // slot capacity
+  const uint8_t* w13mx;     // MXFP8 weights (nkm_pack_mxfp8_experts units) or null
+  const uint8_t* w2mx;
 };
 
 // ------------------------------------------------------------------ PTX (tcgen05, TMEM)
@@ -317,23 +327,69 @@ __global__ void tc_combine_kernel(TcParams p) {
   }
 }
 
+// ------------------------------------------------------------------ MXFP8 weights
+// e8m0 scale byte -> fp32 2^(s - 127) (0 -> 2^-127, 255 -> NaN)
+__device__ __forceinline__ float e8m0_f32(uint32_t s) {
+  return s == 0u ? __uint_as_float(0x00400000u) : (s == 255u ? __uint_as_float(0x7fc00000u) : __uint_as_float(s << 23));
+}
+// two e4m3 codes (low byte -> low half) to f16x2 (exact)
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v16) {
+  uint32_t d;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(d) : "r"(v16));
+  return d;
+}
+// 4 e4m3 codes times a power-of-two scale -> two bf16x2 words (exact: bf16 has fp32's exponent range)
+__device__ __forceinline__ uint2 e4m3x4_bf16(uint32_t w, float sc) {
+  const uint32_t lo = e4m3x2_f16x2(w & 0xffffu), hi = e4m3x2_f16x2(w >> 16);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  return make_uint2(nkm::pack_bf2(a.x * sc, a.y * sc), nkm::pack_bf2(b.x * sc, b.y * sc));
+}
+// Row `row` of an MXFP8 unit (64 codes + 2 scales) into a bf16 K-major tile row with the
+// 128-byte swizzle the MMA descriptor expects (16-byte chunk c of row r at c ^ (r % 8)).
+__device__ __forceinline__ void mx_convert_row(const uint8_t* unit, uint8_t* a_tile, int row) {
+  const uint4* src = reinterpret_cast<const uint4*>(unit + row * 64);
+  const uint32_t sw = *reinterpret_cast<const uint16_t*>(unit + 128 * 64 + row * 2);
+  const float sc0 = e8m0_f32(sw & 0xffu), sc1 = e8m0_f32(sw >> 8);
+  uint8_t* dst = a_tile + row * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {  // 16 codes = 2 output chunks of 8
+    const uint4 c = src[q];
+    const float sc = q < 2 ? sc0 : sc1;
+    const uint2 b0 = e4m3x4_bf16(c.x, sc), b1 = e4m3x4_bf16(c.y, sc);
+    const uint2 b2 = e4m3x4_bf16(c.z, sc), b3 = e4m3x4_bf16(c.w, sc);
+    const int c0 = 2 * q, c1 = 2 * q + 1;
+    *reinterpret_cast<uint4*>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(b0.x, b0.y, b1.x, b1.y);
+    *reinterpret_cast<uint4*>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(b2.x, b2.y, b3.x, b3.y);
+  }
+}
+
 // ------------------------------------------------------------------ the grouped GEMM
 // kGateUp: item = (tile, 64-row block j0 of I): A = gate rows [e*2I + j0, +64) and up rows
 // [e*2I + I + j0, +64) of W13, K = H; out h[slot][j0 + r].
 // !kGateUp: item = (tile, 128-row block m0 of H): A = W2 rows [e*H + m0, +128), K = I;
 // out ypair[slot][m0 + r] = acc * slot_w[slot].
-template <bool kGateUp>
-__global__ void __launch_bounds__(kTcThreads, 1)
+// kMx (MXFP8 weights): the A operand arrives as nkm_pack_mxfp8_experts units (e4m3 codes + e8m0
+// scales of the same 128 rows, one 1-D bulk copy each, kRawMx in flight) and warps 6-9 expand
+// each unit into the bf16 swizzled A tile (exact: code x power of two); the MMA then runs as for
+// bf16 weights.  Warp 6 lane 0 also issues the B (token) tiles of the stage it converts into.
+template <bool kGateUp, bool kMx>
+__global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcParams p) {
+  constexpr int S = kMx ? kStagesMx : kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
-  float* xch = reinterpret_cast<float*>(smem + kStages * kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kXchBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint8_t* raw_base = smem + S * kStageBytes;  // kMx: weight units
+  float* xch = reinterpret_cast<float*>(raw_base + (kMx ? kRawMx * kMxUnit : 0));
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xch) + kXchBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* bfull = acc_empty + 1;      // kMx: B tiles of a stage landed (S)
+  uint64_t* raw_full = bfull + S;       // kMx: weight unit landed (kRawMx)
+  uint64_t* raw_empty = raw_full + kRawMx;  // kMx: weight unit converted (kRawMx)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(raw_empty + kRawMx);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KT = kGateUp ? p.H / kBK : p.I / kBK;      // K chunks
@@ -341,9 +397,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nitems = *p.ntiles * MB;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      nkm::mbar_init(&full[s], 1);
+    for (int s = 0; s < S; ++s) {
+      nkm::mbar_init(&full[s], kMx ? 4 : 1);  // kMx: one arrival per converter warp
       nkm::mbar_init(&empty[s], 1);
+      nkm::mbar_init(&bfull[s], 1);
+    }
+    for (int r = 0; r < kRawMx; ++r) {
+      nkm::mbar_init(&raw_full[r], 1);
+      nkm::mbar_init(&raw_empty[r], 4);
     }
     nkm::mbar_init(acc_full, 1);
     nkm::mbar_init(acc_empty, 4);  // one arrival per epilogue warp
@@ -360,9 +421,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer (kMx: weight units only)
     if (lane == 0) {
-      nkm::prefetch_tensormap(&amap);
+      if (!kMx) nkm::prefetch_tensormap(&amap);
       nkm::prefetch_tensormap(&bmap);
       uint32_t cnt = 0;
       bool ok = true;
@@ -370,8 +431,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int tile = item / MB, mb = item - tile * MB;
         const int e = p.tiles[3 * tile], n0 = p.tiles[3 * tile + 1], ncols = p.tiles[3 * tile + 2];
         for (int kc = 0; kc < KT; ++kc, ++cnt) {
-          const int s = cnt % kStages;
-          if (!wait_bar(&empty[s], ((cnt / kStages) & 1u) ^ 1u, p, abort_flag)) {
+          if (kMx) {
+            const int r = cnt % kRawMx;
+            if (!wait_bar(&raw_empty[r], ((cnt / kRawMx) & 1u) ^ 1u, p, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint8_t* src = kGateUp ? p.w13mx + ((static_cast<size_t>(e) * MB + mb) * KT + kc) * kMxUnit
+                                         : p.w2mx + ((static_cast<size_t>(e) * MB + mb) * KT + kc) * kMxUnit;
+            nkm::mbar_arrive_expect_tx(&raw_full[r], kMxUnit);
+            nkm::bulk_g2s_plain(raw_base + r * kMxUnit, src, kMxUnit, &raw_full[r]);
+            continue;
+          }
+          const int s = cnt % S;
+          if (!wait_bar(&empty[s], ((cnt / S) & 1u) ^ 1u, p, abort_flag)) {
             ok = false;
             break;
           }
@@ -391,9 +464,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (!ok) {  // copies still in flight land before the CTA leaves (bounded)
         const uint64_t t0 = nkm::globaltimer_ns();
-        for (uint32_t c = (cnt >= kStages ? cnt - kStages : 0); c < cnt; ++c)
-          while (!nkm::mbar_try_wait(&full[c % kStages], (c / kStages) & 1u) && nkm::globaltimer_ns() - t0 < 1000000ull) {
+        const uint32_t depth = kMx ? kRawMx : S;
+        for (uint32_t c = (cnt >= depth ? cnt - depth : 0); c < cnt; ++c) {
+          uint64_t* bar = kMx ? &raw_full[c % kRawMx] : &full[c % S];
+          while (!nkm::mbar_try_wait(bar, (c / depth) & 1u) && nkm::globaltimer_ns() - t0 < 1000000ull) {
           }
+        }
       }
     }
   } else if (warp == 1) {
@@ -412,8 +488,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_after();
         for (int kc = 0; kc < KT; ++kc, ++cnt) {
-          const int s = cnt % kStages;
-          if (!wait_bar(&full[s], (cnt / kStages) & 1u, p, abort_flag)) {
+          const int s = cnt % S;
+          if (!wait_bar(&full[s], (cnt / S) & 1u, p, abort_flag) ||
+              (kMx && !wait_bar(&bfull[s], (cnt / S) & 1u, p, abort_flag))) {
             ok = false;
             break;
           }
@@ -433,12 +510,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (cnt > 0) {
         const uint32_t last = cnt - 1;
         const uint64_t t0 = nkm::globaltimer_ns();
-        while (!nkm::mbar_try_wait(&empty[last % kStages], (last / kStages) & 1u) &&
+        while (!nkm::mbar_try_wait(&empty[last % S], (last / S) & 1u) &&
                nkm::globaltimer_ns() - t0 < 2000000000ull) {
         }
       }
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------- epilogue (warps 2..5; TMEM lanes 32 (warp % 4) .. + 31)
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
@@ -484,6 +561,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) nkm::mbar_arrive(acc_empty);
+    }
+  } else if (kMx) {
+    // ---------------- MXFP8 converters (warps 6..9: thread t expands row t of each unit)
+    const int t = threadIdx.x - 192;
+    const bool issuer = t == 0;  // warp 6 lane 0 also issues the stage's B tiles
+    uint32_t cnt = 0, issued = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+      const int tile = item / MB;
+      const int n0 = p.tiles[3 * tile + 1], ncols = p.tiles[3 * tile + 2];
+      for (int kc = 0; kc < KT; ++kc, ++cnt) {
+        const int s = cnt % S, r = cnt % kRawMx;
+        // the stage's previous MMAs are done (A and B areas free)
+        if (!wait_bar(&empty[s], ((cnt / S) & 1u) ^ 1u, p, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* a = stage_base + s * kStageBytes;
+        if (issuer) {
+          nkm::mbar_arrive_expect_tx(&bfull[s], static_cast<uint32_t>(ncols) * 128u);
+          for (int rr = 0; rr < ncols; rr += 16) nkm::tma_load_2d(a + kABytes + rr * 128, &bmap, kc * kBK, n0 + rr, &bfull[s]);
+          ++issued;
+        }
+        if (!wait_bar(&raw_full[r], (cnt / kRawMx) & 1u, p, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mx_convert_row(raw_base + r * kMxUnit, a, t);
+        nkm::fence_proxy_async_smem();  // generic writes of the A tile before the MMA reads it
+        __syncwarp();
+        if (lane == 0) {
+          nkm::mbar_arrive(&raw_empty[r]);
+          nkm::mbar_arrive(&full[s]);
+        }
+      }
+    }
+    if (issuer && issued > 0) {  // B tiles still in flight land before the CTA leaves (bounded)
+      const uint64_t t0 = nkm::globaltimer_ns();
+      for (uint32_t c = (issued >= static_cast<uint32_t>(S) ? issued - S : 0); c < issued; ++c)
+        while (!nkm::mbar_try_wait(&bfull[c % S], (c / S) & 1u) && nkm::globaltimer_ns() - t0 < 1000000ull) {
+        }
     }
   }
   tc_fence_before();
@@ -572,7 +690,29 @@ int tc_check(const nkm_moe_tc_desc* d) {
     return NKM_ERR_ARG;
   if (d->max_tokens <= 0 || d->max_tokens > kMaxTokens) return NKM_ERR_ARG;
   if (!d->ln2 || !d->router || !d->w13 || !d->w2) return NKM_ERR_ARG;
+  if (d->weight_format != NKM_MOE_WEIGHTS_BF16 && d->weight_format != NKM_MOE_WEIGHTS_MXFP8) return NKM_ERR_ARG;
   return NKM_OK;
+}
+
+// MXFP8 expert weights, HF-style codes [count][rows][cols] (e4m3) and scales [count][rows][cols/32]
+// (e8m0), into the units the MXFP8 GEMM streams: unit (c, mb, kc) = 128 rows x 64 codes of
+// columns [64 kc, +64) then the rows' 2 scales.  gate_up (rows = 2I): unit rows 0-63 are gate rows
+// [64 mb, +64), rows 64-127 the up rows [I + 64 mb, +64); otherwise unit rows are [128 mb, +128).
+__global__ void pack_mxfp8_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+                                  uint8_t* __restrict__ dst, int64_t count, int64_t rows, int64_t cols, int gate_up) {
+  const int64_t KT = cols / 64, MB = gate_up ? rows / 128 : rows / 128, half = rows / 2;
+  const int64_t nunits = count * MB * KT;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nunits * kMxUnit;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t u = i / kMxUnit, off = i % kMxUnit;
+    const int64_t c = u / (MB * KT), rem = u % (MB * KT), mb = rem / KT, kc = rem % KT;
+    const int64_t r = off < 128 * 64 ? off / 64 : (off - 128 * 64) / 2;
+    const int64_t src_row = gate_up ? (r < 64 ? 64 * mb + r : half + 64 * mb + (r - 64)) : 128 * mb + r;
+    if (off < 128 * 64)
+      dst[i] = codes[(c * rows + src_row) * cols + 64 * kc + off % 64];
+    else
+      dst[i] = scales[(c * rows + src_row) * (cols / 32) + 2 * kc + (off - 128 * 64) % 2];
+  }
 }
 
 }  // namespace
@@ -632,16 +772,31 @@ extern "C" int nkm_moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const 
   p.hbuf = reinterpret_cast<uint16_t*>(ws + lay.hbuf);
   p.ypair = reinterpret_cast<float*>(ws + lay.ypair);
   p.P = lay.P;
+  const bool mx = d->weight_format == NKM_MOE_WEIGHTS_MXFP8;
+  p.w13mx = mx ? static_cast<const uint8_t*>(d->w13) : nullptr;
+  p.w2mx = mx ? static_cast<const uint8_t*>(d->w2) : nullptr;
   CUtensorMap w13m, w2m, xgm, hm;
+  memset(&w13m, 0, sizeof(w13m));
+  memset(&w2m, 0, sizeof(w2m));
   int rc;
-  if ((rc = encode(&w13m, d->w13, static_cast<uint64_t>(p.E) * 2 * p.I, p.H, 64)) ||
-      (rc = encode(&w2m, d->w2, static_cast<uint64_t>(p.E) * p.H, p.I, 64)) ||
+  if ((!mx && ((rc = encode(&w13m, d->w13, static_cast<uint64_t>(p.E) * 2 * p.I, p.H, 64)) ||
+               (rc = encode(&w2m, d->w2, static_cast<uint64_t>(p.E) * p.H, p.I, 64)))) ||
       (rc = encode(&xgm, p.xg, lay.P, p.H, 16)) || (rc = encode(&hm, p.hbuf, lay.P, p.I, 16)))
     return rc;
+  if (mx && ((reinterpret_cast<uintptr_t>(d->w13) & 15) || (reinterpret_cast<uintptr_t>(d->w2) & 15))) {
+    nkm::set_last_error("MXFP8 weight units must be 16-byte aligned");
+    return NKM_ERR_ARG;
+  }
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess ||
-        cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess ||
+    if (cudaFuncSetAttribute(tc_gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(tc_gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(tc_gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMx) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(tc_gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMx) !=
+            cudaSuccess ||
         cudaFuncSetAttribute(tc_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8192 * 4) != cudaSuccess) {
       nkm::set_last_error("cudaFuncSetAttribute failed");
       return NKM_ERR_CUDA;
@@ -656,8 +811,13 @@ extern "C" int nkm_moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const 
   tc_route_kernel<<<tokens, 256, p.H * 4, stream>>>(p);
   tc_plan_kernel<<<1, 256, 0, stream>>>(p);
   tc_gather_kernel<<<lay.P, 128, 0, stream>>>(p);
-  tc_gemm_kernel<true><<<sms, kTcThreads, kTcSmem, stream>>>(w13m, xgm, p);
-  tc_gemm_kernel<false><<<sms, kTcThreads, kTcSmem, stream>>>(w2m, hm, p);
+  if (mx) {
+    tc_gemm_kernel<true, true><<<sms, kTcThreadsMx, kTcSmemMx, stream>>>(w13m, xgm, p);
+    tc_gemm_kernel<false, true><<<sms, kTcThreadsMx, kTcSmemMx, stream>>>(w2m, hm, p);
+  } else {
+    tc_gemm_kernel<true, false><<<sms, kTcThreads, kTcSmem, stream>>>(w13m, xgm, p);
+    tc_gemm_kernel<false, false><<<sms, kTcThreads, kTcSmem, stream>>>(w2m, hm, p);
+  }
   tc_combine_kernel<<<tokens, 256, 0, stream>>>(p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -674,4 +834,29 @@ extern "C" int nkm_moe_tc_status(void* workspace, nkm_stream_t stream) {
       cudaMemcpy(&st, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return NKM_ERR_CUDA;
   return st;
+}
+
+extern "C" size_t nkm_mxfp8_experts_bytes(int32_t count, int32_t rows, int32_t cols) {
+  if (count <= 0 || rows <= 0 || cols <= 0 || rows % 128 || cols % 64) return 0;
+  return static_cast<size_t>(count) * (rows / 128) * (cols / 64) * kMxUnit;
+}
+
+extern "C" int nkm_pack_mxfp8_experts(const void* codes, const void* scales, void* dst, int32_t count, int32_t rows,
+                                      int32_t cols, int32_t gate_up, nkm_stream_t stream) {
+  if (!codes || !scales || !dst || nkm_mxfp8_experts_bytes(count, rows, cols) == 0 ||
+      (reinterpret_cast<uintptr_t>(dst) & 15)) {
+    nkm::set_last_error("nkm_pack_mxfp8_experts: rows % 128, cols % 64, 16-byte aligned destination required");
+    return NKM_ERR_ARG;
+  }
+  const int64_t n = static_cast<int64_t>(nkm_mxfp8_experts_bytes(count, rows, cols));
+  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 65535));
+  pack_mxfp8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(codes), static_cast<const uint8_t*>(scales), static_cast<uint8_t*>(dst), count, rows,
+      cols, gate_up ? 1 : 0);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    nkm::set_last_error(cudaGetErrorString(e));
+    return NKM_ERR_CUDA;
+  }
+  return NKM_OK;
 }

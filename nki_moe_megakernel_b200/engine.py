@@ -309,23 +309,53 @@ class Qwen3MoeMegakernel:
             raise _lib.NkmError(st, "decode kernel")
 
 
+def pack_mxfp8_experts(codes: torch.Tensor, scales: torch.Tensor, gate_up: bool, stream=None) -> torch.Tensor:
+    """MXFP8 expert matrices (e4m3 codes ``[E, rows, cols]`` as uint8 or float8_e4m3fn, e8m0
+    scales ``[E, rows, cols/32]`` uint8; CUDA) into the units the MXFP8 grouped GEMM streams
+    (``nkm_pack_mxfp8_experts``)."""
+    codes = codes.contiguous().view(torch.uint8) if codes.dtype != torch.uint8 else codes.contiguous()
+    scales = scales.contiguous()
+    E, R, K = codes.shape
+    n = lib().nkm_mxfp8_experts_bytes(E, R, K)
+    if n == 0:
+        raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_mxfp8_experts_bytes")
+    out = torch.empty(n, dtype=torch.uint8, device=codes.device)
+    st = stream if stream is not None else torch.cuda.current_stream(codes.device)
+    check(lib().nkm_pack_mxfp8_experts(codes.data_ptr(), scales.data_ptr(), out.data_ptr(), E, R, K, int(gate_up),
+                                       st.cuda_stream), "nkm_pack_mxfp8_experts")
+    return out
+
+
 class MoeTcBlock:
     """The MoE block on tcgen05/TMEM grouped GEMMs (``nkm_moe_block_tc``) for token counts that
     give the experts several columns each (config 3 and larger batches).  Weights in the plain
-    Hugging Face layouts: gate_up ``[E, 2I, H]`` (gate rows then up rows), down ``[E, H, I]``."""
+    Hugging Face layouts: gate_up ``[E, 2I, H]`` (gate rows then up rows), down ``[E, H, I]``;
+    or MXFP8 (``mxfp8=(gate_up codes, gate_up scales, down codes, down scales)``, OCP MX: e4m3
+    codes and e8m0 scales per 32 along K, in the same row layouts; ``gate_up``/``down`` then
+    unused)."""
 
-    def __init__(self, ln2: torch.Tensor, router: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, *,
-                 eps: float, top_k: int, max_tokens: int, router_bias: Optional[torch.Tensor] = None, device=None):
+    def __init__(self, ln2: torch.Tensor, router: torch.Tensor, gate_up: Optional[torch.Tensor],
+                 down: Optional[torch.Tensor], *, eps: float, top_k: int, max_tokens: int,
+                 router_bias: Optional[torch.Tensor] = None, device=None, mxfp8=None):
         self.device = torch.device(device if device is not None else "cuda")
         self.ln2 = ln2.to(self.device, BF16).contiguous()
         self.router = router.to(self.device, BF16).contiguous()
-        self.w13 = gate_up.to(self.device, BF16).contiguous()
-        self.w2 = down.to(self.device, BF16).contiguous()
         self.router_bias = None if router_bias is None else router_bias.to(self.device, torch.float32).contiguous()
-        E, I2, H = self.w13.shape
+        if mxfp8 is not None:
+            gc, gs, dc, ds = (t.to(self.device) for t in mxfp8)
+            E, I2, H = gc.shape
+            self.w13 = pack_mxfp8_experts(gc, gs, True)
+            self.w2 = pack_mxfp8_experts(dc, ds, False)
+            fmt = _lib.NKM_MOE_WEIGHTS_MXFP8
+        else:
+            self.w13 = gate_up.to(self.device, BF16).contiguous()
+            self.w2 = down.to(self.device, BF16).contiguous()
+            E, I2, H = self.w13.shape
+            fmt = _lib.NKM_MOE_WEIGHTS_BF16
         self.H, self.E, self.K, self.I = H, E, top_k, I2 // 2
         self._desc = _lib.nkm_moe_tc_desc(H, E, top_k, self.I, eps, self.ln2.data_ptr(), self.router.data_ptr(),
-                                          _ptr(self.router_bias), self.w13.data_ptr(), self.w2.data_ptr(), max_tokens)
+                                          _ptr(self.router_bias), self.w13.data_ptr(), self.w2.data_ptr(), max_tokens,
+                                          fmt)
         n = lib().nkm_moe_tc_workspace_bytes(ctypes.byref(self._desc))
         if n == 0:
             raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_moe_tc_workspace_bytes")
@@ -361,8 +391,10 @@ class Qwen3MoeWideDecoder:
       one read of the 622 MB head for the whole batch).
 
     ``layers``: per layer a dict of Hugging Face layout tensors (``wq, wk, wv, wo, q_norm,
-    k_norm, ln1, ln2, router, gate_up, down``, optional ``router_bias``); a list may repeat the same
-    dict (weights shared by several layers; each layer still has its own K/V pages)."""
+    k_norm, ln1, ln2, router, gate_up, down``, optional ``router_bias``; MXFP8 experts as
+    ``mxfp8 = (gate_up codes, gate_up scales, down codes, down scales)`` in place of ``gate_up``
+    and ``down``); a list may repeat the same dict (weights shared by several layers; each layer
+    still has its own K/V pages)."""
 
     def __init__(self, shape: Qwen3MoeShape, layers: Sequence[Dict[str, torch.Tensor]], *, max_batch: int,
                  num_blocks: int, final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
@@ -378,9 +410,9 @@ class Qwen3MoeWideDecoder:
                 continue
             att[id(lw)] = GpuLayer(lw["wq"], lw["wk"], lw["wv"], lw["wo"], lw["q_norm"], lw["k_norm"], lw["ln1"],
                                    None, None, None, None, moe=False)
-            moe[id(lw)] = MoeTcBlock(lw["ln2"], lw["router"], lw["gate_up"], lw["down"], eps=shape.rms_norm_eps,
-                                     top_k=shape.num_experts_per_tok, max_tokens=max_batch,
-                                     router_bias=lw.get("router_bias"), device=self.device)
+            moe[id(lw)] = MoeTcBlock(lw["ln2"], lw["router"], lw.get("gate_up"), lw.get("down"),
+                                     eps=shape.rms_norm_eps, top_k=shape.num_experts_per_tok, max_tokens=max_batch,
+                                     router_bias=lw.get("router_bias"), device=self.device, mxfp8=lw.get("mxfp8"))
         self.moe = [moe[id(lw)] for lw in layers]
         self.attn = Qwen3MoeMegakernel(shape, [att[id(lw)] for lw in layers], max_batch=self.row_chunk,
                                        num_blocks=num_blocks, rope_max_pos=rope_max_pos, device=self.device)

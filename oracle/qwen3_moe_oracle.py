@@ -114,6 +114,29 @@ def rstd_fixed(sumsq: torch.Tensor, n: int, eps: float) -> torch.Tensor:
     return (1.0 / s.to(torch.float64)).to(F32)
 
 
+def mxfp8_quantize(w: torch.Tensor):
+    """OCP MX (Microscaling Formats v1.0) quantisation of ``w [..., K]`` (K % 32 == 0) to MXFP8:
+    per block of 32 along K the shared scale is ``X = 2^(floor(log2(amax)) - 8)`` (8 = the largest
+    e4m3 exponent), stored as the e8m0 byte ``127 + floor(log2(amax)) - 8``; elements are
+    ``e4m3(clip(w / X, +-448))`` (round to nearest even).  An all-zero block gets the smallest
+    scale.  Returns (codes uint8 = e4m3 bits, scales uint8)."""
+    shp = w.shape
+    b = w.to(F32).reshape(*shp[:-1], shp[-1] // 32, 32)
+    amax = b.abs().amax(-1)
+    e = torch.floor(torch.log2(amax.clamp_min(2.0 ** -126))) - 8
+    e = torch.where(amax > 0, e, torch.full_like(e, -127.0)).clamp(-127, 127)
+    q = (b / torch.exp2(e)[..., None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8).reshape(shp), (e + 127).to(torch.uint8)
+
+
+def mxfp8_dequant(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 values of MXFP8 codes ``[..., K]`` (e4m3 bits) with e8m0 scales ``[..., K/32]``."""
+    v = codes.view(torch.float8_e4m3fn).to(F32)
+    shp = v.shape
+    s = torch.exp2(scales.to(F32) - 127.0)
+    return (v.reshape(*shp[:-1], shp[-1] // 32, 32) * s[..., None]).reshape(shp)
+
+
 def rstd_fixed_div(sumsq: torch.Tensor, n: int, eps: float) -> torch.Tensor:
     """``1 / sqrt(sumsq / n + eps)`` with an IEEE fp32 divide by ``n`` (for ``n`` whose reciprocal
     is not exact, as the padded-hidden RMSNorm of the GPT-OSS kernel computes it), then the
