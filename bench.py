@@ -39,6 +39,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--stage-times", action="store_true", help="print a per-stage time breakdown to stderr")
+    ap.add_argument("--gptoss-layers", type=int, default=24,
+                    help="gpt-oss workload: decoder layers (24 = GPT-OSS-20B; fewer for small profiling cases)")
     ap.add_argument("--weights", choices=["bf16", "mxfp8"], default="bf16",
                     help="expert weights of the tcgen05 workloads (moe-tc, wide): bf16 or MXFP8")
     ap.add_argument("--workload", choices=["qwen3", "gpt-oss", "moe-tc", "wide"], default="qwen3",
@@ -563,11 +565,13 @@ def _events_time(torch, stream, fn, steps, warmup):
         fn()
     torch.cuda.synchronize()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    _nvtx(torch, "timed")  # `ncu --nvtx --nvtx-include timed/` lists exactly the timed launches
     evs[0].record(stream)
     for i in range(steps):
         fn()
         evs[i + 1].record(stream)
     torch.cuda.synchronize()
+    _nvtx(torch, None)
     per = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
     return evs[0].elapsed_time(evs[-1]) / steps, per
 
@@ -582,7 +586,7 @@ def run_gpt_oss(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     B, ctx = 16, 4096
-    shape = GptOssShape()
+    shape = GptOssShape(num_hidden_layers=args.gptoss_layers)
     H, D, E, I, V = shape.hidden_size, shape.head_dim, shape.num_local_experts, shape.intermediate_size, shape.vocab_size
     nq, nkv, L = shape.num_attention_heads, shape.num_key_value_heads, shape.num_hidden_layers
     g = torch.Generator(device=dev).manual_seed(args.seed)
@@ -633,7 +637,7 @@ def run_gpt_oss(args):
         "metric": "GPT-OSS-20B decode tokens/s at B=16 ctx 4096 (config 4)", "value": B / (ms / 1e3), "unit": UNIT,
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "p50_ms": statistics.median(per),
         "higher_is_better": True, "dtype": "bf16 activations, MXFP4 experts", "data": "synthetic (seeded random)",
-        "config": {"workload": "gpt-oss-20b decode step (24 layers + LM head)", "global_batch": B, "ctx": ctx,
+        "config": {"workload": f"gpt-oss-20b decode step ({L} layers + LM head)", "global_batch": B, "ctx": ctx,
                    "distinct_experts_per_layer_mean": sum(distinct) / L},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "algorithmic_bytes_per_step": nbytes,

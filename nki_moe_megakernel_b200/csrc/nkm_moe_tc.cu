@@ -15,11 +15,14 @@
 //            epilogue forms h = bf16(bf16(SiLU(bf16 gate)) * bf16 up) (moe_fused_nki.py:506-527)
 //   gemm<0>  down: A = 128 rows of W2[e], B = h; y = acc * routing weight (fp32) per pair
 //   combine  out[t] = bf16(sum over the token's k slots in slot order) (+ residual)
-// Warp roles of the GEMM (192 threads): warp 0 TMA producer (4-stage ring), warp 1 TMEM
-// allocation + MMA issue (one elected lane), warps 2-5 epilogue (warp w reads TMEM lanes
-// 32 (w % 4) .. + 31).  Every mbarrier wait is bounded (2 s); on expiry the CTA records
-// NKM_ERR_TIMEOUT, all roles leave their loops, outstanding copies and MMAs are waited for
-// (bounded) and TMEM is freed before the CTA exits.  No load uses cluster multicast.
+// Warp roles of the GEMM (192 threads): warp 0 TMA producer (8-stage ring of 128-row weight tiles
+// and <= 64-column token tiles), warp 1 TMEM allocation + MMA issue (one elected lane; two 64-column
+// accumulators alternate so the next tile's MMAs overlap this tile's epilogue), warps 2-5 epilogue
+// (warp w reads TMEM lanes 32 (w % 4) .. + 31).  With MXFP8 weights (352 threads) warp 0 streams
+// the packed weight units, warps 6-9 expand them to bf16 tiles, warp 10 loads the token tiles.
+// Every mbarrier wait is bounded (2 s); on expiry the CTA records NKM_ERR_TIMEOUT, all roles
+// leave their loops, outstanding copies and MMAs are waited for (bounded) and TMEM is freed
+// before the CTA exits.  No load uses cluster multicast.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -40,19 +43,23 @@ namespace {
 using nkm::smem_addr;
 
 constexpr int kTcThreads = 192;
-constexpr int kTcThreadsMx = 320;         // + 4 converter warps (MXFP8 weights)
-constexpr int kStages = 4;
-constexpr int kStagesMx = 3;              // bf16 operand stages with MXFP8 weights
+constexpr int kTcThreadsMx = 352;         // + 4 converter warps and a B-tile producer warp (MXFP8 weights)
+constexpr int kStages = 8;
+constexpr int kStagesMx = 6;              // bf16 operand stages with MXFP8 weights
 constexpr int kRawMx = 8;                 // MXFP8 weight units in flight per CTA
 constexpr int kMxUnit = 128 * 64 + 128 * 2;  // 128 rows x 64 e4m3 codes, then 128 rows x 2 e8m0 scales
 constexpr int kBK = 64;                   // K elements per stage (128 bytes: one swizzle atom row)
-constexpr int kMaxN = 256;                // columns of one tile
+constexpr int kMaxN = 64;                 // columns of one tile (an expert with more tokens has several tiles)
+constexpr int kAccCols = 64;              // TMEM columns of one accumulator; two accumulators alternate
 constexpr int kABytes = 128 * 128;        // A stage: 128 rows x 128 bytes
-constexpr int kBBytes = kMaxN * 128;      // B stage: up to 256 rows x 128 bytes
+constexpr int kBBytes = kMaxN * 128;      // B stage: up to 64 rows x 128 bytes
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kXchBytes = 64 * 16 * 4;    // gate/up epilogue exchange (64 rows x 16 columns fp32)
-constexpr int kTcSmem = kStages * kStageBytes + kXchBytes + 256 + 1024;
-constexpr int kTcSmemMx = kStagesMx * kStageBytes + kRawMx * kMxUnit + kXchBytes + 256 + 1024;
+constexpr int kBarBytes = 512;            // mbarriers, TMEM address, abort flag
+constexpr int kTcSmem = kStages * kStageBytes + kXchBytes + kBarBytes + 1024;
+constexpr int kTcSmemMx = kStagesMx * kStageBytes + kRawMx * kMxUnit + kXchBytes + kBarBytes + 1024;
+static_assert(kTcSmem <= 232448, "bf16 GEMM shared memory");
+static_assert((3 * kStages + 2 * kRawMx + 4) * 8 + 8 <= kBarBytes, "barrier area");
 static_assert(kTcSmemMx <= 232448, "MXFP8 GEMM shared memory");
 static_assert(kMxUnit % 16 == 0, "bulk copy size");
 constexpr int kMaxTokens = 512;
@@ -345,22 +352,53 @@ __device__ __forceinline__ uint2 e4m3x4_bf16(uint32_t w, float sc) {
   const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
   return make_uint2(nkm::pack_bf2(a.x * sc, a.y * sc), nkm::pack_bf2(b.x * sc, b.y * sc));
 }
+// Two e4m3 codes with non-zero exponent fields, spread one per 16-bit half (code in the low byte),
+// times 2^(s-127), as bf16x2 bits by integer arithmetic: e4m3 s.eeee.mmm is 2^(e-7) (1 + m/8), so
+// the bf16 fields are the sign, exponent e + 120 + (s - 127) and mantissa m << 4.  e2 holds
+// (120 + s - 127) << 7 in both halves; valid for 7 <= s <= 246 (the exponent stays in 1..254).
+__device__ __forceinline__ uint32_t e4m3x2_bf16x2_int(uint32_t x, uint32_t e2) {
+  return (x & 0x00800080u) * 256u + (x & 0x007f007fu) * 16u + e2;
+}
+// 16 codes (one 16-byte load) times 2^(s-127) to 8 bf16x2 words.  Codes whose exponent field is
+// zero (zero, subnormal), NaN codes, or a scale outside 7..246 take the conversion instructions.
+__device__ __forceinline__ void e4m3x16_bf16(const uint4 c, uint32_t s, float sc, uint32_t (&o)[8]) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+  uint32_t zero_exp = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    zero_exp |= __vcmpeq4(w[i] & 0x78787878u, 0u) | __vcmpeq4(w[i] & 0x7f7f7f7fu, 0x7f7f7f7fu);  // + NaN codes
+  if (zero_exp == 0u && s >= 7u && s <= 246u) {
+    const uint32_t e = s - 7u;  // 120 + s - 127
+    const uint32_t e2 = (e << 7) | (e << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[2 * i] = e4m3x2_bf16x2_int(__byte_perm(w[i], 0u, 0x4140), e2);
+      o[2 * i + 1] = e4m3x2_bf16x2_int(__byte_perm(w[i], 0u, 0x4342), e2);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint2 b = e4m3x4_bf16(w[i], sc);
+      o[2 * i] = b.x;
+      o[2 * i + 1] = b.y;
+    }
+  }
+}
 // Row `row` of an MXFP8 unit (64 codes + 2 scales) into a bf16 K-major tile row with the
 // 128-byte swizzle the MMA descriptor expects (16-byte chunk c of row r at c ^ (r % 8)).
 __device__ __forceinline__ void mx_convert_row(const uint8_t* unit, uint8_t* a_tile, int row) {
   const uint4* src = reinterpret_cast<const uint4*>(unit + row * 64);
   const uint32_t sw = *reinterpret_cast<const uint16_t*>(unit + 128 * 64 + row * 2);
-  const float sc0 = e8m0_f32(sw & 0xffu), sc1 = e8m0_f32(sw >> 8);
+  const uint32_t s0 = sw & 0xffu, s1 = sw >> 8;
+  const float sc0 = e8m0_f32(s0), sc1 = e8m0_f32(s1);
   uint8_t* dst = a_tile + row * 128;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {  // 16 codes = 2 output chunks of 8
-    const uint4 c = src[q];
-    const float sc = q < 2 ? sc0 : sc1;
-    const uint2 b0 = e4m3x4_bf16(c.x, sc), b1 = e4m3x4_bf16(c.y, sc);
-    const uint2 b2 = e4m3x4_bf16(c.z, sc), b3 = e4m3x4_bf16(c.w, sc);
+    uint32_t o[8];
+    e4m3x16_bf16(src[q], q < 2 ? s0 : s1, q < 2 ? sc0 : sc1, o);
     const int c0 = 2 * q, c1 = 2 * q + 1;
-    *reinterpret_cast<uint4*>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(b0.x, b0.y, b1.x, b1.y);
-    *reinterpret_cast<uint4*>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(b2.x, b2.y, b3.x, b3.y);
+    *reinterpret_cast<uint4*>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
   }
 }
 
@@ -372,7 +410,8 @@ __device__ __forceinline__ void mx_convert_row(const uint8_t* unit, uint8_t* a_t
 // kMx (MXFP8 weights): the A operand arrives as nkm_pack_mxfp8_experts units (e4m3 codes + e8m0
 // scales of the same 128 rows, one 1-D bulk copy each, kRawMx in flight) and warps 6-9 expand
 // each unit into the bf16 swizzled A tile (exact: code x power of two); the MMA then runs as for
-// bf16 weights.  Warp 6 lane 0 also issues the B (token) tiles of the stage it converts into.
+// bf16 weights.  Warp 10 issues the B (token) tiles of each stage.  Two TMEM accumulators
+// alternate, so the MMAs of a tile run while the epilogue reads the previous one.
 template <bool kGateUp, bool kMx>
 __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcParams p) {
@@ -384,9 +423,9 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
   float* xch = reinterpret_cast<float*>(raw_base + (kMx ? kRawMx * kMxUnit : 0));
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xch) + kXchBytes);
   uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* bfull = acc_empty + 1;      // kMx: B tiles of a stage landed (S)
+  uint64_t* acc_full = empty + S;       // [2]: accumulator b written
+  uint64_t* acc_empty = acc_full + 2;   // [2]: accumulator b read by the epilogue
+  uint64_t* bfull = acc_empty + 2;      // kMx: B tiles of a stage landed (S)
   uint64_t* raw_full = bfull + S;       // kMx: weight unit landed (kRawMx)
   uint64_t* raw_empty = raw_full + kRawMx;  // kMx: weight unit converted (kRawMx)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(raw_empty + kRawMx);
@@ -406,13 +445,15 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
       nkm::mbar_init(&raw_full[r], 1);
       nkm::mbar_init(&raw_empty[r], 4);
     }
-    nkm::mbar_init(acc_full, 1);
-    nkm::mbar_init(acc_empty, 4);  // one arrival per epilogue warp
+    for (int b = 0; b < 2; ++b) {
+      nkm::mbar_init(&acc_full[b], 1);
+      nkm::mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
     *abort_flag = 0;
     nkm::fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, kMaxN);
+    tmem_alloc(tmem_holder, 2 * kAccCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -481,8 +522,9 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
         const int tile = item / MB;
         const int ncols = p.tiles[3 * tile + 2];
         const uint32_t idesc = idesc_bf16(128, ncols);
-        // the epilogue has read the previous tile's accumulator
-        if (!wait_bar(acc_empty, (acc_round & 1u) ^ 1u, p, abort_flag)) {
+        const uint32_t ab = acc_round & 1u, d_tmem = tmem + ab * kAccCols;
+        // the epilogue has read this accumulator's previous tile (two tiles back)
+        if (!wait_bar(&acc_empty[ab], ((acc_round >> 1) & 1u) ^ 1u, p, abort_flag)) {
           ok = false;
           break;
         }
@@ -500,11 +542,11 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
           const uint64_t ad = sw128_desc(a), bd = sw128_desc(b);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)  // 16 bf16 = 32 bytes per MMA: start address + 2
-            tc_mma(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kc | kk) != 0);
+            tc_mma(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kc | kk) != 0);
           tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
         if (!ok) break;
-        tc_commit(acc_full);
+        tc_commit(&acc_full[ab]);
       }
       // every MMA issued has completed before TMEM is released (bounded)
       if (cnt > 0) {
@@ -521,14 +563,15 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     uint32_t acc_round = 0;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++acc_round) {
-      if (!wait_bar(acc_full, acc_round & 1u, p, abort_flag)) break;
+      const uint32_t ab = acc_round & 1u;
+      if (!wait_bar(&acc_full[ab], (acc_round >> 1) & 1u, p, abort_flag)) break;
       tc_fence_after();
       const int tile = item / MB, mb = item - tile * MB;
       const int n0 = p.tiles[3 * tile + 1], ncols = p.tiles[3 * tile + 2];
       const int row = 32 * q + lane;  // accumulator row of this thread
       for (int c0 = 0; c0 < ncols; c0 += 16) {
         float v[16];
-        tmem_ld16(tmem + lane_base + static_cast<uint32_t>(c0), v);
+        tmem_ld16(tmem + lane_base + ab * kAccCols + static_cast<uint32_t>(c0), v);
         if (kGateUp) {
           // rows 0-63: gate j = row; rows 64-127: up j = row - 64 (exchange through shared memory)
           if (row >= 64) {
@@ -560,35 +603,23 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) nkm::mbar_arrive(acc_empty);
+      if (lane == 0) nkm::mbar_arrive(&acc_empty[ab]);
     }
-  } else if (kMx) {
+  } else if (kMx && warp < 10) {
     // ---------------- MXFP8 converters (warps 6..9: thread t expands row t of each unit)
     const int t = threadIdx.x - 192;
-    const bool issuer = t == 0;  // warp 6 lane 0 also issues the stage's B tiles
-    uint32_t cnt = 0, issued = 0;
+    uint32_t cnt = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-      const int tile = item / MB;
-      const int n0 = p.tiles[3 * tile + 1], ncols = p.tiles[3 * tile + 2];
       for (int kc = 0; kc < KT; ++kc, ++cnt) {
         const int s = cnt % S, r = cnt % kRawMx;
-        // the stage's previous MMAs are done (A and B areas free)
-        if (!wait_bar(&empty[s], ((cnt / S) & 1u) ^ 1u, p, abort_flag)) {
+        // the stage's previous MMAs are done (its A area is free)
+        if (!wait_bar(&empty[s], ((cnt / S) & 1u) ^ 1u, p, abort_flag) ||
+            !wait_bar(&raw_full[r], (cnt / kRawMx) & 1u, p, abort_flag)) {
           ok = false;
           break;
         }
-        uint8_t* a = stage_base + s * kStageBytes;
-        if (issuer) {
-          nkm::mbar_arrive_expect_tx(&bfull[s], static_cast<uint32_t>(ncols) * 128u);
-          for (int rr = 0; rr < ncols; rr += 16) nkm::tma_load_2d(a + kABytes + rr * 128, &bmap, kc * kBK, n0 + rr, &bfull[s]);
-          ++issued;
-        }
-        if (!wait_bar(&raw_full[r], (cnt / kRawMx) & 1u, p, abort_flag)) {
-          ok = false;
-          break;
-        }
-        mx_convert_row(raw_base + r * kMxUnit, a, t);
+        mx_convert_row(raw_base + r * kMxUnit, stage_base + s * kStageBytes, t);
         nkm::fence_proxy_async_smem();  // generic writes of the A tile before the MMA reads it
         __syncwarp();
         if (lane == 0) {
@@ -597,17 +628,37 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
         }
       }
     }
-    if (issuer && issued > 0) {  // B tiles still in flight land before the CTA leaves (bounded)
-      const uint64_t t0 = nkm::globaltimer_ns();
-      for (uint32_t c = (issued >= static_cast<uint32_t>(S) ? issued - S : 0); c < issued; ++c)
-        while (!nkm::mbar_try_wait(&bfull[c % S], (c / S) & 1u) && nkm::globaltimer_ns() - t0 < 1000000ull) {
+  } else if (kMx) {
+    // ---------------- B-tile producer (warp 10): the expert's token tiles of each stage
+    if (lane == 0) {
+      uint32_t cnt = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+        const int tile = item / MB;
+        const int n0 = p.tiles[3 * tile + 1], ncols = p.tiles[3 * tile + 2];
+        for (int kc = 0; kc < KT; ++kc, ++cnt) {
+          const int s = cnt % S;
+          if (!wait_bar(&empty[s], ((cnt / S) & 1u) ^ 1u, p, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* b = stage_base + s * kStageBytes + kABytes;
+          nkm::mbar_arrive_expect_tx(&bfull[s], static_cast<uint32_t>(ncols) * 128u);
+          for (int rr = 0; rr < ncols; rr += 16) nkm::tma_load_2d(b + rr * 128, &bmap, kc * kBK, n0 + rr, &bfull[s]);
         }
+      }
+      if (!ok) {  // B tiles still in flight land before the CTA leaves (bounded)
+        const uint64_t t0 = nkm::globaltimer_ns();
+        for (uint32_t c = (cnt >= static_cast<uint32_t>(S) ? cnt - S : 0); c < cnt; ++c)
+          while (!nkm::mbar_try_wait(&bfull[c % S], (c / S) & 1u) && nkm::globaltimer_ns() - t0 < 1000000ull) {
+          }
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kMaxN);
+  if (warp == 1) tmem_dealloc(tmem, 2 * kAccCols);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {

@@ -23,6 +23,11 @@ pytestmark = pytest.mark.gpu
 
 ATOL = 2e-2
 COS = 0.999
+# The oracle layer is fed the decoder's input of the layer, but its MoE block sees its own attention
+# output: router logits on the two sides then differ by up to ~1e-2, and where the kernel's expert
+# set is a top-k of the oracle's logits within this gap the oracle takes it (main.py validate's
+# default --routing-divergence-tol).
+ROUTE_GAP = 2e-2
 
 
 def _excess(a: torch.Tensor, b: torch.Tensor) -> float:
@@ -81,9 +86,9 @@ def test_wide_batch_64_two_layers(dev):
         lg = O.router_logits_fixed(O.rmsnorm_hidden_faithful(mids[li].to(BF16), lw.ln2, cfg.rms_eps, True), lw.router)
         assert torch.equal(idx[li], O.topk_select(lg, cfg.top_k)), li
         fa = O.decoder_layer(inp.to(BF16), lw, cfg, k0[li].clone(), v0[li].clone(), pos, table, cos16, sin16,
-                             "faithful", O.LayerTrace(topk_hint=idx[li], hint_gap=1e-4))
+                             "faithful", O.LayerTrace(topk_hint=idx[li], hint_gap=ROUTE_GAP))
         f32 = O.decoder_layer(inp.float(), lw, cfg, k0[li].clone(), v0[li].clone(), pos, table, cos32, sin32,
-                              "fp32", O.LayerTrace(topk_hint=idx[li], hint_gap=1e-4))
+                              "fp32", O.LayerTrace(topk_hint=idx[li], hint_gap=ROUTE_GAP))
         rf, r32 = O.compare(outs[li], fa.float()), O.compare(outs[li], f32)
         ex = _excess(outs[li], f32)
         print(f"[wide B=64 layer {li}] vs fp32 {r32} (beyond one bf16 ulp: {ex:.4g}); vs the bf16-faithful "
