@@ -622,6 +622,21 @@ def run_gpt_oss(args):
     eng.check_status()
     distinct = [len(torch.unique(tr["topk_idx"][l])) for l in range(L)]
     del tr
+    if args.stage_times:
+        names = ["qkv", "qkv_fin", "attention", "combine", "o_proj", "o_resid", "norm_router", "gate_up", "down",
+                 "moe_resid"]
+        acc = {}
+        for _ in range(5):
+            ts = eng.decode_step(pos, table, input_ids=ids, stage_times=True)["stage_ns"].cpu().tolist()
+            d = [(ts[i + 1] - ts[i]) / 1e3 for i in range(len(ts) - 1)]
+            for l in range(L):
+                for k, n in enumerate(names):
+                    acc.setdefault(n, []).append(d[1 + 10 * l + k])
+            acc.setdefault("lm_head+out", []).append(d[-1])
+            acc.setdefault("total", []).append((ts[-1] - ts[0]) / 1e3)
+        med = {k: round(statistics.median(v), 2) for k, v in acc.items()}
+        print(json.dumps({"stage_us_median": med, "per_layer_us": round(sum(med[n] for n in names), 2)}),
+              file=sys.stderr, flush=True)
     stream = torch.cuda.current_stream(dev)
     with ClockSampler(0) as clk:
         ms, per = _events_time(torch, stream, lambda: eng.decode_step(pos, table, input_ids=ids, out=out), args.steps,

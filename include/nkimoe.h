@@ -372,6 +372,8 @@ typedef struct nkm_gptoss_step {
   float* trace_router_logits;  /* fp32 [nl, B, E] */
   int32_t* trace_topk_idx;     /* [nl, B, K] */
   float* trace_topk_w;         /* [nl, B, K] */
+  int64_t* trace_stage_ns;     /* [2 + 10 nl + 1] or NULL: globaltimer of CTA 0 at kernel start, after
+                                  every grid barrier (the input copy, then ten per layer) and at the end */
 } nkm_gptoss_step;
 
 typedef struct nkm_gptoss nkm_gptoss;

@@ -78,7 +78,8 @@ class nkm_gptoss_step(ctypes.Structure):
                 ("block_table", c_void_p), ("max_blocks_per_seq", c_int32), ("y_out", c_void_p),
                 ("logits_out", c_void_p), ("first_layer", c_int32), ("num_layers", c_int32),
                 ("trace_qkv", c_void_p), ("trace_resid_mid", c_void_p), ("trace_resid_out", c_void_p),
-                ("trace_router_logits", c_void_p), ("trace_topk_idx", c_void_p), ("trace_topk_w", c_void_p)]
+                ("trace_router_logits", c_void_p), ("trace_topk_idx", c_void_p), ("trace_topk_w", c_void_p),
+                ("trace_stage_ns", c_void_p)]
 
 
 class nkm_moe_tc_desc(ctypes.Structure):

@@ -282,6 +282,7 @@ int nkm_gptoss_decode_step(nkm_gptoss* h, const nkm_gptoss_step* s, nkm_stream_t
   p.tr_rlogits = s->trace_router_logits;
   p.tr_idx = s->trace_topk_idx;
   p.tr_w = s->trace_topk_w;
+  p.tr_stage = s->trace_stage_ns;
   uint8_t* ws = h->ws;
   p.bar = reinterpret_cast<unsigned*>(ws + h->lay.bar);
   p.status = reinterpret_cast<int*>(ws + h->lay.status);

@@ -102,6 +102,7 @@ struct Params {
   float* tr_rlogits;
   int* tr_idx;
   float* tr_w;
+  int64_t* tr_stage;
   unsigned* bar;
   int* status;
   float* resid;
@@ -169,6 +170,7 @@ __device__ __noinline__ bool grid_sync(const Params& p, unsigned& bar_k, int* fl
       __nanosleep(20);
     }
     *flag = ok;
+    if (p.tr_stage && blockIdx.x == 0) p.tr_stage[bar_k + 1] = static_cast<int64_t>(globaltimer_ns());
   }
   ++bar_k;
   __syncthreads();
@@ -1000,6 +1002,7 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
   Route* rt = reinterpret_cast<Route*>(smem + lay.route_off);
   int* flag = reinterpret_cast<int*>(smem + lay.flag_off);
   unsigned bar_k = 0;
+  if (p.tr_stage && blockIdx.x == 0 && threadIdx.x == 0) p.tr_stage[0] = static_cast<int64_t>(globaltimer_ns());
 
   [&]() {
     // residual (fp32) <- embeddings / hidden input
@@ -1075,6 +1078,8 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
       __syncthreads();
       lm_head(p, xs);
     }
+    __syncthreads();
+    if (p.tr_stage && blockIdx.x == 0 && threadIdx.x == 0) p.tr_stage[bar_k + 1] = static_cast<int64_t>(globaltimer_ns());
   }();
   // end of the launch: the last CTA out resets the barrier counter
   __syncthreads();

@@ -18,8 +18,9 @@
 // Warp roles of the GEMM (192 threads): warp 0 TMA producer (8-stage ring of 128-row weight tiles
 // and <= 64-column token tiles), warp 1 TMEM allocation + MMA issue (one elected lane; two 64-column
 // accumulators alternate so the next tile's MMAs overlap this tile's epilogue), warps 2-5 epilogue
-// (warp w reads TMEM lanes 32 (w % 4) .. + 31).  With MXFP8 weights (352 threads) warp 0 streams
-// the packed weight units, warps 6-9 expand them to bf16 tiles, warp 10 loads the token tiles.
+// (warp w reads TMEM lanes 32 (w % 4) .. + 31).  With MXFP8 weights (736 threads) warp 0 streams
+// the packed weight units, warps 6-21 expand them to bf16 tiles (a quarter row per thread), warp
+// 22 loads the token tiles.
 // Every mbarrier wait is bounded (2 s); on expiry the CTA records NKM_ERR_TIMEOUT, all roles
 // leave their loops, outstanding copies and MMAs are waited for (bounded) and TMEM is freed
 // before the CTA exits.  No load uses cluster multicast.
@@ -43,7 +44,8 @@ namespace {
 using nkm::smem_addr;
 
 constexpr int kTcThreads = 192;
-constexpr int kTcThreadsMx = 352;         // + 4 converter warps and a B-tile producer warp (MXFP8 weights)
+constexpr int kConvWarps = 16;            // MXFP8: converter warps (thread = a quarter row of a weight unit)
+constexpr int kTcThreadsMx = 192 + kConvWarps * 32 + 32;  // + converters and a B-tile producer warp
 constexpr int kStages = 8;
 constexpr int kStagesMx = 6;              // bf16 operand stages with MXFP8 weights
 constexpr int kRawMx = 8;                 // MXFP8 weight units in flight per CTA
@@ -185,11 +187,15 @@ __global__ void __launch_bounds__(256) tc_route_kernel(TcParams p) {
   const uint16_t* xr = p.x + static_cast<size_t>(t) * p.H;
   if (warp == 0) {
     float s = 0.f;
-    for (int i = 0; i * 256 < p.H; ++i)
+    for (int i = 0; i * 256 < p.H; ++i) {
+      const uint4 q = *reinterpret_cast<const uint4*>(xr + 256 * i + 8 * lane);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float v = nkm::bf2f(xr[256 * i + 8 * lane + j]);
+        const float v = (j & 1) ? nkm::hi_bf(w[j >> 1]) : nkm::lo_bf(w[j >> 1]);
         s = __fadd_rn(s, __fmul_rn(v, v));
       }
+    }
     s = warp_sum_fixed(s);
     if (lane == 0) {
       const float v = __fadd_rn(__fmul_rn(s, 1.0f / static_cast<float>(p.H)), p.eps);
@@ -207,11 +213,16 @@ __global__ void __launch_bounds__(256) tc_route_kernel(TcParams p) {
   for (int e = warp; e < p.E; e += 8) {
     const uint16_t* wr = p.router + static_cast<size_t>(e) * p.H;
     float acc = 0.f;
-    for (int i = 0; i * 256 < p.H; ++i)
-      for (int j = 0; j < 8; ++j) {
-        const int k = 256 * i + 8 * lane + j;
-        acc = __fadd_rn(acc, __fmul_rn(nkm::bf2f(wr[k]), xs32[k]));
-      }
+    for (int i = 0; i * 256 < p.H; ++i) {
+      const int k = 256 * i + 8 * lane;
+      const uint4 q = nkm::ldnc128(wr + k);
+      const float4 a = *reinterpret_cast<const float4*>(xs32 + k), b = *reinterpret_cast<const float4*>(xs32 + k + 4);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        acc = __fadd_rn(acc, __fmul_rn((j & 1) ? nkm::hi_bf(w[j >> 1]) : nkm::lo_bf(w[j >> 1]), xv[j]));
+    }
     acc = warp_sum_fixed(acc);
     if (p.router_bias) acc = __fadd_rn(acc, p.router_bias[e]);
     if (lane == 0) logits[e] = acc;
@@ -277,10 +288,12 @@ __global__ void __launch_bounds__(256) tc_route_kernel(TcParams p) {
 
 __global__ void __launch_bounds__(256) tc_plan_kernel(TcParams p) {
   __shared__ int cnt[kMaxE], seg[kMaxE];
+  __shared__ int pidx[kMaxTokens * kMaxK];  // the pairs' experts, in pair order
   for (int e = threadIdx.x; e < p.E; e += 256) cnt[e] = 0;
-  __syncthreads();
   const int NP = p.T * p.K;
-  for (int i = threadIdx.x; i < NP; i += 256) atomicAdd(&cnt[p.topk_idx[i]], 1);
+  for (int i = threadIdx.x; i < NP; i += 256) pidx[i] = p.topk_idx[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < NP; i += 256) atomicAdd(&cnt[pidx[i]], 1);
   __syncthreads();
   if (threadIdx.x == 0) {
     int off = 0, nt = 0;
@@ -305,14 +318,18 @@ __global__ void __launch_bounds__(256) tc_plan_kernel(TcParams p) {
     p.slot_w[s] = 0.f;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < NP; i += 256) {
-    const int e = p.topk_idx[i];
-    int rank = 0;
-    for (int j = 0; j < i; ++j) rank += p.topk_idx[j] == e;
-    const int s = seg[e] + rank;
-    p.pair_slot[i] = s;
-    p.slot_tok[s] = i / p.K;
-    p.slot_w[s] = p.topk_w[i];
+  // thread e places expert e's pairs in pair (token) order: every thread reads the same pidx[i]
+  // at the same time (a broadcast), so the scan costs NP shared-memory reads per thread
+  for (int e = threadIdx.x; e < p.E; e += 256) {
+    int s = seg[e];
+    for (int i = 0; i < NP; ++i) {
+      if (pidx[i] == e) {
+        p.pair_slot[i] = s;
+        p.slot_tok[s] = i / p.K;
+        p.slot_w[s] = p.topk_w[i];
+        ++s;
+      }
+    }
   }
 }
 
@@ -384,22 +401,19 @@ __device__ __forceinline__ void e4m3x16_bf16(const uint4 c, uint32_t s, float sc
     }
   }
 }
-// Row `row` of an MXFP8 unit (64 codes + 2 scales) into a bf16 K-major tile row with the
-// 128-byte swizzle the MMA descriptor expects (16-byte chunk c of row r at c ^ (r % 8)).
-__device__ __forceinline__ void mx_convert_row(const uint8_t* unit, uint8_t* a_tile, int row) {
-  const uint4* src = reinterpret_cast<const uint4*>(unit + row * 64);
-  const uint32_t sw = *reinterpret_cast<const uint16_t*>(unit + 128 * 64 + row * 2);
-  const uint32_t s0 = sw & 0xffu, s1 = sw >> 8;
-  const float sc0 = e8m0_f32(s0), sc1 = e8m0_f32(s1);
+// Quarter q (16 codes) of row `row` of an MXFP8 unit (128 rows x 64 codes, then 128 rows x 2
+// scales) into the bf16 K-major tile with the 128-byte swizzle the MMA descriptor expects (16-byte
+// chunk c of row r at c ^ (r % 8)).  Consecutive threads take consecutive quarters: the loads and
+// the stores of a quarter-warp hit distinct banks.
+__device__ __forceinline__ void mx_convert_quarter(const uint8_t* unit, uint8_t* a_tile, int row, int q) {
+  const uint4 src = *reinterpret_cast<const uint4*>(unit + row * 64 + q * 16);
+  const uint32_t s = unit[128 * 64 + row * 2 + (q >> 1)];
+  uint32_t o[8];
+  e4m3x16_bf16(src, s, e8m0_f32(s), o);
   uint8_t* dst = a_tile + row * 128;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {  // 16 codes = 2 output chunks of 8
-    uint32_t o[8];
-    e4m3x16_bf16(src[q], q < 2 ? s0 : s1, q < 2 ? sc0 : sc1, o);
-    const int c0 = 2 * q, c1 = 2 * q + 1;
-    *reinterpret_cast<uint4*>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4*>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
-  }
+  const int c0 = 2 * q, c1 = 2 * q + 1;
+  *reinterpret_cast<uint4*>(dst + ((c0 ^ (row & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(dst + ((c1 ^ (row & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 // ------------------------------------------------------------------ the grouped GEMM
@@ -408,9 +422,9 @@ __device__ __forceinline__ void mx_convert_row(const uint8_t* unit, uint8_t* a_t
 // !kGateUp: item = (tile, 128-row block m0 of H): A = W2 rows [e*H + m0, +128), K = I;
 // out ypair[slot][m0 + r] = acc * slot_w[slot].
 // kMx (MXFP8 weights): the A operand arrives as nkm_pack_mxfp8_experts units (e4m3 codes + e8m0
-// scales of the same 128 rows, one 1-D bulk copy each, kRawMx in flight) and warps 6-9 expand
+// scales of the same 128 rows, one 1-D bulk copy each, kRawMx in flight) and warps 6-21 expand
 // each unit into the bf16 swizzled A tile (exact: code x power of two); the MMA then runs as for
-// bf16 weights.  Warp 10 issues the B (token) tiles of each stage.  Two TMEM accumulators
+// bf16 weights.  Warp 22 issues the B (token) tiles of each stage.  Two TMEM accumulators
 // alternate, so the MMAs of a tile run while the epilogue reads the previous one.
 template <bool kGateUp, bool kMx>
 __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
@@ -437,13 +451,13 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      nkm::mbar_init(&full[s], kMx ? 4 : 1);  // kMx: one arrival per converter warp
+      nkm::mbar_init(&full[s], kMx ? kConvWarps : 1);  // kMx: one arrival per converter warp
       nkm::mbar_init(&empty[s], 1);
       nkm::mbar_init(&bfull[s], 1);
     }
     for (int r = 0; r < kRawMx; ++r) {
       nkm::mbar_init(&raw_full[r], 1);
-      nkm::mbar_init(&raw_empty[r], 4);
+      nkm::mbar_init(&raw_empty[r], kConvWarps);
     }
     for (int b = 0; b < 2; ++b) {
       nkm::mbar_init(&acc_full[b], 1);
@@ -605,8 +619,8 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
       __syncwarp();
       if (lane == 0) nkm::mbar_arrive(&acc_empty[ab]);
     }
-  } else if (kMx && warp < 10) {
-    // ---------------- MXFP8 converters (warps 6..9: thread t expands row t of each unit)
+  } else if (kMx && warp < 6 + kConvWarps) {
+    // ---------------- MXFP8 converters (warps 6..21: thread t expands quarter t % 4 of row t / 4)
     const int t = threadIdx.x - 192;
     uint32_t cnt = 0;
     bool ok = true;
@@ -619,7 +633,7 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
           ok = false;
           break;
         }
-        mx_convert_row(raw_base + r * kMxUnit, stage_base + s * kStageBytes, t);
+        mx_convert_quarter(raw_base + r * kMxUnit, stage_base + s * kStageBytes, t >> 2, t & 3);
         nkm::fence_proxy_async_smem();  // generic writes of the A tile before the MMA reads it
         __syncwarp();
         if (lane == 0) {
@@ -629,7 +643,7 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
       }
     }
   } else if (kMx) {
-    // ---------------- B-tile producer (warp 10): the expert's token tiles of each stage
+    // ---------------- B-tile producer (warp 6 + kConvWarps): the expert's token tiles of each stage
     if (lane == 0) {
       uint32_t cnt = 0;
       bool ok = true;

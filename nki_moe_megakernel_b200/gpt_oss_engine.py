@@ -174,7 +174,9 @@ class GptOssMegakernel:
     def decode_step(self, positions: torch.Tensor, block_table: torch.Tensor, *, x: Optional[torch.Tensor] = None,
                     input_ids: Optional[torch.Tensor] = None, want_logits: bool = True, trace: bool = False,
                     first_layer: int = 0, num_layers: int = 0, out: Optional[Dict[str, torch.Tensor]] = None,
-                    stream=None) -> Dict[str, torch.Tensor]:
+                    stage_times: bool = False, stream=None) -> Dict[str, torch.Tensor]:
+        """One decode step; ``stage_times`` adds ``stage_ns`` (globaltimer of CTA 0 at kernel start,
+        after every grid barrier: the input copy, then ten per layer, and at the end)."""
         s, dev = self.shape, self.device
         B = int(positions.shape[0])
         nl = num_layers or (s.num_hidden_layers - first_layer)
@@ -191,11 +193,14 @@ class GptOssMegakernel:
                   "resid_out": torch.zeros(nl, B, H, device=dev), "router_logits": torch.zeros(nl, B, E, device=dev),
                   "topk_idx": torch.full((nl, B, K), -1, dtype=torch.int32, device=dev),
                   "topk_w": torch.zeros(nl, B, K, device=dev)}
+        if stage_times:
+            tr["stage_ns"] = torch.zeros(3 + 10 * nl, dtype=torch.int64, device=dev)
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         st = _lib.nkm_gptoss_step(B, p(input_ids), p(x), p(positions), p(block_table), int(block_table.shape[1]),
                                   p(res["hidden"]), p(res.get("logits")) if want_logits else None, first_layer, nl,
                                   p(tr.get("qkv")), p(tr.get("resid_mid")), p(tr.get("resid_out")),
-                                  p(tr.get("router_logits")), p(tr.get("topk_idx")), p(tr.get("topk_w")))
+                                  p(tr.get("router_logits")), p(tr.get("topk_idx")), p(tr.get("topk_w")),
+                                  p(tr.get("stage_ns")))
         strm = stream if stream is not None else torch.cuda.current_stream(dev)
         check(lib().nkm_gptoss_decode_step(self._h, ctypes.byref(st), strm.cuda_stream), "nkm_gptoss_decode_step")
         res.update(tr)
