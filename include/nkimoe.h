@@ -392,9 +392,11 @@ int nkm_gptoss_status(nkm_gptoss* h, nkm_stream_t stream);
 
 /* MXFP4 weight packer (load time).  codes: uint8 [count][rows][cols] e2m1 codes 0..15 (bit 3 sign;
  * Hugging Face's *_blocks unpacked low nibble first), scales: uint8 [count][rows][cols/32] e8m0.
- * dst_w receives count*rows*cols/2 bytes, dst_s count*rows*cols/32 bytes, in the kernel's tiled
- * order.  rows % 16 == 0, cols % 32 == 0.  Replaces the MX layout conversion of
+ * dst_w receives count*rows*cols/2 bytes, dst_s nkm_mxfp4_scale_bytes(rows, cols, count) bytes
+ * (per 16-row strip, groups of 8 k-tiles: 16 rows x 8 scales), in the kernel's tiled order.
+ * rows % 16 == 0, cols % 32 == 0.  Replaces the MX layout conversion of
  * gpt_oss_with_megakernel.py:290-327 / selective_expert_mx_impl.py:60. */
+int64_t nkm_mxfp4_scale_bytes(int64_t rows, int64_t cols, int64_t count);
 int nkm_pack_mxfp4(const void* codes, const void* scales, void* dst_w, void* dst_s, int64_t rows, int64_t cols,
                    int64_t count, nkm_stream_t stream);
 

@@ -114,6 +114,7 @@ SIGNATURES = {
     "nkm_gptoss_destroy": (None, [c_void_p]),
     "nkm_gptoss_decode_step": (c_int, [c_void_p, POINTER(nkm_gptoss_step), c_void_p]),
     "nkm_gptoss_status": (c_int, [c_void_p, c_void_p]),
+    "nkm_mxfp4_scale_bytes": (ctypes.c_int64, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
     "nkm_pack_mxfp4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "nkm_moe_tc_workspace_bytes": (c_size_t, [POINTER(nkm_moe_tc_desc)]),
     "nkm_moe_block_tc": (c_int, [POINTER(nkm_moe_tc_desc), c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,

@@ -114,9 +114,10 @@ __global__ void pack_mxfp4_kernel(const uint8_t* __restrict__ codes, const uint8
     const int64_t k = 32 * kt + 8 * (lane & 3) + 2 * (j & 3);
     const uint8_t* src = codes + (c * rows + row) * cols + k;
     dw[i] = static_cast<uint8_t>((src[0] & 15u) | ((src[1] & 15u) << 4));
-    if (byte < 16) {
-      const int64_t srow = 16 * s + byte;
-      ds[unit * 16 + byte] = scales[(c * rows + srow) * KT + kt];
+    if (byte < 16 && kt % 8 == 0) {  // the 8 scales of row 16 s + byte for k-tiles kt .. kt + 7
+      const int64_t srow = 16 * s + byte, G8 = (KT + 7) / 8;
+      uint8_t* d8 = ds + ((c * S + s) * G8 + kt / 8) * 128 + byte * 8;
+      for (int u = 0; u < 8; ++u) d8[u] = kt + u < KT ? scales[(c * rows + srow) * KT + kt + u] : 0;
     }
   }
 }
@@ -310,6 +311,11 @@ int nkm_gptoss_status(nkm_gptoss* h, nkm_stream_t stream) {
     NKG_CUDA(cudaMemset(h->ws, 0, 256));
   }
   return st;
+}
+
+int64_t nkm_mxfp4_scale_bytes(int64_t rows, int64_t cols, int64_t count) {
+  if (rows <= 0 || rows % 16 || cols <= 0 || cols % 32 || count <= 0) return 0;
+  return count * (rows / 16) * ((cols / 32 + 7) / 8) * 128;
 }
 
 int nkm_pack_mxfp4(const void* codes, const void* scales, void* dst_w, void* dst_s, int64_t rows, int64_t cols,

@@ -327,9 +327,14 @@ __device__ __forceinline__ void ft_bf16(const uint8_t* strip, int kt0, int nk, c
 }
 
 // MXFP4 fragment-tiled strip: 256-byte units of 16 rows x 32 k (lane l: 4 bytes of row l/4 then 4
-// bytes of row l/4 + 8, k 8(l%4)..+7, low nibble first), e8m0 scales [kt][16 rows] per strip.  Each
-// unit's product is accumulated from zero and scaled by its rows' scales (exact powers of two).
-template <bool kGlobalB>
+// bytes of row l/4 + 8, k 8(l%4)..+7, low nibble first) and the strip's e8m0 scales in groups of 8
+// k-tiles ([group][16 rows][8], so a lane reads its two rows' 8 scales with two 8-byte loads).
+// Each unit's product is accumulated from zero and scaled by its rows' scales (exact powers of
+// two).  8 k-tiles are in flight per lane; the callers warm L2 with the warp's next unit (one
+// bulk prefetch) while this one streams.
+__device__ __forceinline__ uint32_t byte_of(const uint2 v, int u) {
+  return ((u < 4 ? v.x : v.y) >> (8 * (u & 3))) & 0xffu;
+}
 __device__ __forceinline__ void ft_fp4(const uint8_t* strip, const uint8_t* scales, int nk, const uint16_t* xs,
                                        int stride, const int* cols, int ncols, float (&acc)[kNT][4]) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
@@ -342,14 +347,16 @@ __device__ __forceinline__ void ft_fp4(const uint8_t* strip, const uint8_t* scal
   constexpr int U = 8;
 #pragma unroll 1
   for (int k0 = 0; k0 < nk; k0 += U) {
-    uint2 w[U];
-    uint32_t sg[U], sh[U];
+    uint2 w[U], sg[U / 8], sh[U / 8];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k0 + u < nk) {
-        w[u] = ldnc64(strip + static_cast<size_t>(k0 + u) * 256 + 8 * lane);
-        sg[u] = ldnc_u8(scales + (k0 + u) * 16 + g);
-        sh[u] = ldnc_u8(scales + (k0 + u) * 16 + g + 8);
+    for (int u = 0; u < U; ++u)
+      if (k0 + u < nk) w[u] = ldnc64(strip + static_cast<size_t>(k0 + u) * 256 + 8 * lane);
+#pragma unroll
+    for (int q = 0; q < U / 8; ++q) {
+      if (k0 + 8 * q < nk) {
+        const uint8_t* grp = scales + static_cast<size_t>(k0 / 8 + q) * 128;
+        sg[q] = ldnc64(grp + 8 * g);
+        sh[q] = ldnc64(grp + 8 * (g + 8));
       }
     }
 #pragma unroll
@@ -358,13 +365,11 @@ __device__ __forceinline__ void ft_fp4(const uint8_t* strip, const uint8_t* scal
         uint32_t r0, r1, r2, r3, q0, q1, q2, q3;
         e2m1x8(w[u].x, r0, r1, r2, r3);
         e2m1x8(w[u].y, q0, q1, q2, q3);
-        const float s0 = e8m0(sg[u]), s1 = e8m0(sh[u]);
+        const float s0 = e8m0(byte_of(sg[u / 8], u & 7)), s1 = e8m0(byte_of(sh[u / 8], u & 7));
         const int kk = (k0 + u) * 32;
 #pragma unroll
         for (int nt = 0; nt < kNT; ++nt) {
-          const uint4 b = !brow[nt] ? make_uint4(0u, 0u, 0u, 0u)
-                                    : (kGlobalB ? nkm::ldcg128(brow[nt] + kk)
-                                                : *reinterpret_cast<const uint4*>(brow[nt] + kk));
+          const uint4 b = brow[nt] ? *reinterpret_cast<const uint4*>(brow[nt] + kk) : make_uint4(0u, 0u, 0u, 0u);
           float d[4] = {0.f, 0.f, 0.f, 0.f};
           mma_f16(d, r0, q0, r1, q1, b.x, b.y);
           mma_f16(d, r2, q2, r3, q3, b.z, b.w);
@@ -377,6 +382,8 @@ __device__ __forceinline__ void ft_fp4(const uint8_t* strip, const uint8_t* scal
     }
   }
 }
+// Bytes of one 16-row strip's grouped scales for KT k-tiles.
+__device__ __forceinline__ size_t fp4_strip_scale_bytes(int KT) { return static_cast<size_t>((KT + 7) / 8) * 128; }
 
 // ------------------------------------------------------------------ stages
 // Split-K dense GEMV: units (strip, k chunk) over all warps; partial (chunk kc) of row r, column
@@ -390,6 +397,11 @@ __device__ __noinline__ void dense_splitk(const Params& p, const uint8_t* w, int
   for (int u = gw; u < nunits; u += nw) {
     const int s = u / KC, kc = u - s * KC;
     const int kt0 = KT * kc / KC, kt1 = KT * (kc + 1) / KC;
+    if (lane == 0 && u + nw < nunits) {  // the next unit's weights into L2
+      const int s2 = (u + nw) / KC, kc2 = (u + nw) - s2 * KC;
+      const int a0 = KT * kc2 / KC, a1 = KT * (kc2 + 1) / KC;
+      nkm::prefetch_l2_bulk(w + (static_cast<size_t>(s2) * KT + a0) * 1024, static_cast<uint32_t>(a1 - a0) * 1024u);
+    }
     float acc[kNT][4] = {};
     ft_bf16(w + static_cast<size_t>(s) * KT * 1024, kt0, kt1 - kt0, xs, stride, nullptr, p.B, acc);
 #pragma unroll
@@ -768,16 +780,32 @@ __device__ __noinline__ void router_logits(const Params& p, const Layer& lw, int
     const uint16_t* wr = lw.router + static_cast<size_t>(e) * p.H;
     const float r = rstd[t];
     float acc = 0.f;
-    for (int k = 8 * lane; k < p.H; k += 256) {
-      const float4 a = nkm::ldcg_f4(row + k), bb = nkm::ldcg_f4(row + k + 4);
-      const uint4 gv = *reinterpret_cast<const uint4*>(lw.ln2 + k);
-      const uint4 wv = nkm::ldnc128(wr + k);
-      const float v[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
-      const uint32_t gw4[4] = {gv.x, gv.y, gv.z, gv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    // two 256-wide steps per round: their loads are issued together, then summed in k order
+#pragma unroll 1
+    for (int k0 = 8 * lane; k0 < p.H; k0 += 2 * 256) {
+      float4 a[2], bb[2];
+      uint4 gv[2], wv[2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float xn = __fmul_rn(__fmul_rn(v[j], r), (j & 1) ? hi_bf(gw4[j >> 1]) : lo_bf(gw4[j >> 1]));
-        acc = __fadd_rn(acc, __fmul_rn((j & 1) ? hi_bf(ww[j >> 1]) : lo_bf(ww[j >> 1]), xn));
+      for (int q = 0; q < 2; ++q) {
+        const int k = k0 + 256 * q;
+        if (k < p.H) {
+          a[q] = nkm::ldcg_f4(row + k);
+          bb[q] = nkm::ldcg_f4(row + k + 4);
+          gv[q] = *reinterpret_cast<const uint4*>(lw.ln2 + k);
+          wv[q] = nkm::ldnc128(wr + k);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (k0 + 256 * q < p.H) {
+          const float v[8] = {a[q].x, a[q].y, a[q].z, a[q].w, bb[q].x, bb[q].y, bb[q].z, bb[q].w};
+          const uint32_t gw4[4] = {gv[q].x, gv[q].y, gv[q].z, gv[q].w}, ww[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xn = __fmul_rn(__fmul_rn(v[j], r), (j & 1) ? hi_bf(gw4[j >> 1]) : lo_bf(gw4[j >> 1]));
+            acc = __fadd_rn(acc, __fmul_rn((j & 1) ? hi_bf(ww[j >> 1]) : lo_bf(ww[j >> 1]), xn));
+          }
+        }
       }
     }
     acc = warp_sum(acc);
@@ -886,13 +914,18 @@ __device__ __noinline__ void expert_gateup(const Params& p, const Layer& lw, con
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
   const int S = 2 * p.I / 16, KT = p.H / 32, nunits = rt->nA * S;
-  const size_t ebytes = static_cast<size_t>(2 * p.I) * p.H / 2, sbytes = static_cast<size_t>(2 * p.I) * (p.H / 32);
+  const size_t ebytes = static_cast<size_t>(2 * p.I) * p.H / 2, ssb = fp4_strip_scale_bytes(KT), sbytes = S * ssb;
 #pragma unroll 1
   for (int u = gw; u < nunits; u += nw) {
     const int j = u / S, s = u - j * S, e = rt->act_e[j];
+    if (lane == 0 && u + nw < nunits) {  // the next unit's weights and scales into L2
+      const int j2 = (u + nw) / S, s2 = (u + nw) - j2 * S, e2 = rt->act_e[j2];
+      nkm::prefetch_l2_bulk(lw.w13 + e2 * ebytes + static_cast<size_t>(s2) * KT * 256, static_cast<uint32_t>(KT) * 256u);
+      nkm::prefetch_l2_bulk(lw.s13 + e2 * sbytes + s2 * ssb, static_cast<uint32_t>(ssb));
+    }
     float acc[kNT][4] = {};
-    ft_fp4<false>(lw.w13 + e * ebytes + static_cast<size_t>(s) * KT * 256, lw.s13 + e * sbytes + static_cast<size_t>(s) * KT * 16,
-           KT, xs, p.H + 8, rt->pair_tok + rt->act_off[j], rt->act_cnt[j], acc);
+    ft_fp4(lw.w13 + e * ebytes + static_cast<size_t>(s) * KT * 256, lw.s13 + e * sbytes + s * ssb, KT, xs, p.H + 8,
+           rt->pair_tok + rt->act_off[j], rt->act_cnt[j], acc);
     // rows 16 s + g (even: gate, odd: up) pair up across lanes g, g ^ 1
     const int r0 = 16 * s + g, r1 = r0 + 8;
     const float b0 = __bfloat162float(__ushort_as_bfloat16(lw.b13[static_cast<size_t>(e) * 2 * p.I + r0]));
@@ -920,35 +953,56 @@ __device__ __noinline__ void expert_gateup(const Params& p, const Layer& lw, con
   }
 }
 
-// F: down units (active expert j, 16-row strip s of H): B operand = the expert's h rows (f16,
-// global); y = acc + bias, times the pair's routing weight -> ypair.
-__device__ __noinline__ void expert_down(const Params& p, const Layer& lw, const Route* rt) {
-  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
-  const int S = p.H / 16, KT = p.I / 32, nunits = rt->nA * S;
-  const size_t ebytes = static_cast<size_t>(p.H) * p.I / 2, sbytes = static_cast<size_t>(p.H) * (p.I / 32);
+// F: down projection.  The nA x H/16 (expert, 16-row strip) units in expert-major order are split
+// into contiguous ranges, one per CTA, so a CTA meets at most a few experts: for each it copies the
+// expert's h rows (f16, written in stage E by other CTAs) into shared memory once and its warps
+// take the expert's strips of its range; y = acc + bias, times the pair's routing weight -> ypair.
+__device__ __noinline__ void expert_down(const Params& p, const Layer& lw, const Route* rt, uint16_t* hs) {
+  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3, warp = threadIdx.x >> 5;
+  const int S = p.H / 16, KT = p.I / 32, NS = rt->nA * S;
+  const size_t ebytes = static_cast<size_t>(p.H) * p.I / 2, ssb = fp4_strip_scale_bytes(KT), sbytes = S * ssb;
+  const int hstride = p.I + 8;
+  const int lo = static_cast<int>((static_cast<long long>(NS) * blockIdx.x) / gridDim.x);
+  const int hi = static_cast<int>((static_cast<long long>(NS) * (blockIdx.x + 1)) / gridDim.x);
 #pragma unroll 1
-  for (int u = gw; u < nunits; u += nw) {
-    const int j = u / S, s = u - j * S, e = rt->act_e[j];
-    const int off = rt->act_off[j], n = rt->act_cnt[j];
-    float acc[kNT][4] = {};
-    ft_fp4<true>(lw.w2 + e * ebytes + static_cast<size_t>(s) * KT * 256, lw.s2 + e * sbytes + static_cast<size_t>(s) * KT * 16,
-           KT, p.hbuf + static_cast<size_t>(off) * p.I, p.I, nullptr, n, acc);
-    const int r0 = 16 * s + g, r1 = r0 + 8;
-    const float b0 = __bfloat162float(__ushort_as_bfloat16(lw.b2[static_cast<size_t>(e) * p.H + r0]));
-    const float b1 = __bfloat162float(__ushort_as_bfloat16(lw.b2[static_cast<size_t>(e) * p.H + r1]));
-#pragma unroll
-    for (int nt = 0; nt < kNT; ++nt)
-#pragma unroll
-      for (int ee = 0; ee < 2; ++ee) {
-        const int c = nt * 8 + 2 * t4 + ee;
-        if (c < n) {
-          const float w = rt->pair_w[off + c];
-          float* y = p.ypair + static_cast<size_t>(off + c) * p.H;
-          y[r0] = (acc[nt][ee] + b0) * w;
-          y[r1] = (acc[nt][2 + ee] + b1) * w;
-        }
+  for (int seg = lo; seg < hi;) {
+    const int j = seg / S, seg_end = min(hi, (j + 1) * S);
+    const int e = rt->act_e[j], off = rt->act_off[j], n = rt->act_cnt[j];
+    __syncthreads();  // the previous expert's rows are no longer read
+    for (int i = threadIdx.x; i < n * (p.I / 8); i += kThreads) {
+      const int r = i / (p.I / 8), k = (i - r * (p.I / 8)) * 8;
+      *reinterpret_cast<uint4*>(hs + static_cast<size_t>(r) * hstride + k) =
+          nkm::ldcg128(p.hbuf + static_cast<size_t>(off + r) * p.I + k);
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int st = seg + warp; st < seg_end; st += kWarps) {
+      const int s = st - j * S;
+      if (lane == 0 && st + kWarps < seg_end) {  // the next strip's weights and scales into L2
+        nkm::prefetch_l2_bulk(lw.w2 + e * ebytes + static_cast<size_t>(s + kWarps) * KT * 256,
+                              static_cast<uint32_t>(KT) * 256u);
+        nkm::prefetch_l2_bulk(lw.s2 + e * sbytes + (s + kWarps) * ssb, static_cast<uint32_t>(ssb));
       }
+      float acc[kNT][4] = {};
+      ft_fp4(lw.w2 + e * ebytes + static_cast<size_t>(s) * KT * 256, lw.s2 + e * sbytes + s * ssb, KT, hs, hstride,
+             nullptr, n, acc);
+      const int r0 = 16 * s + g, r1 = r0 + 8;
+      const float b0 = __bfloat162float(__ushort_as_bfloat16(lw.b2[static_cast<size_t>(e) * p.H + r0]));
+      const float b1 = __bfloat162float(__ushort_as_bfloat16(lw.b2[static_cast<size_t>(e) * p.H + r1]));
+#pragma unroll
+      for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+        for (int ee = 0; ee < 2; ++ee) {
+          const int c = nt * 8 + 2 * t4 + ee;
+          if (c < n) {
+            const float w = rt->pair_w[off + c];
+            float* y = p.ypair + static_cast<size_t>(off + c) * p.H;
+            y[r0] = (acc[nt][ee] + b0) * w;
+            y[r1] = (acc[nt][2 + ee] + b1) * w;
+          }
+        }
+    }
+    seg = seg_end;
   }
 }
 
@@ -971,6 +1025,8 @@ __device__ __noinline__ void lm_head(const Params& p, const uint16_t* xs) {
   const int S = p.V / 16, KT = p.H / 32;
 #pragma unroll 1
   for (int s = gw; s < S; s += nw) {
+    if (lane == 0 && s + nw < S)  // the next strip into L2
+      nkm::prefetch_l2_bulk(p.lm_head + static_cast<size_t>(s + nw) * KT * 1024, static_cast<uint32_t>(KT) * 1024u);
     float acc[kNT][4] = {};
     ft_bf16(p.lm_head + static_cast<size_t>(s) * KT * 1024, 0, KT, xs, p.H + 8, nullptr, p.B, acc);
 #pragma unroll
@@ -1061,7 +1117,7 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
       routing(p, rt, layer);  // E
       expert_gateup(p, lw, rt, xs);
       if (!grid_sync(p, bar_k, flag)) return;
-      expert_down(p, lw, rt);  // F
+      expert_down(p, lw, rt, xs);  // F (the f16 rows of stage D are no longer needed)
       if (!grid_sync(p, bar_k, flag)) return;
       moe_residual(p, rt, layer);  // G
       if (!grid_sync(p, bar_k, flag)) return;

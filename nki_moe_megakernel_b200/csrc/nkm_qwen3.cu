@@ -74,7 +74,7 @@ WsLayout layout_ws(const nkm_qwen3_desc& d, int num_sms) {
   w.attn_out = o;
   o = align_up(o + Tm * d.n_q_heads * d.head_dim * 2);
   w.att_part = o;
-  o = align_up(o + (NW + Tm * d.n_kv_heads) * nkm::kPartFloats * 4);
+  o = align_up(o + (NW + Tm * d.n_kv_heads) * nkm::kPartFloats * 4);  // items <= kAttItemsWide per CTA < kWarps
   w.rlogits = o;
   o = align_up(o + Tm * d.n_experts * 4);
   w.hbuf = o;

@@ -28,6 +28,8 @@ constexpr int kMaxBars = 4;                // mbarriers per warp (attention uses
 constexpr int kHeadDim = 128;
 constexpr int kKvBlock = 128;
 constexpr int kAttTile = 32;               // tokens per attention tile (rows of one TMA box)
+constexpr int kAttItemsWide = 4;           // attention items per CTA at batches above 8 (<= kWarps:
+                                           // the partials area holds kWarps items per SM)
 constexpr int kMaxExperts = 256;
 constexpr int kMaxPairs = 256;             // max batch * top_k
 constexpr int kMaxHidden = 2048;           // register-resident row loads: 8 groups of 256
@@ -1951,14 +1953,18 @@ __device__ __forceinline__ void att_items(const Params& p, Fn&& fn) {
     tiles += __shfl_xor_sync(0xffffffffu, tiles, off);
     longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, off));
   }
-  int per = max(1, (tiles + G - 1) / G);
+  // Batches of at most 8 rows: at most one item per CTA.  Larger batches (long and unequal contexts
+  // at B = 32) take up to kAttItemsWide items per CTA of a smaller chunk, so that the round-robin
+  // assignment balances the CTAs' token counts.
+  const int cap = p.T > 8 ? kAttItemsWide * G : G;
+  int per = max(1, (tiles + cap - 1) / cap);
   int nitems = 0;
   for (;; ++per) {
     int mine = lane < p.T ? p.nkv * max(1, (mypos + kAttTile * per - 1) / (kAttTile * per)) : 0;
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, off);
     nitems = mine;
-    if (nitems <= G || per >= longest) break;
+    if (nitems <= cap || per >= longest) break;
   }
   const int CT = kAttTile * per;
   // inclusive prefix of the items of sequences 0..lane

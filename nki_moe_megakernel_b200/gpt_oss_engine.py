@@ -79,7 +79,7 @@ def pack_mxfp4(codes: torch.Tensor, scales: torch.Tensor, stream=None):
     R, K = codes.shape[-2], codes.shape[-1]
     count = codes.numel() // (R * K)
     w = torch.empty(codes.numel() // 2, dtype=torch.uint8, device=codes.device)
-    s = torch.empty(scales.numel(), dtype=torch.uint8, device=codes.device)
+    s = torch.empty(lib().nkm_mxfp4_scale_bytes(R, K, count), dtype=torch.uint8, device=codes.device)
     st = stream if stream is not None else torch.cuda.current_stream(codes.device)
     check(lib().nkm_pack_mxfp4(codes.data_ptr(), scales.data_ptr(), w.data_ptr(), s.data_ptr(), R, K, count,
                                st.cuda_stream), "nkm_pack_mxfp4")
