@@ -1025,8 +1025,6 @@ __device__ __noinline__ void lm_head(const Params& p, const uint16_t* xs) {
   const int S = p.V / 16, KT = p.H / 32;
 #pragma unroll 1
   for (int s = gw; s < S; s += nw) {
-    if (lane == 0 && s + nw < S)  // the next strip into L2
-      nkm::prefetch_l2_bulk(p.lm_head + static_cast<size_t>(s + nw) * KT * 1024, static_cast<uint32_t>(KT) * 1024u);
     float acc[kNT][4] = {};
     ft_bf16(p.lm_head + static_cast<size_t>(s) * KT * 1024, 0, KT, xs, p.H + 8, nullptr, p.B, acc);
 #pragma unroll
