@@ -268,6 +268,8 @@ typedef struct nkm_moe_tc_desc {
   int32_t max_tokens;         /* <= 512 */
   int32_t weight_format;      /* NKM_MOE_WEIGHTS_BF16 or NKM_MOE_WEIGHTS_MXFP8 (e4m3 values, e8m0
                                  scale per 32 along K; expanded exactly to bf16 in shared memory) */
+  int32_t expert_begin;       /* expert parallel: w13 / w2 hold experts [expert_begin, + n_local_experts) */
+  int32_t n_local_experts;    /* 0 = all n_experts (router and routing always cover all experts) */
 } nkm_moe_tc_desc;
 
 #define NKM_MOE_WEIGHTS_BF16 0
@@ -290,6 +292,12 @@ size_t nkm_moe_tc_workspace_bytes(const nkm_moe_tc_desc* desc);
 int nkm_moe_block_tc(const nkm_moe_tc_desc* desc, int32_t tokens, const void* x_in, void* y_out, int32_t residual,
                      int32_t* topk_idx_out, float* topk_w_out, void* workspace, size_t workspace_bytes,
                      nkm_stream_t stream);
+/* Expert parallel: y_part (device fp32 [tokens, H]) = the contributions of this call's local experts
+ * only (routing weights applied, summed over each token's local slots in slot order; no residual,
+ * no rounding): the ranks' partials are then summed (nkm_ep_* below).  Six launches. */
+int nkm_moe_block_tc_partial(const nkm_moe_tc_desc* desc, int32_t tokens, const void* x_in, float* y_part,
+                             int32_t* topk_idx_out, float* topk_w_out, void* workspace, size_t workspace_bytes,
+                             nkm_stream_t stream);
 /* Synchronise and return the status word of the last call on this workspace (0 = ok). */
 int nkm_moe_tc_status(void* workspace, nkm_stream_t stream);
 

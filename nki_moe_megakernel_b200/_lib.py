@@ -85,7 +85,8 @@ class nkm_gptoss_step(ctypes.Structure):
 class nkm_moe_tc_desc(ctypes.Structure):
     _fields_ = [("hidden", c_int32), ("n_experts", c_int32), ("top_k", c_int32), ("moe_inter", c_int32),
                 ("rms_eps", c_float), ("ln2", c_void_p), ("router", c_void_p), ("router_bias", c_void_p),
-                ("w13", c_void_p), ("w2", c_void_p), ("max_tokens", c_int32), ("weight_format", c_int32)]
+                ("w13", c_void_p), ("w2", c_void_p), ("max_tokens", c_int32), ("weight_format", c_int32),
+                ("expert_begin", c_int32), ("n_local_experts", c_int32)]
 
 
 class nkm_sample_params(ctypes.Structure):
@@ -120,6 +121,8 @@ SIGNATURES = {
     "nkm_moe_block_tc": (c_int, [POINTER(nkm_moe_tc_desc), c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p]),
     "nkm_moe_tc_status": (c_int, [c_void_p, c_void_p]),
+    "nkm_moe_block_tc_partial": (c_int, [POINTER(nkm_moe_tc_desc), c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, ctypes.c_size_t, c_void_p]),
     "nkm_mxfp8_experts_bytes": (ctypes.c_size_t, [c_int32, c_int32, c_int32]),
     "nkm_pack_mxfp8_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "nkm_last_error": (c_char_p, []),

@@ -95,6 +95,8 @@ struct TcParams {
   int P;                    // slot capacity
   const uint8_t* w13mx;     // MXFP8 weights (nkm_pack_mxfp8_experts units) or null
   const uint8_t* w2mx;
+  int e_lo, e_hi;           // experts whose weights this call holds (expert parallel: a range)
+  float* y_part;            // fp32 [T, H] sum of the local experts' contributions (expert parallel), or null
 };
 
 // ------------------------------------------------------------------ PTX (tcgen05, TMEM)
@@ -213,15 +215,24 @@ __global__ void __launch_bounds__(256) tc_route_kernel(TcParams p) {
   for (int e = warp; e < p.E; e += 8) {
     const uint16_t* wr = p.router + static_cast<size_t>(e) * p.H;
     float acc = 0.f;
-    for (int i = 0; i * 256 < p.H; ++i) {
-      const int k = 256 * i + 8 * lane;
-      const uint4 q = nkm::ldnc128(wr + k);
-      const float4 a = *reinterpret_cast<const float4*>(xs32 + k), b = *reinterpret_cast<const float4*>(xs32 + k + 4);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-      const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    // the row's loads are issued 8 groups at a time, then summed in k order
+    for (int i0 = 0; i0 * 256 < p.H; i0 += 8) {
+      uint4 q[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        acc = __fadd_rn(acc, __fmul_rn((j & 1) ? nkm::hi_bf(w[j >> 1]) : nkm::lo_bf(w[j >> 1]), xv[j]));
+      for (int u = 0; u < 8; ++u)
+        if ((i0 + u) * 256 < p.H) q[u] = nkm::ldnc128(wr + 256 * (i0 + u) + 8 * lane);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if ((i0 + u) * 256 < p.H) {
+          const int k = 256 * (i0 + u) + 8 * lane;
+          const float4 a = *reinterpret_cast<const float4*>(xs32 + k), b = *reinterpret_cast<const float4*>(xs32 + k + 4);
+          const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+          const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            acc = __fadd_rn(acc, __fmul_rn((j & 1) ? nkm::hi_bf(w[j >> 1]) : nkm::lo_bf(w[j >> 1]), xv[j]));
+        }
+      }
     }
     acc = warp_sum_fixed(acc);
     if (p.router_bias) acc = __fadd_rn(acc, p.router_bias[e]);
@@ -299,7 +310,7 @@ __global__ void __launch_bounds__(256) tc_plan_kernel(TcParams p) {
     int off = 0, nt = 0;
     for (int e = 0; e < p.E; ++e) {
       seg[e] = off;
-      const int n = cnt[e];
+      const int n = (e >= p.e_lo && e < p.e_hi) ? cnt[e] : 0;  // other ranks' experts: no tiles
       for (int c0 = 0; c0 < n; c0 += kMaxN) {
         const int nc = min(kMaxN, n - c0);
         p.tiles[3 * nt] = e;
@@ -318,17 +329,25 @@ __global__ void __launch_bounds__(256) tc_plan_kernel(TcParams p) {
     p.slot_w[s] = 0.f;
   }
   __syncthreads();
-  // thread e places expert e's pairs in pair (token) order: every thread reads the same pidx[i]
-  // at the same time (a broadcast), so the scan costs NP shared-memory reads per thread
-  for (int e = threadIdx.x; e < p.E; e += 256) {
+  // warp w places the pairs of experts w, w + 8, ... in pair (token) order: 32 pairs per ballot,
+  // a pair's rank among its expert's pairs = the matches before it
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = warp; e < p.E; e += 8) {
+    const bool local = e >= p.e_lo && e < p.e_hi;
     int s = seg[e];
-    for (int i = 0; i < NP; ++i) {
-      if (pidx[i] == e) {
-        p.pair_slot[i] = s;
-        p.slot_tok[s] = i / p.K;
-        p.slot_w[s] = p.topk_w[i];
-        ++s;
+    for (int i0 = 0; i0 < NP; i0 += 32) {
+      const int i = i0 + lane;
+      const bool hit = i < NP && pidx[i] == e;
+      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (hit) {
+        const int sl = s + __popc(m & ((1u << lane) - 1u));
+        p.pair_slot[i] = local ? sl : -1;  // -1: the pair's expert lives on another rank
+        if (local) {
+          p.slot_tok[sl] = i / p.K;
+          p.slot_w[sl] = p.topk_w[i];
+        }
       }
+      s += __popc(m);
     }
   }
 }
@@ -345,7 +364,14 @@ __global__ void tc_combine_kernel(TcParams p) {
   const int t = blockIdx.x;
   for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < p.K; ++k) s += p.ypair[static_cast<size_t>(p.pair_slot[t * p.K + k]) * p.H + h];
+    for (int k = 0; k < p.K; ++k) {
+      const int sl = p.pair_slot[t * p.K + k];
+      if (sl >= 0) s += p.ypair[static_cast<size_t>(sl) * p.H + h];
+    }
+    if (p.y_part) {  // expert parallel: this rank's experts only, summed over the ranks later
+      p.y_part[static_cast<size_t>(t) * p.H + h] = s;
+      continue;
+    }
     const float base = p.residual ? nkm::bf2f(p.x[static_cast<size_t>(t) * p.H + h]) : 0.f;
     p.y[static_cast<size_t>(t) * p.H + h] = nkm::f2bf(base + rbf(s));
   }
@@ -492,8 +518,9 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
               ok = false;
               break;
             }
-            const uint8_t* src = kGateUp ? p.w13mx + ((static_cast<size_t>(e) * MB + mb) * KT + kc) * kMxUnit
-                                         : p.w2mx + ((static_cast<size_t>(e) * MB + mb) * KT + kc) * kMxUnit;
+            const size_t el = static_cast<size_t>(e - p.e_lo);  // local expert
+            const uint8_t* src = kGateUp ? p.w13mx + ((el * MB + mb) * KT + kc) * kMxUnit
+                                         : p.w2mx + ((el * MB + mb) * KT + kc) * kMxUnit;
             nkm::mbar_arrive_expect_tx(&raw_full[r], kMxUnit);
             nkm::bulk_g2s_plain(raw_base + r * kMxUnit, src, kMxUnit, &raw_full[r]);
             continue;
@@ -508,11 +535,11 @@ __global__ void __launch_bounds__(kMx ? kTcThreadsMx : kTcThreads, 1)
           const uint32_t bytes = kABytes + static_cast<uint32_t>(ncols) * 128u;
           nkm::mbar_arrive_expect_tx(&full[s], bytes);
           if (kGateUp) {
-            nkm::tma_load_2d(a, &amap, kc * kBK, e * 2 * p.I + mb * 64, &full[s]);
-            nkm::tma_load_2d(a + 64 * 128, &amap, kc * kBK, e * 2 * p.I + p.I + mb * 64, &full[s]);
+            nkm::tma_load_2d(a, &amap, kc * kBK, (e - p.e_lo) * 2 * p.I + mb * 64, &full[s]);
+            nkm::tma_load_2d(a + 64 * 128, &amap, kc * kBK, (e - p.e_lo) * 2 * p.I + p.I + mb * 64, &full[s]);
           } else {
-            nkm::tma_load_2d(a, &amap, kc * kBK, e * p.H + mb * 128, &full[s]);
-            nkm::tma_load_2d(a + 64 * 128, &amap, kc * kBK, e * p.H + mb * 128 + 64, &full[s]);
+            nkm::tma_load_2d(a, &amap, kc * kBK, (e - p.e_lo) * p.H + mb * 128, &full[s]);
+            nkm::tma_load_2d(a + 64 * 128, &amap, kc * kBK, (e - p.e_lo) * p.H + mb * 128 + 64, &full[s]);
           }
           for (int r = 0; r < ncols; r += 16) nkm::tma_load_2d(b + r * 128, &bmap, kc * kBK, n0 + r, &full[s]);
         }
@@ -756,6 +783,8 @@ int tc_check(const nkm_moe_tc_desc* d) {
   if (d->max_tokens <= 0 || d->max_tokens > kMaxTokens) return NKM_ERR_ARG;
   if (!d->ln2 || !d->router || !d->w13 || !d->w2) return NKM_ERR_ARG;
   if (d->weight_format != NKM_MOE_WEIGHTS_BF16 && d->weight_format != NKM_MOE_WEIGHTS_MXFP8) return NKM_ERR_ARG;
+  const int nl = d->n_local_experts > 0 ? d->n_local_experts : d->n_experts;
+  if (d->expert_begin < 0 || d->expert_begin + nl > d->n_experts) return NKM_ERR_ARG;
   return NKM_OK;
 }
 
@@ -787,20 +816,23 @@ extern "C" size_t nkm_moe_tc_workspace_bytes(const nkm_moe_tc_desc* desc) {
   return tc_layout(*desc).total;
 }
 
-extern "C" int nkm_moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const void* x_in, void* y_out,
-                                int32_t residual, int32_t* topk_idx_out, float* topk_w_out, void* workspace,
-                                size_t workspace_bytes, nkm_stream_t stream_) {
+namespace {
+int moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const void* x_in, void* y_out, float* y_part,
+                 int32_t residual, int32_t* topk_idx_out, float* topk_w_out, void* workspace, size_t workspace_bytes,
+                 nkm_stream_t stream_) {
   if (tc_check(d) != NKM_OK) {
     nkm::set_last_error("invalid MoE description: hidden % 256, moe_inter % 64, experts <= 256, top_k <= 8, "
-                        "max_tokens <= 512 and every weight pointer are required");
+                        "max_tokens <= 512, the local expert range inside the experts and every weight pointer are "
+                        "required");
     return NKM_ERR_ARG;
   }
   if (tokens <= 0 || tokens > d->max_tokens) {
     nkm::set_last_error("tokens outside 1..max_tokens");
     return NKM_ERR_ARG;
   }
-  if (!x_in || !y_out || (reinterpret_cast<uintptr_t>(x_in) & 15) || (reinterpret_cast<uintptr_t>(y_out) & 15)) {
-    nkm::set_last_error("x_in and y_out must be 16-byte aligned device pointers");
+  void* out = y_part ? static_cast<void*>(y_part) : y_out;
+  if (!x_in || !out || (reinterpret_cast<uintptr_t>(x_in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) {
+    nkm::set_last_error("x_in and the output must be 16-byte aligned device pointers");
     return NKM_ERR_ARG;
   }
   const TcLayout lay = tc_layout(*d);
@@ -840,12 +872,16 @@ extern "C" int nkm_moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const 
   const bool mx = d->weight_format == NKM_MOE_WEIGHTS_MXFP8;
   p.w13mx = mx ? static_cast<const uint8_t*>(d->w13) : nullptr;
   p.w2mx = mx ? static_cast<const uint8_t*>(d->w2) : nullptr;
+  const int n_local = d->n_local_experts > 0 ? d->n_local_experts : d->n_experts;
+  p.e_lo = d->expert_begin;
+  p.e_hi = d->expert_begin + n_local;
+  p.y_part = y_part;
   CUtensorMap w13m, w2m, xgm, hm;
   memset(&w13m, 0, sizeof(w13m));
   memset(&w2m, 0, sizeof(w2m));
   int rc;
-  if ((!mx && ((rc = encode(&w13m, d->w13, static_cast<uint64_t>(p.E) * 2 * p.I, p.H, 64)) ||
-               (rc = encode(&w2m, d->w2, static_cast<uint64_t>(p.E) * p.H, p.I, 64)))) ||
+  if ((!mx && ((rc = encode(&w13m, d->w13, static_cast<uint64_t>(n_local) * 2 * p.I, p.H, 64)) ||
+               (rc = encode(&w2m, d->w2, static_cast<uint64_t>(n_local) * p.H, p.I, 64)))) ||
       (rc = encode(&xgm, p.xg, lay.P, p.H, 16)) || (rc = encode(&hm, p.hbuf, lay.P, p.I, 16)))
     return rc;
   if (mx && ((reinterpret_cast<uintptr_t>(d->w13) & 15) || (reinterpret_cast<uintptr_t>(d->w2) & 15))) {
@@ -890,6 +926,21 @@ extern "C" int nkm_moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const 
     return NKM_ERR_CUDA;
   }
   return NKM_OK;
+}
+}  // namespace
+
+extern "C" int nkm_moe_block_tc(const nkm_moe_tc_desc* d, int32_t tokens, const void* x_in, void* y_out,
+                                int32_t residual, int32_t* topk_idx_out, float* topk_w_out, void* workspace,
+                                size_t workspace_bytes, nkm_stream_t stream) {
+  return moe_block_tc(d, tokens, x_in, y_out, nullptr, residual, topk_idx_out, topk_w_out, workspace, workspace_bytes,
+                      stream);
+}
+
+extern "C" int nkm_moe_block_tc_partial(const nkm_moe_tc_desc* d, int32_t tokens, const void* x_in, float* y_part,
+                                        int32_t* topk_idx_out, float* topk_w_out, void* workspace,
+                                        size_t workspace_bytes, nkm_stream_t stream) {
+  return moe_block_tc(d, tokens, x_in, nullptr, y_part, 0, topk_idx_out, topk_w_out, workspace, workspace_bytes,
+                      stream);
 }
 
 extern "C" int nkm_moe_tc_status(void* workspace, nkm_stream_t stream) {
