@@ -717,10 +717,15 @@ def run_wide(args):
 
     from nki_moe_megakernel_b200.engine import Qwen3MoeShape, Qwen3MoeWideDecoder
 
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     B, L = 64, args.layers
     shape = Qwen3MoeShape(num_hidden_layers=L)
+    if world > 1:
+        return run_wide_ep(args, rank, world, local, dev, shape)
     H, D, E, I, V = shape.hidden_size, shape.head_dim, shape.num_experts, shape.moe_intermediate_size, shape.vocab_size
     nq, nkv = shape.num_attention_heads, shape.num_key_value_heads
     g = torch.Generator(device=dev).manual_seed(args.seed)
@@ -781,6 +786,84 @@ def run_wide(args):
                    "distinct_experts_per_layer_mean": sum(distinct) / L},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "algorithmic_bytes_per_step": nbytes}}), flush=True)
+
+
+def run_wide_ep(args, rank, world, local, dev, shape):
+    """Config 3 across the node: B=64 rows split over the ranks for attention, experts split for
+    the MoE, NVLink peer-store exchange (``Qwen3MoeWideDecoderEP``); time = max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from nki_moe_megakernel_b200.engine import Qwen3MoeWideDecoderEP
+    from nki_moe_megakernel_b200.sharding import XchgRegion
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    B, L = 64, shape.num_hidden_layers
+    H, D, E, I, V = shape.hidden_size, shape.head_dim, shape.num_experts, shape.moe_intermediate_size, shape.vocab_size
+    nq, nkv = shape.num_attention_heads, shape.num_key_value_heads
+    R, e0, nl = B // world, rank * E // world, E // world
+    g = torch.Generator(device=dev).manual_seed(args.seed)            # replicated tensors
+    gl = torch.Generator(device=dev).manual_seed(args.seed + 1000 + rank)  # this rank's experts
+    n = lambda *sz, gen=g: (torch.randn(*sz, generator=gen, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
+    one = lambda *sz: (1.0 + torch.randn(*sz, generator=g, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
+    mx = args.weights == "mxfp8"
+    layers = []
+    for _ in range(L):
+        lw = {"wq": n(nq * D, H), "wk": n(nkv * D, H), "wv": n(nkv * D, H), "wo": n(H, nq * D), "q_norm": one(D),
+              "k_norm": one(D), "ln1": one(H), "ln2": one(H), "router": n(E, H)}
+        if mx:
+            lw["mxfp8"] = (*_mx_experts(torch, gl, dev, nl, 2 * I, H), *_mx_experts(torch, gl, dev, nl, H, I))
+        else:
+            lw["gate_up"], lw["down"] = n(nl, 2 * I, H, gen=gl), n(nl, H, I, gen=gl)
+        layers.append(lw)
+    ctx = torch.randint(1024, 8193, (B,), generator=torch.Generator().manual_seed(args.seed)).tolist()
+    mine = ctx[rank * R:(rank + 1) * R]
+    need = [c // 128 + 1 for c in mine]
+    NB = sum(need)
+    xchg = XchgRegion(Qwen3MoeWideDecoderEP.exchange_bytes(B, H, world), rank, world, local)
+    ep = Qwen3MoeWideDecoderEP(shape, layers, rank=rank, world=world, xchg=xchg, batch=B, expert_begin=e0, n_local=nl,
+                               num_blocks=NB, final_norm=one(H), lm_head=n(V, H),
+                               embed=torch.randn(V, H, generator=g, device=dev).to(torch.bfloat16),
+                               rope_max_pos=8320, device=dev)
+    for lw in layers:
+        for k in ("wq", "wk", "wv", "wo", "mxfp8"):
+            lw.pop(k, None)
+    torch.cuda.empty_cache()
+    ep.k_pool.normal_(generator=gl)
+    ep.v_pool.normal_(generator=gl)
+    table = torch.full((R, max(need)), -1, dtype=torch.int32)
+    o = 0
+    for b in range(R):
+        table[b, :need[b]] = torch.arange(o, o + need[b], dtype=torch.int32)
+        o += need[b]
+    table_d, pos_d = table.to(dev), torch.tensor(mine, dtype=torch.int32, device=dev)
+    ids_d = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(args.seed + 2 + rank),
+                          dtype=torch.int32).to(dev)
+    dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    ms, per = _events_time(torch, stream, lambda: ep.decode_step(pos_d, table_d, input_ids=ids_d), args.steps,
+                           args.warmup)
+    ep.check_status()
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Qwen3-30B-A3B decode tokens/s at B=64, contexts uniform in [1024, 8192] (config 3)",
+            "value": B / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights; K/V ~N(0,1))",
+            "config": {"workload": "qwen3-30b-a3b decode step at B=64, attention rows split over ranks, experts "
+                                   "split (expert parallel), NVLink peer-store exchange", "global_batch": B,
+                       "ctx_mean": sum(ctx) / B, "layers": L, "expert_weights": args.weights,
+                       "parallelism": f"attention dp{world} + ep{world}"}}), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ep.close()
+    xchg.close()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

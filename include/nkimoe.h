@@ -301,6 +301,21 @@ int nkm_moe_block_tc_partial(const nkm_moe_tc_desc* desc, int32_t tokens, const 
 /* Synchronise and return the status word of the last call on this workspace (0 = ok). */
 int nkm_moe_tc_status(void* workspace, nkm_stream_t stream);
 
+/* Expert-parallel exchange over NVLink peer memory (the token dispatch / combine of the
+ * reference's expert-parallel MoE, selective_expert_impl.py with moe_ep_degree; config 3 across
+ * GPUs).  nkm_ep_push: `bytes` (multiple of 16) from src to dst[q] + dst_offset for q < n_dst
+ * (<= 8; peer pointers from CUDA IPC), then nkm_ep_arrivals_per_push() arrivals (system-scope
+ * release) on each flags[q] (64-bit counters in the receivers' memory).  nkm_ep_wait: polls
+ * *flag (acquire, system scope) until it reaches target, bounded by 2 s (then NKM_ERR_TIMEOUT is
+ * or-ed into *status).  nkm_ep_reduce: y = bf16(x + bf16(sum over q < n in order of
+ * parts[q])) for rows x hidden elements (parts fp32 [n][rows][hidden], x and y bf16). */
+int nkm_ep_push(const void* src, int64_t bytes, void* const* dst, int32_t n_dst, int64_t dst_offset,
+                unsigned long long* const* flags, nkm_stream_t stream);
+int32_t nkm_ep_arrivals_per_push(void);
+int nkm_ep_wait(const unsigned long long* flag, unsigned long long target, int32_t* status, nkm_stream_t stream);
+int nkm_ep_reduce(const float* parts, int32_t n, int32_t rows, int32_t hidden, const void* x_res, void* y_out,
+                  nkm_stream_t stream);
+
 /* ======================================================================================
  * GPT-OSS decode step (the reference's second megakernel,
  * megakernels/gpt_oss/transformer_gpt_oss.py:240-530, model class

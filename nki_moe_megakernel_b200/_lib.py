@@ -121,6 +121,10 @@ SIGNATURES = {
     "nkm_moe_block_tc": (c_int, [POINTER(nkm_moe_tc_desc), c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p]),
     "nkm_moe_tc_status": (c_int, [c_void_p, c_void_p]),
+    "nkm_ep_push": (c_int, [c_void_p, ctypes.c_int64, c_void_p, c_int32, ctypes.c_int64, c_void_p, c_void_p]),
+    "nkm_ep_arrivals_per_push": (c_int32, []),
+    "nkm_ep_wait": (c_int, [c_void_p, ctypes.c_uint64, c_void_p, c_void_p]),
+    "nkm_ep_reduce": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "nkm_moe_block_tc_partial": (c_int, [POINTER(nkm_moe_tc_desc), c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, ctypes.c_size_t, c_void_p]),
     "nkm_mxfp8_experts_bytes": (ctypes.c_size_t, [c_int32, c_int32, c_int32]),

@@ -16,7 +16,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libnkimoe.so")
-SOURCES = ["nkm_qwen3.cu", "nkm_pack.cu", "nkm_sample.cu", "nkm_gptoss.cu", "nkm_moe_tc.cu"]
+SOURCES = ["nkm_qwen3.cu", "nkm_pack.cu", "nkm_sample.cu", "nkm_gptoss.cu", "nkm_moe_tc.cu", "nkm_ep.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

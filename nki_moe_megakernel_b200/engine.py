@@ -332,11 +332,13 @@ class MoeTcBlock:
     Hugging Face layouts: gate_up ``[E, 2I, H]`` (gate rows then up rows), down ``[E, H, I]``;
     or MXFP8 (``mxfp8=(gate_up codes, gate_up scales, down codes, down scales)``, OCP MX: e4m3
     codes and e8m0 scales per 32 along K, in the same row layouts; ``gate_up``/``down`` then
-    unused)."""
+    unused).  ``expert_begin`` / ``n_local_experts``: the weights hold only that range of experts
+    (expert parallel; ``partial`` calls then sum only their contributions)."""
 
     def __init__(self, ln2: torch.Tensor, router: torch.Tensor, gate_up: Optional[torch.Tensor],
                  down: Optional[torch.Tensor], *, eps: float, top_k: int, max_tokens: int,
-                 router_bias: Optional[torch.Tensor] = None, device=None, mxfp8=None):
+                 router_bias: Optional[torch.Tensor] = None, device=None, mxfp8=None, expert_begin: int = 0,
+                 n_local_experts: int = 0):
         self.device = torch.device(device if device is not None else "cuda")
         self.ln2 = ln2.to(self.device, BF16).contiguous()
         self.router = router.to(self.device, BF16).contiguous()
@@ -352,10 +354,11 @@ class MoeTcBlock:
             self.w2 = down.to(self.device, BF16).contiguous()
             E, I2, H = self.w13.shape
             fmt = _lib.NKM_MOE_WEIGHTS_BF16
+        E = int(self.router.shape[0])  # routing covers every expert; the weights may hold a range of them
         self.H, self.E, self.K, self.I = H, E, top_k, I2 // 2
         self._desc = _lib.nkm_moe_tc_desc(H, E, top_k, self.I, eps, self.ln2.data_ptr(), self.router.data_ptr(),
                                           _ptr(self.router_bias), self.w13.data_ptr(), self.w2.data_ptr(), max_tokens,
-                                          fmt)
+                                          fmt, expert_begin, n_local_experts)
         n = lib().nkm_moe_tc_workspace_bytes(ctypes.byref(self._desc))
         if n == 0:
             raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_moe_tc_workspace_bytes")
@@ -464,3 +467,143 @@ class Qwen3MoeWideDecoder:
 
     def close(self) -> None:
         self.attn.close()
+
+
+class Qwen3MoeWideDecoderEP:
+    """Config 3 across the GPUs of one node (one process per GPU): rank r of N owns the rows
+    ``[B r / N, B (r + 1) / N)`` for attention (every rank holds the attention weights; the rows'
+    K/V pages live on their rank) and the experts ``[E r / N, E (r + 1) / N)`` (expert parallel).
+    Per layer:
+
+    * the attention block on the rank's rows (``nkm_qwen3_attention_block``);
+    * the post-attention rows of every rank gathered on every rank over NVLink (``nkm_ep_push``
+      into the peers' exchange regions, ``nkm_ep_wait`` on the rank's own counter);
+    * the MoE block over all B rows with the rank's experts only (routing over all experts,
+      ``nkm_moe_block_tc_partial``), fp32 partial sums;
+    * each owner's rows of those partials pushed to the owner, which adds them in rank order to
+      its residual (``nkm_ep_reduce``: bf16 residual, as on one GPU).
+
+    ``layers[l]``: dict with the attention tensors (``wq, wk, wv, wo, q_norm, k_norm, ln1``),
+    ``ln2``, ``router`` (all experts) and the rank's experts as ``gate_up`` / ``down`` (or
+    ``mxfp8``) for experts ``[expert_begin, expert_begin + n_local)``.  ``xchg``: this rank's
+    ``sharding.XchgRegion`` of at least ``exchange_bytes(B, H, N)`` bytes."""
+
+    @staticmethod
+    def exchange_bytes(batch: int, hidden: int, world: int) -> int:
+        rows = batch // world
+        return 256 + batch * hidden * 2 + world * rows * hidden * 4
+
+    def __init__(self, shape: Qwen3MoeShape, layers: Sequence[Dict[str, torch.Tensor]], *, rank: int, world: int,
+                 xchg, batch: int, expert_begin: int, n_local: int, num_blocks: int,
+                 final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
+                 embed: Optional[torch.Tensor] = None, rope_max_pos: int = 40960, device=None):
+        assert batch % world == 0 and batch // world <= 32, (batch, world)
+        self.shape, self.rank, self.world, self.xchg = shape, rank, world, xchg
+        self.device = torch.device(device if device is not None else "cuda")
+        self.B, self.rows, H = batch, batch // world, shape.hidden_size
+        att, moe = {}, {}
+        for lw in layers:
+            if id(lw) in att:
+                continue
+            att[id(lw)] = GpuLayer(lw["wq"], lw["wk"], lw["wv"], lw["wo"], lw["q_norm"], lw["k_norm"], lw["ln1"],
+                                   None, None, None, None, moe=False)
+            moe[id(lw)] = MoeTcBlock(lw["ln2"], lw["router"], lw.get("gate_up"), lw.get("down"),
+                                     eps=shape.rms_norm_eps, top_k=shape.num_experts_per_tok, max_tokens=batch,
+                                     router_bias=lw.get("router_bias"), device=self.device, mxfp8=lw.get("mxfp8"),
+                                     expert_begin=expert_begin, n_local_experts=n_local)
+        self.moe = [moe[id(lw)] for lw in layers]
+        self.attn = Qwen3MoeMegakernel(shape, [att[id(lw)] for lw in layers], max_batch=self.rows,
+                                       num_blocks=num_blocks, rope_max_pos=rope_max_pos, device=self.device)
+        self.k_pool, self.v_pool = self.attn.k_pool, self.attn.v_pool
+        self.final_norm = None if final_norm is None else final_norm.to(self.device, torch.float32)
+        self.lm_head = None if lm_head is None else lm_head.to(self.device, BF16).contiguous()
+        self.embed = None if embed is None else embed.to(self.device, BF16).contiguous()
+        # exchange region: [0] gather counter, [8] scatter counter, [256..) all rows (bf16), then the
+        # ranks' partials of this rank's rows (fp32 [N][rows][H])
+        self._g_off, self._p_off = 256, 256 + batch * H * 2
+        own = xchg.ptrs[rank]
+        nbytes = self.exchange_bytes(batch, H, world)
+        assert xchg.nbytes >= nbytes, (xchg.nbytes, nbytes)
+        self._gather = _device_view(own + self._g_off, batch * H * 2, self.device).view(BF16).view(batch, H)
+        self._parts = _device_view(own + self._p_off, world * self.rows * H * 4, self.device).view(
+            torch.float32).view(world, self.rows, H)
+        self._arr = int(lib().nkm_ep_arrivals_per_push()) * world
+        self._targets = [0, 0]
+        self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._part = torch.empty(batch, H, dtype=torch.float32, device=self.device)
+        self._dst_g = (ctypes.c_void_p * world)(*[p + self._g_off for p in xchg.ptrs])
+        self._flag_g = (ctypes.c_void_p * world)(*[p for p in xchg.ptrs])
+        self._flag_s = [(ctypes.c_void_p * 1)(p + 8) for p in xchg.ptrs]
+        self._dst_p = [(ctypes.c_void_p * 1)(p + self._p_off) for p in xchg.ptrs]
+
+    def _wait(self, which: int, s) -> None:
+        self._targets[which] += self._arr
+        check(lib().nkm_ep_wait(self.xchg.ptrs[self.rank] + 8 * which, self._targets[which],
+                                self._status.data_ptr(), s.cuda_stream), "nkm_ep_wait")
+
+    def decode_step(self, positions: torch.Tensor, block_table: torch.Tensor, *, x: Optional[torch.Tensor] = None,
+                    input_ids: Optional[torch.Tensor] = None, want_logits: bool = True, trace: bool = False,
+                    stream=None) -> Dict[str, torch.Tensor]:
+        """One decode step for this rank's rows (``positions`` / ``block_table`` / ``x`` or
+        ``input_ids`` of those rows).  Every rank must call it for the same step."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        H, R, r = self.shape.hidden_size, self.rows, self.rank
+        if x is None:
+            x = self.embed[input_ids.long()]
+        h = x.to(BF16).contiguous()
+        tr = {"resid_mid": [], "resid_out": [], "topk_idx": []} if trace else None
+        for layer in range(self.shape.num_hidden_layers):
+            mid = self.attn.attention_block(layer, h, positions, block_table, residual=True, stream=s)["hidden"]
+            # every rank's rows into every rank's gather area
+            check(lib().nkm_ep_push(mid.data_ptr(), R * H * 2, self._dst_g, self.world, r * R * H * 2, self._flag_g,
+                                    s.cuda_stream), "nkm_ep_push")
+            self._wait(0, s)
+            blk = self.moe[layer]
+            idx = torch.empty(self.B, blk.K, dtype=torch.int32, device=self.device)
+            check(lib().nkm_moe_block_tc_partial(ctypes.byref(blk._desc), self.B, self._gather.data_ptr(),
+                                                 self._part.data_ptr(), idx.data_ptr(), None, blk.workspace.data_ptr(),
+                                                 blk.workspace.numel(), s.cuda_stream), "nkm_moe_block_tc_partial")
+            # each owner's rows of this rank's partials into the owner's slot r
+            for q in range(self.world):
+                check(lib().nkm_ep_push(self._part[q * R:(q + 1) * R].data_ptr(), R * H * 4, self._dst_p[q], 1,
+                                        r * R * H * 4, self._flag_s[q], s.cuda_stream), "nkm_ep_push")
+            self._wait(1, s)
+            out = torch.empty_like(mid)
+            check(lib().nkm_ep_reduce(self._parts.data_ptr(), self.world, R, H, mid.data_ptr(), out.data_ptr(),
+                                      s.cuda_stream), "nkm_ep_reduce")
+            h = out
+            if tr is not None:
+                tr["resid_mid"].append(mid.float())
+                tr["resid_out"].append(out.float())
+                tr["topk_idx"].append(idx[r * R:(r + 1) * R])
+        res = {"hidden": h}
+        if want_logits and self.lm_head is not None:
+            xf = h.float()
+            xn = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.shape.rms_norm_eps) * self.final_norm
+            res["logits"] = torch.mm(xn.to(BF16), self.lm_head.t(), out_dtype=torch.float32)
+        if tr is not None:
+            res.update({k: torch.stack(v) for k, v in tr.items()})
+        return res
+
+    def check_status(self) -> None:
+        torch.cuda.synchronize(self.device)
+        st = int(self._status.item())
+        if st:
+            raise _lib.NkmError(st, "expert-parallel exchange")
+        self.attn.check_status()
+        for m in {id(m): m for m in self.moe}.values():
+            st = m.status()
+            if st != 0:
+                raise _lib.NkmError(st, "tcgen05 MoE block")
+
+    def close(self) -> None:
+        self.attn.close()
+
+
+def _device_view(ptr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor over device memory this process owns (the rank's own exchange region)."""
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+    return torch.as_tensor(_Mem(), device=device)

@@ -137,3 +137,96 @@ def test_model_class_tp2_validate(tmp_path):
         pytest.skip("needs 2 GPUs")
     mp.spawn(_main_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     assert [open(tmp_path / f"rc{r}").read() for r in range(2)] == ["0", "0"]
+
+
+def _wide_ep_worker(rank, world, port, out_dir):
+    """Config 3 across GPUs: B=64 rows split over the ranks for attention, experts split for the
+    MoE (nkm_ep_* exchange), two layers, contexts uniform in [1024, 4096]."""
+    import datetime
+
+    from nki_moe_megakernel_b200.engine import Qwen3MoeWideDecoder, Qwen3MoeWideDecoderEP
+    from nki_moe_megakernel_b200.sharding import XchgRegion
+    from tests.qwen_cases import BF16, make_kv, make_layers, qwen_cfg, shape_of
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    L, B = 2, 64
+    cfg = qwen_cfg(n_layers=L)
+    lws = make_layers(cfg, L, seed=71)
+    g = torch.Generator().manual_seed(72)
+    positions = torch.randint(1024, 4097, (B,), generator=g).tolist()
+    NB = sum(p // 128 + 1 for p in positions) + 2
+    k0, v0, table = make_kv(cfg, L, positions, NB, seed=73, nan_fill=False)
+    x = torch.randn(B, cfg.hidden, generator=g).to(BF16)
+    R, E = B // world, cfg.n_experts
+    e0, nl = rank * E // world, E // world
+    keys = ("wq", "wk", "wv", "wo", "q_norm", "k_norm", "ln1", "ln2", "router")
+    dicts = []
+    for lw in lws:
+        d = {k: getattr(lw, k).to(dev) for k in keys}
+        d["gate_up"], d["down"] = lw.gate_up[e0:e0 + nl].to(dev), lw.down[e0:e0 + nl].to(dev)
+        dicts.append(d)
+    xchg = XchgRegion(Qwen3MoeWideDecoderEP.exchange_bytes(B, cfg.hidden, world), rank, world, rank)
+    ep = Qwen3MoeWideDecoderEP(shape_of(cfg, L, 0), dicts, rank=rank, world=world, xchg=xchg, batch=B,
+                               expert_begin=e0, n_local=nl, num_blocks=NB, rope_max_pos=4224, device=dev)
+    ep.k_pool.copy_(k0.to(dev))
+    ep.v_pool.copy_(v0.to(dev))
+    rows = slice(rank * R, (rank + 1) * R)
+    pos = torch.tensor(positions, dtype=torch.int32)
+    dist.barrier()
+    outs = []
+    for _ in range(2):  # the exchange counters carry over steps
+        ep.k_pool.copy_(k0.to(dev))
+        ep.v_pool.copy_(v0.to(dev))
+        res = ep.decode_step(pos[rows].to(dev), table[rows].to(dev), x=x[rows].to(dev), want_logits=False,
+                             trace=True)
+        ep.check_status()
+        outs.append({k: v.cpu() for k, v in res.items()})
+    result = {"outs": outs}
+    del dicts
+    ep.close()
+    torch.cuda.empty_cache()
+    if rank == 0:
+        full = [{k: getattr(lw, k).to(dev) for k in keys + ("gate_up", "down")} for lw in lws]
+        wide = Qwen3MoeWideDecoder(shape_of(cfg, L, 0), full, max_batch=B, num_blocks=NB, rope_max_pos=4224,
+                                   device=dev)
+        wide.k_pool.copy_(k0.to(dev))
+        wide.v_pool.copy_(v0.to(dev))
+        r = wide.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=False, trace=True)
+        wide.check_status()
+        result["ref"] = {k: v.cpu() for k, v in r.items()}
+        wide.close()
+    torch.save(result, os.path.join(out_dir, f"ep{rank}.pt"))
+    dist.barrier()
+    xchg.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_wide_expert_parallel_matches_single_gpu(tmp_path, world):
+    """Config 3 across GPUs (B=64, attention rows split, experts split, exchange over NVLink peer
+    stores): every rank's rows equal the single-GPU B=64 step within max-abs 2e-2 beyond one bf16
+    ulp (the MoE partials are summed per rank, then in rank order), routing equal, two steps in a
+    row identical."""
+    from oracle import qwen3_moe_oracle as O
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.spawn(_wide_ep_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    rs = [torch.load(tmp_path / f"ep{r}.pt") for r in range(world)]
+    ref = rs[0]["ref"]
+    R = 64 // world
+    for rank, r in enumerate(rs):
+        a, b = r["outs"]
+        assert torch.equal(a["hidden"], b["hidden"]), "second step differs"
+        rows = slice(rank * R, (rank + 1) * R)
+        assert torch.equal(a["topk_idx"].long(), ref["topk_idx"][:, rows].long())
+        got, want = a["hidden"].float(), ref["hidden"][rows].float()
+        ulp = torch.exp2(torch.floor(torch.log2(want.abs().clamp_min(1e-30))) - 7)
+        excess = float(((got - want).abs() - ulp).clamp_min(0).max())
+        c = O.compare(got, want)
+        print(f"[wide EP world {world} rank {rank}] vs single GPU {c}, beyond one ulp {excess:.3g}", flush=True)
+        assert excess <= ATOL and c["cosine"] >= COS, (rank, c, excess)
