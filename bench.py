@@ -359,7 +359,7 @@ def multi_gpu_parity(rank, world, local, device):
         layers.append(GpuLayer(wq, wk, wv, wo, r["qn"], r["kn"], r["ln1"], r["ln2"], r["router"], gu, dn))
     lshape = Qwen3MoeShape(num_hidden_layers=L, vocab_size=V, num_attention_heads=len(shard.q_heads),
                            num_key_value_heads=len(shard.kv_heads))
-    xchg = XchgRegion(xchg_bytes(H, B, world), rank, world, local)
+    xchg = XchgRegion(xchg_bytes(H, B, world, V), rank, world, local)
     eng = Qwen3MoeMegakernel(lshape, layers, max_batch=B, num_blocks=NB, final_norm=fnorm, lm_head=lm, embed=embed,
                              device=device, shard=shard, xchg=xchg)
     eng.k_pool.copy_(k0[:, :, shard.kv_heads])
@@ -422,7 +422,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         full = Qwen3MoeShape(num_hidden_layers=args.layers)
         shard = plan_shard(rank, world, full.num_attention_heads, full.num_key_value_heads, full.num_experts)
-        xchg = XchgRegion(xchg_bytes(full.hidden_size, args.batch, world), rank, world, local)
+        xchg = XchgRegion(xchg_bytes(full.hidden_size, args.batch, world, full.vocab_size), rank, world, local)
         dist.barrier()
     parity = multi_gpu_parity(rank, world, local, device) if world > 1 else None
     eng, shape, table, positions, ids = build_engine(args, device, args.seed, shard, xchg)

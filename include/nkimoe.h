@@ -78,7 +78,10 @@ typedef struct nkm_qwen3_desc {
    * w2_ft point at the local experts.  After the O-projection and after the experts, every
    * rank stores its partial sums into the exchange region of every rank (xchg[q], mapped in
    * this process; nkm_qwen3_xchg_bytes each) and all ranks sum them in rank order, so every
-   * rank keeps the same residual stream.  Replaces the TP/EP sharding of the NxDI model
+   * rank keeps the same residual stream.  The LM head is split over the vocabulary: rank r
+   * computes 16-row strips [S r / n_ranks, S (r + 1) / n_ranks) of S = vocab / 16 (lm_head_ft
+   * still points at the whole packed head), stores them into every rank's exchange region, and
+   * every rank returns the full logits.  Replaces the TP/EP sharding of the NxDI model
    * (qwen_with_megakernel.py:102-132, replica groups at :360-362). */
   int32_t n_ranks;
   int32_t rank;

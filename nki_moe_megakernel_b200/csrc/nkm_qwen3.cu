@@ -40,6 +40,15 @@ int fail(int code, const char* fmt, ...) {
 constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
+// Exchange region of a rank: the barrier counter (kXchgHeader bytes), the O-projection and expert
+// partials [2][n_ranks][max_batch][hidden] fp32, then (several ranks) the logits [max_batch][vocab]
+// fp32 that the vocabulary-sharded LM head fills on every rank.
+size_t xlog_offset(const nkm_qwen3_desc& d) {
+  const size_t nr = d.n_ranks > 0 ? static_cast<size_t>(d.n_ranks) : 1;
+  return align_up(static_cast<size_t>(nkm::kXchgHeader) +
+                  2 * nr * static_cast<size_t>(d.max_batch) * static_cast<size_t>(d.hidden) * 4);
+}
+
 // Workspace layout (offsets in bytes from the workspace base).
 struct WsLayout {
   size_t ctrl, ctrl_bytes;  // bar, status, strip/attn/row counters (zeroed every step)
@@ -237,8 +246,8 @@ size_t nkm_qwen3_workspace_bytes(const nkm_qwen3_desc* desc) {
 size_t nkm_qwen3_xchg_bytes(const nkm_qwen3_desc* desc) {
   if (check_desc(desc) != NKM_OK) return 0;
   const size_t nr = desc->n_ranks > 0 ? static_cast<size_t>(desc->n_ranks) : 1;
-  return align_up(static_cast<size_t>(nkm::kXchgHeader) +
-                  2 * nr * static_cast<size_t>(desc->max_batch) * static_cast<size_t>(desc->hidden) * 4);
+  return align_up(xlog_offset(*desc) +
+                  (nr > 1 ? static_cast<size_t>(desc->max_batch) * static_cast<size_t>(desc->vocab) * 4 : 0));
 }
 
 int nkm_qwen3_create(const nkm_qwen3_desc* desc, void* workspace, size_t workspace_bytes, nkm_qwen3** out) {
@@ -361,6 +370,11 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.n_local = d.n_local_experts > 0 ? d.n_local_experts : d.n_experts;
   for (int q = 0; q < nkm::kMaxRanks; ++q) p.xchg[q] = q < p.n_ranks ? static_cast<uint8_t*>(d.xchg[q]) : nullptr;
   p.gbase = reinterpret_cast<unsigned long long*>(h->ws + h->lay.gbase);
+  // the vocabulary's 16-row strips split evenly over the ranks
+  const int vs = d.vocab / 16;
+  p.lm_s0 = static_cast<int>(static_cast<int64_t>(vs) * p.rank / p.n_ranks);
+  p.lm_ns = static_cast<int>(static_cast<int64_t>(vs) * (p.rank + 1) / p.n_ranks) - p.lm_s0;
+  p.xlog_off = static_cast<int64_t>(xlog_offset(d));
   p.first_layer = first;
   p.num_layers = nl;
   p.stages = stages & (NKM_STAGE_ATTN | NKM_STAGE_MOE | NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST |

@@ -71,6 +71,11 @@ struct Params {
   int n_ranks, rank, expert_begin, n_local;
   uint8_t* xchg[kMaxRanks];       // exchange region of every rank (kXchgHeader bytes + partials)
   unsigned long long* gbase;      // workspace: cross-GPU barrier count before this launch
+  // LM head rows of this rank: 16-row strips [lm_s0, lm_s0 + lm_ns) of the vocabulary.  With
+  // several ranks every rank stores its logits into every rank's exchange region at byte offset
+  // xlog_off ([T][V] fp32), and after a cross-GPU barrier copies the whole of it to logits_out.
+  int lm_s0, lm_ns;
+  int64_t xlog_off;
   int first_layer, num_layers, stages, residual;
   const LayerPtrs* layers;
   const uint16_t* final_norm;
@@ -320,6 +325,11 @@ __device__ __forceinline__ float* xchg_part(const Params& p, int q, int which, i
          static_cast<size_t>(which * p.n_ranks + src) * p.T * p.H;
 }
 
+// Vocabulary-sharded LM head: the [T][V] fp32 logits area of rank q's region.
+__device__ __forceinline__ float* xchg_logits(const Params& p, int q) {
+  return reinterpret_cast<float*>(p.xchg[q] + p.xlog_off);
+}
+
 // Barrier over every CTA of every rank: each CTA adds 1 to the counter of every rank (after a
 // system-scope fence: its partial stores into the other ranks' regions become visible first) and
 // waits until its own rank's counter reaches the launch base + (k + 1) * CTAs * ranks.  The
@@ -557,6 +567,12 @@ struct GemvGeom {
   int layer;
 };
 
+// LM head rows of this rank (all of them on one GPU)
+__device__ __forceinline__ GemvGeom lm_geom(const Params& p, int layer) {
+  return GemvGeom{p.lm_head + static_cast<uint64_t>(p.lm_s0) * (p.H / 32) * kUnitBytes, 0, 1, p.lm_ns, p.H / 32, p.H,
+                  layer};
+}
+
 template <int NT>
 struct Acc {
   float v[NT][4];
@@ -627,10 +643,20 @@ __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, con
     const int pair = rt->act_off[seg] + col;
     const float h = rbf(rbf(silu_f(rbf(v0))) * rbf(v1));
     p.hbuf[static_cast<size_t>(pair) * p.I + strip * 8 + g] = f2bf(h);
-  } else {  // GK_LMHEAD
-    float* lo = p.logits_out + static_cast<size_t>(col) * p.V + strip * 16 + g;
-    lo[0] = v0;
-    lo[8] = v1;
+  } else {  // GK_LMHEAD (strip counts from this rank's first vocabulary strip)
+    const size_t off = static_cast<size_t>(col) * p.V + (p.lm_s0 + strip) * 16 + g;
+    if (p.n_ranks > 1) {
+#pragma unroll 1
+      for (int q = 0; q < p.n_ranks; ++q) {
+        float* lo = xchg_logits(p, q) + off;
+        lo[0] = v0;
+        lo[8] = v1;
+      }
+    } else {
+      float* lo = p.logits_out + off;
+      lo[0] = v0;
+      lo[8] = v1;
+    }
   }
 }
 
@@ -2585,7 +2611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (staged) norm_prefetch(p, c, nl.ln1, nullptr);
       }
     } else if (want_lm) {
-      GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer};
+      const GemvGeom gl = lm_geom(p, layer);
       gemv_prime<NT, GK_LMHEAD>(p, c, gl, staged ? 1 : RingGeom<NT>::kGemvSlots);
       if (staged) norm_prefetch(p, c, p.final_norm, nullptr);
     }
@@ -2711,8 +2737,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (staged) norm_staged(p, c, max(layer_end - 1, p.first_layer), false, p.final_norm);
     else norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
-    GemvGeom gl{p.lm_head, 0, 1, p.V / 16, p.H / 32, p.H, layer_end - 1};
-    gemv_stage<NT, GK_LMHEAD>(p, c, gl);
+    gemv_stage<NT, GK_LMHEAD>(p, c, lm_geom(p, layer_end - 1));
+    if (p.n_ranks > 1) {
+      // every rank's strips are in this rank's logits area once all ranks pass the barrier
+      if (!grid_sync_ranks(p, c)) return;
+      const int n16 = p.T * p.V / 4;
+      const float* src = xchg_logits(p, p.rank);
+      float4* dst = reinterpret_cast<float4*>(p.logits_out);
+      for (int i = blockIdx.x * kThreads + threadIdx.x; i < n16; i += gridDim.x * kThreads) dst[i] = ldcg_f4(src + 4 * i);
+    }
   }
   if (p.tr_stage) {
     __syncthreads();

@@ -316,7 +316,8 @@ class NeuronQwen3MoeForCausalLMV3:
             shape.num_attention_heads = len(self.shard.q_heads)
             shape.num_key_value_heads = len(self.shard.kv_heads)
             dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
-            self.xchg = XchgRegion(xchg_bytes(shape.hidden_size, self._rows(), self.shard.world),
+            self.xchg = XchgRegion(xchg_bytes(shape.hidden_size, self._rows(), self.shard.world,
+                                              shape.vocab_size),
                                    self.shard.rank, self.shard.world, dev_index)
         self.kernel = Qwen3MoeMegakernel(shape, self._layers, max_batch=self._rows(),
                                          num_blocks=nc.pa_num_blocks, final_norm=self._head["final_norm"],

@@ -168,3 +168,22 @@ def test_gptoss_create_rejects_bad_descriptions(L):
         h = ctypes.c_void_p()
         assert L.lib().nkm_gptoss_create(ctypes.byref(d), None, 0, ctypes.byref(h)) == L.NKM_ERR_ARG, bad
         assert L.lib().nkm_gptoss_workspace_bytes(ctypes.byref(d)) == 0
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_xchg_bytes_match_host_sizing(L, world):
+    """The exchange region the host allocates (``sharding.xchg_bytes``) is the size the library
+    asks for: header, partials and (several ranks) the vocabulary-sharded LM head's logits."""
+    from nki_moe_megakernel_b200.sharding import xchg_bytes
+
+    H, B, V = 2048, 8, 151936
+    d, _keep = _desc(L, vocab=V, max_batch=B, n_q_heads=32 // world, n_kv_heads=max(1, 4 // world))
+    d.n_ranks, d.rank = world, world - 1
+    d.expert_begin, d.n_local_experts = 128 // world * (world - 1), 128 // world
+    if world > 1:
+        for q in range(world):
+            d.xchg[q] = 256 * (q + 1)  # only validated for alignment, never dereferenced here
+    need = L.lib().nkm_qwen3_xchg_bytes(ctypes.byref(d))
+    assert need == xchg_bytes(H, B, world, V)
+    if world > 1:
+        assert need >= B * V * 4 + 2 * world * B * H * 4

@@ -22,6 +22,7 @@ pytestmark = pytest.mark.gpu
 
 ATOL = 2e-2
 COS = 0.999
+V = 257 * 16
 
 
 def _free_port():
@@ -58,29 +59,36 @@ def _worker(rank, world, port, out_dir):
         gu, dn = shard_experts(lw.gate_up, lw.down, shard)
         t = [a.to(dev) for a in (wq, wk, wv, wo, lw.q_norm, lw.k_norm, lw.ln1, lw.ln2, lw.router, gu, dn)]
         layers.append(GpuLayer(*t))
-    lshape = shape_of(cfg, 2, 0)
+    # LM head of V = 257 strips of 16 rows: the ranks' vocabulary slices differ in size
+    gh = torch.Generator().manual_seed(34)
+    fnorm = (1.0 + 0.1 * torch.randn(cfg.hidden, generator=gh)).to(BF16)
+    lm = (0.02 * torch.randn(V, cfg.hidden, generator=gh)).to(BF16)
+    lshape = shape_of(cfg, 2, V)
     lshape.num_attention_heads, lshape.num_key_value_heads = len(shard.q_heads), len(shard.kv_heads)
-    xchg = XchgRegion(xchg_bytes(cfg.hidden, B, world), rank, world, rank)
-    eng = Qwen3MoeMegakernel(lshape, layers, max_batch=B, num_blocks=NB, device=dev, shard=shard, xchg=xchg)
+    xchg = XchgRegion(xchg_bytes(cfg.hidden, B, world, lshape.vocab_size), rank, world, rank)
+    eng = Qwen3MoeMegakernel(lshape, layers, max_batch=B, num_blocks=NB, final_norm=fnorm.to(dev), lm_head=lm.to(dev),
+                             device=dev, shard=shard, xchg=xchg)
     eng.k_pool.copy_(k0[:, :, shard.kv_heads].to(dev))
     eng.v_pool.copy_(v0[:, :, shard.kv_heads].to(dev))
     dist.barrier()
-    outs = []
+    outs, logits = [], []
     for _ in range(2):  # two steps in a row: the cross-GPU barrier count carries over launches
-        res = eng.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=False)
+        res = eng.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=True)
         torch.cuda.synchronize()
         outs.append(res["hidden"].cpu())
+        logits.append(res["logits"].cpu())
     st = eng.status()
-    result = {"status": st, "hidden": outs, "k_pool": eng.k_pool.cpu(), "v_pool": eng.v_pool.cpu(),
+    result = {"status": st, "hidden": outs, "logits": logits, "k_pool": eng.k_pool.cpu(), "v_pool": eng.v_pool.cpu(),
               "kv_heads": shard.kv_heads}
     if rank == 0:
-        ref = Qwen3MoeMegakernel(shape_of(cfg, 2, 0), gpu_layers(lws, dev), max_batch=B, num_blocks=NB, device=dev)
+        ref = Qwen3MoeMegakernel(shape_of(cfg, 2, V), gpu_layers(lws, dev), max_batch=B, num_blocks=NB,
+                                 final_norm=fnorm.to(dev), lm_head=lm.to(dev), device=dev)
         ref.k_pool.copy_(k0.to(dev))
         ref.v_pool.copy_(v0.to(dev))
-        r = ref.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=False)
+        r = ref.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=True)
         torch.cuda.synchronize()
-        result.update(ref_status=ref.status(), ref_hidden=r["hidden"].cpu(), ref_k=ref.k_pool.cpu(),
-                      ref_v=ref.v_pool.cpu())
+        result.update(ref_status=ref.status(), ref_hidden=r["hidden"].cpu(), ref_logits=r["logits"].cpu(),
+                      ref_k=ref.k_pool.cpu(), ref_v=ref.v_pool.cpu())
         ref.close()
     torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
@@ -100,10 +108,14 @@ def test_tp_ep_ranks_match_single_gpu(tmp_path, world):
     r0 = rs[0]
     assert all(r["status"] == 0 for r in rs) and r0["ref_status"] == 0
     for r in rs[1:]:
-        for a, b in zip(r0["hidden"], r["hidden"]):
+        for a, b in zip(r0["hidden"] + r0["logits"], r["hidden"] + r["logits"]):
             assert torch.equal(a, b), "ranks disagree"
     assert torch.equal(r0["hidden"][0], r0["hidden"][1]), "second step differs"
+    assert torch.equal(r0["logits"][0], r0["logits"][1]), "second step differs"
     c = O.compare(r0["hidden"][0].float(), r0["ref_hidden"].float())
+    assert c["max_abs"] <= ATOL and c["cosine"] >= COS, c
+    # the vocabulary-sharded LM head: every rank returns all V logits
+    c = O.compare(r0["logits"][0], r0["ref_logits"])
     assert c["max_abs"] <= ATOL and c["cosine"] >= COS, c
     for r in rs:
         h = r["kv_heads"]
