@@ -78,7 +78,9 @@ typedef struct nkm_qwen3_desc {
    * w2_ft point at the local experts.  After the O-projection and after the experts, every
    * rank stores its partial sums into the exchange region of every rank (xchg[q], mapped in
    * this process; nkm_qwen3_xchg_bytes each) and all ranks sum them in rank order, so every
-   * rank keeps the same residual stream.  The LM head is split over the vocabulary: rank r
+   * rank keeps the same residual stream.  The partials travel as 8-byte words that carry the
+   * exchange's sequence number next to the value, so a rank reads them as soon as they land,
+   * with no cross-GPU barrier.  The LM head is split over the vocabulary: rank r
    * computes 16-row strips [S r / n_ranks, S (r + 1) / n_ranks) of S = vocab / 16 (lm_head_ft
    * still points at the whole packed head), stores them into every rank's exchange region, and
    * every rank returns the full logits.  Replaces the TP/EP sharding of the NxDI model
@@ -161,7 +163,10 @@ int nkm_qwen3_decode_step(nkm_qwen3* h, const nkm_qwen3_step* step, nkm_stream_t
 
 /* Synchronise `stream` and return the device status word (0 = ok).  Device errors are
  * sticky: they accumulate over steps until this call reads and clears them (a step that
- * starts while a fatal error is recorded returns at its first barrier). */
+ * starts while a fatal error is recorded returns at its first barrier).  With n_ranks > 1, a
+ * non-zero status also clears this rank's exchange region and restarts its exchange sequence:
+ * after a failed step every rank calls this once all ranks' launches have ended, and the group
+ * synchronises (a host barrier) before its next step. */
 int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream);
 
 /* Single fused attention block on layer `layer` (residual=0: returns the O-projection

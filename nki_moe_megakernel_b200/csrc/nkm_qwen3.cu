@@ -41,18 +41,18 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
 // Exchange region of a rank: the barrier counter (kXchgHeader bytes), the O-projection and expert
-// partials [2][n_ranks][max_batch][hidden] fp32, then (several ranks) the logits [max_batch][vocab]
-// fp32 that the vocabulary-sharded LM head fills on every rank.
+// partials as tagged 8-byte words [2 kinds][2 slots][n_ranks][max_batch][hidden], then (several
+// ranks) the logits [max_batch][vocab] fp32 that the vocabulary-sharded LM head fills on every rank.
 size_t xlog_offset(const nkm_qwen3_desc& d) {
   const size_t nr = d.n_ranks > 0 ? static_cast<size_t>(d.n_ranks) : 1;
   return align_up(static_cast<size_t>(nkm::kXchgHeader) +
-                  2 * nr * static_cast<size_t>(d.max_batch) * static_cast<size_t>(d.hidden) * 4);
+                  4 * nr * static_cast<size_t>(d.max_batch) * static_cast<size_t>(d.hidden) * 8);
 }
 
 // Workspace layout (offsets in bytes from the workspace base).
 struct WsLayout {
   size_t ctrl, ctrl_bytes;  // bar, status, strip/attn/row counters (zeroed every step)
-  size_t bar, status, gbase, strip_cnt, attn_cnt, row_cnt;
+  size_t bar, status, gbase, xseq, strip_cnt, attn_cnt, row_cnt;
   size_t layers, resid, qkv, attn_out, att_part, rlogits, hbuf, ypair, gpart;
   size_t total;
 };
@@ -69,6 +69,7 @@ WsLayout layout_ws(const nkm_qwen3_desc& d, int num_sms) {
   w.bar = o;
   w.status = o + 16;  // bar[0] = barrier arrival count, bar[2] = CTAs that left the launch
   w.gbase = o + 24;   // u64: cross-GPU barrier count before the next launch
+  w.xseq = o + 32;    // u32[2]: partial exchanges of each kind before the next launch
   w.strip_cnt = o + 256;
   w.attn_cnt = w.strip_cnt + kMaxStrips * 4;
   w.row_cnt = w.attn_cnt + align_up(Tm * d.n_kv_heads * 4);
@@ -370,6 +371,7 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.n_local = d.n_local_experts > 0 ? d.n_local_experts : d.n_experts;
   for (int q = 0; q < nkm::kMaxRanks; ++q) p.xchg[q] = q < p.n_ranks ? static_cast<uint8_t*>(d.xchg[q]) : nullptr;
   p.gbase = reinterpret_cast<unsigned long long*>(h->ws + h->lay.gbase);
+  p.xseq = reinterpret_cast<unsigned*>(h->ws + h->lay.xseq);
   // the vocabulary's 16-row strips split evenly over the ranks
   const int vs = d.vocab / 16;
   p.lm_s0 = static_cast<int>(static_cast<int64_t>(vs) * p.rank / p.n_ranks);
@@ -420,7 +422,9 @@ static int launch_step(nkm_qwen3* h, const nkm_qwen3_step* s, int first, int nl,
   p.gpart = reinterpret_cast<float*>(ws + h->lay.gpart);
 
   const int nt = nt_for_batch(p.T);
-  const bool ext = (stages & (NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST)) != 0;
+  // the extended kernels also carry the exchange of a group of several ranks: the single-GPU
+  // decode kernels stay free of that code
+  const bool ext = (stages & (NKM_STAGE_QKV_IN | NKM_STAGE_KV_FIRST)) != 0 || p.n_ranks > 1;
   const int ki = ext ? (nt == 1 ? 3 : 4) : (nt == 1 ? 0 : (nt == 2 ? 1 : 2));
   void* args[3] = {&p, &h->kmap, &h->vmap};
   NKM_CUDA(cudaLaunchCooperativeKernel(decode_kernel_fn(ki), dim3(h->num_sms), dim3(nkm::kThreads), args, h->smem[ki],
@@ -471,7 +475,11 @@ int nkm_qwen3_status(nkm_qwen3* h, nkm_stream_t stream) {
     // the status is sticky until read; after a fault the barrier and counters may be mid-way
     // (with several ranks, every rank calls this before the group continues)
     NKM_CUDA(cudaMemset(h->ws + h->lay.ctrl, 0, h->lay.ctrl_bytes));
-    if (h->desc.n_ranks > 1) NKM_CUDA(cudaMemset(h->desc.xchg[h->desc.rank], 0, nkm::kXchgHeader));
+    // the exchange sequence restarts with the cleared control words: clear the tagged partials too
+    if (h->desc.n_ranks > 1) {
+      NKM_CUDA(cudaMemset(h->desc.xchg[h->desc.rank], 0, nkm_qwen3_xchg_bytes(&h->desc)));
+      NKM_CUDA(cudaDeviceSynchronize());
+    }
   }
   return st;
 }

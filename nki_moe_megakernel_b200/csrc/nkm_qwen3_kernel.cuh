@@ -71,6 +71,7 @@ struct Params {
   int n_ranks, rank, expert_begin, n_local;
   uint8_t* xchg[kMaxRanks];       // exchange region of every rank (kXchgHeader bytes + partials)
   unsigned long long* gbase;      // workspace: cross-GPU barrier count before this launch
+  unsigned* xseq;                 // workspace: partial exchanges of each kind before this launch
   // LM head rows of this rank: 16-row strips [lm_s0, lm_s0 + lm_ns) of the vocabulary.  With
   // several ranks every rank stores its logits into every rank's exchange region at byte offset
   // xlog_off ([T][V] fp32), and after a cross-GPU barrier copies the whole of it to logits_out.
@@ -318,11 +319,43 @@ __device__ __forceinline__ bool grid_barrier(const Params& p, Ctx& c) {
 }
 
 // ------------------------------------------------------------------ ranks (TP + EP)
-// Partial tile `which` (0: O-projection, 1: experts) stored by rank `src` in rank q's region:
-// [2][n_ranks][T][H] fp32 after the header.
-__device__ __forceinline__ float* xchg_part(const Params& p, int q, int which, int src) {
-  return reinterpret_cast<float*>(p.xchg[q] + kXchgHeader) +
-         static_cast<size_t>(which * p.n_ranks + src) * p.T * p.H;
+// Partial sums exchanged between ranks, as tagged words (tag in the high 32 bits, the fp32 value
+// in the low 32): exchange number n of kind `which` (0: O-projection, 1: experts) stored by rank
+// `src` lands in rank q's region at [which][n % 2][src][T][H] after the header, tagged n + 1.  A
+// reader waits until every word it needs carries the tag of the exchange it is in; two slots per
+// kind suffice because a rank produces exchange n + 2 only after every rank has read exchange n
+// (it needs their exchange n + 1, which each rank produces after reading exchange n).
+__device__ __forceinline__ unsigned long long* xchg_ll(const Params& p, int q, int which, unsigned n, int src) {
+  return reinterpret_cast<unsigned long long*>(p.xchg[q] + kXchgHeader) +
+         static_cast<size_t>((which * 2 + static_cast<int>(n & 1u)) * p.n_ranks + src) * p.T * p.H;
+}
+// Sequence number of `layer`'s exchange of kind `which`: the exchanges before this launch (written
+// by the previous launch's last CTA, constant during this one) plus one per earlier layer.
+__device__ __forceinline__ unsigned xseq_of(const Params& p, int which, int layer) {
+  return __ldg(p.xseq + which) + static_cast<unsigned>(layer - p.first_layer);
+}
+__device__ __forceinline__ unsigned long long ll_word(unsigned n, float v) {
+  return (static_cast<unsigned long long>(n + 1u) << 32) | __float_as_uint(v);
+}
+// Store value v of element `off` of this rank's partial of exchange n into every rank's region.
+__device__ __forceinline__ void ll_put(const Params& p, int which, unsigned n, size_t off, float v) {
+  const unsigned long long w = ll_word(n, v);
+#pragma unroll 1
+  for (int q = 0; q < p.n_ranks; ++q) st_relaxed_sys_u64(xchg_ll(p, q, which, n, p.rank) + off, w);
+}
+// Out of line (the single-GPU path never calls them): the elements off + d[i] of `layer`'s
+// partial of kind `which`, values v[i].
+__device__ __noinline__ void ll_put2(const Params& p, int which, int layer, size_t off, float v0, float v1, int d1) {
+  const unsigned n = xseq_of(p, which, layer);
+  ll_put(p, which, n, off, v0);
+  ll_put(p, which, n, off + d1, v1);
+}
+__device__ __noinline__ void ll_put4(const Params& p, int which, int layer, size_t off, float4 v) {
+  const unsigned n = xseq_of(p, which, layer);
+  ll_put(p, which, n, off, v.x);
+  ll_put(p, which, n, off + 1, v.y);
+  ll_put(p, which, n, off + 2, v.z);
+  ll_put(p, which, n, off + 3, v.w);
 }
 
 // Vocabulary-sharded LM head: the [T][V] fp32 logits area of rank q's region.
@@ -373,43 +406,76 @@ __device__ __noinline__ bool grid_sync_ranks(const Params& p, Ctx& c) {
   return *c.flag != 0;
 }
 
-// After grid_sync_ranks: resid[t][row] += bf16(sum over ranks, in rank order, of partial
-// `which`), for the 16-row strips s = blockIdx.x, blockIdx.x + gridDim.x, ...  Every rank
-// computes the same sums, so the residual streams stay identical.
-__device__ __noinline__ void rank_reduce(const Params& p, int which, int layer) {
-  const int S = p.H / 16, n = p.T * 16;
+// resid[t][row] += bf16(sum over ranks, in rank order, of exchange n of kind `which`), for the
+// 16-row strips s = blockIdx.x, blockIdx.x + gridDim.x, ...: each element waits (bounded) until
+// every rank's word for it carries exchange n's tag.  Every rank computes the same sums, so the
+// residual streams stay identical.  Returns false once the launch has failed.
+__device__ __noinline__ bool rank_reduce(const Params& p, int which, int layer, unsigned n) {
+  const int S = p.H / 16, ne = p.T * 16;
+  const unsigned tag = n + 1u;
   float* trace = which == 0 ? p.tr_mid : p.tr_out;
 #pragma unroll 1
   for (int s = blockIdx.x; s < S; s += gridDim.x) {
 #pragma unroll 1
-    for (int e = threadIdx.x; e < n; e += kThreads) {
+    for (int e = threadIdx.x; e < ne; e += kThreads) {
       const int t = e >> 4, row = s * 16 + (e & 15);
       const size_t off = static_cast<size_t>(t) * p.H + row;
-      float v[kMaxRanks];
+      unsigned long long w[kMaxRanks];
+      unsigned pend = 0u;
 #pragma unroll
-      for (int q = 0; q < kMaxRanks; ++q) v[q] = q < p.n_ranks ? ldcg_f(xchg_part(p, p.rank, which, q) + off) : 0.f;
+      for (int q = 0; q < kMaxRanks; ++q) {
+        w[q] = q < p.n_ranks ? ld_relaxed_sys_u64(xchg_ll(p, p.rank, which, n, q) + off) : 0ull;
+        if (q < p.n_ranks && static_cast<unsigned>(w[q] >> 32) != tag) pend |= 1u << q;
+      }
+      if (pend) {
+        uint64_t t0 = 0;
+#pragma unroll 1
+        for (uint32_t it = 0; pend; ++it) {
+          if ((it & 15u) == 0) {
+            const uint64_t now = globaltimer_ns();
+            if (it == 0) t0 = now;
+            if ((ld_volatile_i32(p.status) & kStatusFatal) || now - t0 > kWaitLimitNs) {
+              set_status(p, kStatusFatal);
+              return false;
+            }
+          }
+          __nanosleep(32);
+#pragma unroll
+          for (int q = 0; q < kMaxRanks; ++q) {
+            if (pend & (1u << q)) {
+              w[q] = ld_relaxed_sys_u64(xchg_ll(p, p.rank, which, n, q) + off);
+              if (static_cast<unsigned>(w[q] >> 32) == tag) pend &= ~(1u << q);
+            }
+          }
+        }
+      }
       float a = 0.f;
 #pragma unroll
       for (int q = 0; q < kMaxRanks; ++q)
-        if (q < p.n_ranks) a += v[q];
+        if (q < p.n_ranks) a += __uint_as_float(static_cast<unsigned>(w[q]));
       float* x = p.resid + off;
       const float nv = (p.residual ? *x : 0.f) + rbf(a);
       *x = nv;
       if (trace) trace[static_cast<size_t>(layer - p.first_layer) * p.T * p.H + off] = nv;
     }
   }
+  return true;
 }
 
-// Rank-partial exchange: cross-GPU barrier, reduction into the residual, grid barrier.
+// Rank-partial exchange of `layer`: the rank-order reduction into the residual (it waits for the
+// other ranks' tagged words), then a grid barrier (the next stage reads whole residual rows).
 __device__ __forceinline__ bool rank_exchange(const Params& p, Ctx& c, int which, int layer) {
-  if (!grid_sync_ranks(p, c)) return false;
-  rank_reduce(p, which, layer);
-  return grid_barrier(p, c);
+  const bool ok = rank_reduce(p, which, layer, xseq_of(p, which, layer));
+  // the barrier runs either way: every CTA passes the same barriers, and a failed wait has set
+  // the fatal status that ends it early
+  const bool ok2 = grid_barrier(p, c);
+  return ok && ok2;
 }
 
 // End of a launch: the last CTA out zeroes the barrier counter for the next launch on this
 // workspace (launches on one workspace are stream-ordered).
-__device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c) {
+// multi: this launch belongs to a group of several ranks (only kernels built with kExt run one)
+__device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c, bool multi) {
   if ((ld_volatile_i32(p.status) & kStatusFatal) && lane_id() == 0) {
     // a failed wait ends the launch early: wait for the next phase of each of this warp's
     // mbarriers (and the norm-prefetch barrier for thread 0), each wait bounded by 1 ms.  A copy
@@ -430,8 +496,13 @@ __device__ __forceinline__ void launch_exit(const Params& p, const Ctx& c) {
   if (threadIdx.x == 0) {
     const unsigned old = atom_acqrel_add_u32(p.bar + 2, 1u);
     if (old == gridDim.x - 1) {
-      if (p.n_ranks > 1)
+      if (multi) {
         *p.gbase = c.gbase + static_cast<unsigned long long>(c.gbar_k) * gridDim.x * static_cast<unsigned>(p.n_ranks);
+        // every layer of the launch took one exchange of each kind its stages run (every other
+        // CTA has left the launch: nothing reads the counts any more)
+        if (p.stages & 1) p.xseq[0] += static_cast<unsigned>(p.num_layers);
+        if (p.stages & 2) p.xseq[1] += static_cast<unsigned>(p.num_layers);
+      }
       *reinterpret_cast<volatile unsigned*>(p.bar) = 0u;
       *reinterpret_cast<volatile unsigned*>(p.bar + 2) = 0u;
     }
@@ -619,13 +690,7 @@ __device__ __forceinline__ void gemv_store(const Params& p, const Route* rt, con
     }
   } else if (kind == GK_OPROJ && p.n_ranks > 1) {
     // tensor parallel: this rank's partial sum over its heads, stored in every rank's region
-    const size_t off = static_cast<size_t>(col) * p.H + strip * 16 + g;
-#pragma unroll 1
-    for (int q = 0; q < p.n_ranks; ++q) {
-      float* d = xchg_part(p, q, 0, p.rank) + off;
-      d[0] = v0;
-      d[8] = v1;
-    }
+    ll_put2(p, 0, G.layer, static_cast<size_t>(col) * p.H + strip * 16 + g, v0, v1, 8);
   } else if (kind == GK_OPROJ) {
     const int r0 = strip * 16 + g;
     float* x = p.resid + static_cast<size_t>(col) * p.H;
@@ -1332,9 +1397,7 @@ __device__ __noinline__ void down_flush(const Params& p, float* tile, int layer,
     for (int q = lane; q < n4; q += 32) {
       const int t = q >> 2, row = s * 16 + 4 * (q & 3);
       const size_t off = static_cast<size_t>(t) * p.H + row;
-      const float4 tv = tile4[q];
-#pragma unroll 1
-      for (int r = 0; r < p.n_ranks; ++r) *reinterpret_cast<float4*>(xchg_part(p, r, 1, p.rank) + off) = tv;
+      ll_put4(p, 1, layer, off, tile4[q]);
       tile4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncwarp();
@@ -2506,6 +2569,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const SmemLayout lay(p.H, NT);
   const int warp = threadIdx.x >> 5, lane = lane_id();
+  // several ranks: only the kExt kernels carry the exchange code (the host launches them then)
+  const bool multi = kExt && p.n_ranks > 1;
   Ctx c;
   c.ring_bytes = lay.ring_bytes;
   c.nslot = lay.ring_bytes / kSlotBytes;
@@ -2526,7 +2591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.stage_idx = 0;
   c.bar_k = 0;
   c.gbar_k = 0;
-  c.gbase = p.n_ranks > 1 ? *p.gbase : 0ull;
+  c.gbase = multi ? *p.gbase : 0ull;
   c.plan = reinterpret_cast<AttPlan*>(smem + lay.plan_off);
   c.red = reinterpret_cast<float*>(smem + lay.red_off);
   c.att_pb = -1;
@@ -2660,7 +2725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (staged && !(p.stages & 2)) bf16_rearm(p.qkv, p.T * p.R);
       // stage D's gamma and router row stream during the barrier
       const bool pre_d = (p.stages & 2) && staged;
-      if (p.n_ranks > 1) {
+      if (multi) {
         // tensor parallel: sum the ranks' O-projection partials into the residual
         __syncthreads();  // the rings and the strip-reduction area are free
         if (!(p.stages & 2)) prime_after(layer);
@@ -2704,15 +2769,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // F: down + affinity + combine + residual
       down_stage<NT>(p, c, gf);
       if (staged) logits_rearm(p);  // every CTA read this layer's logits before the last barrier
-      if (p.n_ranks > 1) {
+      if (multi) {
         // expert parallel: sum the ranks' expert partials into the residual (a rank without
         // active experts contributes zeros)
         if (c.rt->nA == 0) {
           const int n = p.T * p.H;
-#pragma unroll 1
-          for (int r = 0; r < p.n_ranks; ++r)
-            for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads)
-              xchg_part(p, r, 1, p.rank)[i] = 0.f;
+          const unsigned xs = xseq_of(p, 1, layer);
+          for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) ll_put(p, 1, xs, i, 0.f);
         }
         prime_after(layer);
         if (!rank_exchange(p, c, 1, layer)) return;
@@ -2738,7 +2801,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     else norm_rows_to_smem(p, c, p.final_norm, false);
     __syncthreads();
     gemv_stage<NT, GK_LMHEAD>(p, c, lm_geom(p, layer_end - 1));
-    if (p.n_ranks > 1) {
+    if (multi) {
       // every rank's strips are in this rank's logits area once all ranks pass the barrier
       if (!grid_sync_ranks(p, c)) return;
       const int n16 = p.T * p.V / 4;
@@ -2752,7 +2815,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     stamp(p, c);
   }
   }();
-  launch_exit(p, c);
+  launch_exit(p, c, multi);
 }
 
 }  // namespace nkm

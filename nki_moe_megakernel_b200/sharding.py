@@ -78,9 +78,9 @@ def shard_experts(gate_up: torch.Tensor, down: torch.Tensor, shard: RankShard):
 
 def xchg_bytes(hidden: int, max_batch: int, world: int, vocab: int) -> int:
     """Bytes of one rank's exchange region (``nkm_qwen3_xchg_bytes``): a 256-byte header (the
-    cross-GPU barrier counter), fp32 partials [2][world][max_batch][hidden] and, with several
-    ranks, the fp32 logits [max_batch][vocab] of the vocabulary-sharded LM head."""
-    n = (256 + 2 * world * max_batch * hidden * 4 + 255) // 256 * 256
+    cross-GPU barrier counter), the partials as tagged 8-byte words [2][2][world][max_batch][hidden]
+    and, with several ranks, the fp32 logits [max_batch][vocab] of the vocabulary-sharded LM head."""
+    n = (256 + 4 * world * max_batch * hidden * 8 + 255) // 256 * 256
     if world > 1:
         n += max_batch * vocab * 4
     return (n + 255) // 256 * 256
