@@ -449,11 +449,14 @@ def run_ours(args):
     if args.stage_times:
         print_stage_times(eng, pos_d, table_d, ids_d, args)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    # the clock sampler starts first: its start-up time differs between ranks, and the ranks must
+    # enter the timed region together (a rank that starts late makes the others wait in the
+    # step's first exchange)
     with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         _nvtx(torch, "timed")  # lets `ncu --nvtx --nvtx-include timed/` list exactly the timed launches
         evs[0].record(stream)
         for i in range(args.steps):
@@ -560,10 +563,15 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def _events_time(torch, stream, fn, steps, warmup):
+def _events_time(torch, stream, fn, steps, warmup, barrier=None):
+    """Mean and per-step ms of ``steps`` calls of fn after ``warmup``; ``barrier`` (several ranks)
+    lines the ranks up after the warm-up, right before the timed region."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if barrier is not None:
+        barrier()
+        torch.cuda.synchronize()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     _nvtx(torch, "timed")  # `ncu --nvtx --nvtx-include timed/` lists exactly the timed launches
     evs[0].record(stream)
@@ -578,15 +586,32 @@ def _events_time(torch, stream, fn, steps, warmup):
 
 def run_gpt_oss(args):
     """GPT-OSS-20B decode step (config 4): 24 layers (sliding/full alternating), B=16, context
-    4096, MXFP4 experts, vocab 201088, seeded random weights, one GPU."""
+    4096, MXFP4 experts, vocab 201088, seeded random weights.  Under torchrun (N GPUs) the ranks
+    split the KV-head groups and the experts (``sharding.shard_gptoss_layer``) and the LM head
+    over the vocabulary, every rank building the same weights from the seed and keeping its part;
+    time = max over ranks."""
     import torch
+    import torch.distributed as dist
 
     from nki_moe_megakernel_b200.gpt_oss_engine import GptOssGpuLayer, GptOssMegakernel, GptOssShape
 
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     B, ctx = 16, 4096
     shape = GptOssShape(num_hidden_layers=args.gptoss_layers)
+    shard = xchg = None
+    if world > 1:
+        import dataclasses
+        import datetime
+
+        from nki_moe_megakernel_b200.sharding import XchgRegion, gptoss_xchg_bytes, plan_shard, shard_gptoss_layer
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        shard = plan_shard(rank, world, shape.num_attention_heads, shape.num_key_value_heads, shape.num_local_experts)
+        xchg = XchgRegion(gptoss_xchg_bytes(shape.hidden_size, B, world, shape.vocab_size), rank, world, local)
     H, D, E, I, V = shape.hidden_size, shape.head_dim, shape.num_local_experts, shape.intermediate_size, shape.vocab_size
     nq, nkv, L = shape.num_attention_heads, shape.num_key_value_heads, shape.num_hidden_layers
     g = torch.Generator(device=dev).manual_seed(args.seed)
@@ -603,14 +628,18 @@ def run_gpt_oss(args):
                  gu_scales=torch.randint(119, 122, (E, 2 * I, H // 32), generator=g, device=dev, dtype=torch.uint8),
                  dn_codes=torch.randint(0, 16, (E, H, I), generator=g, device=dev, dtype=torch.uint8),
                  dn_scales=torch.randint(119, 122, (E, H, I // 32), generator=g, device=dev, dtype=torch.uint8))
+        if shard is not None:
+            t = shard_gptoss_layer(t, shard, D)
         layers.append(GptOssGpuLayer(t, shape.is_sliding(l)))
         del t
         torch.cuda.empty_cache()
     nb = ctx // 128 + 1
     NB = B * nb
-    eng = GptOssMegakernel(shape, layers, max_batch=B, num_blocks=NB, max_context=ctx + 128, final_norm=1 + n(H),
+    eshape = shape if shard is None else dataclasses.replace(shape, num_attention_heads=len(shard.q_heads),
+                                                             num_key_value_heads=len(shard.kv_heads))
+    eng = GptOssMegakernel(eshape, layers, max_batch=B, num_blocks=NB, max_context=ctx + 128, final_norm=1 + n(H),
                            lm_head=n(V, H), embed=torch.randn(V, H, generator=g, device=dev).to(torch.bfloat16),
-                           device=dev)
+                           device=dev, shard=shard, xchg=xchg)
     eng.k_pool.normal_(generator=g)
     eng.v_pool.normal_(generator=g)
     table = torch.randperm(NB, generator=torch.Generator().manual_seed(args.seed)).view(B, nb).to(torch.int32).to(dev)
@@ -618,9 +647,11 @@ def run_gpt_oss(args):
     ids = torch.randint(0, V, (B,), generator=torch.Generator().manual_seed(1), dtype=torch.int32).to(dev)
     out = {"hidden": torch.empty(B, H, dtype=torch.bfloat16, device=dev),
            "logits": torch.empty(B, V, dtype=torch.float32, device=dev)}
+    if world > 1:
+        dist.barrier()
     tr = eng.decode_step(pos, table, input_ids=ids, trace=True)
     eng.check_status()
-    distinct = [len(torch.unique(tr["topk_idx"][l])) for l in range(L)]
+    distinct = [len(torch.unique(tr["topk_idx"][l])) for l in range(L)]  # routing is replicated: whole model
     del tr
     if args.stage_times:
         names = ["qkv", "qkv_fin", "attention", "combine", "o_proj", "o_resid", "norm_router", "gate_up", "down",
@@ -638,26 +669,41 @@ def run_gpt_oss(args):
         print(json.dumps({"stage_us_median": med, "per_layer_us": round(sum(med[n] for n in names), 2)}),
               file=sys.stderr, flush=True)
     stream = torch.cuda.current_stream(dev)
-    with ClockSampler(0) as clk:
+    with ClockSampler(local) as clk:
         ms, per = _events_time(torch, stream, lambda: eng.decode_step(pos, table, input_ids=ids, out=out), args.steps,
-                               args.warmup)
+                               args.warmup, barrier=dist.barrier if world > 1 else None)
     eng.check_status()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     attn_w = ((nq + 2 * nkv) * D * H + H * nq * D) * 2 + ((nq + 2 * nkv) * D + H + nq + 2 * H + E) * 2 + E * H * 2
     expert = (2 * I * H) // 2 + 2 * I * (H // 32) + 2 * I * 2 + (H * I) // 2 + H * (I // 32) + H * 2
     kv = sum(B * (min(ctx, shape.sliding_window - 1) if shape.is_sliding(l) else ctx) * nkv * D * 2 * 2 for l in range(L))
     nbytes = L * attn_w + sum(distinct) * expert + kv + L * B * nkv * D * 2 * 2 + V * H * 2
     peak, peak_kind = measured_peaks()
     achieved = nbytes / (ms / 1e3) / 1e9
-    print(json.dumps({
-        "metric": "GPT-OSS-20B decode tokens/s at B=16 ctx 4096 (config 4)", "value": B / (ms / 1e3), "unit": UNIT,
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "p50_ms": statistics.median(per),
-        "higher_is_better": True, "dtype": "bf16 activations, MXFP4 experts", "data": "synthetic (seeded random)",
-        "config": {"workload": f"gpt-oss-20b decode step ({L} layers + LM head)", "global_batch": B, "ctx": ctx,
-                   "distinct_experts_per_layer_mean": sum(distinct) / L},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "algorithmic_bytes_per_step": nbytes,
-                     "kernel": "gptoss_decode_kernel (one launch per step)"},
-        "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "GPT-OSS-20B decode tokens/s at B=16 ctx 4096 (config 4)", "value": B / (ms / 1e3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "p50_ms": statistics.median(per), "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16 activations, MXFP4 experts", "data": "synthetic (seeded random)",
+            "config": {"workload": f"gpt-oss-20b decode step ({L} layers + LM head)", "global_batch": B, "ctx": ctx,
+                       "distinct_experts_per_layer_mean": sum(distinct) / L,
+                       "parallelism": "single GPU" if world == 1 else f"tp{world} (KV-head groups) + ep{world}, "
+                                                                      "LM head split over the vocabulary"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak / world, "peak_kind": peak_kind, "algorithmic_bytes_per_step": nbytes,
+                         "kernel": "gptoss_decode_kernel (one launch per step per GPU)",
+                         "note": "frac against the peak of all the step's GPUs"},
+            "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        eng.close()
+        xchg.close()
+        dist.destroy_process_group()
 
 
 def _mx_experts(torch, g, dev, E, rows, cols):
@@ -844,7 +890,7 @@ def run_wide_ep(args, rank, world, local, dev, shape):
     dist.barrier()
     stream = torch.cuda.current_stream(dev)
     ms, per = _events_time(torch, stream, lambda: ep.decode_step(pos_d, table_d, input_ids=ids_d), args.steps,
-                           args.warmup)
+                           args.warmup, barrier=dist.barrier)
     ep.check_status()
     t = torch.tensor([ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -384,6 +384,22 @@ typedef struct nkm_gptoss_desc {
                               +-240)), read = stored / scale (attention_block_tkg.py:213-218, 1694) */
   float k_scale;           /* used when kv_fp8 */
   float v_scale;
+  /* Tensor + expert parallelism across the GPUs of one node (one process per GPU), as in
+   * nkm_qwen3_desc.  n_ranks <= 1: the whole model on this GPU.  n_ranks > 1: n_q_heads and
+   * n_kv_heads are this rank's heads (its KV-head group with their query heads; the layer's
+   * wqkv/bqkv/wo/sinks hold those), and the expert tensors hold its experts [expert_begin,
+   * expert_begin + n_local_experts) of n_experts (router, norms, embedding, LM head replicated).
+   * After the O-projection and after the experts every rank stores its partial sums as tagged
+   * 8-byte words into the exchange region of every rank (xchg[q]: each rank's region mapped in
+   * this process, nkm_gptoss_xchg_bytes each, zeroed before the first step) and adds all ranks'
+   * partials in rank order, so every rank keeps the same residual.  The LM head is split over
+   * the vocabulary (rank r: 16-row strips [S r / n, S (r + 1) / n), S = vocab / 16) and every rank
+   * returns the full logits.  Replaces the TP/EP sharding of gpt_oss_with_megakernel.py. */
+  int32_t n_ranks;
+  int32_t rank;
+  int32_t expert_begin;
+  int32_t n_local_experts;
+  void* xchg[8];
 } nkm_gptoss_desc;
 
 typedef struct nkm_gptoss_step {
@@ -411,6 +427,9 @@ typedef struct nkm_gptoss nkm_gptoss;
 
 /* Workspace bytes of a GPT-OSS handle (caller allocates, 256-byte aligned). */
 size_t nkm_gptoss_workspace_bytes(const nkm_gptoss_desc* desc);
+/* Bytes of the exchange region each rank allocates when n_ranks > 1 (256-byte aligned, zeroed,
+ * shared with the other ranks by CUDA IPC). */
+size_t nkm_gptoss_xchg_bytes(const nkm_gptoss_desc* desc);
 /* Replaces compile()/load() of the reference's GPT-OSS model (gpt_oss_with_megakernel.py). */
 int nkm_gptoss_create(const nkm_gptoss_desc* desc, void* workspace, size_t workspace_bytes, nkm_gptoss** out);
 void nkm_gptoss_destroy(nkm_gptoss* h);
@@ -418,7 +437,9 @@ void nkm_gptoss_destroy(nkm_gptoss* h);
  * get_multilayer_kernel_jit(L, mxfp4)(X, Wqkv_*, bqkv_*, Wo_*, bo_*, Sink_*, ..., K_*, V_*, cos, sin,
  * position_ids, position_ids_window) (transformer_gpt_oss.py:540-636). */
 int nkm_gptoss_decode_step(nkm_gptoss* h, const nkm_gptoss_step* step, nkm_stream_t stream);
-/* Synchronise and return (and clear) the device status word. */
+/* Synchronise and return (and clear) the device status word.  With n_ranks > 1 a non-zero status
+ * also clears this rank's exchange region and restarts its exchange sequence: after a failed step
+ * every rank calls this once all ranks' launches have ended, then the group synchronises. */
 int nkm_gptoss_status(nkm_gptoss* h, nkm_stream_t stream);
 
 /* MXFP4 weight packer (load time).  codes: uint8 [count][rows][cols] e2m1 codes 0..15 (bit 3 sign;

@@ -70,7 +70,8 @@ class nkm_gptoss_desc(ctypes.Structure):
                 ("rope_cos", POINTER(c_float)), ("rope_sin", POINTER(c_float)), ("rope_max_pos", c_int32),
                 ("k_pool", c_void_p), ("v_pool", c_void_p), ("num_blocks", c_int32), ("block_size", c_int32),
                 ("max_batch", c_int32), ("max_context", c_int32), ("kv_fp8", c_int32), ("k_scale", c_float),
-                ("v_scale", c_float)]
+                ("v_scale", c_float), ("n_ranks", c_int32), ("rank", c_int32), ("expert_begin", c_int32),
+                ("n_local_experts", c_int32), ("xchg", c_void_p * 8)]
 
 
 class nkm_gptoss_step(ctypes.Structure):
@@ -111,6 +112,7 @@ SIGNATURES = {
     "nkm_sample_logits": (c_int, [c_void_p, c_int32, c_int32, POINTER(nkm_sample_params), c_void_p, c_void_p,
                                   c_void_p, c_size_t, c_void_p]),
     "nkm_gptoss_workspace_bytes": (c_size_t, [POINTER(nkm_gptoss_desc)]),
+    "nkm_gptoss_xchg_bytes": (c_size_t, [POINTER(nkm_gptoss_desc)]),
     "nkm_gptoss_create": (c_int, [POINTER(nkm_gptoss_desc), c_void_p, c_size_t, POINTER(c_void_p)]),
     "nkm_gptoss_destroy": (None, [c_void_p]),
     "nkm_gptoss_decode_step": (c_int, [c_void_p, POINTER(nkm_gptoss_step), c_void_p]),

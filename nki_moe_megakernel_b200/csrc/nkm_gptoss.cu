@@ -33,9 +33,18 @@ constexpr size_t kAlign = 256;
 size_t al(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
 struct GLayout {
-  size_t bar, status, layers, resid, part, qbuf, att_part, attn_out, rlogits, hbuf, ypair, total;
+  size_t bar, status, xseq, layers, resid, part, qbuf, att_part, attn_out, rlogits, hbuf, ypair, total;
   int max_units;
 };
+
+int n_ranks_of(const nkm_gptoss_desc& d) { return d.n_ranks > 1 ? d.n_ranks : 1; }
+
+// Exchange region: header, the partials as tagged words [2 kinds][2 slots][n_ranks][B][H], then
+// (several ranks) the logits as tagged words [2 slots][B][V].
+size_t xlog_offset(const nkm_gptoss_desc& d) {
+  return al(static_cast<size_t>(nkg::kXchgHeader) +
+            4 * static_cast<size_t>(n_ranks_of(d)) * d.max_batch * static_cast<size_t>(d.hidden) * 8);
+}
 
 int kc_for(int strips, int kt, int warps) {
   int kc = (warps + strips - 1) / strips;
@@ -51,6 +60,7 @@ GLayout glayout(const nkm_gptoss_desc& d) {
   size_t o = 0;
   w.bar = 0;
   w.status = 16;
+  w.xseq = 32;  // u32[3]: exchanges of each kind before the next launch (several ranks)
   o = 256;
   w.layers = o;
   o = al(o + sizeof(nkg::Layer) * d.n_layers);
@@ -95,6 +105,16 @@ int gcheck(const nkm_gptoss_desc* d) {
   if (d->max_context <= 0) return gfail(NKM_ERR_ARG, "max_context must be positive");
   if (d->sliding_window <= 0) return gfail(NKM_ERR_ARG, "sliding_window must be positive");
   if (d->kv_fp8 && !(d->k_scale > 0.f && d->v_scale > 0.f)) return gfail(NKM_ERR_ARG, "FP8 K/V needs positive scales");
+  const int nr = n_ranks_of(*d);
+  if (nr > 8) return gfail(NKM_ERR_ARG, "n_ranks must be in 1..8");
+  if (d->rank < 0 || d->rank >= nr) return gfail(NKM_ERR_ARG, "rank outside 0..n_ranks-1");
+  const int nle = d->n_local_experts > 0 ? d->n_local_experts : d->n_experts;
+  if (d->expert_begin < 0 || d->expert_begin + nle > d->n_experts) return gfail(NKM_ERR_ARG, "local experts outside 0..n_experts");
+  if (nr == 1 && (d->expert_begin != 0 || nle != d->n_experts)) return gfail(NKM_ERR_ARG, "a single rank holds every expert");
+  if (nr > 1)
+    for (int q = 0; q < nr; ++q)
+      if (!d->xchg[q] || (reinterpret_cast<uintptr_t>(d->xchg[q]) & 255))
+        return gfail(NKM_ERR_ARG, "xchg[q] must be a 256-byte aligned device pointer for every rank");
   return NKM_OK;
 }
 
@@ -139,6 +159,12 @@ extern "C" {
 size_t nkm_gptoss_workspace_bytes(const nkm_gptoss_desc* desc) {
   if (gcheck(desc) != NKM_OK) return 0;
   return glayout(*desc).total;
+}
+
+size_t nkm_gptoss_xchg_bytes(const nkm_gptoss_desc* desc) {
+  if (gcheck(desc) != NKM_OK) return 0;
+  const size_t logits = n_ranks_of(*desc) > 1 ? 2 * static_cast<size_t>(desc->max_batch) * desc->vocab * 8 : 0;
+  return al(xlog_offset(*desc) + logits);
 }
 
 int nkm_gptoss_create(const nkm_gptoss_desc* desc, void* workspace, size_t workspace_bytes, nkm_gptoss** out) {
@@ -295,6 +321,18 @@ int nkm_gptoss_decode_step(nkm_gptoss* h, const nkm_gptoss_step* s, nkm_stream_t
   p.rlogits = reinterpret_cast<float*>(ws + h->lay.rlogits);
   p.hbuf = reinterpret_cast<uint16_t*>(ws + h->lay.hbuf);
   p.ypair = reinterpret_cast<float*>(ws + h->lay.ypair);
+  p.n_ranks = n_ranks_of(d);
+  p.rank = p.n_ranks > 1 ? d.rank : 0;
+  p.expert_begin = d.expert_begin;
+  p.n_local = d.n_local_experts > 0 ? d.n_local_experts : d.n_experts;
+  for (int q = 0; q < 8; ++q) p.xchg[q] = q < p.n_ranks && p.n_ranks > 1 ? static_cast<uint8_t*>(d.xchg[q]) : nullptr;
+  p.xseq = reinterpret_cast<unsigned*>(ws + h->lay.xseq);
+  p.xlog_off = static_cast<int64_t>(xlog_offset(d));
+  {  // the vocabulary's 16-row strips split evenly over the ranks
+    const int vs = d.vocab / 16;
+    p.lm_s0 = static_cast<int>(static_cast<int64_t>(vs) * p.rank / p.n_ranks);
+    p.lm_ns = static_cast<int>(static_cast<int64_t>(vs) * (p.rank + 1) / p.n_ranks) - p.lm_s0;
+  }
   void* args[1] = {&p};
   NKG_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(&nkg::gptoss_decode_kernel), dim3(h->num_sms),
                                        dim3(nkg::kThreads), args, h->smem, reinterpret_cast<cudaStream_t>(stream)));
@@ -308,7 +346,11 @@ int nkm_gptoss_status(nkm_gptoss* h, nkm_stream_t stream) {
   NKG_CUDA(cudaMemcpy(&st, h->ws + h->lay.status, sizeof(int), cudaMemcpyDeviceToHost));
   if (st) {
     gfail(st, (st & NKM_ERR_TIMEOUT) ? "device status: wait timeout" : "device status: index out of range");
-    NKG_CUDA(cudaMemset(h->ws, 0, 256));
+    NKG_CUDA(cudaMemset(h->ws, 0, 256));  // barrier, status and the exchange sequence
+    if (n_ranks_of(h->desc) > 1) {
+      NKG_CUDA(cudaMemset(h->desc.xchg[h->desc.rank], 0, nkm_gptoss_xchg_bytes(&h->desc)));
+      NKG_CUDA(cudaDeviceSynchronize());
+    }
   }
   return st;
 }

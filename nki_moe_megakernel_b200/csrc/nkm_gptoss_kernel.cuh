@@ -113,6 +113,13 @@ struct Params {
   float* rlogits;
   uint16_t* hbuf;
   float* ypair;
+  // tensor + expert parallelism (n_ranks > 1): nq / nkv above are this rank's heads; its experts
+  // are [expert_begin, expert_begin + n_local) of E (the layer tensors hold only those); it
+  // computes the LM head's vocabulary strips [lm_s0, lm_s0 + lm_ns)
+  int n_ranks, rank, expert_begin, n_local, lm_s0, lm_ns;
+  uint8_t* xchg[8];     // exchange region of every rank (CUDA IPC mappings)
+  unsigned* xseq;       // [3] exchanges of each kind before this launch (workspace)
+  int64_t xlog_off;     // byte offset of the logits exchange within a region
 };
 
 struct Route {
@@ -128,17 +135,37 @@ struct Route {
   int pair_of[kMaxPairs];
 };
 
-// Shared memory: activation rows (bf16 or f16, stride Kx + 8 halves) | rstd | route | flag.
+// Expert weight rings: each warp streams its MXFP4 strips through kRingSlots shared-memory slots
+// with 1-D bulk copies; a slot holds kCK k-tiles (256 bytes each: 16 rows x 32 inputs) and their
+// grouped scales (128 bytes per 8 k-tiles).
+constexpr int kCK = 16;
+constexpr int kRingSlots = 2;
+constexpr int kSlotW = kCK * 256;
+constexpr int kSlotBytes = kSlotW + (kCK / 8) * 128;
+
+// Shared memory: activation rows (bf16 or f16, stride Kx + 8 halves) | rstd | route | flag |
+// expert rings | their mbarriers | each warp's ring phase bits.
 struct Smem {
-  uint32_t xs_off, rstd_off, route_off, flag_off, total;
+  uint32_t xs_off, rstd_off, route_off, flag_off, ring_off, bar_off, phase_off, total;
   __host__ __device__ explicit Smem(int B, int kmax) {
     xs_off = 0;
     uint32_t xs = static_cast<uint32_t>(B) * static_cast<uint32_t>(kmax + 8) * 2u;
     rstd_off = (xs + 15u) & ~15u;
     route_off = rstd_off + kMaxB * 4;
     flag_off = route_off + static_cast<uint32_t>((sizeof(Route) + 15) & ~size_t(15));
-    total = flag_off + 16;
+    ring_off = (flag_off + 16u + 127u) & ~127u;
+    bar_off = ring_off + static_cast<uint32_t>(kWarps * kRingSlots * kSlotBytes);
+    phase_off = bar_off + static_cast<uint32_t>(kWarps * kRingSlots * 8);
+    total = phase_off + kWarps * 4;
   }
+};
+
+// A warp's ring: slots (kRingSlots x kSlotBytes), their mbarriers and the phase bits (kept in
+// shared memory between stages).
+struct Ring {
+  uint8_t* buf;
+  uint64_t* bar;
+  uint32_t* phase;
 };
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
@@ -175,6 +202,71 @@ __device__ __noinline__ bool grid_sync(const Params& p, unsigned& bar_k, int* fl
   ++bar_k;
   __syncthreads();
   return *flag != 0;
+}
+
+// ------------------------------------------------------------------ ranks (TP + EP)
+// The ranks exchange tagged 8-byte words: the fp32 value in the low half, the exchange's
+// sequence number + 1 in the high half, stored and loaded as one single-copy-atomic access, so a
+// reader that sees the tag it expects also sees the value (no fence, flag or barrier).  Kinds:
+// 0 the O-projection partials and 1 the expert partials ([kind][n % 2][src rank][B][H] after the
+// header), 2 the logits ([n % 2][B][V] from xlog_off; each rank stores its vocabulary strips).
+// Two slots per kind: a rank produces exchange n + 2 of a kind only after reading every rank's
+// exchange n + 1, which each rank produces only after reading exchange n.
+constexpr int kXchgHeader = 256;
+__device__ __forceinline__ unsigned long long* xw_part(const Params& p, int q, int kind, unsigned n, int src) {
+  return reinterpret_cast<unsigned long long*>(p.xchg[q] + kXchgHeader) +
+         static_cast<size_t>((kind * 2 + static_cast<int>(n & 1u)) * p.n_ranks + src) * p.B * p.H;
+}
+__device__ __forceinline__ unsigned long long* xw_logits(const Params& p, int q, unsigned n) {
+  return reinterpret_cast<unsigned long long*>(p.xchg[q] + p.xlog_off) + static_cast<size_t>(n & 1u) * p.B * p.V;
+}
+// sequence number of `layer`'s exchange of kind 0 or 1, or (kind 2) of this launch's logits
+__device__ __forceinline__ unsigned xseq_of(const Params& p, int kind, int layer) {
+  return __ldg(p.xseq + kind) + (kind == 2 ? 0u : static_cast<unsigned>(layer - p.first_layer));
+}
+__device__ __forceinline__ unsigned long long xword(unsigned n, float v) {
+  return (static_cast<unsigned long long>(n + 1u) << 32) | __float_as_uint(v);
+}
+// element i of this rank's partial of exchange n (kind 0 / 1) into every rank's region
+__device__ __forceinline__ void put_part(const Params& p, int kind, unsigned n, size_t i, float v) {
+  const unsigned long long w = xword(n, v);
+#pragma unroll 1
+  for (int q = 0; q < p.n_ranks; ++q) nkm::st_relaxed_sys_u64(xw_part(p, q, kind, n, p.rank) + i, w);
+}
+// The value of a tagged word once it carries exchange n's tag (bounded wait; false once the
+// launch has failed).
+__device__ __forceinline__ bool take_word(const Params& p, const unsigned long long* a, unsigned n, float& v) {
+  unsigned long long w = nkm::ld_relaxed_sys_u64(a);
+  if (static_cast<unsigned>(w >> 32) != n + 1u) {
+    uint64_t t0 = 0;
+#pragma unroll 1
+    for (uint32_t it = 0;; ++it) {
+      if ((it & 15u) == 0) {
+        const uint64_t now = globaltimer_ns();
+        if (it == 0) t0 = now;
+        if ((nkm::ld_volatile_i32(p.status) & kStatusFatal) || now - t0 > kWaitLimitNs) {
+          set_status(p, kStatusFatal);
+          return false;
+        }
+      }
+      __nanosleep(32);
+      w = nkm::ld_relaxed_sys_u64(a);
+      if (static_cast<unsigned>(w >> 32) == n + 1u) break;
+    }
+  }
+  v = __uint_as_float(static_cast<unsigned>(w));
+  return true;
+}
+// Sum over the ranks, in rank order, of element i of exchange n (kind 0 / 1).
+__device__ __forceinline__ bool rank_sum(const Params& p, int kind, unsigned n, size_t i, float& s) {
+  s = 0.f;
+#pragma unroll 1
+  for (int q = 0; q < p.n_ranks; ++q) {
+    float v;
+    if (!take_word(p, xw_part(p, p.rank, kind, n, q) + i, n, v)) return false;
+    s += v;
+  }
+  return true;
 }
 
 // ------------------------------------------------------------------ small helpers
@@ -287,88 +379,94 @@ __device__ __noinline__ void norm_rows(const Params& p, const uint16_t* gamma, u
 }
 
 // ------------------------------------------------------------------ GEMV engines
-// bf16 fragment-tiled strip (1 KB units of 16 rows x 32 k; lane l: row l/4 and l/4 + 8, k 8(l%4)..+7)
-// times shared-memory columns: acc[nt] += W[strip, kt0 .. kt0+nk) x^T for columns nt*8 + g.
-// cols: shared-memory row of each column (nullptr: column c is row c); ncols columns valid.
-__device__ __forceinline__ void ft_bf16(const uint8_t* strip, int kt0, int nk, const uint16_t* xs, int stride,
-                                        const int* cols, int ncols, float (&acc)[kNT][4]) {
-  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const uint16_t* brow[kNT];
-#pragma unroll
-  for (int nt = 0; nt < kNT; ++nt) {
-    const int c = nt * 8 + g;
-    brow[nt] = c < ncols ? xs + static_cast<size_t>(cols ? cols[c] : c) * stride + 8 * t4 : nullptr;
-  }
-  constexpr int U = 8;
+// Weights stream through each warp's shared-memory ring (1-D bulk copies, kRingSlots chunks in
+// flight across unit boundaries); the activations are rows in shared memory.
+// * bf16 fragment-tiled strips: 1 KB units of 16 rows x 32 k (lane l: row l/4 and l/4 + 8,
+//   k 8(l%4)..+7).
+// * MXFP4 fragment-tiled strips: 256-byte units of 16 rows x 32 k (lane l: 4 bytes of row l/4 then
+//   4 bytes of row l/4 + 8, k 8(l%4)..+7, low nibble first), with the strip's e8m0 scales in groups
+//   of 8 k-tiles ([group][16 rows][8], so a lane reads its two rows' 8 scales with two 8-byte
+//   loads).  Each unit's product is accumulated from zero and scaled by its rows' scales (exact
+//   powers of two).
+// Only the 8-column tiles that hold tokens are multiplied (an expert of a 16-row batch usually
+// has at most 8 tokens).
+__device__ __forceinline__ uint32_t byte_of(const uint2 v, int u) {
+  return ((u < 4 ? v.x : v.y) >> (8 * (u & 3))) & 0xffu;
+}
+// Bytes of one 16-row strip's grouped scales for KT k-tiles.
+__device__ __forceinline__ size_t fp4_strip_scale_bytes(int KT) { return static_cast<size_t>((KT + 7) / 8) * 128; }
+
+// ---- expert weight rings (bulk copies into shared memory)
+__device__ __forceinline__ uint2 lds64(const void* ptr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_addr(ptr)));
+  return v;
+}
+// Lane 0: nk k-tiles of a strip's weights (w) and their scale groups (sc) into ring slot `slot`.
+__device__ __forceinline__ void ring_issue(const Ring& r, int slot, const uint8_t* w, const uint8_t* sc, int nk,
+                                           uint64_t pol) {
+  const uint32_t wb = static_cast<uint32_t>(nk) * 256u, sb = static_cast<uint32_t>((nk + 7) / 8) * 128u;
+  uint8_t* dst = r.buf + slot * kSlotBytes;
+  nkm::fence_proxy_async_smem();
+  nkm::mbar_arrive_expect_tx(&r.bar[slot], wb + sb);
+  nkm::bulk_g2s(dst, w, wb, &r.bar[slot], pol);
+  nkm::bulk_g2s(dst + kSlotW, sc, sb, &r.bar[slot], pol);
+}
+// Bounded wait for phase `par` of slot `slot`; false once the launch has failed (a wait that
+// lasts beyond any normal one also polls the status word, so one failure ends every wait).
+__device__ __noinline__ bool ring_wait(const Params& p, const Ring& r, int slot, uint32_t par) {
+  uint64_t t0 = 0;
 #pragma unroll 1
-  for (int k0 = 0; k0 < nk; k0 += U) {
-    uint4 a0[U], a1[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k0 + u < nk) {
-        const uint8_t* unit = strip + static_cast<size_t>(kt0 + k0 + u) * 1024;
-        a0[u] = nkm::ldnc128(unit + 16 * lane);
-        a1[u] = nkm::ldnc128(unit + 512 + 16 * lane);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k0 + u < nk) {
-        const int kk = (kt0 + k0 + u) * 32;
-#pragma unroll
-        for (int nt = 0; nt < kNT; ++nt) {
-          const uint4 b = brow[nt] ? *reinterpret_cast<const uint4*>(brow[nt] + kk) : make_uint4(0u, 0u, 0u, 0u);
-          mma_bf16(acc[nt], a0[u].x, a1[u].x, a0[u].y, a1[u].y, b.x, b.y);
-          mma_bf16(acc[nt], a0[u].z, a1[u].z, a0[u].w, a1[u].w, b.z, b.w);
+  for (uint32_t it = 0;; ++it) {
+    if (nkm::mbar_try_wait(&r.bar[slot], par)) return true;
+    if ((it & 63u) == 63u) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > 20000ull) {
+        if (nkm::ld_volatile_i32(p.status) & kStatusFatal) return false;
+        if (now - t0 > kWaitLimitNs) {
+          if (lane_id() == 0) set_status(p, kStatusFatal);
+          return false;
         }
       }
     }
   }
 }
-
-// MXFP4 fragment-tiled strip: 256-byte units of 16 rows x 32 k (lane l: 4 bytes of row l/4 then 4
-// bytes of row l/4 + 8, k 8(l%4)..+7, low nibble first) and the strip's e8m0 scales in groups of 8
-// k-tiles ([group][16 rows][8], so a lane reads its two rows' 8 scales with two 8-byte loads).
-// Each unit's product is accumulated from zero and scaled by its rows' scales (exact powers of
-// two).  8 k-tiles are in flight per lane; the callers warm L2 with the warp's next unit (one
-// bulk prefetch) while this one streams.
-__device__ __forceinline__ uint32_t byte_of(const uint2 v, int u) {
-  return ((u < 4 ? v.x : v.y) >> (8 * (u & 3))) & 0xffu;
-}
-__device__ __forceinline__ void ft_fp4(const uint8_t* strip, const uint8_t* scales, int nk, const uint16_t* xs,
-                                       int stride, const int* cols, int ncols, float (&acc)[kNT][4]) {
-  const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
-  const uint16_t* brow[kNT];
-#pragma unroll
-  for (int nt = 0; nt < kNT; ++nt) {
-    const int c = nt * 8 + g;
-    brow[nt] = c < ncols ? xs + static_cast<size_t>(cols ? cols[c] : c) * stride + 8 * t4 : nullptr;
-  }
-  constexpr int U = 8;
+// After a failed wait: the copies this warp still has in flight land in its slots; wait for
+// each (1 ms bound) before the warp leaves the stage.
+__device__ __noinline__ void ring_drain(const Ring& r, uint32_t inflight, uint32_t phase) {
 #pragma unroll 1
-  for (int k0 = 0; k0 < nk; k0 += U) {
-    uint2 w[U], sg[U / 8], sh[U / 8];
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (k0 + u < nk) w[u] = ldnc64(strip + static_cast<size_t>(k0 + u) * 256 + 8 * lane);
-#pragma unroll
-    for (int q = 0; q < U / 8; ++q) {
-      if (k0 + 8 * q < nk) {
-        const uint8_t* grp = scales + static_cast<size_t>(k0 / 8 + q) * 128;
-        sg[q] = ldnc64(grp + 8 * g);
-        sh[q] = ldnc64(grp + 8 * (g + 8));
-      }
+  for (int sl = 0; sl < kRingSlots; ++sl) {
+    if (!(inflight & (1u << sl))) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while (!nkm::mbar_try_wait(&r.bar[sl], (phase >> sl) & 1u) && globaltimer_ns() - t0 < 1000000ull) {
     }
+  }
+}
+// nk k-tiles of one ring slot (k-tile kt of the slot is input block kbase + kt) against the
+// activation rows brow[nt] (f16 in shared memory), accumulated into acc.
+template <int NTA>  // n-tiles with tokens (1: at most 8 of them)
+__device__ __forceinline__ void fp4_slot(const uint8_t* slot, int nk, int kbase, const uint16_t* const (&brow)[kNT],
+                                         float (&acc)[kNT][4]) {
+  const int lane = lane_id(), g = lane >> 2;
+#pragma unroll 1
+  for (int k8 = 0; k8 < nk; k8 += 8) {
+    const uint8_t* grp = slot + kSlotW + (k8 >> 3) * 128;
+    const uint2 sg = lds64(grp + 8 * g), sh = lds64(grp + 8 * (g + 8));
+    uint2 w[8];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (k0 + u < nk) {
+    for (int u = 0; u < 8; ++u) w[u] = k8 + u < nk ? lds64(slot + (k8 + u) * 256 + 8 * lane) : make_uint2(0u, 0u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (k8 + u < nk) {
         uint32_t r0, r1, r2, r3, q0, q1, q2, q3;
         e2m1x8(w[u].x, r0, r1, r2, r3);
         e2m1x8(w[u].y, q0, q1, q2, q3);
-        const float s0 = e8m0(byte_of(sg[u / 8], u & 7)), s1 = e8m0(byte_of(sh[u / 8], u & 7));
-        const int kk = (k0 + u) * 32;
+        const float s0 = e8m0(byte_of(sg, u)), s1 = e8m0(byte_of(sh, u));
+        const int kk = (kbase + k8 + u) * 32;
 #pragma unroll
-        for (int nt = 0; nt < kNT; ++nt) {
+        for (int nt = 0; nt < NTA; ++nt) {
           const uint4 b = brow[nt] ? *reinterpret_cast<const uint4*>(brow[nt] + kk) : make_uint4(0u, 0u, 0u, 0u);
           float d[4] = {0.f, 0.f, 0.f, 0.f};
           mma_f16(d, r0, q0, r1, q1, b.x, b.y);
@@ -382,40 +480,130 @@ __device__ __forceinline__ void ft_fp4(const uint8_t* strip, const uint8_t* scal
     }
   }
 }
-// Bytes of one 16-row strip's grouped scales for KT k-tiles.
-__device__ __forceinline__ size_t fp4_strip_scale_bytes(int KT) { return static_cast<size_t>((KT + 7) / 8) * 128; }
+
+// ---- bf16 strips through the same rings (the dense GEMVs and the LM head): 4 k-tiles of 1 KB
+// (16 rows x 32 inputs, fragment-tiled) per slot
+constexpr int kCKb = kSlotW / 1024;
+__device__ __forceinline__ uint4 lds128(const void* ptr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_addr(ptr)));
+  return v;
+}
+template <int NTA>
+__device__ __forceinline__ void bf16_slot(const uint8_t* slot, int nk, int kbase, const uint16_t* const (&brow)[kNT],
+                                          float (&acc)[kNT][4]) {
+  const int lane = lane_id();
+#pragma unroll
+  for (int k = 0; k < kCKb; ++k) {
+    if (k < nk) {
+      const uint4 a0 = lds128(slot + k * 1024 + 16 * lane), a1 = lds128(slot + k * 1024 + 512 + 16 * lane);
+      const int kk = (kbase + k) * 32;
+#pragma unroll
+      for (int nt = 0; nt < NTA; ++nt) {
+        const uint4 b = brow[nt] ? *reinterpret_cast<const uint4*>(brow[nt] + kk) : make_uint4(0u, 0u, 0u, 0u);
+        mma_bf16(acc[nt], a0.x, a1.x, a0.y, a1.y, b.x, b.y);
+        mma_bf16(acc[nt], a0.z, a1.z, a0.w, a1.w, b.z, b.w);
+      }
+    }
+  }
+}
+// This warp's units u = first, first + step, ... < nunits of a bf16 GEMV: unit(u, base, kt0, nk)
+// gives the strip's weights and the unit's k-tile range; the weights stream through the ring
+// (kRingSlots chunks of kCKb k-tiles in flight, across unit boundaries), and epi(u, acc) takes
+// each unit's accumulators.  The activation rows are brow[] (ncols of them).  False once the
+// launch has failed.
+template <class UnitFn, class EpiFn>
+__device__ __forceinline__ bool stream_bf16(const Params& p, const Ring& R, int first, int step, int nunits,
+                                            const uint16_t* const (&brow)[kNT], int ncols, UnitFn unit, EpiFn epi) {
+  const int lane = lane_id();
+  const uint64_t pol = nkm::policy_evict_first();
+  uint32_t phase = *R.phase, inflight = 0;
+  int pu = first, pk = 0;  // producer: unit and its next k-tile offset
+  auto issue = [&](int slot) {
+    if (pu >= nunits) return;
+    const uint8_t* base;
+    int kt0, nk;
+    unit(pu, base, kt0, nk);
+    const int n = min(kCKb, nk - pk);
+    if (lane == 0) {
+      nkm::fence_proxy_async_smem();
+      nkm::mbar_arrive_expect_tx(&R.bar[slot], static_cast<uint32_t>(n) * 1024u);
+      nkm::bulk_g2s(R.buf + slot * kSlotBytes, base + static_cast<size_t>(kt0 + pk) * 1024, static_cast<uint32_t>(n) * 1024u,
+                    &R.bar[slot], pol);
+    }
+    inflight |= 1u << slot;
+    pk += n;
+    if (pk >= nk) {
+      pk = 0;
+      pu += step;
+    }
+  };
+#pragma unroll
+  for (int sl = 0; sl < kRingSlots; ++sl) issue(sl);
+  int cs = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int u = first; u < nunits && ok; u += step) {
+    const uint8_t* base;
+    int kt0, nk;
+    unit(u, base, kt0, nk);
+    float acc[kNT][4] = {};
+#pragma unroll 1
+    for (int k = 0; k < nk; k += kCKb) {
+      if (!ring_wait(p, R, cs, (phase >> cs) & 1u)) {
+        ok = false;
+        break;
+      }
+      phase ^= 1u << cs;
+      inflight &= ~(1u << cs);
+      if (ncols > 8) bf16_slot<2>(R.buf + cs * kSlotBytes, min(kCKb, nk - k), kt0 + k, brow, acc);
+      else bf16_slot<1>(R.buf + cs * kSlotBytes, min(kCKb, nk - k), kt0 + k, brow, acc);
+      __syncwarp();
+      issue(cs);
+      cs = cs + 1 == kRingSlots ? 0 : cs + 1;
+    }
+    if (!ok) break;
+    epi(u, acc);
+  }
+  if (!ok) ring_drain(R, inflight, phase);
+  if (lane == 0) *R.phase = phase;
+  __syncwarp();
+  return ok;
+}
 
 // ------------------------------------------------------------------ stages
 // Split-K dense GEMV: units (strip, k chunk) over all warps; partial (chunk kc) of row r, column
 // c at part[(kc * rows + r) * B + c].
 __device__ __noinline__ void dense_splitk(const Params& p, const uint8_t* w, int rows, int KT, int KC,
-                                          const uint16_t* xs, int stride) {
+                                          const uint16_t* xs, int stride, const Ring& R) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int S = rows / 16, nunits = S * KC;
   const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
-#pragma unroll 1
-  for (int u = gw; u < nunits; u += nw) {
-    const int s = u / KC, kc = u - s * KC;
-    const int kt0 = KT * kc / KC, kt1 = KT * (kc + 1) / KC;
-    if (lane == 0 && u + nw < nunits) {  // the next unit's weights into L2
-      const int s2 = (u + nw) / KC, kc2 = (u + nw) - s2 * KC;
-      const int a0 = KT * kc2 / KC, a1 = KT * (kc2 + 1) / KC;
-      nkm::prefetch_l2_bulk(w + (static_cast<size_t>(s2) * KT + a0) * 1024, static_cast<uint32_t>(a1 - a0) * 1024u);
-    }
-    float acc[kNT][4] = {};
-    ft_bf16(w + static_cast<size_t>(s) * KT * 1024, kt0, kt1 - kt0, xs, stride, nullptr, p.B, acc);
+  const uint16_t* brow[kNT];
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt) {
+  for (int nt = 0; nt < kNT; ++nt) brow[nt] = nt * 8 + g < p.B ? xs + static_cast<size_t>(nt * 8 + g) * stride + 8 * t4 : nullptr;
+  stream_bf16(
+      p, R, gw, nw, nunits, brow, p.B,
+      [&](int u, const uint8_t*& base, int& kt0, int& nk) {
+        const int s = u / KC, kc = u - s * KC;
+        base = w + static_cast<size_t>(s) * KT * 1024;
+        kt0 = KT * kc / KC;
+        nk = KT * (kc + 1) / KC - kt0;
+      },
+      [&](int u, float (&acc)[kNT][4]) {
+        const int s = u / KC, kc = u - s * KC;
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int c = nt * 8 + 2 * t4 + e;
-        if (c < p.B) {
-          p.part[(static_cast<size_t>(kc) * rows + s * 16 + g) * p.B + c] = acc[nt][e];
-          p.part[(static_cast<size_t>(kc) * rows + s * 16 + g + 8) * p.B + c] = acc[nt][2 + e];
+        for (int nt = 0; nt < kNT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = nt * 8 + 2 * t4 + e;
+            if (c < p.B) {
+              p.part[(static_cast<size_t>(kc) * rows + s * 16 + g) * p.B + c] = acc[nt][e];
+              p.part[(static_cast<size_t>(kc) * rows + s * 16 + g + 8) * p.B + c] = acc[nt][2 + e];
+            }
+          }
         }
-      }
-    }
-  }
+      });
 }
 
 __device__ __forceinline__ int seq_pos(const Params& p, int b) {
@@ -755,9 +943,29 @@ __device__ __noinline__ void attention_combine(const Params& p, const Layer& lw)
   }
 }
 
-// C2 / G: residual additions over the grid (one thread per element).
+// C2 / G: residual additions over the grid (one thread per element).  With several ranks each
+// thread first stores its elements of this rank's partial into every rank's region, then adds
+// the ranks' partials in rank order (the O-projection bias once, after the sum).
 __device__ __noinline__ void oproj_residual(const Params& p, const Layer& lw, int layer) {
   const int n = p.B * p.H;
+  if (p.n_ranks > 1) {
+    const unsigned x = xseq_of(p, 0, layer);
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) {
+      const int b = i / p.H, r = i - b * p.H;
+      float s = 0.f;
+      for (int kc = 0; kc < p.kc_o; ++kc) s += nkm::ldcg_f(p.part + (static_cast<size_t>(kc) * p.H + r) * p.B + b);
+      put_part(p, 0, x, i, s);
+    }
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) {
+      const int r = i % p.H;
+      float s;
+      if (!rank_sum(p, 0, x, i, s)) return;
+      const float v = nkm::ldcg_f(p.resid + i) + __fadd_rn(s, __bfloat162float(__ushort_as_bfloat16(lw.bo[r])));
+      p.resid[i] = v;
+      if (p.tr_mid) p.tr_mid[static_cast<size_t>(layer - p.first_layer) * n + i] = v;
+    }
+    return;
+  }
   for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) {
     const int b = i / p.H, r = i - b * p.H;
     float s = 0.f;
@@ -877,9 +1085,11 @@ __device__ __noinline__ void routing(const Params& p, Route* rt, int layer) {
   if (i < NP) atomicAdd(&rt->cnt[rt->topk_idx[i]], 1);
   __syncthreads();
   if (threadIdx.x == 0) {  // active experts ascending; cnt[e] becomes the pair offset of expert e
+    // (with several ranks only this rank's experts [expert_begin, expert_begin + n_local) enter)
     int off = 0, na = 0;
+    const int e_lo = p.expert_begin, e_hi = p.expert_begin + p.n_local;
     for (int e = 0; e < E; ++e) {
-      const int n = rt->cnt[e];
+      const int n = (e >= e_lo && e < e_hi) ? rt->cnt[e] : 0;
       rt->cnt[e] = off;
       if (n > 0) {
         rt->act_e[na] = e;
@@ -896,10 +1106,13 @@ __device__ __noinline__ void routing(const Params& p, Route* rt, int layer) {
     const int e = rt->topk_idx[i], t = i / K;
     int rank = 0;
     for (int j = 0; j < i; ++j) rank += rt->topk_idx[j] == e;
+    const bool local = e >= p.expert_begin && e < p.expert_begin + p.n_local;
     const int pr = rt->cnt[e] + rank;
-    rt->pair_tok[pr] = t;
-    rt->pair_w[pr] = rt->topk_w[i];
-    rt->pair_of[i] = pr;
+    if (local) {
+      rt->pair_tok[pr] = t;
+      rt->pair_w[pr] = rt->topk_w[i];
+    }
+    rt->pair_of[i] = local ? pr : -1;
     if (blockIdx.x == 0 && p.tr_idx) {
       p.tr_idx[static_cast<size_t>(layer - p.first_layer) * NP + i] = e;
       p.tr_w[static_cast<size_t>(layer - p.first_layer) * NP + i] = rt->topk_w[i];
@@ -910,22 +1123,61 @@ __device__ __noinline__ void routing(const Params& p, Route* rt, int layer) {
 
 // E: gate/up units (active expert j, 16-row strip s of the interleaved 2I rows): the expert's
 // tokens gathered from the f16 rows in shared memory; bias, clamp, SwiGLU; h (f16) per pair.
-__device__ __noinline__ void expert_gateup(const Params& p, const Layer& lw, const Route* rt, const uint16_t* xs) {
+// Warp gw takes units gw, gw + nw, ...; their weights and scales stream through the warp's ring
+// (kRingSlots chunks of kCK k-tiles in flight, across unit boundaries).
+__device__ __noinline__ void expert_gateup(const Params& p, const Layer& lw, const Route* rt, const uint16_t* xs,
+                                           const Ring& R) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
-  const int S = 2 * p.I / 16, KT = p.H / 32, nunits = rt->nA * S;
+  const int S = 2 * p.I / 16, KT = p.H / 32, NC = (KT + kCK - 1) / kCK, nunits = rt->nA * S;
   const size_t ebytes = static_cast<size_t>(2 * p.I) * p.H / 2, ssb = fp4_strip_scale_bytes(KT), sbytes = S * ssb;
+  const uint64_t pol = nkm::policy_evict_first();
+  uint32_t phase = *R.phase, inflight = 0;
+  int pu = gw, pc = 0;  // producer: unit and chunk of the next copy
+  auto issue = [&](int slot) {
+    if (pu >= nunits) return;
+    const int j = pu / S, s = pu - j * S, e = rt->act_e[j] - p.expert_begin;  // this rank's expert index
+    const int nk = min(kCK, KT - pc * kCK);
+    if (lane == 0)
+      ring_issue(R, slot, lw.w13 + e * ebytes + static_cast<size_t>(s) * KT * 256 + static_cast<size_t>(pc) * kCK * 256,
+                 lw.s13 + e * sbytes + s * ssb + static_cast<size_t>(pc) * (kCK / 8) * 128, nk, pol);
+    inflight |= 1u << slot;
+    if (++pc == NC) {
+      pc = 0;
+      pu += nw;
+    }
+  };
+#pragma unroll
+  for (int sl = 0; sl < kRingSlots; ++sl) issue(sl);
+  int cs = 0;
+  bool ok = true;
 #pragma unroll 1
-  for (int u = gw; u < nunits; u += nw) {
-    const int j = u / S, s = u - j * S, e = rt->act_e[j];
-    if (lane == 0 && u + nw < nunits) {  // the next unit's weights and scales into L2
-      const int j2 = (u + nw) / S, s2 = (u + nw) - j2 * S, e2 = rt->act_e[j2];
-      nkm::prefetch_l2_bulk(lw.w13 + e2 * ebytes + static_cast<size_t>(s2) * KT * 256, static_cast<uint32_t>(KT) * 256u);
-      nkm::prefetch_l2_bulk(lw.s13 + e2 * sbytes + s2 * ssb, static_cast<uint32_t>(ssb));
+  for (int u = gw; u < nunits && ok; u += nw) {
+    const int j = u / S, s = u - j * S, e = rt->act_e[j] - p.expert_begin;
+    const int* cols = rt->pair_tok + rt->act_off[j];
+    const int ncols = rt->act_cnt[j];
+    const uint16_t* brow[kNT];
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt) {
+      const int c = nt * 8 + g;
+      brow[nt] = c < ncols ? xs + static_cast<size_t>(cols[c]) * (p.H + 8) + 8 * t4 : nullptr;
     }
     float acc[kNT][4] = {};
-    ft_fp4(lw.w13 + e * ebytes + static_cast<size_t>(s) * KT * 256, lw.s13 + e * sbytes + s * ssb, KT, xs, p.H + 8,
-           rt->pair_tok + rt->act_off[j], rt->act_cnt[j], acc);
+#pragma unroll 1
+    for (int c = 0; c < NC; ++c) {
+      if (!ring_wait(p, R, cs, (phase >> cs) & 1u)) {
+        ok = false;
+        break;
+      }
+      phase ^= 1u << cs;
+      inflight &= ~(1u << cs);
+      if (ncols > 8) fp4_slot<2>(R.buf + cs * kSlotBytes, min(kCK, KT - c * kCK), c * kCK, brow, acc);
+      else fp4_slot<1>(R.buf + cs * kSlotBytes, min(kCK, KT - c * kCK), c * kCK, brow, acc);
+      __syncwarp();
+      issue(cs);
+      cs = cs + 1 == kRingSlots ? 0 : cs + 1;
+    }
+    if (!ok) break;
     // rows 16 s + g (even: gate, odd: up) pair up across lanes g, g ^ 1
     const int r0 = 16 * s + g, r1 = r0 + 8;
     const float b0 = __bfloat162float(__ushort_as_bfloat16(lw.b13[static_cast<size_t>(e) * 2 * p.I + r0]));
@@ -937,7 +1189,7 @@ __device__ __noinline__ void expert_gateup(const Params& p, const Layer& lw, con
         const float v0 = acc[nt][ee] + b0, v1 = acc[nt][2 + ee] + b1;
         const float w0 = __shfl_xor_sync(0xffffffffu, v0, 4), w1 = __shfl_xor_sync(0xffffffffu, v1, 4);
         const int c = nt * 8 + 2 * t4 + ee;
-        if ((g & 1) == 0 && c < rt->act_cnt[j]) {
+        if ((g & 1) == 0 && c < ncols) {
           const int pr = rt->act_off[j] + c;
           // (v0: gate row r0, w0: up row r0 + 1), (v1: gate row r1, w1: up row r1 + 1)
           const float gate0 = fminf(v0, p.limit), up0 = fminf(fmaxf(w0, -p.limit), p.limit);
@@ -951,23 +1203,65 @@ __device__ __noinline__ void expert_gateup(const Params& p, const Layer& lw, con
       }
     }
   }
+  if (!ok) ring_drain(R, inflight, phase);
+  if (lane == 0) *R.phase = phase;
+  __syncwarp();
 }
 
 // F: down projection.  The nA x H/16 (expert, 16-row strip) units in expert-major order are split
 // into contiguous ranges, one per CTA, so a CTA meets at most a few experts: for each it copies the
 // expert's h rows (f16, written in stage E by other CTAs) into shared memory once and its warps
-// take the expert's strips of its range; y = acc + bias, times the pair's routing weight -> ypair.
-__device__ __noinline__ void expert_down(const Params& p, const Layer& lw, const Route* rt, uint16_t* hs) {
+// take the expert's strips of its range (warp w: the range's strips w, w + 8, ... of that expert);
+// y = acc + bias, times the pair's routing weight -> ypair.  Each warp's weights stream through its
+// ring in the order it computes them, across strips and experts (the copies do not depend on h).
+__device__ __noinline__ void expert_down(const Params& p, const Layer& lw, const Route* rt, uint16_t* hs,
+                                         const Ring& R) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3, warp = threadIdx.x >> 5;
-  const int S = p.H / 16, KT = p.I / 32, NS = rt->nA * S;
+  const int S = p.H / 16, KT = p.I / 32, NC = (KT + kCK - 1) / kCK, NS = rt->nA * S;
   const size_t ebytes = static_cast<size_t>(p.H) * p.I / 2, ssb = fp4_strip_scale_bytes(KT), sbytes = S * ssb;
   const int hstride = p.I + 8;
   const int lo = static_cast<int>((static_cast<long long>(NS) * blockIdx.x) / gridDim.x);
   const int hi = static_cast<int>((static_cast<long long>(NS) * (blockIdx.x + 1)) / gridDim.x);
+  // this warp's units in computing order: its first unit in the expert segments from `seg` on,
+  // and the unit after st (-1: none)
+  auto first_from = [&](int seg) {
+#pragma unroll 1
+    while (seg < hi) {
+      const int e_end = min(hi, (seg / S + 1) * S);
+      if (seg + warp < e_end) return seg + warp;
+      seg = e_end;
+    }
+    return -1;
+  };
+  auto next_unit = [&](int st) {
+    const int seg_end = min(hi, (st / S + 1) * S);
+    return st + kWarps < seg_end ? st + kWarps : first_from(seg_end);
+  };
+  const int first = first_from(lo);
+  const uint64_t pol = nkm::policy_evict_first();
+  uint32_t phase = *R.phase, inflight = 0;
+  int pu = first, pc = 0;
+  auto issue = [&](int slot) {
+    if (pu < 0) return;
+    const int j = pu / S, s = pu - j * S, e = rt->act_e[j] - p.expert_begin;
+    const int nk = min(kCK, KT - pc * kCK);
+    if (lane == 0)
+      ring_issue(R, slot, lw.w2 + e * ebytes + static_cast<size_t>(s) * KT * 256 + static_cast<size_t>(pc) * kCK * 256,
+                 lw.s2 + e * sbytes + s * ssb + static_cast<size_t>(pc) * (kCK / 8) * 128, nk, pol);
+    inflight |= 1u << slot;
+    if (++pc == NC) {
+      pc = 0;
+      pu = next_unit(pu);
+    }
+  };
+#pragma unroll
+  for (int sl = 0; sl < kRingSlots; ++sl) issue(sl);
+  int cs = 0;
+  bool ok = true;
 #pragma unroll 1
   for (int seg = lo; seg < hi;) {
     const int j = seg / S, seg_end = min(hi, (j + 1) * S);
-    const int e = rt->act_e[j], off = rt->act_off[j], n = rt->act_cnt[j];
+    const int e = rt->act_e[j] - p.expert_begin, off = rt->act_off[j], n = rt->act_cnt[j];
     __syncthreads();  // the previous expert's rows are no longer read
     for (int i = threadIdx.x; i < n * (p.I / 8); i += kThreads) {
       const int r = i / (p.I / 8), k = (i - r * (p.I / 8)) * 8;
@@ -975,17 +1269,31 @@ __device__ __noinline__ void expert_down(const Params& p, const Layer& lw, const
           nkm::ldcg128(p.hbuf + static_cast<size_t>(off + r) * p.I + k);
     }
     __syncthreads();
+    const uint16_t* brow[kNT];
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt) {
+      const int c = nt * 8 + g;
+      brow[nt] = c < n ? hs + static_cast<size_t>(c) * hstride + 8 * t4 : nullptr;
+    }
 #pragma unroll 1
-    for (int st = seg + warp; st < seg_end; st += kWarps) {
+    for (int st = seg + warp; st < seg_end && ok; st += kWarps) {
       const int s = st - j * S;
-      if (lane == 0 && st + kWarps < seg_end) {  // the next strip's weights and scales into L2
-        nkm::prefetch_l2_bulk(lw.w2 + e * ebytes + static_cast<size_t>(s + kWarps) * KT * 256,
-                              static_cast<uint32_t>(KT) * 256u);
-        nkm::prefetch_l2_bulk(lw.s2 + e * sbytes + (s + kWarps) * ssb, static_cast<uint32_t>(ssb));
-      }
       float acc[kNT][4] = {};
-      ft_fp4(lw.w2 + e * ebytes + static_cast<size_t>(s) * KT * 256, lw.s2 + e * sbytes + s * ssb, KT, hs, hstride,
-             nullptr, n, acc);
+#pragma unroll 1
+      for (int c = 0; c < NC; ++c) {
+        if (!ring_wait(p, R, cs, (phase >> cs) & 1u)) {
+          ok = false;
+          break;
+        }
+        phase ^= 1u << cs;
+        inflight &= ~(1u << cs);
+        if (n > 8) fp4_slot<2>(R.buf + cs * kSlotBytes, min(kCK, KT - c * kCK), c * kCK, brow, acc);
+        else fp4_slot<1>(R.buf + cs * kSlotBytes, min(kCK, KT - c * kCK), c * kCK, brow, acc);
+        __syncwarp();
+        issue(cs);
+        cs = cs + 1 == kRingSlots ? 0 : cs + 1;
+      }
+      if (!ok) break;
       const int r0 = 16 * s + g, r1 = r0 + 8;
       const float b0 = __bfloat162float(__ushort_as_bfloat16(lw.b2[static_cast<size_t>(e) * p.H + r0]));
       const float b1 = __bfloat162float(__ushort_as_bfloat16(lw.b2[static_cast<size_t>(e) * p.H + r1]));
@@ -1004,10 +1312,35 @@ __device__ __noinline__ void expert_down(const Params& p, const Layer& lw, const
     }
     seg = seg_end;
   }
+  if (!ok) ring_drain(R, inflight, phase);
+  if (lane == 0) *R.phase = phase;
+  __syncwarp();
 }
 
 __device__ __noinline__ void moe_residual(const Params& p, const Route* rt, int layer) {
   const int n = p.B * p.H;
+  if (p.n_ranks > 1) {
+    // this rank's experts' slots (in slot order; the other slots are other ranks') to every rank,
+    // then the ranks' sums in rank order
+    const unsigned x = xseq_of(p, 1, layer);
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) {
+      const int b = i / p.H, r = i - b * p.H;
+      float s = 0.f;
+      for (int k = 0; k < p.K; ++k) {
+        const int pr = rt->pair_of[b * p.K + k];
+        if (pr >= 0) s += nkm::ldcg_f(p.ypair + static_cast<size_t>(pr) * p.H + r);
+      }
+      put_part(p, 1, x, i, s);
+    }
+    for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) {
+      float s;
+      if (!rank_sum(p, 1, x, i, s)) return;
+      const float v = nkm::ldcg_f(p.resid + i) + s;
+      p.resid[i] = v;
+      if (p.tr_out) p.tr_out[static_cast<size_t>(layer - p.first_layer) * n + i] = v;
+    }
+    return;
+  }
   for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) {
     const int b = i / p.H, r = i - b * p.H;
     float s = 0.f;
@@ -1018,25 +1351,68 @@ __device__ __noinline__ void moe_residual(const Params& p, const Route* rt, int 
   }
 }
 
-// LM head: one warp per 16-row strip of the vocabulary (whole K).
-__device__ __noinline__ void lm_head(const Params& p, const uint16_t* xs) {
+// LM head: one warp per 16-row strip of this rank's part of the vocabulary (whole K).  With
+// several ranks the logits go as tagged words into every rank's region (lm_copy gathers them).
+__device__ __noinline__ void lm_head(const Params& p, const uint16_t* xs, const Ring& R) {
   const int lane = lane_id(), g = lane >> 2, t4 = lane & 3;
   const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
-  const int S = p.V / 16, KT = p.H / 32;
+  const int KT = p.H / 32;
+  const bool multi = p.n_ranks > 1;
+  const unsigned x = multi ? xseq_of(p, 2, 0) : 0u;
+  const uint16_t* brow[kNT];
+#pragma unroll
+  for (int nt = 0; nt < kNT; ++nt) brow[nt] = nt * 8 + g < p.B ? xs + static_cast<size_t>(nt * 8 + g) * (p.H + 8) + 8 * t4 : nullptr;
+  stream_bf16(
+      p, R, gw, nw, p.lm_ns, brow, p.B,
+      [&](int u, const uint8_t*& base, int& kt0, int& nk) {
+        base = p.lm_head + static_cast<size_t>(p.lm_s0 + u) * KT * 1024;
+        kt0 = 0;
+        nk = KT;
+      },
+      [&](int u, float (&acc)[kNT][4]) {
+        const int s = p.lm_s0 + u;
+#pragma unroll
+        for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+          for (int ee = 0; ee < 2; ++ee) {
+            const int c = nt * 8 + 2 * t4 + ee;
+            if (c < p.B) {
+              const size_t i0 = static_cast<size_t>(c) * p.V + 16 * s + g;
+              if (multi) {
+                const unsigned long long w0 = xword(x, acc[nt][ee]), w1 = xword(x, acc[nt][2 + ee]);
 #pragma unroll 1
-  for (int s = gw; s < S; s += nw) {
-    float acc[kNT][4] = {};
-    ft_bf16(p.lm_head + static_cast<size_t>(s) * KT * 1024, 0, KT, xs, p.H + 8, nullptr, p.B, acc);
+                for (int q = 0; q < p.n_ranks; ++q) {
+                  nkm::st_relaxed_sys_u64(xw_logits(p, q, x) + i0, w0);
+                  nkm::st_relaxed_sys_u64(xw_logits(p, q, x) + i0 + 8, w1);
+                }
+              } else {
+                p.logits_out[i0] = acc[nt][ee];
+                p.logits_out[i0 + 8] = acc[nt][2 + ee];
+              }
+            }
+          }
+      });
+}
+
+// Several ranks: every rank's logits, from this rank's region into logits_out (each word waited
+// for until it carries this launch's tag).
+__device__ __noinline__ void lm_copy(const Params& p) {
+  const unsigned x = xseq_of(p, 2, 0);
+  const unsigned long long* src = xw_logits(p, p.rank, x);
+  const size_t n = static_cast<size_t>(p.B) * p.V, st = static_cast<size_t>(gridDim.x) * kThreads;
+  constexpr int U = 8;  // independent loads in flight per thread
+  for (size_t i0 = blockIdx.x * static_cast<size_t>(kThreads) + threadIdx.x; i0 < n; i0 += U * st) {
+    unsigned long long w[U];
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt)
+    for (int u = 0; u < U; ++u) w[u] = i0 + u * st < n ? nkm::ld_relaxed_sys_u64(src + i0 + u * st) : 0ull;
 #pragma unroll
-      for (int ee = 0; ee < 2; ++ee) {
-        const int c = nt * 8 + 2 * t4 + ee;
-        if (c < p.B) {
-          p.logits_out[static_cast<size_t>(c) * p.V + 16 * s + g] = acc[nt][ee];
-          p.logits_out[static_cast<size_t>(c) * p.V + 16 * s + g + 8] = acc[nt][2 + ee];
-        }
-      }
+    for (int u = 0; u < U; ++u) {
+      const size_t i = i0 + u * st;
+      if (i >= n) break;
+      float v = __uint_as_float(static_cast<unsigned>(w[u]));
+      if (static_cast<unsigned>(w[u] >> 32) != x + 1u && !take_word(p, src + i, x, v)) return;
+      p.logits_out[i] = v;
+    }
   }
 }
 
@@ -1055,6 +1431,16 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
   float* rstd = reinterpret_cast<float*>(smem + lay.rstd_off);
   Route* rt = reinterpret_cast<Route*>(smem + lay.route_off);
   int* flag = reinterpret_cast<int*>(smem + lay.flag_off);
+  const int warp_i = threadIdx.x >> 5;
+  const Ring ring{smem + lay.ring_off + warp_i * kRingSlots * kSlotBytes,
+                  reinterpret_cast<uint64_t*>(smem + lay.bar_off) + warp_i * kRingSlots,
+                  reinterpret_cast<uint32_t*>(smem + lay.phase_off) + warp_i};
+  if (lane_id() == 0) {
+    for (int sl = 0; sl < kRingSlots; ++sl) nkm::mbar_init(&ring.bar[sl], 1);
+    *ring.phase = 0u;
+    nkm::fence_mbar_init();
+  }
+  __syncthreads();
   unsigned bar_k = 0;
   if (p.tr_stage && blockIdx.x == 0 && threadIdx.x == 0) p.tr_stage[0] = static_cast<int64_t>(globaltimer_ns());
 
@@ -1087,7 +1473,7 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
       // A
       norm_rows(p, lw.ln1, xs, rstd, false);
       __syncthreads();
-      dense_splitk(p, lw.wqkv, p.R, p.H / 32, p.kc_qkv, xs, p.H + 8);
+      dense_splitk(p, lw.wqkv, p.R, p.H / 32, p.kc_qkv, xs, p.H + 8, ring);
       if (!grid_sync(p, bar_k, flag)) return;
       qkv_finalize(p, lw, layer);  // A2
       if (!grid_sync(p, bar_k, flag)) return;
@@ -1103,7 +1489,7 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
           *reinterpret_cast<uint4*>(xs + static_cast<size_t>(t) * stride + k) = v;
         }
         __syncthreads();
-        dense_splitk(p, lw.wo, p.H, Kq / 32, p.kc_o, xs, stride);
+        dense_splitk(p, lw.wo, p.H, Kq / 32, p.kc_o, xs, stride, ring);
       }
       if (!grid_sync(p, bar_k, flag)) return;
       oproj_residual(p, lw, layer);  // C2
@@ -1113,9 +1499,9 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
       router_logits(p, lw, layer, rstd);
       if (!grid_sync(p, bar_k, flag)) return;
       routing(p, rt, layer);  // E
-      expert_gateup(p, lw, rt, xs);
+      expert_gateup(p, lw, rt, xs, ring);
       if (!grid_sync(p, bar_k, flag)) return;
-      expert_down(p, lw, rt, xs);  // F (the f16 rows of stage D are no longer needed)
+      expert_down(p, lw, rt, xs, ring);  // F (the f16 rows of stage D are no longer needed)
       if (!grid_sync(p, bar_k, flag)) return;
       moe_residual(p, rt, layer);  // G
       if (!grid_sync(p, bar_k, flag)) return;
@@ -1130,7 +1516,8 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
     if (p.want_lm) {
       norm_rows(p, p.final_norm, xs, rstd, false);
       __syncthreads();
-      lm_head(p, xs);
+      lm_head(p, xs, ring);
+      if (p.n_ranks > 1) lm_copy(p);
     }
     __syncthreads();
     if (p.tr_stage && blockIdx.x == 0 && threadIdx.x == 0) p.tr_stage[bar_k + 1] = static_cast<int64_t>(globaltimer_ns());
@@ -1140,6 +1527,11 @@ __global__ void __launch_bounds__(kThreads, 1) gptoss_decode_kernel(const __grid
   if (threadIdx.x == 0) {
     const unsigned old = nkm::atom_acqrel_add_u32(p.bar + 2, 1u);
     if (old == gridDim.x - 1) {
+      if (p.n_ranks > 1) {  // the exchanges this launch took (every other CTA has left it)
+        p.xseq[0] += static_cast<unsigned>(p.num_layers);
+        p.xseq[1] += static_cast<unsigned>(p.num_layers);
+        if (p.want_lm) p.xseq[2] += 1u;
+      }
       *reinterpret_cast<volatile unsigned*>(p.bar) = 0u;
       *reinterpret_cast<volatile unsigned*>(p.bar + 2) = 0u;
     }

@@ -121,9 +121,13 @@ class GptOssMegakernel:
     def __init__(self, shape: GptOssShape, layers: Sequence[GptOssGpuLayer], *, max_batch: int, num_blocks: int,
                  max_context: int, final_norm: Optional[torch.Tensor] = None, lm_head: Optional[torch.Tensor] = None,
                  embed: Optional[torch.Tensor] = None, device=None, kv_fp8: bool = False, k_scale: float = 1.0,
-                 v_scale: float = 1.0):
+                 v_scale: float = 1.0, shard=None, xchg=None):
         """``kv_fp8``: the K/V pools hold e4m3 bytes (``uint8``): stored = e4m3(clip(x * scale,
-        +-240)), read = stored / scale."""
+        +-240)), read = stored / scale.  ``shard`` (``sharding.RankShard``) and ``xchg``
+        (``sharding.XchgRegion`` of ``sharding.gptoss_xchg_bytes``) make this instance one rank of
+        a tensor + expert parallel group: ``shape`` then carries the rank's head counts and
+        ``layers`` its heads and experts (``sharding.shard_gptoss_layer``), while
+        ``num_local_experts`` stays the model's expert count."""
         self.shape = shape
         self.device = torch.device(device if device is not None else "cuda")
         self.layers = list(layers)
@@ -150,6 +154,19 @@ class GptOssMegakernel:
             ctypes.cast(self.rope_sin.data_ptr(), ctypes.POINTER(ctypes.c_float)), self.rope_max,
             self.k_pool.data_ptr(), self.v_pool.data_ptr(), num_blocks, shape.block_size, max_batch, max_context,
             int(kv_fp8), k_scale, v_scale)
+        self.shard = shard
+        if shard is not None and shard.world > 1:
+            if xchg is None:
+                raise ValueError("a rank of a parallel group needs its exchange region")
+            self._desc.n_ranks, self._desc.rank = shard.world, shard.rank
+            self._desc.expert_begin, self._desc.n_local_experts = shard.expert_begin, shard.n_local_experts
+            for q, ptr_q in enumerate(xchg.ptrs):
+                self._desc.xchg[q] = ptr_q
+            need = lib().nkm_gptoss_xchg_bytes(ctypes.byref(self._desc))
+            if need == 0 or need > xchg.nbytes:
+                raise _lib.NkmError(_lib.NKM_ERR_ARG, f"exchange region of {xchg.nbytes} bytes, need {need}")
+        else:
+            self._desc.n_ranks, self._desc.n_local_experts = 1, shape.num_local_experts
         nbytes = lib().nkm_gptoss_workspace_bytes(ctypes.byref(self._desc))
         if nbytes == 0:
             raise _lib.NkmError(_lib.NKM_ERR_ARG, "nkm_gptoss_workspace_bytes")

@@ -133,3 +133,30 @@ def _check(err, what):
     code = int(err) if not isinstance(err, tuple) else int(err[0])
     if code != 0:
         raise RuntimeError(f"{what} failed with CUDA error {code}")
+
+
+def shard_gptoss_layer(t: dict, shard: RankShard, head_dim: int) -> dict:
+    """The rank's part of one GPT-OSS layer (the tensor names of ``GptOssGpuLayer``): query,
+    key and value rows and biases of its heads, O-projection columns and sink logits of its query
+    heads, and its experts' MXFP4 codes, scales and biases.  Norms and router stay whole."""
+    o = dict(t)
+    o["wq"], o["wk"], o["wv"], o["wo"] = shard_attention(t["wq"], t["wk"], t["wv"], t["wo"], shard, head_dim)
+    o["bq"] = _rows(t["bq"], shard.q_heads, head_dim)
+    o["bk"] = _rows(t["bk"], shard.kv_heads, head_dim)
+    o["bv"] = _rows(t["bv"], shard.kv_heads, head_dim)
+    o["sinks"] = t["sinks"][torch.tensor(shard.q_heads, device=t["sinks"].device)].contiguous()
+    sl = slice(shard.expert_begin, shard.expert_begin + shard.n_local_experts)
+    for k in ("gu_codes", "gu_scales", "gu_b", "dn_codes", "dn_scales", "dn_b"):
+        o[k] = t[k][sl].contiguous()
+    return o
+
+
+def gptoss_xchg_bytes(hidden: int, max_batch: int, world: int, vocab: int) -> int:
+    """Bytes of one rank's GPT-OSS exchange region (``nkm_gptoss_xchg_bytes``): a 256-byte
+    header, the partials as tagged 8-byte words [2 kinds][2 slots][world][max_batch][hidden] and,
+    with several ranks, the logits as tagged words [2 slots][max_batch][vocab]."""
+    a = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    n = a(256 + 4 * world * max_batch * hidden * 8)
+    if world > 1:
+        n += 2 * max_batch * vocab * 8
+    return a(n)

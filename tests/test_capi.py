@@ -132,6 +132,8 @@ int main(void) {
   printf("sample %zu\n", sizeof(nkm_sample_params));
   printf("desc.layers %zu\n", offsetof(nkm_gptoss_desc, layers));
   printf("desc.max_context %zu\n", offsetof(nkm_gptoss_desc, max_context));
+  printf("desc.n_ranks %zu\n", offsetof(nkm_gptoss_desc, n_ranks));
+  printf("desc.xchg %zu\n", offsetof(nkm_gptoss_desc, xchg));
   printf("step.trace_topk_w %zu\n", offsetof(nkm_gptoss_step, trace_topk_w));
   printf("layer.sliding %zu\n", offsetof(nkm_gptoss_layer, sliding));
   return 0;
@@ -150,12 +152,16 @@ int main(void) {
     assert int(got["sample"]) == ctypes.sizeof(L.nkm_sample_params)
     assert int(got["desc.layers"]) == L.nkm_gptoss_desc.layers.offset
     assert int(got["desc.max_context"]) == L.nkm_gptoss_desc.max_context.offset
+    assert int(got["desc.n_ranks"]) == L.nkm_gptoss_desc.n_ranks.offset
+    assert int(got["desc.xchg"]) == L.nkm_gptoss_desc.xchg.offset
     assert int(got["step.trace_topk_w"]) == L.nkm_gptoss_step.trace_topk_w.offset
     assert int(got["layer.sliding"]) == L.nkm_gptoss_layer.sliding.offset
 
 
 def test_gptoss_create_rejects_bad_descriptions(L):
-    for bad in (dict(head_dim=128), dict(hidden=2000), dict(max_batch=17), dict(top_k=9), dict(inter=100)):
+    for bad in (dict(head_dim=128), dict(hidden=2000), dict(max_batch=17), dict(top_k=9), dict(inter=100),
+                dict(n_ranks=9), dict(n_ranks=2, rank=0, n_local_experts=16),  # no exchange regions
+                dict(expert_begin=4), dict(n_ranks=2, rank=2)):
         base = dict(hidden=2880, hidden_actual=0, n_q_heads=64, n_kv_heads=8, head_dim=64, n_experts=32, top_k=4,
                     inter=2880, n_layers=1, vocab=0, rms_eps=1e-5, swiglu_limit=7.0, swiglu_alpha=1.702,
                     sliding_window=128, block_size=128, max_batch=16, max_context=4096)
@@ -187,3 +193,27 @@ def test_xchg_bytes_match_host_sizing(L, world):
     assert need == xchg_bytes(H, B, world, V)
     if world > 1:
         assert need >= B * V * 4 + 2 * world * B * H * 4
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_gptoss_xchg_bytes_match_host_sizing(L, world):
+    """GPT-OSS: the host's exchange-region size (``sharding.gptoss_xchg_bytes``) is the library's."""
+    from nki_moe_megakernel_b200.sharding import gptoss_xchg_bytes
+
+    H, B, V = 2880, 16, 201088
+    base = dict(hidden=H, hidden_actual=0, n_q_heads=64 // world, n_kv_heads=8 // world, head_dim=64, n_experts=32,
+                top_k=4, inter=2880, n_layers=1, vocab=V, rms_eps=1e-5, swiglu_limit=7.0, swiglu_alpha=1.702,
+                sliding_window=128, block_size=128, max_batch=B, max_context=4096, n_ranks=world, rank=world - 1,
+                expert_begin=32 // world * (world - 1), n_local_experts=32 // world)
+    d = L.nkm_gptoss_desc()
+    for k, v in base.items():
+        setattr(d, k, v)
+    layer = (L.nkm_gptoss_layer * 1)()
+    d.layers = layer
+    if world > 1:
+        for q in range(world):
+            d.xchg[q] = 256 * (q + 1)  # only validated for alignment, never dereferenced here
+    need = L.lib().nkm_gptoss_xchg_bytes(ctypes.byref(d))
+    assert need == gptoss_xchg_bytes(H, B, world, V)
+    if world > 1:
+        assert need >= 2 * B * V * 8 + 4 * world * B * H * 8

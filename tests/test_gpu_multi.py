@@ -242,3 +242,105 @@ def test_wide_expert_parallel_matches_single_gpu(tmp_path, world):
         c = O.compare(got, want)
         print(f"[wide EP world {world} rank {rank}] vs single GPU {c}, beyond one ulp {excess:.3g}", flush=True)
         assert excess <= ATOL and c["cosine"] >= COS, (rank, c, excess)
+
+
+def _gptoss_worker(rank, world, port, out_dir):
+    """GPT-OSS at full width (2 layers: sliding then full), B=4, across `world` ranks: heads and
+    experts split, LM head split over the vocabulary; rank 0 also runs the single-GPU kernel."""
+    import datetime
+
+    from nki_moe_megakernel_b200.gpt_oss_engine import GptOssGpuLayer, GptOssMegakernel, GptOssShape
+    from nki_moe_megakernel_b200.sharding import XchgRegion, gptoss_xchg_bytes, plan_shard, shard_gptoss_layer
+    from oracle import gpt_oss_oracle as G
+    from tests.qwen_cases import BF16, make_kv
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180))
+    cfg = G.GptOssConfig(n_layers=2)
+    gen = torch.Generator().manual_seed(951)
+    lws = [G.random_layer(cfg, gen) for _ in range(2)]
+    fnorm = (1.0 + 0.1 * torch.randn(cfg.hidden, generator=gen)).to(BF16)
+    lm = (0.02 * torch.randn(V, cfg.hidden, generator=gen)).to(BF16)
+    positions = [300, 17, 128, 1000]
+    B = len(positions)
+    NB = sum(p // 128 + 1 for p in positions) + 2
+    k0, v0, table = make_kv(cfg, 2, positions, NB, seed=952)
+    vt0 = v0.transpose(-1, -2).contiguous()
+    x = torch.randn(B, cfg.hidden, generator=gen).to(BF16)
+    pos = torch.tensor(positions, dtype=torch.int32)
+    keys = ("wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "sinks", "ln1", "ln2", "router", "router_b", "gu_codes",
+            "gu_scales", "gu_b", "dn_codes", "dn_scales", "dn_b")
+
+    def shape(nq, nkv):
+        return GptOssShape(hidden_size=cfg.hidden, num_attention_heads=nq, num_key_value_heads=nkv,
+                           head_dim=cfg.head_dim, num_local_experts=cfg.n_experts, num_experts_per_tok=cfg.top_k,
+                           intermediate_size=cfg.inter, num_hidden_layers=2, vocab_size=V, rms_norm_eps=cfg.rms_eps,
+                           sliding_window=cfg.sliding_window)
+
+    shard = plan_shard(rank, world, cfg.n_q_heads, cfg.n_kv_heads, cfg.n_experts)
+    layers = []
+    for i, lw in enumerate(lws):
+        t = shard_gptoss_layer({k: getattr(lw, k) for k in keys}, shard, cfg.head_dim)
+        layers.append(GptOssGpuLayer({k: v.to(dev) for k, v in t.items()}, cfg.is_sliding(i)))
+    xchg = XchgRegion(gptoss_xchg_bytes(cfg.hidden, B, world, V), rank, world, rank)
+    eng = GptOssMegakernel(shape(len(shard.q_heads), len(shard.kv_heads)), layers, max_batch=B, num_blocks=NB,
+                           max_context=1152, final_norm=fnorm.to(dev), lm_head=lm.to(dev), device=dev, shard=shard,
+                           xchg=xchg)
+    eng.k_pool.copy_(k0[:, :, shard.kv_heads].to(dev))
+    eng.v_pool.copy_(vt0[:, :, shard.kv_heads].to(dev))
+    dist.barrier()
+    outs, logits = [], []
+    for _ in range(2):
+        res = eng.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=True)
+        torch.cuda.synchronize()
+        outs.append(res["hidden"].cpu())
+        logits.append(res["logits"].cpu())
+    result = {"status": eng.status(), "hidden": outs, "logits": logits}
+    if rank == 0:
+        full = [GptOssGpuLayer({k: getattr(lw, k).to(dev) for k in keys}, cfg.is_sliding(i)) for i, lw in enumerate(lws)]
+        ref = GptOssMegakernel(shape(cfg.n_q_heads, cfg.n_kv_heads), full, max_batch=B, num_blocks=NB,
+                               max_context=1152, final_norm=fnorm.to(dev), lm_head=lm.to(dev), device=dev)
+        ref.k_pool.copy_(k0.to(dev))
+        ref.v_pool.copy_(vt0.to(dev))
+        r = ref.decode_step(pos.to(dev), table.to(dev), x=x.to(dev), want_logits=True)
+        torch.cuda.synchronize()
+        result.update(ref_status=ref.status(), ref_hidden=r["hidden"].cpu(), ref_logits=r["logits"].cpu())
+        ref.close()
+    torch.save(result, os.path.join(out_dir, f"g{rank}.pt"))
+    dist.barrier()
+    eng.close()
+    xchg.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gptoss_ranks_match_single_gpu(tmp_path, world):
+    """Config 4 across GPUs: every rank reports status 0, the ranks' hidden states and logits
+    are bit-identical to each other and over two steps, and within max-abs 2e-2 / cosine 0.999
+    of the single-GPU kernel (itself pinned against the fp32 oracle in test_gpu_gpt_oss.py)."""
+    from oracle import qwen3_moe_oracle as O
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.spawn(_gptoss_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    rs = [torch.load(tmp_path / f"g{r}.pt") for r in range(world)]
+    r0 = rs[0]
+    assert all(r["status"] == 0 for r in rs) and r0["ref_status"] == 0
+    for r in rs[1:]:
+        for a, b in zip(r0["hidden"] + r0["logits"], r["hidden"] + r["logits"]):
+            assert torch.equal(a, b), "ranks disagree"
+    assert torch.equal(r0["hidden"][0], r0["hidden"][1]) and torch.equal(r0["logits"][0], r0["logits"][1])
+    # the hidden rows are bf16 of a residual that grows to tens: the ranks' rank-order sums may
+    # round a value to the other bf16 neighbour, so the bound applies beyond one bf16 ulp
+    h, hr = r0["hidden"][0].float(), r0["ref_hidden"].float()
+    ulp = torch.exp2(torch.floor(torch.log2(hr.abs().clamp_min(1e-30))) - 7)
+    excess = float(((h - hr).abs() - ulp).clamp_min(0).max())
+    c = O.compare(h, hr)
+    print(f"[gpt-oss x{world}] hidden {c} (beyond one bf16 ulp: {excess:.4g})")
+    assert excess <= ATOL and c["cosine"] >= COS, (c, excess)
+    c = O.compare(r0["logits"][0], r0["ref_logits"])
+    print(f"[gpt-oss x{world}] logits {c}")
+    assert c["max_abs"] <= ATOL and c["cosine"] >= COS, c

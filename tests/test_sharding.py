@@ -53,6 +53,34 @@ def test_shard_weights_slices():
     assert torch.equal(g, gu[4:]) and torch.equal(d, dn[4:])
 
 
+@pytest.mark.parametrize("world", [2, 8])
+def test_gptoss_layer_shards_cover_the_layer(world):
+    """GPT-OSS (64 query / 8 KV heads of 64, 32 experts): the ranks' query/key/value rows and
+    biases, O-projection columns, sinks and experts put back together give the whole layer, and
+    each rank's query heads are the ones of its KV heads."""
+    from nki_moe_megakernel_b200.sharding import shard_gptoss_layer
+
+    D, H, E = 64, 4, 32
+    g = torch.Generator().manual_seed(0)
+    t = {"wq": torch.randn(64 * D, H, generator=g), "bq": torch.randn(64 * D, generator=g),
+         "wk": torch.randn(8 * D, H, generator=g), "bk": torch.randn(8 * D, generator=g),
+         "wv": torch.randn(8 * D, H, generator=g), "bv": torch.randn(8 * D, generator=g),
+         "wo": torch.randn(H, 64 * D, generator=g), "sinks": torch.randn(64, generator=g),
+         "ln1": torch.randn(H, generator=g)}
+    for k in ("gu_codes", "gu_scales", "gu_b", "dn_codes", "dn_scales", "dn_b"):
+        t[k] = torch.randn(E, 3, generator=g)
+    parts = [shard_gptoss_layer(t, plan_shard(r, world, 64, 8, E), D) for r in range(world)]
+    for k in ("wq", "bq", "wk", "bk", "wv", "bv", "sinks", "gu_codes", "gu_scales", "gu_b", "dn_codes", "dn_scales",
+              "dn_b"):
+        assert torch.equal(torch.cat([p[k] for p in parts], 0), t[k]), k
+    assert torch.equal(torch.cat([p["wo"] for p in parts], 1), t["wo"])
+    assert all(torch.equal(p["ln1"], t["ln1"]) for p in parts)
+    for r, p in enumerate(parts):
+        s = plan_shard(r, world, 64, 8, E)
+        assert s.q_heads == [h * 8 + j for h in s.kv_heads for j in range(8)]
+        assert p["wq"].shape[0] == len(s.q_heads) * D and p["gu_codes"].shape[0] == E // world
+
+
 def _free_port():
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
