@@ -217,13 +217,35 @@ def _wide_ep_worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
+ROUTE_GAP = 2e-2  # router near tie: the k-th and (k+1)-th plain-fp32 logits closer than this
+
+
+def _near_tie_rows(idx_a: torch.Tensor, idx_b: torch.Tensor, mid: torch.Tensor, lw, cfg) -> tuple:
+    """Rows whose top-k sets differ, and whether every such row is a router near tie on the
+    reference's post-attention rows ``mid`` (plain fp32 RMSNorm + router)."""
+    from oracle import qwen3_moe_oracle as O
+
+    sa, sb = torch.sort(idx_a.long(), -1).values, torch.sort(idx_b.long(), -1).values
+    diff = (sa != sb).any(-1).nonzero().flatten().tolist()
+    if not diff:
+        return [], True
+    logits = O.rmsnorm_fp32(mid[diff].float(), lw.ln2, cfg.rms_eps) @ lw.router.float().t()
+    top = torch.sort(logits, -1, descending=True).values
+    gaps = top[:, cfg.top_k - 1] - top[:, cfg.top_k]
+    return diff, bool((gaps < ROUTE_GAP).all())
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_wide_expert_parallel_matches_single_gpu(tmp_path, world):
     """Config 3 across GPUs (B=64, attention rows split, experts split, exchange over NVLink peer
-    stores): every rank's rows equal the single-GPU B=64 step within max-abs 2e-2 beyond one bf16
-    ulp (the MoE partials are summed per rank, then in rank order), routing equal, two steps in a
-    row identical."""
+    stores): two steps in a row identical on every rank; every rank's rows equal the single-GPU
+    B=64 step within max-abs 2e-2 beyond one bf16 ulp (the MoE partials are summed per rank, then
+    in rank order).  Routing: at 2 ranks (32 rows per rank, the single-GPU step's attention
+    launch) the expert sets are equal; with fewer rows per rank the attention GEMVs split their
+    sums differently, and a row's expert set may differ only at a router near tie (such a row is
+    then left out of the hidden comparison from that layer on; at most a quarter of a rank's rows)."""
     from oracle import qwen3_moe_oracle as O
+    from tests.qwen_cases import make_layers, qwen_cfg
 
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -231,16 +253,26 @@ def test_wide_expert_parallel_matches_single_gpu(tmp_path, world):
     rs = [torch.load(tmp_path / f"ep{r}.pt") for r in range(world)]
     ref = rs[0]["ref"]
     R = 64 // world
+    cfg = qwen_cfg(n_layers=2)
+    lws = make_layers(cfg, 2, seed=71)  # the workers' weights
     for rank, r in enumerate(rs):
         a, b = r["outs"]
         assert torch.equal(a["hidden"], b["hidden"]), "second step differs"
         rows = slice(rank * R, (rank + 1) * R)
-        assert torch.equal(a["topk_idx"].long(), ref["topk_idx"][:, rows].long())
-        got, want = a["hidden"].float(), ref["hidden"][rows].float()
+        flipped = set()
+        for li in range(a["topk_idx"].shape[0]):
+            diff, near = _near_tie_rows(a["topk_idx"][li], ref["topk_idx"][li][rows], ref["resid_mid"][li][rows],
+                                        lws[li], cfg)
+            assert not diff or (R != 32 and near), (rank, li, diff)
+            flipped.update(diff)
+        keep = [i for i in range(R) if i not in flipped]
+        assert len(flipped) <= R // 4, (rank, sorted(flipped))
+        got, want = a["hidden"][keep].float(), ref["hidden"][rows][keep].float()
         ulp = torch.exp2(torch.floor(torch.log2(want.abs().clamp_min(1e-30))) - 7)
         excess = float(((got - want).abs() - ulp).clamp_min(0).max())
         c = O.compare(got, want)
-        print(f"[wide EP world {world} rank {rank}] vs single GPU {c}, beyond one ulp {excess:.3g}", flush=True)
+        print(f"[wide EP world {world} rank {rank}] vs single GPU {c}, beyond one ulp {excess:.3g}; rows with a "
+              f"near-tie routing difference: {sorted(flipped)}", flush=True)
         assert excess <= ATOL and c["cosine"] >= COS, (rank, c, excess)
 
 
